@@ -1,0 +1,430 @@
+"""GSA layer forward throughput on B200 (tokens/s), 128K-context workload.
+
+Workload (one "step"): one GatedSparseAttention forward, d_model 4096, 32 query / 8 KV heads of
+128, 8 indexer heads of 64, k_base 2048 (k_min 256, k_max 4096, adaptive), value and output gates
+on, bf16, batch 1 x 131072 tokens, x ~ N(0,1), weights from the default init with seed 0.
+With N > 1 GPUs (torchrun) the query sequence is sharded: rank r owns a contiguous block of
+131072 / N tokens, K / V / indexer keys are all-gathered over NCCL and the adaptive-k variance
+sum is all-reduced; ``value`` is 131072 / (max over ranks of the step time).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--seq-len L]
+
+``--impl reference`` times the reference algorithm's CPU path (the oracle restatement of the
+reference's PyTorch ops, oracle/gsa_oracle.py) on the host cores, sampled and extrapolated.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "gated-sparse-attention_b200"))
+
+import torch  # noqa: E402
+
+WORKLOAD = dict(d_model=4096, n_heads=32, n_kv_heads=8, d_indexer=64, n_indexer_heads=8,
+                k_base=2048, k_min=256, k_max=4096)
+METRIC = "GSA layer fwd tokens/sec at 128K ctx (1/2/4/8 B200); % HBM / tensor roofline"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+# ---------------------------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------------------
+# distributed helpers
+# ---------------------------------------------------------------------------------------------
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+
+    t = torch.tensor([v], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------------------------
+def sdpa_algorithmic_bytes(cfg, cnt: torch.Tensor) -> float:
+    """Bytes the sparse SDPA must move: the gathered K and V rows (Hk*D bf16 each per selected
+    key), q / gate read and out write (H*D bf16 each per row), and the int32 indices."""
+    Hk, H, D = cfg.n_kv_heads, cfg.n_heads, cfg.d_head
+    sum_k = float(cnt.double().sum().item())
+    rows = cnt.numel()
+    return sum_k * (2 * Hk * D * 2 + 4) + rows * 3 * H * D * 2
+
+
+def run_ours(args, world, rank):
+    from gsa_b200 import GSAConfig, GatedSparseAttention, ops
+    from gsa_b200.sharded import enable_query_sharding
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    L = args.seq_len
+    cfg = GSAConfig(**WORKLOAD, max_position_embeddings=max(131072, L))
+    torch.manual_seed(0)
+    m = GatedSparseAttention(cfg).eval().to(torch.bfloat16).to(dev)
+    if world > 1:
+        import torch.distributed as dist
+
+        enable_query_sharding(m, dist.group.WORLD)
+    assert L % world == 0
+    Lr = L // world
+    gen = torch.Generator().manual_seed(1)
+    x_full = torch.randn(1, L, cfg.d_model, generator=gen, dtype=torch.float32)
+    x_host = x_full[:, rank * Lr:(rank + 1) * Lr].to(torch.bfloat16).contiguous().pin_memory()
+    del x_full
+    x = x_host.to(dev)
+    torch.cuda.synchronize()
+
+    def step():
+        return m(x)[0]
+
+    # warm-up
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    ops.check_device_error()
+
+    # timed region (device events), clocks sampled meanwhile
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index if world == 1 else int(os.environ.get("LOCAL_RANK", "0"))) as clk:
+        barrier(world)
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(args.steps):
+            step()
+        end.record()
+        torch.cuda.synchronize()
+        barrier(world)
+    ms_local = start.elapsed_time(end) / args.steps
+    ms = max_over_ranks(ms_local, world)
+    value = L / (ms / 1e3)
+
+    # end to end through the public API: pinned host x -> device, layer, output -> host
+    out_host = torch.empty(1, Lr, cfg.d_model, dtype=torch.bfloat16).pin_memory()
+    barrier(world)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        xd = x_host.to(dev, non_blocking=True)
+        out = m(xd)[0]
+        out_host.copy_(out, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    e2e = {"value": L / (e2e_ms / 1e3), "unit": "tokens/s",
+           "h2d_bytes_per_step": x_host.numel() * x_host.element_size() * world,
+           "d2h_bytes_per_step": out_host.numel() * out_host.element_size() * world,
+           "ms_per_step": e2e_ms}
+
+    # stage breakdown and the SDPA kernel alone (roofline)
+    cap = {}
+    marks = []
+
+    def mark(name):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        marks.append((name, ev))
+
+    with torch.no_grad():
+        e_start = torch.cuda.Event(enable_timing=True)
+        e_start.record()
+        m._forward_impl(x, None, None, False, False, mark=mark, capture=cap)
+    torch.cuda.synchronize()
+    stages, prev = {}, e_start
+    for name, ev in marks:
+        stages[name] = round(prev.elapsed_time(ev), 3)
+        prev = ev
+    n_chunks = cap["n_chunks"]
+    launches_per_step = 1 + 2 * n_chunks + (3 if cfg.use_adaptive_k else 1) + 1 + 1
+    sdpa_bytes = sdpa_algorithmic_bytes(cfg, cap["cnt"])
+    reps = 3
+    s0 = torch.cuda.Event(enable_timing=True)
+    s1 = torch.cuda.Event(enable_timing=True)
+    with torch.no_grad():
+        ops.sparse_sdpa(cap["dims"], cap["q"], cap["k"], cap["v"], cap["sel"], cap["cnt"], cap["gate"], m.scale)
+        torch.cuda.synchronize()
+        s0.record()
+        for _ in range(reps):
+            ops.sparse_sdpa(cap["dims"], cap["q"], cap["k"], cap["v"], cap["sel"], cap["cnt"], cap["gate"],
+                            m.scale)
+        s1.record()
+        torch.cuda.synchronize()
+    sdpa_ms = s0.elapsed_time(s1) / reps
+    pk, pk_kind = peaks()
+    achieved = sdpa_bytes / (sdpa_ms / 1e3) / 1e9
+    traffic = None
+    prof = ROOT / "profiles" / "sparse_sdpa_traffic.json"
+    if prof.exists():
+        d = json.loads(prof.read_text())
+        # dram bytes per launch scale with the selected keys of the captured case
+        traffic = d.get("dram_bytes_per_algorithmic_byte", None)
+        if traffic is not None:
+            traffic = traffic * sdpa_bytes
+    roofline = {"kernel": "gsa::sdpa_tc_kernel<128,4>", "bound": "hbm", "achieved": round(achieved, 1),
+                "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
+                "peak_kind": pk_kind, "traffic": traffic, "algorithmic_bytes": sdpa_bytes,
+                "kernel_ms": round(sdpa_ms, 3), "mean_k": float(cap["cnt"].double().mean().item())}
+
+    clocks = clk.summary()
+    res = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: x ~ N(0,1) seed 1, default-init weights seed 0",
+        "config": {"workload": f"GSA layer fwd B=1 L={L} d4096 h32/8x128 idx8x64 k2048[256,4096] bf16",
+                   "batch": 1, "seq_len": L, "parallelism": f"query-sequence shards x{world}",
+                   "l2": "inputs larger than L2 (x 1 GiB, K/V 256 MiB each)"},
+        "e2e": e2e, "roofline": roofline, "gpu_launches": launches_per_step * args.steps,
+        "stages_ms": stages, "clocks": clocks,
+    }
+    return res
+
+
+# ---------------------------------------------------------------------------------------------
+# CPU path of the reference algorithm (oracle restatement), sampled and extrapolated
+# ---------------------------------------------------------------------------------------------
+def cpu_reference_estimate(L: int, proj_rows: int, chunk_rows: int, n_chunks: int, seed: int = 0):
+    """Seconds for one full-layer CPU forward at sequence length L, estimated from samples.
+
+    Timed with the oracle's restatement of the reference's torch ops (bf16, torch.no_grad):
+      * projections + G2 + RoPE + G1 logits + o_proj on ``proj_rows`` rows, scaled by L/rows;
+      * indexer + variance for ``n_chunks`` chunks of ``chunk_rows`` queries at evenly spaced
+        offsets, scaled by the causal (query, key) pair count;
+      * top-k + sparse attention for the same chunks, scaled by L / sampled rows.
+    Returns (seconds, description)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import torch.nn.functional as F
+
+    import gsa_oracle as O
+
+    torch.set_num_threads(len(os.sched_getaffinity(0)))
+    from gsa_b200 import GSAConfig, GatedSparseAttention
+
+    cfg = GSAConfig(**WORKLOAD)
+    torch.manual_seed(seed)
+    m = GatedSparseAttention(cfg).eval().to(torch.bfloat16)
+    W = {k: v for k, v in m.state_dict().items()}
+    oc = O.OracleConfig.from_config(cfg)
+    gen = torch.Generator().manual_seed(1)
+    dt = torch.bfloat16
+    H, Hk, D = cfg.n_heads, cfg.n_kv_heads, cfg.d_head
+    with torch.no_grad():
+        # 1. dense projections and gates, per row
+        xs = torch.randn(1, proj_rows, cfg.d_model, generator=gen).to(dt)
+        pos = torch.arange(proj_rows).unsqueeze(0)
+        t0 = time.perf_counter()
+        q, k, v = O.project(W, oc, xs, pos, m.rotary_emb.cos_cached, m.rotary_emb.sin_cached)
+        F.linear(xs, W["indexer.q_proj.weight"])
+        F.linear(xs, W["indexer.k_proj.weight"])
+        g = F.linear(xs, W["output_gate.gate_proj.weight"], W["output_gate.gate_proj.bias"])
+        gated = q * O.gate_activation(g.view(1, proj_rows, H, D), "sigmoid")
+        F.linear(gated.reshape(1, proj_rows, -1), W["o_proj.weight"])
+        t_proj = (time.perf_counter() - t0) * L / proj_rows
+        # 2./3. indexer, variance, top-k, sparse attention on sampled query chunks
+        kI = torch.randn(1, L, cfg.d_indexer, generator=gen).to(dt)
+        K = torch.randn(1, L, Hk, D, generator=gen).to(dt)
+        V = torch.randn(1, L, Hk, D, generator=gen).to(dt)
+        t_idx = t_sel = 0.0
+        pairs_sampled = 0
+        rows_sampled = 0
+        k_eff = min(cfg.k_max, L)
+        for c in range(n_chunks):
+            t_pos = int((c + 0.5) * L / n_chunks)
+            n_keys = t_pos + chunk_rows
+            xq = torch.randn(1, chunk_rows, cfg.d_model, generator=gen).to(dt)
+            t1 = time.perf_counter()
+            q_idx = F.linear(xq, W["indexer.q_proj.weight"]).view(1, chunk_rows, cfg.n_indexer_heads, cfg.d_indexer)
+            wts = torch.sigmoid(F.linear(xq, W["indexer.weight_proj.weight"], W["indexer.weight_proj.bias"]))
+            raw = torch.einsum("bqhd,bkd->bhqk", q_idx, kI[:, :n_keys]) * (1.0 / math.sqrt(cfg.d_indexer))
+            sc = (torch.sigmoid(raw + W["indexer.bias"].view(1, -1, 1, 1)) * wts.permute(0, 2, 1).unsqueeze(-1)).sum(1)
+            tt = torch.arange(chunk_rows).view(-1, 1) + t_pos
+            sc = sc.masked_fill((torch.arange(n_keys).view(1, -1) > tt).unsqueeze(0), float("-inf"))
+            full = torch.full((1, chunk_rows, L), float("-inf"), dtype=sc.dtype)
+            full[:, :, :n_keys] = sc
+            var, valid = O.row_variance(full)
+            t2 = time.perf_counter()
+            kv = O.adaptive_k(var, valid, var.mean(), cfg.k_base, cfg.k_min, cfg.k_max, 1.0)
+            idx, msk = O.topk_select(full, k_eff, kv)
+            qc = torch.randn(1, chunk_rows, H, D, generator=gen).to(dt)
+            O.sparse_attention(qc, K, V, idx, msk, cfg.n_heads // cfg.n_kv_heads, 1.0 / math.sqrt(D))
+            t3 = time.perf_counter()
+            t_idx += t2 - t1
+            t_sel += t3 - t2
+            pairs_sampled += sum(t_pos + i + 1 for i in range(chunk_rows))
+            rows_sampled += chunk_rows
+        total_pairs = L * (L + 1) / 2
+        est = t_proj + t_idx * total_pairs / pairs_sampled + t_sel * L / rows_sampled
+    desc = (f"sampled + extrapolated: projections/gates/o_proj on {proj_rows} rows x L/{proj_rows}; "
+            f"indexer+variance on {n_chunks} chunks of {chunk_rows} queries x causal pairs; "
+            f"top-k+sparse attention on the same chunks x L/{rows_sampled}")
+    return est, desc
+
+
+def run_reference(args, world, rank):
+    """Reference arm: the reference algorithm's CPU path, timed on this box's host cores."""
+    L = args.seq_len
+    samples = []
+    desc = ""
+    for i in range(args.warmup + args.steps):
+        est, desc = cpu_reference_estimate(L, proj_rows=64, chunk_rows=8, n_chunks=2, seed=0)
+        if i >= args.warmup:
+            samples.append(est)
+    sec = statistics.median(samples)
+    v = L / sec
+    cores = len(os.sched_getaffinity(0))
+    return {"metric": METRIC, "value": round(v, 3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 1), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: x ~ N(0,1), default-init weights seed 0",
+            "config": {"workload": f"GSA layer fwd B=1 L={L} d4096 h32/8x128 idx8x64 k2048[256,4096] bf16",
+                       "batch": 1, "seq_len": L, "parallelism": "host CPU"},
+            "impl": "reference",
+            "cpu_baseline": {"value": round(v, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
+                             "sample": desc},
+            "e2e": {"value": round(v, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--seq-len", type=int, default=131072)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        if rank != 0:
+            return
+        res = run_reference(args, world, rank)
+        res["n_gpus"] = world
+        print(json.dumps(res))
+        return
+
+    world, rank, local = dist_setup(args.gpus)
+    try:
+        res = run_ours(args, world, rank)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            est, desc = cpu_reference_estimate(args.seq_len, proj_rows=128, chunk_rows=16, n_chunks=2)
+            res["cpu_baseline"] = {"value": round(args.seq_len / est, 3), "unit": "tokens/s",
+                                   "cores": len(os.sched_getaffinity(0)), "kind": "port", "sample": desc}
+        if rank == 0:
+            print(json.dumps(res))
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,229 @@
+// extern "C" entry points of libgsa_b200.so: argument validation, launch configuration and
+// the chunked indexer + top-k loop.  Declarations and reference citations: include/gsa_b200.h.
+#include <mutex>
+
+#include "kernels.cuh"
+
+namespace gsa {
+
+__device__ int g_device_error;
+
+// ---------------------------------------------------------------------------------------------
+// Per-device state: address of the error word and the SM count.
+// ---------------------------------------------------------------------------------------------
+struct DeviceInfo {
+  int* err = nullptr;
+  int num_sms = 0;
+  bool ready = false;
+};
+static std::mutex g_mu;
+static DeviceInfo g_dev[64];
+
+static int device_info(DeviceInfo** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return GSA_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (!d.ready) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return GSA_ERR_CUDA;
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return GSA_ERR_CUDA;
+    d.err = static_cast<int*>(p);
+    d.num_sms = sms;
+    d.ready = true;
+  }
+  *out = &d;
+  return GSA_OK;
+}
+
+static bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+static bool dims_ok(const gsa_dims* d) {
+  return d && d->d_model > 0 && d->n_heads > 0 && d->n_kv_heads > 0 && d->n_heads % d->n_kv_heads == 0 &&
+         d->d_head > 0 && d->d_head % 2 == 0 && d->n_idx_heads > 0 && d->d_idx > 0;
+}
+
+}  // namespace gsa
+
+using namespace gsa;
+
+extern "C" {
+
+const char* gsa_version(void) { return "gsa_b200 0.1.0 (sm_100a)"; }
+
+int gsa_get_device_error(int* code_out, gsa_stream_t stream) {
+  DeviceInfo* di;
+  int st = device_info(&di);
+  if (st) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int h = 0;
+  if (cudaMemcpyAsync(&h, di->err, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess) return GSA_ERR_CUDA;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return GSA_ERR_CUDA;
+  if (cudaMemsetAsync(di->err, 0, sizeof(int), s) != cudaSuccess) return GSA_ERR_CUDA;
+  if (code_out) *code_out = h;
+  return GSA_OK;
+}
+
+int gsa_proj_epilogue(const gsa_dims* dims, const gsa_proj_layout* layout, int dtype, int64_t T,
+                      const void* proj, int64_t proj_ld, const int64_t* positions, const void* cos_tab,
+                      const void* sin_tab, int tab_dtype, int64_t tab_rows, void* q_out, void* k_out,
+                      void* v_out, void* g1_out, float* w_out, float* shift_out, gsa_stream_t stream) {
+  if (!dims_ok(dims) || !layout || T < 0 || (dtype != GSA_DTYPE_F32 && dtype != GSA_DTYPE_BF16) ||
+      (tab_dtype != GSA_DTYPE_F32 && tab_dtype != GSA_DTYPE_BF16))
+    return GSA_ERR_BAD_ARG;
+  if (T == 0) return GSA_OK;
+  if (!proj || !positions || !cos_tab || !sin_tab || !q_out || !k_out || !v_out || !w_out || !shift_out ||
+      tab_rows <= 0 || layout->q < 0 || layout->k < 0 || layout->v < 0 || layout->wi < 0)
+    return GSA_ERR_BAD_ARG;
+  if (dims->gate_act < GSA_ACT_SIGMOID || dims->gate_act > GSA_ACT_SILU) return GSA_ERR_UNSUPPORTED;
+  DeviceInfo* di;
+  int st = device_info(&di);
+  if (st) return st;
+  EpiArgs a{*dims, *layout, dtype, T, proj, proj_ld, positions, cos_tab, sin_tab, tab_dtype, tab_rows,
+            q_out, k_out, v_out, g1_out, w_out, shift_out, di->err};
+  return launch_proj_epilogue(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int gsa_indexer_scores(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int64_t Lkv, int64_t q_pos0,
+                       int causal, int write_masked, const void* qI, int64_t qi_ld, int64_t qi_bstride,
+                       const void* kI, int64_t ki_ld, int64_t ki_bstride, const float* w, const float* bias,
+                       float scale, const float* shift, float* scores, int64_t scores_ld, double* row_stats,
+                       gsa_stream_t stream) {
+  if (!dims_ok(dims) || B < 0 || Lq < 0 || Lkv < 0 || (dtype != GSA_DTYPE_F32 && dtype != GSA_DTYPE_BF16))
+    return GSA_ERR_BAD_ARG;
+  if (B == 0 || Lq == 0 || Lkv == 0) return GSA_OK;
+  if (!qI || !kI || !w || !bias || !scores || scores_ld < Lkv) return GSA_ERR_BAD_ARG;
+  if (dims->idx_act != GSA_ACT_SIGMOID && dims->idx_act != GSA_ACT_RELU) return GSA_ERR_UNSUPPORTED;
+  IdxArgs a{dtype, Lq, Lkv, q_pos0, causal, write_masked, dims->n_idx_heads, dims->d_idx, dims->idx_act,
+            qI, qi_ld, qi_bstride, kI, ki_ld, ki_bstride, w, bias, scale, shift, scores, scores_ld, row_stats};
+  return launch_indexer_simt(a, B, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int gsa_row_stats(int64_t R, int64_t n_cols, const float* scores, int64_t scores_ld, double* row_stats,
+                  gsa_stream_t stream) {
+  if (R < 0 || n_cols < 0 || scores_ld < n_cols) return GSA_ERR_BAD_ARG;
+  if (R == 0) return GSA_OK;
+  if (!scores || !row_stats) return GSA_ERR_BAD_ARG;
+  return launch_row_stats(R, n_cols, scores, scores_ld, row_stats, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int gsa_topk_candidates(int64_t R, int64_t Lq, int64_t n_cols, int64_t q_pos0, int causal, const float* scores,
+                        int64_t scores_ld, int32_t k_eff, int32_t* cand_idx, float* cand_score,
+                        int32_t* cand_count, gsa_stream_t stream) {
+  if (R < 0 || Lq <= 0 || n_cols < 0 || k_eff < 1 || scores_ld < n_cols || n_cols > 0x7fffffffLL)
+    return GSA_ERR_BAD_ARG;
+  if (R == 0) return GSA_OK;
+  if (!scores || !cand_idx || !cand_score || !cand_count) return GSA_ERR_BAD_ARG;
+  return launch_topk_candidates(R, Lq, n_cols, q_pos0, causal, scores, scores_ld, k_eff, cand_idx, cand_score,
+                                cand_count, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int gsa_row_variance(int64_t R, int64_t n_cols, int dtype, const double* row_stats, const float* shift,
+                     float* var_out, double* var_total, gsa_stream_t stream) {
+  if (R < 0 || n_cols < 0 || (dtype != GSA_DTYPE_F32 && dtype != GSA_DTYPE_BF16)) return GSA_ERR_BAD_ARG;
+  if (!var_total) return GSA_ERR_BAD_ARG;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (R == 0) {
+    return cudaMemsetAsync(var_total, 0, 2 * sizeof(double), s) == cudaSuccess ? GSA_OK : GSA_ERR_CUDA;
+  }
+  if (!row_stats || !var_out) return GSA_ERR_BAD_ARG;
+  return launch_row_variance(R, n_cols, dtype, row_stats, shift, var_out, var_total, s);
+}
+
+int gsa_adaptive_k(int64_t R, int64_t n_cols, int dtype, const gsa_topk_params* p, const float* var,
+                   const double* var_total, const double* row_stats, int32_t* k_out, gsa_stream_t stream) {
+  if (R < 0 || n_cols < 0 || !p || (dtype != GSA_DTYPE_F32 && dtype != GSA_DTYPE_BF16)) return GSA_ERR_BAD_ARG;
+  if (R == 0) return GSA_OK;
+  if (!k_out || (p->use_adaptive && (!var || !var_total || !row_stats))) return GSA_ERR_BAD_ARG;
+  return launch_adaptive_k(R, n_cols, dtype, *p, var, var_total, row_stats, k_out,
+                           reinterpret_cast<cudaStream_t>(stream));
+}
+
+int gsa_select_finalize(int64_t R, int32_t k_eff, const int32_t* cand_idx, const float* cand_score,
+                        const int32_t* cand_count, const int32_t* k, int32_t* sel_idx, int64_t sel_ld,
+                        int32_t* sel_count, uint8_t* sel_mask, gsa_stream_t stream) {
+  if (R < 0 || k_eff < 1 || sel_ld < k_eff) return GSA_ERR_BAD_ARG;
+  if (R == 0) return GSA_OK;
+  if (!cand_idx || !cand_score || !cand_count || !k || !sel_idx || !sel_count) return GSA_ERR_BAD_ARG;
+  return launch_select_finalize(R, k_eff, cand_idx, cand_score, cand_count, k, sel_idx, sel_ld, sel_count,
+                                sel_mask, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int gsa_apply_gate(int dtype, int act, int64_t n, const void* x, const void* logits, void* out, void* gate_out,
+                   gsa_stream_t stream) {
+  if (n < 0 || (dtype != GSA_DTYPE_F32 && dtype != GSA_DTYPE_BF16)) return GSA_ERR_BAD_ARG;
+  if (act < GSA_ACT_SIGMOID || act > GSA_ACT_SILU) return GSA_ERR_UNSUPPORTED;
+  if (n == 0) return GSA_OK;
+  if (!x || !logits || !out) return GSA_ERR_BAD_ARG;
+  return launch_apply_gate(dtype, act, n, x, logits, out, gate_out, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int gsa_sparse_sdpa(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int64_t Lkv, const void* q,
+                    const void* k, const void* v, const int32_t* sel_idx, int64_t sel_ld, const int32_t* sel_count,
+                    const void* gate, void* out, float scale, gsa_stream_t stream) {
+  if (!dims_ok(dims) || B < 0 || Lq < 0 || Lkv < 0 || sel_ld < 0) return GSA_ERR_BAD_ARG;
+  if (B * Lq == 0) return GSA_OK;
+  if (!q || !k || !v || !sel_idx || !sel_count || !out) return GSA_ERR_BAD_ARG;
+  DeviceInfo* di;
+  int st = device_info(&di);
+  if (st) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == GSA_DTYPE_BF16) {
+    if (!aligned(k, 16) || !aligned(v, 16) || !aligned(q, 4)) return GSA_ERR_BAD_ARG;
+    SdpaArgs a{B, Lq, Lkv, dims->n_kv_heads,
+               static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
+               static_cast<const __nv_bfloat16*>(v), sel_idx, sel_ld, sel_count,
+               static_cast<const __nv_bfloat16*>(gate), static_cast<__nv_bfloat16*>(out),
+               scale * 1.4426950408889634f, 0, di->err};
+    return launch_sdpa_bf16(a, dims->d_head, dims->n_heads / dims->n_kv_heads, di->num_sms, s);
+  }
+  if (dtype == GSA_DTYPE_F32) {
+    SdpaF32Args a{B, Lq, Lkv, dims->n_heads, dims->n_kv_heads, dims->d_head,
+                  static_cast<const float*>(q), static_cast<const float*>(k), static_cast<const float*>(v),
+                  sel_idx, sel_ld, sel_count, static_cast<const float*>(gate), static_cast<float*>(out),
+                  scale, di->err};
+    return launch_sdpa_f32(a, s);
+  }
+  return GSA_ERR_BAD_ARG;
+}
+
+int64_t gsa_workspace_size(int64_t chunk_rows, int64_t n_cols) {
+  if (chunk_rows <= 0 || n_cols <= 0) return 0;
+  const int64_t ld = (n_cols + 3) / 4 * 4;
+  return chunk_rows * ld * (int64_t)sizeof(float);
+}
+
+int gsa_indexer_select(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int64_t Lkv, int64_t q_pos0,
+                       int causal, const void* qI, int64_t qi_ld, int64_t qi_bstride, const void* kI,
+                       int64_t ki_ld, int64_t ki_bstride, const float* w, const float* bias, float scale,
+                       const float* shift, int32_t k_eff, int32_t* cand_idx, float* cand_score,
+                       int32_t* cand_count, double* row_stats, int64_t chunk_rows, void* workspace,
+                       int64_t workspace_bytes, gsa_stream_t stream) {
+  if (!dims_ok(dims) || B < 0 || Lq < 0 || Lkv < 0 || chunk_rows <= 0 || k_eff < 1) return GSA_ERR_BAD_ARG;
+  if (B * Lq == 0 || Lkv == 0) return GSA_OK;
+  if (workspace_bytes < gsa_workspace_size(chunk_rows, Lkv) || !workspace) return GSA_ERR_WORKSPACE;
+  if (!aligned(workspace, 16)) return GSA_ERR_BAD_ARG;
+  const int64_t ld = (Lkv + 3) / 4 * 4;
+  float* scratch = static_cast<float*>(workspace);
+  const size_t esz = dtype == GSA_DTYPE_BF16 ? 2 : 4;
+  const int HI = dims->n_idx_heads;
+  for (int64_t b = 0; b < B; ++b) {
+    for (int64_t t0 = 0; t0 < Lq; t0 += chunk_rows) {
+      const int64_t n = (Lq - t0) < chunk_rows ? (Lq - t0) : chunk_rows;
+      const int64_t r0 = b * Lq + t0;
+      const void* q_ptr = static_cast<const char*>(qI) + (b * qi_bstride + t0 * qi_ld) * (int64_t)esz;
+      const void* k_ptr = static_cast<const char*>(kI) + (b * ki_bstride) * (int64_t)esz;
+      int st = gsa_indexer_scores(dims, dtype, 1, n, Lkv, q_pos0 + t0, causal, 0, q_ptr, qi_ld, 0, k_ptr, ki_ld,
+                                  0, w + r0 * HI, bias, scale, shift ? shift + r0 : nullptr, scratch, ld,
+                                  row_stats ? row_stats + r0 * 3 : nullptr, stream);
+      if (st) return st;
+      st = gsa_topk_candidates(n, n, Lkv, q_pos0 + t0, causal, scratch, ld, k_eff, cand_idx + r0 * k_eff,
+                               cand_score + r0 * k_eff, cand_count + r0, stream);
+      if (st) return st;
+    }
+  }
+  return GSA_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,143 @@
+// Shared device helpers for the GSA sm_100a kernels: bf16 conversion, torch-compatible
+// rounding, mbarrier / bulk-copy PTX wrappers with bounded waits, and the error word.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "gsa_b200.h"
+
+namespace gsa {
+
+// ---------------------------------------------------------------------------------------------
+// Element access for the two activation dtypes (GSA_DTYPE_F32 / GSA_DTYPE_BF16).
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ float load_elem(const void* p, int64_t i, int dtype) {
+  if (dtype == GSA_DTYPE_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+  return reinterpret_cast<const float*>(p)[i];
+}
+
+__device__ __forceinline__ void store_elem(void* p, int64_t i, float v, int dtype) {
+  if (dtype == GSA_DTYPE_BF16) reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+  else reinterpret_cast<float*>(p)[i] = v;
+}
+
+// Round a float to the activation dtype and back.  torch evaluates each bf16 elementwise op
+// in fp32 and rounds the result to bf16; calling this after every op reproduces that.
+__device__ __forceinline__ float rnd(float v, int dtype) {
+  return dtype == GSA_DTYPE_BF16 ? __bfloat162float(__float2bfloat16_rn(v)) : v;
+}
+
+// fp32 ops that the compiler may not contract into FMAs (torch evaluates them one by one).
+__device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }
+
+// Logistic sigmoid evaluated as 1 / (1 + e^-x) with the accurate expf.
+__device__ __forceinline__ float sigmoid_precise(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+// Gate activations of the value / output gates (value_gate.py:98-106).
+__device__ __forceinline__ float gate_act(float x, int act, int dtype) {
+  if (act == GSA_ACT_SIGMOID) return rnd(sigmoid_precise(x), dtype);
+  if (act == GSA_ACT_TANH) {
+    float t = rnd(tanhf(x), dtype);
+    return rnd(rnd(t + 1.0f, dtype) / 2.0f, dtype);
+  }
+  // silu: x * sigmoid(x), evaluated by torch as one fused op
+  return rnd(x / (1.0f + expf(-x)), dtype);
+}
+
+// Monotone map of an fp32 bit pattern to an unsigned key: larger float -> larger key.
+__device__ __forceinline__ uint32_t float_key(float f) {
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Error word.  Kernels never trap: a failed bounded wait or a bad index sets a code here and
+// the kernel returns; the host reads it back through gsa_get_device_error().
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ void set_error(int* err, int code) {
+  if (err) atomicCAS(err, 0, code);
+}
+
+// ---------------------------------------------------------------------------------------------
+// mbarrier + bulk copy (TMA) wrappers.
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+                   smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: returns false (and records GSA_ERR_TIMEOUT) if the phase never completes.
+// Each try_wait suspends for a hardware-chosen interval, so the limit is generous in time.
+constexpr uint32_t kWaitLimit = 1u << 22;
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+  }
+  set_error(err, GSA_ERR_TIMEOUT);
+  return false;
+}
+
+// 1-D bulk copy global -> shared, completing on an mbarrier (both addresses 16-byte aligned,
+// size a multiple of 16).
+__device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------------------------
+// Block-wide helpers.
+// ---------------------------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ T warp_sum(T v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+}  // namespace gsa

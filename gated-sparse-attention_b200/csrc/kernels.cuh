@@ -1,0 +1,98 @@
+// Argument blocks and launchers of the GSA kernels, shared by the kernel translation units
+// and the C-ABI layer (abi.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace gsa {
+
+struct EpiArgs {
+  gsa_dims d;
+  gsa_proj_layout lay;
+  int dtype;
+  int64_t T;
+  const void* proj;
+  int64_t proj_ld;
+  const int64_t* positions;
+  const void* cos_tab;
+  const void* sin_tab;
+  int tab_dtype;
+  int64_t tab_rows;
+  void* q_out;
+  void* k_out;
+  void* v_out;
+  void* g1_out;
+  float* w_out;
+  float* shift_out;
+  int* err;
+};
+
+struct IdxArgs {
+  int dtype;
+  int64_t Lq, Lkv, q_pos0;
+  int causal, write_masked;
+  int HI, dI, act;
+  const void* qI;
+  int64_t qi_ld, qi_bstride;
+  const void* kI;
+  int64_t ki_ld, ki_bstride;
+  const float* w;
+  const float* bias;
+  float scale;
+  const float* shift;
+  float* scores;
+  int64_t scores_ld;
+  double* row_stats;
+};
+
+struct SdpaArgs {
+  int64_t B, Lq, Lkv;
+  int Hk;
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  const int32_t* sel_idx;
+  int64_t sel_ld;
+  const int32_t* sel_count;
+  const __nv_bfloat16* gate;
+  __nv_bfloat16* out;
+  float scale_log2;
+  int nstages;
+  int* err;
+};
+
+struct SdpaF32Args {
+  int64_t B, Lq, Lkv;
+  int H, Hk, D;
+  const float* q;
+  const float* k;
+  const float* v;
+  const int32_t* sel_idx;
+  int64_t sel_ld;
+  const int32_t* sel_count;
+  const float* gate;
+  float* out;
+  float scale;
+  int* err;
+};
+
+int launch_proj_epilogue(const EpiArgs& a, cudaStream_t stream);
+int launch_apply_gate(int dtype, int act, int64_t n, const void* x, const void* logits, void* out, void* gate_out,
+                      cudaStream_t stream);
+int launch_indexer_simt(const IdxArgs& a, int64_t B, cudaStream_t stream);
+int launch_topk_candidates(int64_t R, int64_t Lq, int64_t n_cols, int64_t q_pos0, int causal, const float* scores,
+                           int64_t ld, int32_t k_eff, int32_t* cand_idx, float* cand_score, int32_t* cand_count,
+                           cudaStream_t stream);
+int launch_select_finalize(int64_t R, int32_t k_eff, const int32_t* cand_idx, const float* cand_score,
+                           const int32_t* cand_count, const int32_t* k, int32_t* sel_idx, int64_t sel_ld,
+                           int32_t* sel_count, uint8_t* sel_mask, cudaStream_t stream);
+int launch_row_stats(int64_t R, int64_t n_cols, const float* scores, int64_t ld, double* stats,
+                     cudaStream_t stream);
+int launch_row_variance(int64_t R, int64_t n_cols, int dtype, const double* stats, const float* shift,
+                        float* var_out, double* total, cudaStream_t stream);
+int launch_adaptive_k(int64_t R, int64_t n_cols, int dtype, const gsa_topk_params& p, const float* var,
+                      const double* var_total, const double* stats, int32_t* k_out, cudaStream_t stream);
+int launch_sdpa_bf16(SdpaArgs a, int D, int nrep, int num_sms, cudaStream_t stream);
+int launch_sdpa_f32(const SdpaF32Args& a, cudaStream_t stream);
+
+}  // namespace gsa

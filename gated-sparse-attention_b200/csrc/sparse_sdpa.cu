@@ -1,0 +1,356 @@
+// GQA sparse SDPA with the G1 output gate fused into the epilogue
+// (gated_sparse_attention.py:234-290, output_gate.py:124-126).
+//
+// For every row r = (b, t): one set of sel_count[r] key positions is shared by all heads
+// (gated_sparse_attention.py:239, 265-266).  A selected key row is the contiguous
+// [Hk, D] slice of K (and of V): 2 KiB each at 8 x 128 bf16.  The kernel is HBM-bound on
+// those gathers, so it is built around moving whole key rows:
+//
+//   * one producer warp issues one 1-D bulk copy (cp.async.bulk, TMA engine) per selected K
+//     row and per V row into a shared-memory ring of stages (16 keys per stage), completing
+//     on the stage's mbarrier; rows are padded by 16 bytes so ldmatrix reads are conflict free;
+//   * one consumer warp per KV group computes S^T = K_g Q_g^T with mma.sync (keys are the M
+//     dimension, the n_rep query heads of the group the N dimension), an online softmax in
+//     registers, transposes P with movmatrix and accumulates O^T += V_g^T P^T;
+//   * the epilogue divides by the softmax sum, multiplies by the G1 gate and stores.
+//
+// CTAs are persistent (grid = resident CTAs), each walks rows r = blockIdx.x + i * gridDim.x
+// and keeps its copy pipeline running across row boundaries.  All waits are bounded.
+#include "kernels.cuh"
+
+namespace gsa {
+
+constexpr int kKeysPerStage = 16;
+constexpr int kMaxRowBytes = 16 * 256 * 2;
+__device__ __align__(128) uint8_t g_zero_row[kMaxRowBytes];
+
+
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ uint32_t movm_t(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+__device__ __forceinline__ void mma_bf16(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ int row_count(const SdpaArgs& a, int64_t row) {
+  int c = a.sel_count[row];
+  if (c < 0) c = 0;
+  if (c > a.sel_ld) c = (int)a.sel_ld;
+  return c;
+}
+
+template <int D, int NREP>
+__global__ void __launch_bounds__(17 * 32) sdpa_tc_kernel(SdpaArgs a) {
+  static_assert(D % 16 == 0 && NREP >= 1 && NREP <= 8, "tile shape");
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int Hk = a.Hk;
+  const int row_bytes = Hk * D * 2;
+  const int rs = row_bytes + 16;
+  const int stage_bytes = 2 * kKeysPerStage * rs;
+  const int nst = a.nstages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + nst;
+  uint8_t* stages = smem + 256;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t R = a.B * a.Lq;
+  const int H = Hk * NREP;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < nst; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], (uint32_t)Hk);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == Hk) {
+    // ------------------------------ producer warp ------------------------------
+    uint32_t it = 0;
+    bool ok = true;
+    for (int64_t row = blockIdx.x; row < R && ok; row += gridDim.x) {
+      const int64_t b = row / a.Lq;
+      const int cnt = row_count(a, row);
+      const int32_t* idx = a.sel_idx + row * a.sel_ld;
+      const uint8_t* kbase = reinterpret_cast<const uint8_t*>(a.k) + b * a.Lkv * row_bytes;
+      const uint8_t* vbase = reinterpret_cast<const uint8_t*>(a.v) + b * a.Lkv * row_bytes;
+      const int nkb = (cnt + kKeysPerStage - 1) / kKeysPerStage;
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const int s = it % nst;
+        const uint32_t ph = (it / nst) & 1u;
+        if (!mbar_wait(&empty[s], ph ^ 1u, a.err)) { ok = false; break; }
+        if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(2 * kKeysPerStage * row_bytes));
+        __syncwarp();
+        const int slot = lane & 15;
+        const int key = kb * kKeysPerStage + slot;
+        const uint8_t* src = g_zero_row;
+        if (key < cnt) {
+          const int32_t j = idx[key];
+          if (j >= 0 && j < a.Lkv) src = (lane < 16 ? kbase : vbase) + (int64_t)j * row_bytes;
+          else set_error(a.err, GSA_ERR_INDEX);
+        }
+        uint8_t* dst = stages + s * stage_bytes + (lane < 16 ? 0 : kKeysPerStage * rs) + slot * rs;
+        bulk_g2s(dst, src, (uint32_t)row_bytes, &full[s]);
+      }
+    }
+    // drain: every issued copy must land before the CTA may exit
+    const uint32_t first = it > (uint32_t)nst ? it - (uint32_t)nst : 0u;
+    for (uint32_t i = first; i < it; ++i) mbar_wait(&full[i % nst], (i / nst) & 1u, a.err);
+    return;
+  }
+
+  // -------------------------------- consumer warps --------------------------------
+  const int g = warp;
+  const int grp = lane >> 2, tq = lane & 3;
+  const int mi = lane >> 3, r8 = lane & 7;
+  uint32_t it = 0;
+  for (int64_t row = blockIdx.x; row < R; row += gridDim.x) {
+    const int cnt = row_count(a, row);
+    const __nv_bfloat16* qrow = a.q + (row * H + (int64_t)g * NREP) * D;
+    uint32_t qf[D / 16][2];
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      if (grp < NREP) {
+        qf[kk][0] = *reinterpret_cast<const uint32_t*>(qrow + grp * D + kk * 16 + tq * 2);
+        qf[kk][1] = *reinterpret_cast<const uint32_t*>(qrow + grp * D + kk * 16 + tq * 2 + 8);
+      } else {
+        qf[kk][0] = 0u;
+        qf[kk][1] = 0u;
+      }
+    }
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    float o[D / 16][4];
+#pragma unroll
+    for (int mt = 0; mt < D / 16; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+
+    const int nkb = (cnt + kKeysPerStage - 1) / kKeysPerStage;
+    bool ok = true;
+    for (int kb = 0; kb < nkb; ++kb, ++it) {
+      const int s = it % nst;
+      const uint32_t ph = (it / nst) & 1u;
+      if (!mbar_wait(&full[s], ph, a.err)) { ok = false; break; }
+      const uint8_t* Ks = stages + s * stage_bytes;
+      const uint8_t* Vs = Ks + kKeysPerStage * rs;
+      float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const int key = r8 + ((mi & 1) ? 8 : 0);
+        const int dim = kk * 16 + ((mi & 2) ? 8 : 0);
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(smem_u32(Ks + key * rs + (g * D + dim) * 2), a0, a1, a2, a3);
+        mma_bf16(c, a0, a1, a2, a3, qf[kk][0], qf[kk][1]);
+      }
+      const int valid = cnt - kb * kKeysPerStage;
+      const bool v0 = grp < valid, v1 = grp + 8 < valid;
+      float x0 = v0 ? c[0] * a.scale_log2 : -INFINITY;
+      float x1 = v0 ? c[1] * a.scale_log2 : -INFINITY;
+      float x2 = v1 ? c[2] * a.scale_log2 : -INFINITY;
+      float x3 = v1 ? c[3] * a.scale_log2 : -INFINITY;
+      float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+      }
+      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+      const float corr0 = exp2f(m0 - mn0), corr1 = exp2f(m1 - mn1);
+      const float p0 = exp2f(x0 - mn0), p1 = exp2f(x1 - mn1);
+      const float p2 = exp2f(x2 - mn0), p3 = exp2f(x3 - mn1);
+      l0 = l0 * corr0 + p0 + p2;
+      l1 = l1 * corr1 + p1 + p3;
+      m0 = mn0;
+      m1 = mn1;
+#pragma unroll
+      for (int mt = 0; mt < D / 16; ++mt) {
+        o[mt][0] *= corr0;
+        o[mt][1] *= corr1;
+        o[mt][2] *= corr0;
+        o[mt][3] *= corr1;
+      }
+      const uint32_t b0 = movm_t(pack_bf16(p0, p1));
+      const uint32_t b1 = movm_t(pack_bf16(p2, p3));
+#pragma unroll
+      for (int mt = 0; mt < D / 16; ++mt) {
+        const int key = r8 + ((mi & 2) ? 8 : 0);
+        const int dim = mt * 16 + ((mi & 1) ? 8 : 0);
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4_t(smem_u32(Vs + key * rs + (g * D + dim) * 2), a0, a1, a2, a3);
+        mma_bf16(o[mt], a0, a1, a2, a3, b0, b1);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    if (!ok) return;
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+      l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+    }
+    const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f;
+    const float inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
+    const int h0 = tq * 2, h1 = tq * 2 + 1;
+#pragma unroll
+    for (int mt = 0; mt < D / 16; ++mt) {
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int dim = mt * 16 + grp + half * 8;
+        if (h0 < NREP) {
+          const int64_t off = (row * H + g * NREP + h0) * D + dim;
+          float y = __bfloat162float(__float2bfloat16_rn(o[mt][half * 2 + 0] * inv0));
+          if (a.gate) y *= __bfloat162float(a.gate[off]);
+          a.out[off] = __float2bfloat16_rn(y);
+        }
+        if (h1 < NREP) {
+          const int64_t off = (row * H + g * NREP + h1) * D + dim;
+          float y = __bfloat162float(__float2bfloat16_rn(o[mt][half * 2 + 1] * inv1));
+          if (a.gate) y *= __bfloat162float(a.gate[off]);
+          a.out[off] = __float2bfloat16_rn(y);
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Precise fp32 kernel: one warp per (row, head), exact expf, fp32 accumulation.  Used for the
+// layer's fp32 configuration.
+// ---------------------------------------------------------------------------------------------
+
+
+__global__ void sdpa_f32_kernel(SdpaF32Args a) {
+  const int64_t row = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nw = blockDim.x >> 5;
+  const int64_t b = row / a.Lq;
+  const int n_rep = a.H / a.Hk;
+  int cnt = a.sel_count[row];
+  if (cnt < 0) cnt = 0;
+  if (cnt > a.sel_ld) cnt = (int)a.sel_ld;
+  const int32_t* idx = a.sel_idx + row * a.sel_ld;
+  constexpr int kMaxPerLane = 8;  // D <= 256
+  for (int h = warp; h < a.H; h += nw) {
+    const int g = h / n_rep;
+    const float* qh = a.q + (row * a.H + h) * a.D;
+    float qv[kMaxPerLane], ov[kMaxPerLane];
+    for (int i = 0; i < kMaxPerLane; ++i) {
+      int d = lane + 32 * i;
+      qv[i] = d < a.D ? qh[d] : 0.f;
+      ov[i] = 0.f;
+    }
+    float m = -INFINITY, l = 0.f;
+    for (int j = 0; j < cnt; ++j) {
+      int s = idx[j];
+      if (s < 0 || s >= a.Lkv) { set_error(a.err, GSA_ERR_INDEX); continue; }
+      const float* kr = a.k + ((b * a.Lkv + s) * a.Hk + g) * a.D;
+      const float* vr = a.v + ((b * a.Lkv + s) * a.Hk + g) * a.D;
+      float dot = 0.f;
+      for (int i = 0; i < kMaxPerLane; ++i) {
+        int d = lane + 32 * i;
+        if (d < a.D) dot = fmaf(qv[i], kr[d], dot);
+      }
+      dot = warp_sum(dot) * a.scale;
+      float mn = fmaxf(m, dot);
+      float corr = expf(m - mn), p = expf(dot - mn);
+      l = l * corr + p;
+      for (int i = 0; i < kMaxPerLane; ++i) {
+        int d = lane + 32 * i;
+        if (d < a.D) ov[i] = ov[i] * corr + p * vr[d];
+      }
+      m = mn;
+    }
+    float inv = l > 0.f ? 1.f / l : 0.f;
+    for (int i = 0; i < kMaxPerLane; ++i) {
+      int d = lane + 32 * i;
+      if (d < a.D) {
+        int64_t off = (row * a.H + h) * a.D + d;
+        float y = ov[i] * inv;
+        if (a.gate) y = fmul(y, a.gate[off]);
+        a.out[off] = y;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+struct SdpaCfg {
+  int nstages;
+  size_t smem;
+};
+
+template <int D, int NREP>
+static int launch_tc(SdpaArgs a, int num_sms, cudaStream_t stream) {
+  const int row_bytes = a.Hk * D * 2;
+  const int stage_bytes = 2 * kKeysPerStage * (row_bytes + 16);
+  const int max_smem = 227 * 1024;
+  int nst = (max_smem - 256) / stage_bytes;
+  if (nst > 8) nst = 8;
+  if (nst < 2) return GSA_ERR_UNSUPPORTED;
+  a.nstages = nst;
+  const size_t smem = 256 + (size_t)nst * stage_bytes;
+  auto kern = sdpa_tc_kernel<D, NREP>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return GSA_ERR_LAUNCH;
+  int per_sm = 0;
+  const int threads = (a.Hk + 1) * 32;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem) != cudaSuccess || per_sm < 1)
+    return GSA_ERR_LAUNCH;
+  const int64_t R = a.B * a.Lq;
+  int64_t grid = (int64_t)num_sms * per_sm;
+  if (grid > R) grid = R;
+  kern<<<(unsigned)grid, threads, smem, stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? GSA_OK : GSA_ERR_LAUNCH;
+}
+
+template <int D>
+static int dispatch_nrep(SdpaArgs a, int nrep, int num_sms, cudaStream_t stream) {
+  switch (nrep) {
+    case 1: return launch_tc<D, 1>(a, num_sms, stream);
+    case 2: return launch_tc<D, 2>(a, num_sms, stream);
+    case 4: return launch_tc<D, 4>(a, num_sms, stream);
+    case 8: return launch_tc<D, 8>(a, num_sms, stream);
+    default: return GSA_ERR_UNSUPPORTED;
+  }
+}
+
+int launch_sdpa_bf16(SdpaArgs a, int D, int nrep, int num_sms, cudaStream_t stream) {
+  if (a.B * a.Lq == 0) return GSA_OK;
+  if (a.Hk < 1 || a.Hk > 16 || a.Hk * D * 2 > kMaxRowBytes) return GSA_ERR_UNSUPPORTED;
+  switch (D) {
+    case 64: return dispatch_nrep<64>(a, nrep, num_sms, stream);
+    case 128: return dispatch_nrep<128>(a, nrep, num_sms, stream);
+    default: return GSA_ERR_UNSUPPORTED;
+  }
+}
+
+int launch_sdpa_f32(const SdpaF32Args& a, cudaStream_t stream) {
+  const int64_t R = a.B * a.Lq;
+  if (R == 0) return GSA_OK;
+  if (a.D > 256) return GSA_ERR_UNSUPPORTED;
+  int warps = a.H < 8 ? a.H : 8;
+  sdpa_f32_kernel<<<(unsigned)R, warps * 32, 0, stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? GSA_OK : GSA_ERR_LAUNCH;
+}
+
+}  // namespace gsa

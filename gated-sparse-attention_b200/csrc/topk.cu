@@ -1,0 +1,418 @@
+// Variance-adaptive top-k selection (adaptive_topk.py:68-193), without sorting.
+//
+// The reference takes torch.topk(scores, k_eff) sorted descending and keeps sorted position
+// p iff p < k_t and the score is finite.  The kept set is exactly "the k_t largest finite
+// scores"; order inside the set does not matter to the attention that consumes it.  So:
+//
+//   gsa_topk_candidates  k_eff largest per row by a 3-pass radix select on the fp32 bit
+//                        pattern (11 + 11 + 10 bits), ties broken lower column first,
+//                        output compacted in ascending column order.  Variance-independent.
+//   gsa_row_variance     unbiased per-row variance from fp64 row sums, rounded to the dtype,
+//                        and the deterministic layer-wide sum of the rounded variances.
+//   gsa_adaptive_k       k_t in the reference's dtype arithmetic (each op rounded).
+//   gsa_select_finalize  k_t largest of each row's candidates, same radix select.
+//
+// One CTA per row.  Histograms use warp-aggregated shared-memory atomics.
+#include "kernels.cuh"
+
+namespace gsa {
+
+constexpr int kSelThreads = 512;
+constexpr int kBins = 2048;
+
+// Block-wide exclusive scan of one uint32 per thread; returns the exclusive prefix and
+// writes the block total to *total.  `ws` needs kSelThreads/32 + 1 words.
+__device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* ws, uint32_t* total) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  uint32_t x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) ws[wid] = x;
+  __syncthreads();
+  if (wid == 0) {
+    uint32_t w = lane < nw ? ws[lane] : 0u;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      uint32_t y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < nw) ws[lane] = w;  // inclusive warp-total prefix
+  }
+  __syncthreads();
+  uint32_t warp_off = wid > 0 ? ws[wid - 1] : 0u;
+  *total = ws[nw - 1];
+  __syncthreads();
+  return warp_off + x - v;
+}
+
+// Row source: either a plain fp32 row, or a candidate list (scores + column ids).
+struct RowSrc {
+  const float* vals;
+  int64_t n;
+};
+
+__device__ __forceinline__ bool valid_key(float f) { return !(f == -INFINITY) && !(f != f); }
+
+// Adds the histogram of digit (key >> shift) & mask over elements whose key matches
+// `prefix` on the bits above (shift + digit width).  Warp-aggregated atomics.
+__device__ void histogram_pass(const RowSrc& src, uint32_t* hist, int shift, uint32_t digit_mask,
+                               int prefix_shift, uint32_t prefix, bool use_prefix,
+                               uint32_t* finite_count) {
+  uint32_t my_finite = 0;
+  const int lane = threadIdx.x & 31;
+  const int64_t n = src.n;
+  const int64_t n_iter = (n + blockDim.x - 1) / blockDim.x;
+  for (int64_t it = 0; it < n_iter; ++it) {
+    int64_t i = it * blockDim.x + threadIdx.x;
+    bool act = false;
+    uint32_t digit = 0;
+    if (i < n) {
+      float f = src.vals[i];
+      if (valid_key(f)) {
+        uint32_t key = float_key(f);
+        ++my_finite;
+        if (!use_prefix || (key >> prefix_shift) == prefix) {
+          act = true;
+          digit = (key >> shift) & digit_mask;
+        }
+      }
+    }
+    uint32_t active = __ballot_sync(0xffffffffu, act);
+    if (act) {
+      uint32_t peers = __match_any_sync(active, digit);
+      int leader = __ffs(peers) - 1;
+      if (lane == leader) atomicAdd(&hist[digit], (uint32_t)__popc(peers));
+    }
+  }
+  if (finite_count) {
+    uint32_t wsum = warp_sum(my_finite);
+    if (lane == 0) atomicAdd(finite_count, wsum);
+  }
+}
+
+// Finds the digit d such that count(digits > d) < K <= count(digits >= d), scanning bins from
+// the top.  Writes d and count(digits > d) to out[0..1].
+__device__ void find_digit(const uint32_t* hist, int nbins, uint32_t K, uint32_t* ws, uint32_t* out) {
+  const int per = (nbins + blockDim.x - 1) / blockDim.x;
+  // thread i owns bins [nbins-1 - i*per, ..., nbins - (i+1)*per] (descending)
+  uint32_t local = 0;
+  for (int j = 0; j < per; ++j) {
+    int bin = nbins - 1 - (threadIdx.x * per + j);
+    if (bin >= 0) local += hist[bin];
+  }
+  uint32_t total;
+  uint32_t before = block_exclusive_scan(local, ws, &total);
+  if (before < K && before + local >= K) {
+    uint32_t acc = before;
+    for (int j = 0; j < per; ++j) {
+      int bin = nbins - 1 - (threadIdx.x * per + j);
+      if (bin < 0) break;
+      uint32_t c = hist[bin];
+      if (acc + c >= K) {
+        out[0] = (uint32_t)bin;
+        out[1] = acc;
+        break;
+      }
+      acc += c;
+    }
+  }
+  __syncthreads();
+}
+
+// Computes the selection threshold of the K largest valid values of `src`:
+//   sel[0] = threshold key tau, sel[1] = number of values equal to tau to take (in column
+//   order), sel[2] = number of finite values, sel[3] = 1 if every finite value is taken.
+__device__ void radix_threshold(const RowSrc& src, uint32_t K, uint32_t* hist, uint32_t* ws,
+                                uint32_t* sel) {
+  for (int i = threadIdx.x; i < kBins; i += blockDim.x) hist[i] = 0;
+  if (threadIdx.x == 0) { sel[2] = 0; sel[3] = 0; }
+  __syncthreads();
+  histogram_pass(src, hist, 21, 0x7FFu, 0, 0, false, &sel[2]);
+  __syncthreads();
+  const uint32_t finite = sel[2];
+  if (finite <= K) {
+    if (threadIdx.x == 0) { sel[0] = 0; sel[1] = 0; sel[3] = 1; }
+    __syncthreads();
+    return;
+  }
+  uint32_t* dig = ws + 40;  // two words after the scan scratch
+  find_digit(hist, kBins, K, ws, dig);
+  uint32_t d1 = dig[0], above1 = dig[1];
+  uint32_t K2 = K - above1;
+  __syncthreads();
+  for (int i = threadIdx.x; i < kBins; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  histogram_pass(src, hist, 10, 0x7FFu, 21, d1, true, nullptr);
+  __syncthreads();
+  find_digit(hist, kBins, K2, ws, dig);
+  uint32_t d2 = dig[0], above2 = dig[1];
+  uint32_t K3 = K2 - above2;
+  __syncthreads();
+  for (int i = threadIdx.x; i < 1024; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  histogram_pass(src, hist, 0, 0x3FFu, 10, (d1 << 11) | d2, true, nullptr);
+  __syncthreads();
+  find_digit(hist, 1024, K3, ws, dig);
+  uint32_t d3 = dig[0], above3 = dig[1];
+  if (threadIdx.x == 0) {
+    sel[0] = (d1 << 21) | (d2 << 10) | d3;
+    sel[1] = K3 - above3;
+    sel[3] = 0;
+  }
+  __syncthreads();
+}
+
+// Writes the selected elements (key > tau, plus the first `need_eq` with key == tau in column
+// order; or every finite element when take_all) in ascending column order.  Returns the count.
+// out_col(i) maps a source position to the column written to out_idx.
+template <typename ColMap>
+__device__ uint32_t collect(const RowSrc& src, uint32_t tau, uint32_t need_eq, bool take_all,
+                            int32_t* out_idx, float* out_score, ColMap out_col, uint32_t* ws,
+                            uint32_t cap, uint8_t* out_mask = nullptr) {
+  const int64_t n = src.n;
+  constexpr int PER = 4;
+  const int64_t chunk = (int64_t)blockDim.x * PER;
+  uint32_t out_base = 0, eq_seen = 0;
+  for (int64_t c0 = 0; c0 < n; c0 += chunk) {
+    uint32_t gt_cnt = 0, eq_cnt = 0;
+    float v[PER];
+    uint8_t kind[PER];  // 0 none, 1 gt, 2 eq
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      int64_t i = c0 + (int64_t)threadIdx.x * PER + j;
+      kind[j] = 0;
+      v[j] = 0.f;
+      if (i < n) {
+        float f = src.vals[i];
+        v[j] = f;
+        if (valid_key(f)) {
+          uint32_t key = float_key(f);
+          if (take_all || key > tau) { kind[j] = 1; ++gt_cnt; }
+          else if (key == tau) { kind[j] = 2; ++eq_cnt; }
+        }
+      }
+    }
+    uint32_t packed = gt_cnt | (eq_cnt << 16), total;
+    uint32_t pre = block_exclusive_scan(packed, ws, &total);
+    uint32_t gt_pre = pre & 0xFFFFu, eq_pre = pre >> 16;
+    uint32_t remaining = need_eq > eq_seen ? need_eq - eq_seen : 0u;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      if (kind[j] == 0) continue;
+      bool take = kind[j] == 1 || eq_pre < remaining;
+      if (take && out_base + gt_pre + min(eq_pre, remaining) < cap) {
+        uint32_t pos = out_base + gt_pre + min(eq_pre, remaining);
+        int64_t i = c0 + (int64_t)threadIdx.x * PER + j;
+        out_idx[pos] = out_col(i);
+        if (out_score) out_score[pos] = v[j];
+        if (out_mask) out_mask[i] = 1;
+      }
+      if (kind[j] == 1) ++gt_pre; else ++eq_pre;
+    }
+    uint32_t gt_tot = total & 0xFFFFu, eq_tot = total >> 16;
+    out_base += gt_tot + min(eq_tot, remaining);
+    eq_seen += eq_tot;
+  }
+  return min(out_base, cap);
+}
+
+struct IdentityCol {
+  __device__ int32_t operator()(int64_t i) const { return (int32_t)i; }
+};
+struct CandCol {
+  const int32_t* cols;
+  __device__ int32_t operator()(int64_t i) const { return cols[i]; }
+};
+
+__global__ void __launch_bounds__(kSelThreads) topk_candidates_kernel(
+    int64_t Lq, int64_t n_cols, int64_t q_pos0, int causal, const float* scores, int64_t ld,
+    int32_t k_eff, int32_t* cand_idx, float* cand_score, int32_t* cand_count) {
+  __shared__ uint32_t hist[kBins];
+  __shared__ uint32_t ws[48];
+  __shared__ uint32_t sel[4];
+  const int64_t r = blockIdx.x;
+  int64_t n = n_cols;
+  if (causal) n = min(n_cols, q_pos0 + (r % Lq) + 1);
+  if (n < 0) n = 0;
+  RowSrc src{scores + r * ld, n};
+  radix_threshold(src, (uint32_t)k_eff, hist, ws, sel);
+  uint32_t cnt = collect(src, sel[0], sel[1], sel[3] != 0, cand_idx + r * k_eff,
+                         cand_score + r * k_eff, IdentityCol{}, ws, (uint32_t)k_eff);
+  if (threadIdx.x == 0) cand_count[r] = (int32_t)cnt;
+}
+
+__global__ void __launch_bounds__(kSelThreads) select_finalize_kernel(
+    int32_t k_eff, const int32_t* cand_idx, const float* cand_score, const int32_t* cand_count,
+    const int32_t* k, int32_t* sel_idx, int64_t sel_ld, int32_t* sel_count, uint8_t* sel_mask) {
+  __shared__ uint32_t hist[kBins];
+  __shared__ uint32_t ws[48];
+  __shared__ uint32_t sel[4];
+  const int64_t r = blockIdx.x;
+  int32_t c = cand_count[r];
+  int32_t kr = k[r];
+  if (kr < 0) kr = 0;
+  if (c < 0) c = 0;
+  if (c > k_eff) c = k_eff;
+  RowSrc src{cand_score + r * k_eff, c};
+  uint8_t* mrow = sel_mask ? sel_mask + r * k_eff : nullptr;
+  if (mrow) {
+    for (int i = threadIdx.x; i < k_eff; i += blockDim.x) mrow[i] = 0;
+    __syncthreads();
+  }
+  uint32_t cnt;
+  if (kr == 0 || c == 0) {
+    cnt = 0;
+  } else if (kr >= c) {
+    // every candidate is kept: copy in order
+    for (int i = threadIdx.x; i < c; i += blockDim.x) {
+      sel_idx[r * sel_ld + i] = cand_idx[r * k_eff + i];
+      if (mrow) mrow[i] = 1;
+    }
+    cnt = (uint32_t)c;
+  } else {
+    radix_threshold(src, (uint32_t)kr, hist, ws, sel);
+    cnt = collect(src, sel[0], sel[1], sel[3] != 0, sel_idx + r * sel_ld, nullptr,
+                  CandCol{cand_idx + r * k_eff}, ws, (uint32_t)kr, mrow);
+  }
+  if (threadIdx.x == 0) sel_count[r] = (int32_t)cnt;
+}
+
+// Row statistics of a materialised score matrix: sum, sum of squares, finite count (fp64).
+__global__ void row_stats_kernel(int64_t n_cols, const float* scores, int64_t ld, double* stats) {
+  const int64_t r = blockIdx.x;
+  const float* row = scores + r * ld;
+  double s1 = 0.0, s2 = 0.0, c = 0.0;
+  for (int64_t i = threadIdx.x; i < n_cols; i += blockDim.x) {
+    float f = row[i];
+    if (valid_key(f)) {
+      double d = f;
+      s1 += d;
+      s2 += d * d;
+      c += 1.0;
+    }
+  }
+  __shared__ double red[3][32];
+  s1 = warp_sum(s1); s2 = warp_sum(s2); c = warp_sum(c);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (lane == 0) { red[0][wid] = s1; red[1][wid] = s2; red[2][wid] = c; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double a = 0, b = 0, cc = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) { a += red[0][w]; b += red[1][w]; cc += red[2][w]; }
+    stats[r * 3 + 0] += a;
+    stats[r * 3 + 1] += b;
+    stats[r * 3 + 2] += cc;
+  }
+}
+
+// Unbiased variance over all N entries (masked ones count as 0), from sums taken relative to
+// a per-row shift c.  With y = x - c: the N - n masked entries have y = -c.
+__device__ __forceinline__ double row_var(const double* st, double c, double N) {
+  double n = st[2];
+  double sy = st[0] - (N - n) * c;
+  double syy = st[1] + (N - n) * c * c;
+  return (syy - sy * sy / N) / (N - 1.0);
+}
+
+constexpr int kVarThreads = 256;
+
+__global__ void row_variance_kernel(int64_t R, double N, int dtype, const double* stats,
+                                    const float* shift, float* var_out) {
+  const int64_t r = (int64_t)blockIdx.x * kVarThreads + threadIdx.x;
+  if (r >= R) return;
+  double c = shift ? (double)shift[r] : 0.0;
+  var_out[r] = rnd((float)row_var(stats + r * 3, c, N), dtype);
+}
+
+// Sum of the rounded per-row variances in a fixed order (one CTA), so the layer mean is
+// deterministic: total[0] = sum, total[1] = row count.
+__global__ void __launch_bounds__(1024) sum_variance_kernel(int64_t R, const float* var, double* total) {
+  __shared__ double red[1024];
+  double s = 0;
+  for (int64_t i = threadIdx.x; i < R; i += blockDim.x) s += (double)var[i];
+  red[threadIdx.x] = s;
+  __syncthreads();
+  for (int o = 512; o > 0; o >>= 1) {
+    if ((int)threadIdx.x < o) red[threadIdx.x] += red[threadIdx.x + o];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) { total[0] = red[0]; total[1] = (double)R; }
+}
+
+// k_t in the reference's arithmetic: every op of adaptive_topk.py:96-102,133-136 evaluated in
+// fp32 and rounded to the activation dtype, then the min with the valid count in fp32 and
+// truncation toward zero (.long()).
+__global__ void adaptive_k_kernel(int64_t R, int64_t n_cols, int dtype, gsa_topk_params p,
+                                  const float* var, const double* var_total,
+                                  const double* stats, int32_t* k_out) {
+  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= R) return;
+  if (!p.use_adaptive) {
+    k_out[r] = (int32_t)min((int64_t)p.k_base, n_cols);
+    return;
+  }
+  float mean = rnd(__fdiv_rn((float)var_total[0], (float)var_total[1]), dtype);
+  float den = rnd(fadd(mean, 1e-8f), dtype);
+  float vn = rnd(__fdiv_rn(var[r], den), dtype);
+  float vt = rnd(fmul(vn, p.temperature), dtype);
+  float ks = rnd(__fdiv_rn(1.0f, rnd(fadd(1.0f, vt), dtype)), dtype);
+  float ka = rnd(fmul((float)p.k_base, rnd(fadd(0.5f, ks), dtype)), dtype);
+  float lo = rnd((float)p.k_min, dtype), hi = rnd((float)p.k_max, dtype);
+  float kc = fminf(fmaxf(ka, lo), hi);
+  if (ka != ka) kc = ka;  // clamp keeps NaN
+  float valid = (float)stats[r * 3 + 2];
+  float km = (kc != kc) ? kc : fminf(kc, valid);
+  int32_t kt;
+  if (km != km) kt = 0;
+  else kt = (int32_t)truncf(km);
+  k_out[r] = kt;
+}
+
+// ---------------------------------------------------------------------------------------------
+int launch_topk_candidates(int64_t R, int64_t Lq, int64_t n_cols, int64_t q_pos0, int causal,
+                           const float* scores, int64_t ld, int32_t k_eff, int32_t* cand_idx,
+                           float* cand_score, int32_t* cand_count, cudaStream_t stream) {
+  if (R == 0) return GSA_OK;
+  if (R > 0x7fffffffLL) return GSA_ERR_BAD_ARG;
+  topk_candidates_kernel<<<(unsigned)R, kSelThreads, 0, stream>>>(Lq, n_cols, q_pos0, causal, scores, ld,
+                                                                 k_eff, cand_idx, cand_score, cand_count);
+  return cudaGetLastError() == cudaSuccess ? GSA_OK : GSA_ERR_LAUNCH;
+}
+
+int launch_select_finalize(int64_t R, int32_t k_eff, const int32_t* cand_idx, const float* cand_score,
+                           const int32_t* cand_count, const int32_t* k, int32_t* sel_idx, int64_t sel_ld,
+                           int32_t* sel_count, uint8_t* sel_mask, cudaStream_t stream) {
+  if (R == 0) return GSA_OK;
+  select_finalize_kernel<<<(unsigned)R, kSelThreads, 0, stream>>>(k_eff, cand_idx, cand_score, cand_count,
+                                                                 k, sel_idx, sel_ld, sel_count, sel_mask);
+  return cudaGetLastError() == cudaSuccess ? GSA_OK : GSA_ERR_LAUNCH;
+}
+
+int launch_row_stats(int64_t R, int64_t n_cols, const float* scores, int64_t ld, double* stats,
+                     cudaStream_t stream) {
+  if (R == 0) return GSA_OK;
+  row_stats_kernel<<<(unsigned)R, 256, 0, stream>>>(n_cols, scores, ld, stats);
+  return cudaGetLastError() == cudaSuccess ? GSA_OK : GSA_ERR_LAUNCH;
+}
+
+int launch_row_variance(int64_t R, int64_t n_cols, int dtype, const double* stats, const float* shift,
+                        float* var_out, double* total, cudaStream_t stream) {
+  if (R == 0) return GSA_OK;
+  row_variance_kernel<<<(unsigned)((R + kVarThreads - 1) / kVarThreads), kVarThreads, 0, stream>>>(
+      R, (double)n_cols, dtype, stats, shift, var_out);
+  sum_variance_kernel<<<1, 1024, 0, stream>>>(R, var_out, total);
+  return cudaGetLastError() == cudaSuccess ? GSA_OK : GSA_ERR_LAUNCH;
+}
+
+int launch_adaptive_k(int64_t R, int64_t n_cols, int dtype, const gsa_topk_params& p, const float* var,
+                      const double* var_total, const double* stats, int32_t* k_out, cudaStream_t stream) {
+  if (R == 0) return GSA_OK;
+  adaptive_k_kernel<<<(unsigned)((R + 255) / 256), 256, 0, stream>>>(R, n_cols, dtype, p, var, var_total,
+                                                                    stats, k_out);
+  return cudaGetLastError() == cudaSuccess ? GSA_OK : GSA_ERR_LAUNCH;
+}
+
+}  // namespace gsa

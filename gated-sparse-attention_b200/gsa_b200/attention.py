@@ -1,0 +1,570 @@
+"""GSA modules with the reference's API, computing through the sm_100a kernels.
+
+Class names, constructor arguments, submodule and parameter names, buffers, return values and
+error types follow the reference package ``gsa.attention`` (alfredcs/Gated-Sparse-Attention):
+
+  GatedSparseAttention   gsa/attention/gated_sparse_attention.py:23-323
+  GatedLightningIndexer  gsa/attention/gated_indexer.py:16-175
+  AdaptiveTopKSelector   gsa/attention/adaptive_topk.py:14-211
+  ValueGate              gsa/attention/value_gate.py:16-127
+  OutputGate             gsa/attention/output_gate.py:15-142
+  RotaryEmbedding        gsa/attention/rope.py:11-148
+  apply_rotary_pos_emb   gsa/attention/rope.py:151-185
+
+Submodules are created, and their weights initialised, in the reference's order, so
+``torch.manual_seed(s); GatedSparseAttention(cfg)`` yields the same weights in both packages and
+state dicts load either way.
+
+The forward path of ``GatedSparseAttention`` is: one fused projection GEMM (cuBLAS), then the
+library's kernels for RoPE / G2 / G1 gate / indexer weights, the chunked indexer + top-k
+candidates, the adaptive k, the final selection, and the gathered sparse SDPA with the G1 gate
+in its epilogue; ``o_proj`` is a cuBLAS GEMM.  No [B, L, L] score tensor and no gathered
+[B, L, k, H, D] tensor is ever formed.  Inputs must be CUDA tensors in float32 or bfloat16;
+there is no CPU path.  The layer computes forward only: calling backward through its output
+raises ``NotImplementedError``.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional, Tuple
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import ops
+from ._lib import ProjLayout
+
+_ACTS = ("sigmoid", "tanh", "silu")
+
+
+# ---------------------------------------------------------------------------------------------
+# RoPE
+# ---------------------------------------------------------------------------------------------
+class RotaryEmbedding(nn.Module):
+    """RoPE tables (standard, NTK, YaRN).  Same buffers and arithmetic as rope.py:11-148."""
+
+    def __init__(self, dim: int, max_position_embeddings: int = 131072, base: float = 10000.0,
+                 scaling_config=None, device=None):
+        super().__init__()
+        self.dim = dim
+        self.max_position_embeddings = max_position_embeddings
+        self.base = base
+        self.scaling_config = scaling_config or {}
+        self.register_buffer("inv_freq", self._compute_inv_freq(device), persistent=False)
+        self._set_cos_sin_cache(max_position_embeddings, device=device, dtype=torch.float32)
+
+    def _compute_inv_freq(self, device=None) -> torch.Tensor:
+        kind = self.scaling_config.get("type", None)
+        ar = torch.arange(0, self.dim, 2, device=device).float()
+        if kind == "yarn":  # rope.py:73-101
+            factor = self.scaling_config.get("factor", 1.0)
+            orig = self.scaling_config.get("original_max_position_embeddings", 4096)
+            beta_fast = self.scaling_config.get("beta_fast", 32)
+            beta_slow = self.scaling_config.get("beta_slow", 1)
+            pos_freqs = self.base ** (ar / self.dim)
+            extra = 1.0 / pos_freqs
+            inter = 1.0 / (factor * pos_freqs)
+            low = max(int(math.floor(self.dim * math.log(orig / (beta_fast * 2 * math.pi))
+                                     / (2 * math.log(self.base)))), 0)
+            high = min(int(math.ceil(self.dim * math.log(orig / (beta_slow * 2 * math.pi))
+                                     / (2 * math.log(self.base)))), self.dim // 2 - 1)
+            inv = inter.clone()
+            inv[:low] = extra[:low]
+            if high > low:
+                smooth = (torch.arange(low, high + 1, device=device).float() - low) / (high - low)
+                inv[low:high + 1] = (1 - smooth) * extra[low:high + 1] + smooth * inter[low:high + 1]
+            return inv
+        if kind == "ntk":  # rope.py:66-71
+            factor = self.scaling_config.get("factor", 1.0)
+            b = self.base * factor ** (self.dim / (self.dim - 2))
+            return 1.0 / (b ** (ar / self.dim))
+        # standard; "dynamic_ntk" uses the standard frequencies (rope.py:53-57)
+        return 1.0 / (self.base ** (ar / self.dim))
+
+    def _set_cos_sin_cache(self, seq_len: int, device=None, dtype=torch.float32):
+        # rope.py:103-115, including its use of the cache dtype for the position ramp
+        self.max_seq_len_cached = seq_len
+        t = torch.arange(seq_len, device=device, dtype=dtype)
+        freqs = torch.outer(t, self.inv_freq)
+        emb = torch.cat((freqs, freqs), dim=-1)
+        self.register_buffer("cos_cached", emb.cos(), persistent=False)
+        self.register_buffer("sin_cached", emb.sin(), persistent=False)
+
+    def ensure(self, seq_len: int):
+        """Extend the tables to ``seq_len`` positions if needed (rope.py:136-142)."""
+        if seq_len > self.max_seq_len_cached:
+            self._set_cos_sin_cache(seq_len, device=self.cos_cached.device, dtype=self.cos_cached.dtype)
+
+    def forward(self, positions: torch.Tensor, seq_len: Optional[int] = None):
+        if seq_len is None:
+            seq_len = int(positions.max().item()) + 1
+        self.ensure(seq_len)
+        return self.cos_cached[positions], self.sin_cached[positions]
+
+
+def apply_rotary_pos_emb(q, k, cos, sin):
+    """rotate-half RoPE on q [B,L,H,D] and k [B,L,Hk,D] (rope.py:151-185).  The attention layer
+    applies RoPE inside its projection-epilogue kernel; this function is the standalone API."""
+    cos = cos.unsqueeze(2)
+    sin = sin.unsqueeze(2)
+
+    def rot(x):
+        h = x.shape[-1] // 2
+        return x * cos + torch.cat([-x[..., h:], x[..., :h]], dim=-1) * sin
+
+    return rot(q), rot(k)
+
+
+# ---------------------------------------------------------------------------------------------
+# Gates
+# ---------------------------------------------------------------------------------------------
+def _gate_stats(scores: Optional[torch.Tensor], per_head: bool = False) -> dict:
+    if scores is None:
+        return {}
+    s = scores.float()
+    out = {"mean": s.mean().item(), "std": s.std().item(), "min": s.min().item(),
+           "max": s.max().item(), "sparsity": (s < 0.1).float().mean().item()}
+    if per_head:
+        out["per_head_mean"] = s.mean(dim=(0, 1, 3)).tolist() if s.dim() == 4 else None
+    return out
+
+
+class ValueGate(nn.Module):
+    """G2: v * act(h W^T + b) per KV-head element (value_gate.py:16-127)."""
+
+    def __init__(self, d_model: int, n_kv_heads: int, d_head: int, bias_init: float = 0.5,
+                 activation: str = "sigmoid"):
+        super().__init__()
+        self.d_model = d_model
+        self.n_kv_heads = n_kv_heads
+        self.d_head = d_head
+        self.activation = activation
+        self.gate_proj = nn.Linear(d_model, n_kv_heads * d_head, bias=True)
+        self._init_weights(bias_init)
+        self.last_gate_scores: Optional[torch.Tensor] = None
+
+    def _init_weights(self, bias_init: float):
+        nn.init.xavier_uniform_(self.gate_proj.weight, gain=0.1)
+        nn.init.constant_(self.gate_proj.bias, bias_init)
+
+    def forward(self, v: torch.Tensor, hidden_states: torch.Tensor) -> torch.Tensor:
+        if self.activation not in _ACTS:
+            raise ValueError(f"Unknown activation: {self.activation}")
+        logits = self.gate_proj(hidden_states).view_as(v)
+        out, gate = ops.apply_gate(v, logits, self.activation, want_gate=not self.training)
+        if not self.training:
+            self.last_gate_scores = gate
+        return out
+
+    def get_gate_statistics(self) -> dict:
+        return _gate_stats(self.last_gate_scores)
+
+
+class OutputGate(nn.Module):
+    """G1: o * act(h W^T + b), per head element or per head scalar (output_gate.py:15-142)."""
+
+    def __init__(self, d_model: int, n_heads: int, d_head: int, bias_init: float = 0.5,
+                 activation: str = "sigmoid", per_head: bool = True):
+        super().__init__()
+        self.d_model = d_model
+        self.n_heads = n_heads
+        self.d_head = d_head
+        self.activation = activation
+        self.per_head = per_head
+        out = n_heads * d_head if per_head else n_heads
+        self.gate_proj = nn.Linear(d_model, out, bias=True)
+        self._init_weights(bias_init)
+        self.last_gate_scores: Optional[torch.Tensor] = None
+
+    def _init_weights(self, bias_init: float):
+        nn.init.xavier_uniform_(self.gate_proj.weight, gain=0.1)
+        nn.init.constant_(self.gate_proj.bias, bias_init)
+
+    def forward(self, attn_output: torch.Tensor, hidden_states: torch.Tensor) -> torch.Tensor:
+        if self.activation not in _ACTS:
+            raise ValueError(f"Unknown activation: {self.activation}")
+        B, L, H, D = attn_output.shape
+        logits = self.gate_proj(hidden_states)
+        logits = logits.view(B, L, H, D) if self.per_head else logits.view(B, L, H, 1).expand(B, L, H, D)
+        out, gate = ops.apply_gate(attn_output, logits, self.activation, want_gate=not self.training)
+        if not self.training:
+            self.last_gate_scores = gate if self.per_head else gate[..., :1]
+        return out
+
+    def get_gate_statistics(self) -> dict:
+        return _gate_stats(self.last_gate_scores, per_head=True)
+
+
+# ---------------------------------------------------------------------------------------------
+# Indexer and selector
+# ---------------------------------------------------------------------------------------------
+class GatedLightningIndexer(nn.Module):
+    """I[t,s] = sum_j sigmoid(h_t W_j^Iw) * act(q^I_{t,j} . k^I_s / sqrt(d_I) + b_j)
+    (gated_indexer.py:16-175).  ``forward`` materialises [B, Lq, Lkv] scores for callers that
+    want them; the attention layer never does."""
+
+    def __init__(self, d_model: int, d_indexer: int = 64, n_indexer_heads: int = 4,
+                 activation: str = "sigmoid", use_causal_mask: bool = True):
+        super().__init__()
+        self.d_model = d_model
+        self.d_indexer = d_indexer
+        self.n_indexer_heads = n_indexer_heads
+        self.activation = activation
+        self.use_causal_mask = use_causal_mask
+        self.q_proj = nn.Linear(d_model, n_indexer_heads * d_indexer, bias=False)
+        self.k_proj = nn.Linear(d_model, d_indexer, bias=False)
+        self.weight_proj = nn.Linear(d_model, n_indexer_heads, bias=True)
+        self.bias = nn.Parameter(torch.zeros(n_indexer_heads))
+        self.scale = 1.0 / math.sqrt(d_indexer)
+        self._init_weights()
+
+    def _init_weights(self):
+        nn.init.xavier_uniform_(self.q_proj.weight, gain=1.0)
+        nn.init.xavier_uniform_(self.k_proj.weight, gain=1.0)
+        nn.init.xavier_uniform_(self.weight_proj.weight, gain=0.1)
+        nn.init.zeros_(self.weight_proj.bias)
+        nn.init.zeros_(self.bias)
+
+    def _dims(self):
+        return ops.make_dims(self.d_model, 1, 1, 2, self.n_indexer_heads, self.d_indexer,
+                             "sigmoid", self.activation)
+
+    def forward(self, hidden_states: torch.Tensor, positions: Optional[torch.Tensor] = None,
+                kv_hidden_states: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if self.activation not in ("sigmoid", "relu"):
+            raise ValueError(f"Unknown activation: {self.activation}")
+        if kv_hidden_states is None:
+            kv_hidden_states = hidden_states
+        B, Lq, _ = hidden_states.shape
+        Lkv = kv_hidden_states.shape[1]
+        with torch.no_grad():
+            q_idx = F.linear(hidden_states, self.q_proj.weight)
+            k_idx = F.linear(kv_hidden_states, self.k_proj.weight)
+            w = torch.sigmoid(self.weight_proj(hidden_states))
+            causal = self.use_causal_mask and Lq == Lkv
+            scores = ops.indexer_scores(self._dims(), q_idx, k_idx, w, self.bias, self.scale,
+                                        q_pos0=0, causal=causal, write_masked=True)
+        return scores.to(hidden_states.dtype)
+
+    def get_indexer_statistics(self, hidden_states: torch.Tensor) -> dict:
+        with torch.no_grad():
+            scores = self.forward(hidden_states)
+            valid = scores[scores != float("-inf")].float()
+            return {"mean": valid.mean().item(), "std": valid.std().item(),
+                    "min": valid.min().item(), "max": valid.max().item(),
+                    "sparsity": (valid < 0.1).float().mean().item(),
+                    "head_weights": torch.sigmoid(self.weight_proj.bias).tolist()}
+
+
+class AdaptiveTopKSelector(nn.Module):
+    """Per-row k_t from the score variance and the top-k_t selection (adaptive_topk.py:14-211).
+
+    Returns ``(indices, mask)`` [B, Lq, k_eff]: ``indices`` holds the k_eff best columns of each
+    row in ascending column order and ``mask`` marks the k_t of them that are kept.  The
+    reference returns the same candidate columns sorted by score; every consumer uses the
+    (indices, mask) pair as a set, so the two are interchangeable."""
+
+    def __init__(self, k_base: int = 2048, k_min: int = 256, k_max: int = 4096,
+                 use_adaptive: bool = True, temperature: float = 1.0,
+                 adaptive_method: str = "variance"):
+        super().__init__()
+        self.k_base = k_base
+        self.k_min = k_min
+        self.k_max = k_max
+        self.use_adaptive = use_adaptive
+        self.temperature = temperature
+        self.adaptive_method = adaptive_method
+        if adaptive_method == "learned":  # parameters kept for state-dict compatibility
+            self.k_predictor = nn.Sequential(nn.Linear(3, 32), nn.ReLU(), nn.Linear(32, 1), nn.Sigmoid())
+
+    def forward(self, scores: torch.Tensor, seq_q: int, seq_kv: int, return_k_values: bool = False):
+        B, Lq, Lkv = scores.shape
+        if self.use_adaptive and self.adaptive_method != "variance":
+            if self.adaptive_method in ("entropy", "learned"):
+                raise NotImplementedError(
+                    f"adaptive_method={self.adaptive_method!r} has no kernel; the attention layer "
+                    "uses 'variance'")
+            raise ValueError(f"Unknown adaptive method: {self.adaptive_method}")
+        k_eff = min(self.k_max, seq_kv) if self.use_adaptive else min(self.k_base, seq_kv)
+        s2d = scores.reshape(B * Lq, Lkv).float()
+        cand_idx, cand_score, cand_count = ops.topk_candidates(s2d, k_eff)
+        if self.use_adaptive:
+            stats = ops.row_stats(s2d)
+            var, total = ops.row_variance(stats, Lkv, scores.dtype)
+            k = ops.adaptive_k(stats, var, total, Lkv, scores.dtype, self.k_base, self.k_min,
+                               self.k_max, True, self.temperature)
+        else:
+            k = torch.full((B * Lq,), min(self.k_base, seq_kv), device=scores.device, dtype=torch.int32)
+        _, _, mask = ops.select_finalize(cand_idx, cand_score, cand_count, k, want_mask=True)
+        indices = cand_idx.long().view(B, Lq, k_eff)
+        mask = mask.bool().view(B, Lq, k_eff)
+        if return_k_values:
+            return indices, mask, k.long().view(B, Lq)
+        return indices, mask
+
+    def get_selection_statistics(self, scores: torch.Tensor) -> dict:
+        with torch.no_grad():
+            _, mask, k_values = self.forward(scores, scores.shape[1], scores.shape[2], return_k_values=True)
+            return {"k_mean": k_values.float().mean().item(), "k_std": k_values.float().std().item(),
+                    "k_min": k_values.min().item(), "k_max": k_values.max().item(),
+                    "coverage": mask.float().mean().item()}
+
+
+# ---------------------------------------------------------------------------------------------
+# KV cache
+# ---------------------------------------------------------------------------------------------
+class GSAKVCache(tuple):
+    """The (k, v) cache pair of the reference (post-RoPE k, post-G2 v, [B, Lkv, Hk, D]) that
+    also carries the indexer keys k^I [B, Lkv, d_I].  It is a 2-tuple, so code written for the
+    reference's cache keeps working; when it is passed back as ``past_key_value`` the indexer
+    scores the new queries against every cached key."""
+
+    def __new__(cls, k, v, indexer_keys=None):
+        obj = super().__new__(cls, (k, v))
+        obj.indexer_keys = indexer_keys
+        return obj
+
+
+class _ForwardOnly(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, out, *_):
+        return out.view_as(out)
+
+    @staticmethod
+    def backward(ctx, *grads):
+        raise NotImplementedError("the B200 GSA layer implements the forward pass only")
+
+
+# ---------------------------------------------------------------------------------------------
+# The layer
+# ---------------------------------------------------------------------------------------------
+class GatedSparseAttention(nn.Module):
+    """Gated Sparse Attention layer (gated_sparse_attention.py:23-323), forward on sm_100a."""
+
+    def __init__(self, config):
+        super().__init__()
+        self.config = config
+        self.d_model = config.d_model
+        self.n_heads = config.n_heads
+        self.n_kv_heads = config.n_kv_heads
+        self.d_head = config.d_head
+        self.n_rep = self.n_heads // self.n_kv_heads
+        self.scale = 1.0 / math.sqrt(self.d_head)
+
+        self.q_proj = nn.Linear(self.d_model, self.n_heads * self.d_head, bias=False)
+        self.k_proj = nn.Linear(self.d_model, self.n_kv_heads * self.d_head, bias=False)
+        self.v_proj = nn.Linear(self.d_model, self.n_kv_heads * self.d_head, bias=False)
+        self.o_proj = nn.Linear(self.n_heads * self.d_head, self.d_model, bias=False)
+        self.indexer = GatedLightningIndexer(d_model=self.d_model, d_indexer=config.d_indexer,
+                                             n_indexer_heads=config.n_indexer_heads,
+                                             activation=config.indexer_activation)
+        self.topk_selector = AdaptiveTopKSelector(k_base=config.k_base, k_min=config.k_min,
+                                                  k_max=config.k_max, use_adaptive=config.use_adaptive_k,
+                                                  temperature=config.adaptive_k_temperature)
+        self.value_gate = (ValueGate(self.d_model, self.n_kv_heads, self.d_head, bias_init=config.gate_bias_init)
+                           if config.use_value_gate else None)
+        self.output_gate = (OutputGate(self.d_model, self.n_heads, self.d_head, bias_init=config.gate_bias_init)
+                            if config.use_output_gate else None)
+        self.rotary_emb = RotaryEmbedding(dim=self.d_head, max_position_embeddings=config.max_position_embeddings,
+                                          base=config.rope_base, scaling_config=config.rope_scaling)
+        self.attn_dropout = nn.Dropout(config.attention_dropout)
+        self.dense_residual_alpha = config.dense_residual_alpha
+        self._init_weights()
+        self._fused = None
+        # set by gsa_b200.sharded.enable_query_sharding: this rank's share of the query sequence
+        self.query_shards = None
+
+    def _init_weights(self):
+        for module in [self.q_proj, self.k_proj, self.v_proj]:
+            nn.init.xavier_uniform_(module.weight, gain=1.0 / math.sqrt(2))
+        nn.init.xavier_uniform_(self.o_proj.weight, gain=1.0 / math.sqrt(2 * self.config.n_layers))
+
+    def _repeat_kv(self, x: torch.Tensor) -> torch.Tensor:
+        """[B, L, Hk, D] -> [B, L, H, D] (gated_sparse_attention.py:123-137)."""
+        B, L, Hk, D = x.shape
+        if self.n_rep == 1:
+            return x
+        return x.unsqueeze(3).expand(B, L, Hk, self.n_rep, D).reshape(B, L, self.n_heads, D)
+
+    # -- fused projection weight ------------------------------------------------------------
+    def _segments(self):
+        H, Hk, D = self.n_heads, self.n_kv_heads, self.d_head
+        ix = self.indexer
+        segs = [("q", self.q_proj.weight, None), ("k", self.k_proj.weight, None),
+                ("v", self.v_proj.weight, None)]
+        if self.value_gate is not None:
+            segs.append(("g2", self.value_gate.gate_proj.weight, self.value_gate.gate_proj.bias))
+        if self.output_gate is not None:
+            if not self.output_gate.per_head:
+                raise NotImplementedError("the fused layer supports the per-head output gate only")
+            segs.append(("g1", self.output_gate.gate_proj.weight, self.output_gate.gate_proj.bias))
+        segs += [("qi", ix.q_proj.weight, None), ("ki", ix.k_proj.weight, None),
+                 ("wi", ix.weight_proj.weight, ix.weight_proj.bias)]
+        return segs
+
+    def fused_projection(self):
+        """(W [Ncat, d_model], b [Ncat], ProjLayout): every projection of the layer stacked so
+        that one GEMM produces all of them; Ncat is padded to a multiple of 64.  Cached until a
+        parameter changes."""
+        segs = self._segments()
+        key = tuple((n, w.data_ptr(), w._version, None if b is None else (b.data_ptr(), b._version))
+                    for n, w, b in segs)
+        if self._fused is not None and self._fused[0] == key:
+            return self._fused[1:]
+        ws, bs, offs, off = [], [], {}, 0
+        for name, w, b in segs:
+            offs[name] = off
+            ws.append(w.detach())
+            bs.append(b.detach() if b is not None else torch.zeros(w.shape[0], device=w.device, dtype=w.dtype))
+            off += w.shape[0]
+        pad = (-off) % 64
+        if pad:
+            ws.append(torch.zeros(pad, self.d_model, device=ws[0].device, dtype=ws[0].dtype))
+            bs.append(torch.zeros(pad, device=ws[0].device, dtype=ws[0].dtype))
+        W = torch.cat(ws, 0).contiguous()
+        bvec = torch.cat(bs, 0).contiguous()
+        layout = ProjLayout(*(offs.get(n, -1) for n in ("q", "k", "v", "g2", "g1", "qi", "ki", "wi")))
+        self._fused = (key, W, bvec, layout)
+        return W, bvec, layout
+
+    def _dims(self):
+        return ops.make_dims(self.d_model, self.n_heads, self.n_kv_heads, self.d_head,
+                             self.config.n_indexer_heads, self.config.d_indexer,
+                             self.value_gate.activation if self.value_gate is not None else
+                             (self.output_gate.activation if self.output_gate is not None else "sigmoid"),
+                             self.indexer.activation)
+
+    # -- forward ----------------------------------------------------------------------------
+    def forward(self, hidden_states: torch.Tensor, positions: Optional[torch.Tensor] = None,
+                attention_mask: Optional[torch.Tensor] = None,
+                past_key_value: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
+                use_cache: bool = False, output_attentions: bool = False):
+        x = hidden_states
+        if not x.is_cuda:
+            raise RuntimeError("GatedSparseAttention (B200) runs on CUDA tensors only")
+        if self.training and self.attn_dropout.p > 0:
+            raise NotImplementedError("attention dropout in training mode is not implemented")
+        if (self.value_gate is not None and self.output_gate is not None
+                and self.value_gate.activation != self.output_gate.activation):
+            raise NotImplementedError("value and output gates must share one activation")
+        with torch.no_grad():
+            out, present, weights = self._forward_impl(x, positions, past_key_value, use_cache,
+                                                       output_attentions)
+        if torch.is_grad_enabled() and (x.requires_grad or self.q_proj.weight.requires_grad):
+            out = _ForwardOnly.apply(out, x, self.q_proj.weight)
+        return out, present, weights if output_attentions else None
+
+    def _forward_impl(self, x, positions, past_key_value, use_cache, output_attentions,
+                      mark=None, capture=None):
+        """The forward computation.  ``mark(name)`` (optional) is called after each stage and
+        ``capture`` (optional dict) receives the SDPA inputs; both are for measurement."""
+        mark = mark or (lambda name: None)
+        B, L, _ = x.shape
+        dt = x.dtype
+        ops.dtype_code(dt)
+        H, Hk, D = self.n_heads, self.n_kv_heads, self.d_head
+        HI, dI = self.config.n_indexer_heads, self.config.d_indexer
+        cfg = self.config
+        sp = self.query_shards
+        if sp is not None and past_key_value is not None:
+            raise NotImplementedError("query-sharded layers run prefill without a KV cache")
+        past_len = past_key_value[0].shape[1] if past_key_value is not None else 0
+        if sp is not None:
+            past_len = sp.start(L)  # absolute position of this rank's first token
+        if positions is None:
+            positions = torch.arange(past_len, past_len + L, device=x.device).unsqueeze(0).expand(B, -1)
+            max_pos = past_len + L - 1
+        else:
+            max_pos = int(positions.max().item())  # the reference syncs here too (rope.py:133-134)
+        self.rotary_emb.ensure(max_pos + 1)
+        W, bvec, layout = self.fused_projection()
+        if W.dtype != dt:
+            raise RuntimeError(f"layer parameters are {W.dtype} but the input is {dt}")
+        dims = self._dims()
+
+        proj = torch.addmm(bvec, x.reshape(B * L, self.d_model), W.t())
+        mark("proj_gemm")
+        q, k, v, g1, w, shift = ops.proj_epilogue(dims, layout, proj, positions,
+                                                  self.rotary_emb.cos_cached, self.rotary_emb.sin_cached,
+                                                  self.output_gate is not None)
+        mark("proj_epilogue")
+        q = q.view(B, L, H, D)
+        k = k.view(B, L, Hk, D)
+        v = v.view(B, L, Hk, D)
+        proj3 = proj.view(B, L, proj.shape[1])
+        qI = proj3[..., layout.qi:layout.qi + HI * dI]
+        kI = proj3[..., layout.ki:layout.ki + dI]
+
+        indexer_keys = None
+        if sp is not None:
+            # every rank needs all keys up to its last query: gather K, V and k^I in rank order
+            kI_all = sp.gather(kI)
+            k_all = sp.gather(k)
+            v_all = sp.gather(v)
+            q_pos0 = sp.start(L)
+            indexer_keys = kI_all
+        elif past_key_value is None:
+            k_all, v_all, kI_all, q_pos0 = k, v, kI, 0
+            indexer_keys = kI.contiguous()
+        else:
+            k_all = torch.cat([past_key_value[0], k], dim=1)
+            v_all = torch.cat([past_key_value[1], v], dim=1)
+            past_kI = getattr(past_key_value, "indexer_keys", None)
+            if past_kI is not None:
+                # scores against every cached key, offset-causal for the new rows
+                kI_all = torch.cat([past_kI, kI.contiguous()], dim=1)
+                q_pos0 = past_len
+                indexer_keys = kI_all
+            else:
+                # a plain (k, v) cache: the reference scores the new tokens only
+                # (gated_sparse_attention.py:197-213), selecting among positions [0, L)
+                kI_all, q_pos0 = kI, 0
+        present = GSAKVCache(k_all, v_all, indexer_keys) if use_cache else None
+        mark("kv")
+
+        n_cols = kI_all.shape[1]
+        k_eff = min(cfg.k_max, n_cols) if cfg.use_adaptive_k else min(cfg.k_base, n_cols)
+        cand_idx, cand_score, cand_count, stats = ops.indexer_select(
+            dims, qI, kI_all, w, self.indexer.bias, self.indexer.scale, shift, k_eff,
+            q_pos0=q_pos0, causal=True)
+        mark("indexer_topk")
+        if cfg.use_adaptive_k:
+            var, total = ops.row_variance(stats, n_cols, dt, shift)
+            if sp is not None:
+                total = sp.allreduce(total)
+        else:
+            var = total = None
+        kt = ops.adaptive_k(stats, var, total, n_cols, dt, cfg.k_base, cfg.k_min, cfg.k_max,
+                            cfg.use_adaptive_k, cfg.adaptive_k_temperature)
+        sel, cnt, mask = ops.select_finalize(cand_idx, cand_score, cand_count, kt, want_mask=output_attentions)
+        mark("adaptive_k_select")
+        attn = ops.sparse_sdpa(dims, q, k_all, v_all, sel, cnt, g1, self.scale)
+        mark("sparse_sdpa")
+        out = F.linear(attn.view(B, L, H * D), self.o_proj.weight)
+        mark("o_proj")
+        if capture is not None:
+            capture.update(dims=dims, q=q, k=k_all, v=v_all, sel=sel, cnt=cnt, gate=g1, k_t=kt,
+                           n_chunks=ops.last_chunk_count)
+
+        weights = None
+        if output_attentions:
+            weights = self._attention_weights(q, k_all, cand_idx.long().view(B, L, k_eff),
+                                              mask.bool().view(B, L, k_eff))
+        return out, present, weights
+
+    def _attention_weights(self, q, k, indices, mask):
+        """Softmax weights [B, L, H, k_eff] aligned with ``indices`` (analysis output, small
+        shapes only; gated_sparse_attention.py:268-285)."""
+        B, L, H, D = q.shape
+        k_eff = indices.shape[-1]
+        if B * L * H * k_eff * D > (1 << 28):
+            raise NotImplementedError("output_attentions is limited to small shapes")
+        kr = self._repeat_kv(k)
+        idx = indices.unsqueeze(-1).unsqueeze(-1).expand(B, L, k_eff, H, D)
+        kg = torch.gather(kr.unsqueeze(1).expand(B, L, kr.shape[1], H, D), 2, idx).permute(0, 1, 3, 2, 4)
+        s = torch.einsum("bqhd,bqhkd->bqhk", q.float(), kg.float()) * self.scale
+        m = mask.unsqueeze(2)
+        p = torch.softmax(s.masked_fill(~m, float("-inf")), dim=-1).masked_fill(~m, 0.0)
+        return p.to(q.dtype)

@@ -1,0 +1,241 @@
+"""Tensor-level wrappers over the C ABI (include/gsa_b200.h).
+
+Each function checks devices, dtypes and layouts, allocates its outputs with torch (the ABI
+itself allocates nothing), and calls one entry point on the current CUDA stream.  Nothing here
+computes on the CPU: a tensor that is not on a CUDA device is an error.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import torch
+
+from . import _lib
+from ._lib import ACT, DTYPE_BF16, DTYPE_F32, Dims, ProjLayout, TopkParams
+
+DEBUG = os.environ.get("GSA_DEBUG", "0") == "1"
+# number of (indexer, top-k) chunk launches of the last indexer_select call
+last_chunk_count = 0
+
+
+def _p(t):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _stream():
+    return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    if dt == torch.float32:
+        return DTYPE_F32
+    if dt == torch.bfloat16:
+        return DTYPE_BF16
+    raise NotImplementedError(f"GSA B200 kernels support float32 and bfloat16, got {dt}")
+
+
+def _cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("GSA B200 ops take CUDA tensors only (there is no CPU path)")
+
+
+def check_device_error():
+    """Raise if a kernel recorded a device-side error (bounded wait timeout, bad index)."""
+    code = C.c_int(0)
+    _lib.call("gsa_get_device_error", C.byref(code), _stream())
+    if code.value:
+        raise _lib.GSAError("device", code.value)
+
+
+def _after(name):
+    if DEBUG:
+        torch.cuda.synchronize()
+        check_device_error()
+
+
+def make_dims(d_model, n_heads, n_kv_heads, d_head, n_idx_heads, d_idx, gate_act="sigmoid",
+              idx_act="sigmoid") -> Dims:
+    return Dims(d_model, n_heads, n_kv_heads, d_head, n_idx_heads, d_idx, ACT[gate_act], ACT[idx_act])
+
+
+def proj_epilogue(dims: Dims, layout: ProjLayout, proj: torch.Tensor, positions: torch.Tensor,
+                  cos_tab: torch.Tensor, sin_tab: torch.Tensor, has_g1: bool):
+    """q, k (RoPE), v (G2), g1 gate, indexer head weights w and row shift from the fused
+    projection output ``proj`` [T, Ncat]."""
+    _cuda(proj, positions, cos_tab, sin_tab)
+    T = proj.shape[0]
+    H, Hk, D, HI = dims.n_heads, dims.n_kv_heads, dims.d_head, dims.n_idx_heads
+    dt = proj.dtype
+    q = torch.empty(T, H, D, device=proj.device, dtype=dt)
+    k = torch.empty(T, Hk, D, device=proj.device, dtype=dt)
+    v = torch.empty(T, Hk, D, device=proj.device, dtype=dt)
+    g1 = torch.empty(T, H, D, device=proj.device, dtype=dt) if has_g1 else None
+    w = torch.empty(T, HI, device=proj.device, dtype=torch.float32)
+    shift = torch.empty(T, device=proj.device, dtype=torch.float32)
+    pos = positions.reshape(-1).to(torch.int64).contiguous()
+    assert proj.stride(1) == 1 and pos.numel() == T
+    cos_tab = cos_tab.contiguous()
+    sin_tab = sin_tab.contiguous()
+    _lib.call("gsa_proj_epilogue", C.byref(dims), C.byref(layout), dtype_code(dt), T, _p(proj),
+              proj.stride(0), _p(pos), _p(cos_tab), _p(sin_tab), dtype_code(cos_tab.dtype),
+              cos_tab.shape[0], _p(q), _p(k), _p(v), _p(g1), _p(w), _p(shift), _stream())
+    _after("proj_epilogue")
+    return q, k, v, g1, w, shift
+
+
+def indexer_scores(dims: Dims, qI: torch.Tensor, kI: torch.Tensor, w: torch.Tensor,
+                   bias: torch.Tensor, scale: float, q_pos0: int = 0, causal: bool = True,
+                   write_masked: bool = True, shift=None, row_stats=None) -> torch.Tensor:
+    """Materialised indexer scores [B, Lq, Lkv] fp32.  qI [B, Lq, H_I*d_I] and kI [B, Lkv, d_I]
+    may be row-strided views (last dim contiguous)."""
+    _cuda(qI, kI, w, bias)
+    B, Lq, _ = qI.shape
+    Lkv = kI.shape[1]
+    assert qI.stride(2) == 1 and kI.stride(2) == 1 and qI.dtype == kI.dtype
+    ld = (Lkv + 3) // 4 * 4
+    fill = float("-inf") if write_masked else 0.0
+    scores = torch.full((B * Lq, ld), fill, device=qI.device, dtype=torch.float32)
+    w = w.reshape(B * Lq, -1).float().contiguous()
+    bias = bias.float().contiguous()
+    _lib.call("gsa_indexer_scores", C.byref(dims), dtype_code(qI.dtype), B, Lq, Lkv, q_pos0,
+              int(causal), int(write_masked), _p(qI), qI.stride(1), qI.stride(0), _p(kI),
+              kI.stride(1), kI.stride(0), _p(w), _p(bias), float(scale), _p(shift), _p(scores), ld,
+              _p(row_stats), _stream())
+    _after("indexer_scores")
+    return scores[:, :Lkv].reshape(B, Lq, Lkv)
+
+
+def row_stats(scores2d: torch.Tensor) -> torch.Tensor:
+    """fp64 [R, 3] = (sum, sum of squares, finite count) per row of a fp32 [R, n] matrix."""
+    _cuda(scores2d)
+    s = scores2d.float()
+    if s.stride(1) != 1:
+        s = s.contiguous()
+    R, n = s.shape
+    stats = torch.zeros(R, 3, device=s.device, dtype=torch.float64)
+    _lib.call("gsa_row_stats", R, n, _p(s), s.stride(0), _p(stats), _stream())
+    _after("row_stats")
+    return stats
+
+
+def topk_candidates(scores2d: torch.Tensor, k_eff: int, Lq: int | None = None, q_pos0: int = 0,
+                    causal: bool = False):
+    """k_eff largest finite scores per row, ascending column order (int32 idx, fp32 score,
+    int32 count).  Unfilled slots hold column 0."""
+    _cuda(scores2d)
+    s = scores2d if scores2d.dtype == torch.float32 else scores2d.float()
+    if s.stride(1) != 1:
+        s = s.contiguous()
+    R, n = s.shape
+    idx = torch.zeros(R, k_eff, device=s.device, dtype=torch.int32)
+    sc = torch.zeros(R, k_eff, device=s.device, dtype=torch.float32)
+    cnt = torch.empty(R, device=s.device, dtype=torch.int32)
+    _lib.call("gsa_topk_candidates", R, Lq or R, n, q_pos0, int(causal), _p(s), s.stride(0),
+              int(k_eff), _p(idx), _p(sc), _p(cnt), _stream())
+    _after("topk_candidates")
+    return idx, sc, cnt
+
+
+def row_variance(stats: torch.Tensor, n_cols: int, dt: torch.dtype, shift=None):
+    R = stats.shape[0]
+    var = torch.empty(R, device=stats.device, dtype=torch.float32)
+    total = torch.empty(2, device=stats.device, dtype=torch.float64)
+    _lib.call("gsa_row_variance", R, n_cols, dtype_code(dt), _p(stats), _p(shift), _p(var),
+              _p(total), _stream())
+    _after("row_variance")
+    return var, total
+
+
+def adaptive_k(stats, var, total, n_cols: int, dt: torch.dtype, k_base: int, k_min: int,
+               k_max: int, use_adaptive: bool, temperature: float) -> torch.Tensor:
+    R = stats.shape[0]
+    k = torch.empty(R, device=stats.device, dtype=torch.int32)
+    p = TopkParams(k_base, k_min, k_max, int(use_adaptive), float(temperature))
+    _lib.call("gsa_adaptive_k", R, n_cols, dtype_code(dt), C.byref(p), _p(var), _p(total),
+              _p(stats), _p(k), _stream())
+    _after("adaptive_k")
+    return k
+
+
+def select_finalize(cand_idx, cand_score, cand_count, k, want_mask: bool = False):
+    R, k_eff = cand_idx.shape
+    sel = torch.empty(R, k_eff, device=cand_idx.device, dtype=torch.int32)
+    cnt = torch.empty(R, device=cand_idx.device, dtype=torch.int32)
+    mask = torch.empty(R, k_eff, device=cand_idx.device, dtype=torch.uint8) if want_mask else None
+    _lib.call("gsa_select_finalize", R, k_eff, _p(cand_idx), _p(cand_score), _p(cand_count), _p(k),
+              _p(sel), k_eff, _p(cnt), _p(mask), _stream())
+    _after("select_finalize")
+    return sel, cnt, mask
+
+
+def sparse_sdpa(dims: Dims, q, k, v, sel_idx, sel_count, gate, scale: float) -> torch.Tensor:
+    """q [B, Lq, H, D]; k, v [B, Lkv, Hk, D]; sel [B*Lq, ld] int32; gate like q or None."""
+    _cuda(q, k, v, sel_idx, sel_count, gate)
+    B, Lq = q.shape[0], q.shape[1]
+    Lkv = k.shape[1]
+    q = q.contiguous()
+    k = k.contiguous()
+    v = v.contiguous()
+    gate = gate.contiguous() if gate is not None else None
+    out = torch.empty_like(q)
+    _lib.call("gsa_sparse_sdpa", C.byref(dims), dtype_code(q.dtype), B, Lq, Lkv, _p(q), _p(k), _p(v),
+              _p(sel_idx), sel_idx.stride(0), _p(sel_count), _p(gate), _p(out), float(scale),
+              _stream())
+    _after("sparse_sdpa")
+    return out
+
+
+def apply_gate(x: torch.Tensor, logits: torch.Tensor, act: str, want_gate: bool = False):
+    _cuda(x, logits)
+    x = x.contiguous()
+    logits = logits.contiguous()
+    assert x.shape == logits.shape and x.dtype == logits.dtype
+    out = torch.empty_like(x)
+    gate = torch.empty_like(x) if want_gate else None
+    _lib.call("gsa_apply_gate", dtype_code(x.dtype), ACT[act], x.numel(), _p(x), _p(logits), _p(out),
+              _p(gate), _stream())
+    _after("apply_gate")
+    return out, gate
+
+
+def workspace_bytes(chunk_rows: int, n_cols: int) -> int:
+    return int(_lib.lib().gsa_workspace_size(chunk_rows, n_cols))
+
+
+def indexer_select(dims: Dims, qI, kI, w, bias, scale: float, shift, k_eff: int, q_pos0: int = 0,
+                   causal: bool = True, chunk_rows: int | None = None, row_stats=None,
+                   workspace=None):
+    """Indexer + top-k candidates for all rows, chunk by chunk (no [Lq, Lkv] score matrix).
+
+    qI [B, Lq, H_I*d_I], kI [B, Lkv, d_I] (row-strided views allowed).  Returns
+    (cand_idx, cand_score, cand_count, row_stats) with rows = B*Lq."""
+    _cuda(qI, kI, w, bias)
+    B, Lq, _ = qI.shape
+    Lkv = kI.shape[1]
+    R = B * Lq
+    dev = qI.device
+    if chunk_rows is None:
+        # bound the score scratch to ~1 GiB
+        chunk_rows = max(1, min(Lq, (1 << 30) // (4 * ((Lkv + 3) // 4 * 4))))
+    global last_chunk_count
+    last_chunk_count = B * ((Lq + chunk_rows - 1) // chunk_rows)
+    need = workspace_bytes(chunk_rows, Lkv)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, device=dev, dtype=torch.uint8)
+    cand_idx = torch.zeros(R, k_eff, device=dev, dtype=torch.int32)
+    cand_score = torch.empty(R, k_eff, device=dev, dtype=torch.float32)
+    cand_count = torch.empty(R, device=dev, dtype=torch.int32)
+    if row_stats is None:
+        row_stats = torch.zeros(R, 3, device=dev, dtype=torch.float64)
+    w = w.reshape(R, -1).float().contiguous()
+    bias = bias.float().contiguous()
+    _lib.call("gsa_indexer_select", C.byref(dims), dtype_code(qI.dtype), B, Lq, Lkv, q_pos0,
+              int(causal), _p(qI), qI.stride(1), qI.stride(0), _p(kI), kI.stride(1), kI.stride(0),
+              _p(w), _p(bias), float(scale), _p(shift), int(k_eff),
+              _p(cand_idx), _p(cand_score), _p(cand_count), _p(row_stats), chunk_rows,
+              _p(workspace), workspace.numel(), _stream())
+    _after("indexer_select")
+    return cand_idx, cand_score, cand_count, row_stats

@@ -1,0 +1,209 @@
+/*
+ * gsa_b200.h -- C ABI of the B200 (sm_100a) implementation of the Gated Sparse Attention
+ * forward path.
+ *
+ * Every entry point takes raw device pointers, sizes, a dtype code and a cudaStream_t, runs
+ * stream-ordered, allocates nothing, and returns an int status (GSA_OK or a GSA_ERR_* code).
+ * No exception crosses the ABI.  Scratch memory is passed in by the caller; its size comes
+ * from gsa_workspace_size().  Activations are row-major; a "row" is one (batch, token) pair.
+ *
+ * Reference interfaces replaced (alfredcs/Gated-Sparse-Attention, paths inside that project):
+ *   GatedSparseAttention.forward          gsa/attention/gated_sparse_attention.py:139-232
+ *   ValueGate.forward (G2)                gsa/attention/value_gate.py:77-113
+ *   RotaryEmbedding / apply_rotary_pos_emb gsa/attention/rope.py:117-185
+ *   GatedLightningIndexer.forward         gsa/attention/gated_indexer.py:88-155
+ *   AdaptiveTopKSelector                  gsa/attention/adaptive_topk.py:68-193
+ *   _sparse_attention / _gather_along_seq gsa/attention/gated_sparse_attention.py:234-323
+ *   OutputGate.forward (G1)               gsa/attention/output_gate.py:86-126
+ */
+#ifndef GSA_B200_H_
+#define GSA_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* cudaStream_t without pulling in the CUDA headers. */
+typedef struct CUstream_st* gsa_stream_t;
+
+enum {
+  GSA_OK = 0,
+  GSA_ERR_BAD_ARG = 1,         /* a size, stride, pointer or alignment the kernels cannot take */
+  GSA_ERR_UNSUPPORTED = 2,     /* a dtype / head size / activation with no kernel */
+  GSA_ERR_WORKSPACE = 3,       /* workspace smaller than gsa_workspace_size() */
+  GSA_ERR_TIMEOUT = 4,         /* a bounded device-side wait gave up (read via gsa_get_device_error) */
+  GSA_ERR_LAUNCH = 5,          /* kernel launch failed */
+  GSA_ERR_INDEX = 6,           /* a device-side index check failed (read via gsa_get_device_error) */
+  GSA_ERR_CUDA = 7             /* another CUDA runtime error */
+};
+
+enum { GSA_DTYPE_F32 = 0, GSA_DTYPE_BF16 = 1 };
+enum { GSA_ACT_SIGMOID = 0, GSA_ACT_TANH = 1, GSA_ACT_SILU = 2, GSA_ACT_RELU = 3 };
+
+/* Shape of one GSA layer (GSAConfig fields, gsa/config.py:24-74). */
+typedef struct {
+  int32_t d_model;
+  int32_t n_heads;
+  int32_t n_kv_heads;
+  int32_t d_head;
+  int32_t n_idx_heads;  /* n_indexer_heads */
+  int32_t d_idx;        /* d_indexer */
+  int32_t gate_act;     /* GSA_ACT_SIGMOID | TANH | SILU */
+  int32_t idx_act;      /* GSA_ACT_SIGMOID | RELU */
+} gsa_dims;
+
+/* Column offsets (in elements) of each projection inside one row of the fused projection
+ * output ``proj`` = x . [W_q | W_k | W_v | W_g2 | W_g1 | W_qI | W_kI | W_w]^T (+ biases).
+ * -1 marks a segment that is absent (gate disabled). */
+typedef struct {
+  int64_t q, k, v, g2, g1, qi, ki, wi;
+} gsa_proj_layout;
+
+/* Adaptive-k parameters (AdaptiveTopKSelector.__init__, adaptive_topk.py:29-57). */
+typedef struct {
+  int32_t k_base, k_min, k_max;
+  int32_t use_adaptive;
+  float temperature;
+} gsa_topk_params;
+
+/* Last error code recorded by a kernel on the current device (0 if none); clears it. */
+int gsa_get_device_error(int* code_out, gsa_stream_t stream);
+
+/* Library version string. */
+const char* gsa_version(void);
+
+/*
+ * Projection epilogue: RoPE on q and k (rope.py:151-185), G2 v <- v * act(g2)
+ * (value_gate.py:95-113), the G1 gate act(g1) (output_gate.py:101-117), the indexer head
+ * weights w = sigmoid(wI) (gated_indexer.py:121) and the per-row score centre
+ * shift = 0.5 * sum_j w_j.  ``proj`` rows already hold x.W^T + bias for every segment.
+ * Replaces gated_sparse_attention.py:175-186 after the GEMM, and the G1 logits of :226-227.
+ *   proj          [T, proj_ld]            dtype
+ *   positions     [T] int64
+ *   cos_tab/sin_tab [tab_rows, d_head]    tab_dtype (the module's RoPE buffers)
+ *   q_out [T, H, D], k_out [T, Hk, D], v_out [T, Hk, D], g1_out [T, H, D] (NULL if no G1),
+ *   w_out [T, H_I] fp32, shift_out [T] fp32
+ */
+int gsa_proj_epilogue(const gsa_dims* dims, const gsa_proj_layout* layout, int dtype, int64_t T,
+                      const void* proj, int64_t proj_ld, const int64_t* positions,
+                      const void* cos_tab, const void* sin_tab, int tab_dtype, int64_t tab_rows,
+                      void* q_out, void* k_out, void* v_out, void* g1_out, float* w_out,
+                      float* shift_out, gsa_stream_t stream);
+
+/*
+ * Gated indexer scores, I[t,s] = sum_j w[t,j] * act(scale * <qI[t,j], kI[s]> + bias[j])
+ * (gated_indexer.py:106-145), for query rows t in [0, Lq) of each batch against keys
+ * s in [0, Lkv).  With ``causal`` set, key s is masked for query row t when
+ * s > q_pos0 + t (gated_indexer.py:148-153 with a query offset); masked entries are written
+ * as -inf only if ``write_masked`` is set.
+ *   qI  [B, Lq, H_I*d_I] rows of stride qi_ld (elements), batch stride qi_bstride
+ *   kI  [B, Lkv, d_I]    rows of stride ki_ld, batch stride ki_bstride
+ *   w   [B*Lq, H_I] fp32 ; bias [H_I] fp32
+ *   scores [B*Lq, scores_ld] fp32
+ *   row_stats [B*Lq, 3] fp64 accumulated (+=) : sum(x - shift), sum((x - shift)^2), count
+ *     over unmasked entries; NULL to skip.  shift [B*Lq] fp32 or NULL (0).
+ */
+int gsa_indexer_scores(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int64_t Lkv,
+                       int64_t q_pos0, int causal, int write_masked, const void* qI,
+                       int64_t qi_ld, int64_t qi_bstride, const void* kI, int64_t ki_ld,
+                       int64_t ki_bstride, const float* w, const float* bias, float scale,
+                       const float* shift, float* scores, int64_t scores_ld, double* row_stats,
+                       gsa_stream_t stream);
+
+/*
+ * Row statistics of a materialised score matrix (adaptive_topk.py:84-88): per row
+ * sum(x), sum(x^2) and the count of finite entries, accumulated into row_stats[R, 3] (fp64,
+ * caller zeroes).  scores [R, scores_ld] fp32, first ``n_cols`` columns.
+ */
+int gsa_row_stats(int64_t R, int64_t n_cols, const float* scores, int64_t scores_ld,
+                  double* row_stats, gsa_stream_t stream);
+
+/*
+ * Top-k candidates: for every row r, the k_eff largest finite scores among the first n_r
+ * columns, ties broken lower column first, written in ascending column order
+ * (the candidate set of adaptive_topk.py:174-177).  n_r = n_cols, or, with ``causal``,
+ * min(n_cols, q_pos0 + (r % Lq) + 1).  cand_count[r] = min(k_eff, finite entries).
+ *   scores [R, scores_ld] fp32 ; cand_idx [R, k_eff] int32 ; cand_score [R, k_eff] fp32
+ */
+int gsa_topk_candidates(int64_t R, int64_t Lq, int64_t n_cols, int64_t q_pos0, int causal,
+                        const float* scores, int64_t scores_ld, int32_t k_eff,
+                        int32_t* cand_idx, float* cand_score, int32_t* cand_count,
+                        gsa_stream_t stream);
+
+/*
+ * Per-row variance over all N_r = n_cols entries with masked entries counted as 0, unbiased
+ * (adaptive_topk.py:84-93), rounded to the activation dtype; plus the layer-wide sum of the
+ * rounded variances and the row count, var_total[2] (fp64, overwritten).  row_stats as
+ * produced by gsa_indexer_scores / gsa_row_stats, shift as passed there (NULL = 0).
+ */
+int gsa_row_variance(int64_t R, int64_t n_cols, int dtype, const double* row_stats,
+                     const float* shift, float* var_out, double* var_total, gsa_stream_t stream);
+
+/*
+ * Adaptive k (adaptive_topk.py:96-136 and :161-172): k[r] from var[r], the layer mean
+ * var_total[0] / var_total[1] and the valid count, in the activation dtype's arithmetic;
+ * with use_adaptive == 0, k[r] = min(k_base, n_cols).  valid count = row_stats[r,2].
+ */
+int gsa_adaptive_k(int64_t R, int64_t n_cols, int dtype, const gsa_topk_params* p,
+                   const float* var, const double* var_total, const double* row_stats,
+                   int32_t* k_out, gsa_stream_t stream);
+
+/*
+ * Final selection: the top k[r] of each row's candidates (ties lower column first), in
+ * ascending column order, into sel_idx[R, sel_ld]; sel_count[r] = min(k[r], cand_count[r]).
+ * Reproduces the mask p < k_t of adaptive_topk.py:181-189.  If sel_mask [R, k_eff] (uint8)
+ * is given, sel_mask[r, p] = 1 iff candidate p of row r is selected (the reference's
+ * (indices, mask) pair with indices = the candidates).
+ */
+int gsa_select_finalize(int64_t R, int32_t k_eff, const int32_t* cand_idx,
+                        const float* cand_score, const int32_t* cand_count, const int32_t* k,
+                        int32_t* sel_idx, int64_t sel_ld, int32_t* sel_count,
+                        uint8_t* sel_mask, gsa_stream_t stream);
+
+/*
+ * Elementwise gate out = x * act(logits) over n elements, each op rounded to the dtype as
+ * torch evaluates it (value_gate.py:98-113, output_gate.py:111-126).  gate_out (nullable)
+ * receives act(logits) (the modules' last_gate_scores).
+ */
+int gsa_apply_gate(int dtype, int act, int64_t n, const void* x, const void* logits, void* out,
+                   void* gate_out, gsa_stream_t stream);
+
+/*
+ * GQA sparse SDPA with the G1 epilogue (gated_sparse_attention.py:234-290 and
+ * output_gate.py:124-126): for every row r = (b, t), softmax(scale * q K_sel^T) V_sel per
+ * head over the sel_count[r] keys sel_idx[r, :] shared by all heads, times gate[r] if given.
+ *   q [B, Lq, H, D] ; k, v [B, Lkv, Hk, D] (contiguous, 16-byte aligned rows) ; gate like q
+ *   out [B, Lq, H, D] in dtype.  sel indices are key positions inside the batch's sequence.
+ */
+int gsa_sparse_sdpa(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int64_t Lkv,
+                    const void* q, const void* k, const void* v, const int32_t* sel_idx,
+                    int64_t sel_ld, const int32_t* sel_count, const void* gate, void* out,
+                    float scale, gsa_stream_t stream);
+
+/*
+ * Workspace for gsa_indexer_select: bytes needed for a query chunk of ``chunk_rows`` rows
+ * against n_cols keys.
+ */
+int64_t gsa_workspace_size(int64_t chunk_rows, int64_t n_cols);
+
+/*
+ * Indexer + top-k candidates over all query rows, chunk by chunk, so that at most
+ * chunk_rows x Lkv scores exist at any time (in ``workspace``).  Row statistics for the
+ * adaptive k are accumulated into row_stats (caller zeroes).  Same tensors as
+ * gsa_indexer_scores and gsa_topk_candidates; causal prefill when ``causal``.
+ */
+int gsa_indexer_select(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int64_t Lkv,
+                       int64_t q_pos0, int causal, const void* qI, int64_t qi_ld,
+                       int64_t qi_bstride, const void* kI, int64_t ki_ld, int64_t ki_bstride,
+                       const float* w, const float* bias, float scale, const float* shift,
+                       int32_t k_eff, int32_t* cand_idx, float* cand_score,
+                       int32_t* cand_count, double* row_stats, int64_t chunk_rows,
+                       void* workspace, int64_t workspace_bytes, gsa_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GSA_B200_H_ */

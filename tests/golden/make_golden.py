@@ -1,0 +1,182 @@
+"""Generate golden fixtures for the GSA forward path by running the reference itself.
+
+This script imports the unmodified reference package ``gsa`` (alfredcs/Gated-Sparse-Attention)
+from a checkout given by ``--reference`` (default ``/root/reference``), runs its own modules on
+seeded inputs, and writes small safetensors files next to this script.  It is the only place
+that executes reference code; the fixtures it writes are what the tests read.
+
+Two shims are needed to import the reference unmodified:
+  * ``gsa/__init__.py:14`` imports ``gsa/utils/checkpoint.py``, which imports ``omegaconf``
+    (not installed here).  A stub module providing ``DictConfig`` and ``OmegaConf`` is created
+    in a temporary directory and put first on ``sys.path``.
+  * ``sys.pycache_prefix`` points at a temporary directory so that no ``.pyc`` shipped inside
+    the reference checkout is ever read.
+
+Each fixture follows the reference forward step by step
+(``gsa/attention/gated_sparse_attention.py:139-232``) through the reference's own submodules,
+and checks that the step-by-step output equals ``module(x, positions)`` bit for bit.
+
+Usage:  python tests/golden/make_golden.py [--reference PATH]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import tempfile
+from pathlib import Path
+
+import torch
+from safetensors.torch import save_file
+
+HERE = Path(__file__).resolve().parent
+
+# name -> (config kwargs, batch, seq_len, dtype, rows to sample or None for all rows)
+FIXTURES = {
+    # small shapes, every tensor stored in full
+    "tiny_fp32_b2_l192": (dict(d_model=256, n_heads=4, n_kv_heads=2, d_indexer=32,
+                               n_indexer_heads=4, k_base=48, k_min=16, k_max=96,
+                               max_position_embeddings=1024), 2, 192, "float32", None),
+    "tiny_bf16_b2_l192": (dict(d_model=256, n_heads=4, n_kv_heads=2, d_indexer=32,
+                               n_indexer_heads=4, k_base=48, k_min=16, k_max=96,
+                               max_position_embeddings=1024), 2, 192, "bfloat16", None),
+    "tiny_fixedk_nogate_fp32_l128": (dict(d_model=256, n_heads=4, n_kv_heads=2, d_indexer=32,
+                                          n_indexer_heads=2, k_base=32, k_min=16, k_max=64,
+                                          use_adaptive_k=False, use_value_gate=False,
+                                          use_output_gate=False,
+                                          max_position_embeddings=1024), 1, 128, "float32", None),
+    # the CPU-runnable 2048-token layer: d_model 512, 8/2 heads, 4 indexer heads of dim 32,
+    # k_base 256 clipped to [128, 512]
+    "c1_fp32_l2048": (dict(d_model=512, n_heads=8, n_kv_heads=2, d_indexer=32, n_indexer_heads=4,
+                           k_base=256, k_min=128, k_max=512), 1, 2048, "float32", 24),
+    # the 4096-wide layer (32/8 heads of 128, 8 indexer heads of 64) at a length the
+    # reference's eager gather can hold, with k scaled down so that selection is sparse
+    "w4096_bf16_l384": (dict(d_model=4096, n_heads=32, n_kv_heads=8, d_indexer=64,
+                             n_indexer_heads=8, k_base=64, k_min=32, k_max=128), 1, 384,
+                        "bfloat16", 24),
+}
+
+WEIGHT_SEED = 0
+INPUT_SEED = 1
+
+
+def _import_reference(ref_root: Path):
+    tmp = Path(tempfile.mkdtemp(prefix="gsa_ref_shim_"))
+    stub = tmp / "omegaconf"
+    stub.mkdir()
+    (stub / "__init__.py").write_text(
+        "class DictConfig(dict):\n    pass\n\n"
+        "class OmegaConf:\n    @staticmethod\n    def to_container(cfg, resolve=True):\n"
+        "        return dict(cfg)\n")
+    sys.pycache_prefix = str(tmp / "pycache")
+    sys.path.insert(0, str(tmp))
+    sys.path.insert(0, str(ref_root))
+    import gsa  # noqa: F401  (the reference package)
+    from gsa import GSAConfig, GatedSparseAttention
+    from gsa.attention.rope import apply_rotary_pos_emb
+    return GSAConfig, GatedSparseAttention, apply_rotary_pos_emb
+
+
+def _sample_rows(L: int, n: int | None):
+    if n is None:
+        return torch.arange(L)
+    head = [0, 1, 2, 3, 7, 15, 31, 63]
+    rest = torch.linspace(64, L - 1, n - len(head)).round().long().tolist()
+    rows = sorted(set(h for h in head if h < L) | set(rest))
+    return torch.tensor(rows, dtype=torch.long)
+
+
+def _checksums(module) -> dict:
+    out = {}
+    for name, p in module.state_dict().items():
+        t = p.detach().double()
+        out[name] = [float(t.sum()), float((t * t).sum()), [float(v) for v in t.flatten()[:4]]]
+    return out
+
+
+@torch.no_grad()
+def make_fixture(name, spec, refs):
+    GSAConfig, GatedSparseAttention, apply_rotary_pos_emb = refs
+    cfg_kwargs, B, L, dtype_name, n_rows = spec
+    dtype = getattr(torch, dtype_name)
+    cfg = GSAConfig(**cfg_kwargs)
+
+    torch.manual_seed(WEIGHT_SEED)
+    m = GatedSparseAttention(cfg).eval()
+    m = m.to(dtype)
+    gen = torch.Generator().manual_seed(INPUT_SEED)
+    x = torch.randn(B, L, cfg.d_model, generator=gen).to(dtype)
+    positions = torch.arange(L).unsqueeze(0).expand(B, -1)
+
+    # reference forward, step by step (gated_sparse_attention.py:167-230)
+    q = m.q_proj(x).view(B, L, m.n_heads, m.d_head)
+    k = m.k_proj(x).view(B, L, m.n_kv_heads, m.d_head)
+    v = m.v_proj(x).view(B, L, m.n_kv_heads, m.d_head)
+    if m.value_gate is not None:
+        v = m.value_gate(v, x)
+    cos, sin = m.rotary_emb(positions)
+    q, k = apply_rotary_pos_emb(q, k, cos, sin)
+    scores = m.indexer(x, positions, kv_hidden_states=None)
+    indices, mask, k_values = m.topk_selector(scores, L, scores.shape[-1], return_k_values=True)
+    attn, _ = m._sparse_attention(q, k, v, indices, mask)
+    gated = m.output_gate(attn, x) if m.output_gate is not None else attn
+    out = m.o_proj(gated.reshape(B, L, -1))
+
+    full, _, _ = m(x, positions=positions)
+    assert torch.equal(full, out), f"{name}: step-by-step forward differs from module forward"
+
+    # the per-row variance exactly as adaptive_topk.py:84-93 computes it
+    valid = scores != float("-inf")
+    var = scores.masked_fill(~valid, 0).var(dim=-1)
+
+    rows = _sample_rows(L, n_rows)
+    t = {
+        "rows": rows.to(torch.int32),
+        "k_values": k_values.to(torch.int32),
+        "var": var,
+        "q": q[:, rows].contiguous(),
+        "k": k.contiguous() if n_rows is None else k[:, rows].contiguous(),
+        "v": v.contiguous() if n_rows is None else v[:, rows].contiguous(),
+        "scores": scores[:, rows].contiguous(),
+        "indices": indices[:, rows].to(torch.int32).contiguous(),
+        "mask": mask[:, rows].to(torch.uint8).contiguous(),
+        "attn": attn[:, rows].contiguous(),
+        "out": out[:, rows].contiguous(),
+    }
+    if n_rows is None:
+        t["x"] = x.contiguous()
+    meta = {
+        "config": json.dumps(cfg_kwargs),
+        "batch": str(B),
+        "seq_len": str(L),
+        "dtype": dtype_name,
+        "weight_seed": str(WEIGHT_SEED),
+        "input_seed": str(INPUT_SEED),
+        "param_checksums": json.dumps(_checksums(m)),
+        "x_checksum": json.dumps([float(x.double().sum()), float((x.double() ** 2).sum())]),
+        "var_mean": repr(float(var.mean())),
+        "torch": torch.__version__,
+    }
+    path = HERE / f"{name}.safetensors"
+    save_file(t, str(path), metadata=meta)
+    print(f"{name}: {path.stat().st_size / 1024:.0f} KiB, k_values mean "
+          f"{k_values.float().mean():.1f}, rows {len(rows)}")
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default=os.environ.get("GSA_REFERENCE", "/root/reference"))
+    ap.add_argument("--only", default=None)
+    args = ap.parse_args()
+    torch.set_num_threads(os.cpu_count() or 1)
+    refs = _import_reference(Path(args.reference))
+    for name, spec in FIXTURES.items():
+        if args.only and name != args.only:
+            continue
+        make_fixture(name, spec, refs)
+
+
+if __name__ == "__main__":
+    main()

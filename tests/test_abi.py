@@ -1,0 +1,59 @@
+"""The C ABI library loads and exports every entry point include/gsa_b200.h declares (CPU only:
+no entry point that touches the GPU is called)."""
+
+import ctypes
+import re
+
+from conftest import ROOT
+
+HEADER = ROOT / "include" / "gsa_b200.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^\s*(?:int|int64_t|const char\s*\*)\s+(gsa_\w+)\s*\(", text, re.M)))
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    assert "gsa_sparse_sdpa" in names and "gsa_indexer_select" in names
+    assert len(names) >= 12
+
+
+def test_library_exports_every_declared_symbol():
+    from gsa_b200 import _lib
+
+    lib = ctypes.CDLL(str(_lib.LIB_PATH))
+    for name in declared_functions():
+        assert hasattr(lib, name), f"{name} declared in gsa_b200.h but not exported"
+
+
+def test_binding_covers_header():
+    from gsa_b200 import _lib
+
+    assert sorted(_lib.exported_symbols()) == declared_functions()
+
+
+def test_version_and_workspace_without_gpu():
+    from gsa_b200 import _lib
+
+    lib = _lib.lib()
+    assert b"sm_100a" in lib.gsa_version()
+    assert lib.gsa_workspace_size(128, 1000) == 128 * 1000 * 4
+    assert lib.gsa_workspace_size(3, 5) == 3 * 8 * 4
+    assert lib.gsa_workspace_size(0, 5) == 0
+
+
+def test_bad_arguments_are_rejected_before_any_launch():
+    """Argument validation returns GSA_ERR_BAD_ARG without touching the device."""
+    from gsa_b200 import _lib
+
+    lib = _lib.lib()
+    # negative sizes / null pointers
+    assert lib.gsa_topk_candidates(-1, 1, 10, 0, 0, None, 10, 4, None, None, None, None) == 1
+    assert lib.gsa_topk_candidates(4, 4, 10, 0, 0, None, 10, 0, None, None, None, None) == 1
+    assert lib.gsa_select_finalize(4, 8, None, None, None, None, None, 4, None, None, None) == 1
+    assert lib.gsa_row_stats(4, 10, None, 5, None, None) == 1
+    assert lib.gsa_apply_gate(7, 0, 10, None, None, None, None, None) == 1
+    # empty work is a no-op success
+    assert lib.gsa_topk_candidates(0, 1, 10, 0, 0, None, 10, 4, None, None, None, None) == 0

@@ -1,0 +1,192 @@
+"""Parity of the CUDA path with the reference (golden fixtures) and the CPU oracle.
+
+Tolerances (from the task's parity bar):
+  * indexer scores: 1e-3 relative (fp32), 2e-2 relative (bf16), elementwise;
+  * layer output: 2e-2 relative (bf16, Frobenius norm of the error over the norm of the
+    reference); fp32 layer output 1e-3;
+  * selected index sets: bit-exact when the selection runs on the reference's scores, compared
+    as sets over mask-valid entries; a row is excused only when the reference itself has a tie
+    at its k_t boundary (counted and reported).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN_NAMES, golden_inputs, load_golden
+import gsa_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def rel_fro(a, b):
+    a = a.double().cpu()
+    b = b.double().cpu()
+    return float((a - b).norm() / b.norm().clamp_min(1e-30))
+
+
+def sets_from(indices, mask):
+    out = []
+    for r in range(indices.shape[0]):
+        out.append(np.sort(indices[r][mask[r].bool()].cpu().numpy().astype(np.int64)))
+    return out
+
+
+@pytest.fixture(scope="module", params=GOLDEN_NAMES)
+def gcase(request, cuda_ok):
+    g, meta = load_golden(request.param)
+    cfg, m, x = golden_inputs(meta)
+    return request.param, g, meta, cfg, m.to(DEV), x.to(DEV)
+
+
+# ---------------------------------------------------------------------------------------------
+def test_projection_epilogue(gcase):
+    from gsa_b200 import ops
+
+    name, g, meta, cfg, m, x = gcase
+    B, L, _ = x.shape
+    W, b, layout = m.fused_projection()
+    proj = torch.addmm(b, x.reshape(B * L, -1), W.t())
+    pos = torch.arange(L, device=DEV).unsqueeze(0).expand(B, -1)
+    q, k, v, g1, w, shift = ops.proj_epilogue(m._dims(), layout, proj, pos, m.rotary_emb.cos_cached,
+                                              m.rotary_emb.sin_cached, m.output_gate is not None)
+    torch.cuda.synchronize()
+    ops.check_device_error()
+    rows = g["rows"].long().to(DEV)
+    tol = 1e-4 if x.dtype == torch.float32 else 2e-2
+    assert rel_fro(q.view(B, L, cfg.n_heads, -1)[:, rows], g["q"]) < tol
+    kk = k.view(B, L, cfg.n_kv_heads, -1)
+    vv = v.view(B, L, cfg.n_kv_heads, -1)
+    if g["k"].shape[1] != L:
+        kk, vv = kk[:, rows], vv[:, rows]
+    assert rel_fro(kk, g["k"]) < tol
+    assert rel_fro(vv, g["v"]) < tol
+
+
+def test_indexer_scores(gcase):
+    name, g, meta, cfg, m, x = gcase
+    rows = g["rows"].long().to(DEV)
+    s = m.indexer(x).float()
+    ref = g["scores"].float().to(DEV)
+    ours = s[:, rows]
+    inf_ref = torch.isinf(ref)
+    assert torch.equal(torch.isinf(ours), inf_ref)
+    rtol = 1e-3 if x.dtype == torch.float32 else 2e-2
+    err = (ours[~inf_ref] - ref[~inf_ref]).abs()
+    bound = rtol * ref[~inf_ref].abs() + (1e-6 if x.dtype == torch.float32 else 1e-3)
+    assert bool((err <= bound).all()), float((err / ref[~inf_ref].abs()).max())
+
+
+def test_selection_on_reference_scores_is_bit_exact(gcase):
+    """Variance, k_t and the selected sets from the reference's own scores."""
+    from gsa_b200 import ops
+
+    name, g, meta, cfg, m, x = gcase
+    B, L, _ = x.shape
+    rows = g["rows"].long()
+    scores = g["scores"].float().to(DEV)  # [B, rows, L]
+    R = scores.shape[1]
+    k_eff = min(cfg.k_max, L) if cfg.use_adaptive_k else min(cfg.k_base, L)
+    full_rows = R == L
+    excused = 0
+    for b in range(B):
+        s2d = scores[b].contiguous()
+        if full_rows and cfg.use_adaptive_k:
+            # whole layer's rows present: run the selector end to end
+            pass
+        kv = g["k_values"][b][rows].to(DEV).int()
+        cand_idx, cand_score, cand_count = ops.topk_candidates(s2d, k_eff)
+        sel, cnt, mask = ops.select_finalize(cand_idx, cand_score, cand_count, kv, want_mask=True)
+        torch.cuda.synchronize()
+        ops.check_device_error()
+        ours = [np.sort(sel[r, :cnt[r]].cpu().numpy().astype(np.int64)) for r in range(R)]
+        ref = sets_from(g["indices"][b], g["mask"][b])
+        ties = set(O.boundary_tie_rows(g["scores"][b].float(), g["k_values"][b][rows]).tolist())
+        for r in range(R):
+            if r in ties:
+                excused += 1
+                continue
+            assert np.array_equal(ours[r], ref[r]), (name, b, r)
+        # the selected mask agrees with the candidate indices
+        m_sets = sets_from(cand_idx.long().cpu(), mask.cpu())
+        for r in range(R):
+            assert np.array_equal(m_sets[r], ours[r])
+    print(f"{name}: rows excused for boundary ties: {excused}")
+
+
+def test_variance_and_k_on_reference_scores(gcase):
+    """Per-row variance and k_t from the reference's scores (all rows of the small fixtures)."""
+    from gsa_b200 import AdaptiveTopKSelector
+
+    name, g, meta, cfg, m, x = gcase
+    B, L, _ = x.shape
+    if g["scores"].shape[1] != L:
+        pytest.skip("fixture stores sampled rows only; the layer mean needs every row")
+    sel = AdaptiveTopKSelector(cfg.k_base, cfg.k_min, cfg.k_max, cfg.use_adaptive_k,
+                               cfg.adaptive_k_temperature)
+    scores = g["scores"].to(DEV)
+    idx, mask, kv = sel(scores, L, L, return_k_values=True)
+    torch.cuda.synchronize()
+    ref_k = g["k_values"].long()
+    near = torch.zeros_like(ref_k, dtype=torch.bool)
+    if cfg.use_adaptive_k:
+        var_ref = g["var"]
+        valid = (g["scores"] != float("-inf")).sum(-1).float()
+        pre = O.adaptive_k_prefloor(var_ref, valid, var_ref.mean(), cfg.k_base, cfg.k_min, cfg.k_max,
+                                    cfg.adaptive_k_temperature).double()
+        near = (pre - pre.round()).abs() < 1e-3
+    diff = (kv.cpu() != ref_k) & ~near
+    assert int(diff.sum()) == 0, f"{int(diff.sum())} rows with a different k_t"
+    ties = 0
+    for b in range(B):
+        ours = sets_from(idx[b].cpu(), mask[b].cpu())
+        ref = sets_from(g["indices"][b], g["mask"][b])
+        tie_rows = set(O.boundary_tie_rows(g["scores"][b].float(), g["k_values"][b]).tolist())
+        for r in range(L):
+            if r in tie_rows or bool(near[b, r]):
+                ties += 1
+                continue
+            assert np.array_equal(ours[r], ref[r]), (name, b, r)
+    print(f"{name}: rows excused (tie or k_t within 1e-3 of an integer): {ties}")
+
+
+def test_sparse_sdpa_on_reference_selection(gcase):
+    from gsa_b200 import ops
+
+    name, g, meta, cfg, m, x = gcase
+    B, L, _ = x.shape
+    if g["k"].shape[1] != L:
+        pytest.skip("fixture stores sampled K/V rows only")
+    rows = g["rows"].long()
+    q = g["q"].to(DEV)  # [B, R, H, D]
+    k = g["k"].to(DEV)
+    v = g["v"].to(DEV)
+    R = q.shape[1]
+    k_eff = g["indices"].shape[-1]
+    sel = torch.zeros(B * R, k_eff, dtype=torch.int32)
+    cnt = torch.zeros(B * R, dtype=torch.int32)
+    for b in range(B):
+        for r in range(R):
+            s = g["indices"][b, r][g["mask"][b, r].bool()]
+            sel[b * R + r, :len(s)] = s.int()
+            cnt[b * R + r] = len(s)
+    out = ops.sparse_sdpa(m._dims(), q, k, v, sel.to(DEV), cnt.to(DEV), None, m.scale)
+    torch.cuda.synchronize()
+    ops.check_device_error()
+    tol = 1e-4 if q.dtype == torch.float32 else 2e-2
+    assert rel_fro(out, g["attn"]) < tol
+
+
+def test_layer_output(gcase):
+    name, g, meta, cfg, m, x = gcase
+    rows = g["rows"].long().to(DEV)
+    out, _, _ = m(x)
+    torch.cuda.synchronize()
+    from gsa_b200 import ops
+    ops.check_device_error()
+    err = rel_fro(out[:, rows], g["out"])
+    tol = 1e-3 if x.dtype == torch.float32 else 2e-2
+    print(f"{name}: layer output rel err {err:.2e}")
+    assert err < tol
