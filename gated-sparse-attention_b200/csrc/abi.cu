@@ -97,7 +97,27 @@ int gsa_indexer_scores(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, i
   if (dims->idx_act != GSA_ACT_SIGMOID && dims->idx_act != GSA_ACT_RELU) return GSA_ERR_UNSUPPORTED;
   IdxArgs a{dtype, Lq, Lkv, q_pos0, causal, write_masked, dims->n_idx_heads, dims->d_idx, dims->idx_act,
             qI, qi_ld, qi_bstride, kI, ki_ld, ki_bstride, w, bias, scale, shift, scores, scores_ld, row_stats};
-  return launch_indexer_simt(a, B, reinterpret_cast<cudaStream_t>(stream));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (indexer_tc_eligible(a)) {
+    // tensor-core kernel: bf16, d_I = 64, H_I in {4, 8}, sigmoid; one launch per batch row
+    DeviceInfo* di;
+    int st = device_info(&di);
+    if (st) return st;
+    const int64_t HI = dims->n_idx_heads;
+    for (int64_t b = 0; b < B; ++b) {
+      IdxArgs ab = a;
+      ab.qI = static_cast<const __nv_bfloat16*>(qI) + b * qi_bstride;
+      ab.kI = static_cast<const __nv_bfloat16*>(kI) + b * ki_bstride;
+      ab.w = w + b * Lq * HI;
+      ab.shift = shift ? shift + b * Lq : nullptr;
+      ab.scores = scores + b * Lq * scores_ld;
+      ab.row_stats = row_stats ? row_stats + b * Lq * 3 : nullptr;
+      st = launch_indexer_tc(ab, di->err, s);
+      if (st) return st;
+    }
+    return GSA_OK;
+  }
+  return launch_indexer_simt(a, B, s);
 }
 
 int gsa_row_stats(int64_t R, int64_t n_cols, const float* scores, int64_t scores_ld, double* row_stats,

@@ -1,0 +1,405 @@
+// Gated lightning indexer on the 5th-generation tensor cores (tcgen05 + TMEM, TMA-fed).
+//
+//   I[t,s] = sum_j w[t,j] * sigmoid(scale * <qI[t,j,:], kI[s,:]> + b[j])      (gated_indexer.py:114-145)
+//
+// The one dense contraction of the layer.  Its shape: every query row has H_I heads of d_I = 64
+// and all heads share one key vector kI[s] (gated_indexer.py:66-67, 126).  So the MMA is
+//
+//   D[s, (t,j)] = kI[s, :] . qI[t, j, :]       M = 128 keys, N = 256 (token, head) pairs, K = 64
+//
+// A = a 128-key tile of kI (16 KiB, TMA, ring of stages), B = the (TOK x H_I) x 64 query block
+// of the CTA (32 KiB, loaded once; TOK = 256 / H_I tokens), D in TMEM (256 fp32 columns,
+// double-buffered in the 512-column TMEM).  TMEM lane = key, column = token * H_I + head, so an
+// epilogue thread owns one key and finds the H_I heads of a token in adjacent columns: the head
+// reduction needs no data exchange, and for a fixed token the 32 lanes of a warp hold 32
+// consecutive keys, so score stores are coalesced 128-byte rows.
+//
+// Epilogue (the bound: H_I sigmoids per (t, s) pair, on the MUFU pipe):
+//   sigmoid(z) = 0.5 + 0.5 tanh(z / 2)  =>  I[t,s] = c_t + sum_j (w_tj / 2) tanh((scale*acc + b_j) / 2)
+// with c_t = sum_j w_tj / 2, i.e. one FFMA, one tanh.approx and one FFMA per (t, s, j).  The
+// tanh form's error (< 1e-3 relative on the score) is inside the bf16 parity bar (2e-2); the
+// fp32 layer runs on the precise CUDA-core kernel instead.
+//
+// Roles (320 threads): warp 0 = TMA producer, warp 1 = TMEM allocator + MMA issuer (one lane),
+// warps 2..9 = epilogue (two warps per TMEM lane quarter, each taking half of the tokens).
+// Work item (CTA) = one query block x a range of up to kTilesPerCta key tiles; causal tiles
+// beyond the block's last query are never visited.  Every wait is bounded.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "kernels.cuh"
+
+namespace gsa {
+
+namespace tc {
+
+constexpr int kKeys = 128;          // M: keys per tile (TMEM lanes)
+constexpr int kN = 256;             // N: (token, head) pairs per tile
+constexpr int kDI = 64;             // K: indexer dim (one 128-byte swizzle atom)
+constexpr int kStages = 6;          // kI tile ring
+constexpr int kTilesPerCta = 32;    // key tiles per work item
+constexpr int kThreads = 320;
+constexpr int kATileBytes = kKeys * kDI * 2;  // 16 KiB
+constexpr int kBTileBytes = kN * kDI * 2;     // 32 KiB
+constexpr int kSmemBytes = 1024 + kBTileBytes + kStages * kATileBytes + kN * 4 + 2 * 64 * 4 + 256;
+
+struct Params {
+  int n_rows;
+  int64_t Lkv;
+  int64_t q_pos0;
+  int causal;
+  float half_scale;
+  const float* bias;
+  const float* w;
+  const float* shift;
+  float* scores;
+  int64_t ld;
+  double* row_stats;
+  int* err;
+};
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor, kind::f16: D f32, A and B bf16, both K-major, M = 128, N = 256.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kN >> 3) << 17) |
+                            ((uint32_t)(kKeys >> 4) << 24);
+
+__device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accum));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ float tanh_fast(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <int HI>
+__global__ void __launch_bounds__(kThreads, 1)
+    indexer_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ, Params p) {
+  constexpr int TOK = kN / HI;        // tokens per query block
+  constexpr int TOK_HALF = TOK / 2;   // tokens per epilogue warp
+  constexpr int TOK_PER_LD = 32 / HI; // tokens per 32-column TMEM load
+  extern __shared__ uint8_t smem_raw[];
+
+  // ---- work item ----
+  const int blk = blockIdx.y;
+  const int tok0 = blk * TOK;
+  const int ntok = min(TOK, p.n_rows - tok0);
+  if (ntok <= 0) return;
+  const int64_t pos_last = p.q_pos0 + tok0 + ntok - 1;
+  const int64_t key_limit = p.causal ? min(p.Lkv, pos_last + 1) : p.Lkv;
+  const int tiles_total = (int)((key_limit + kKeys - 1) / kKeys);
+  const int t_begin = blockIdx.x * kTilesPerCta;
+  const int t_end = min(tiles_total, t_begin + kTilesPerCta);
+  if (t_begin >= t_end) return;
+  const int n_my = t_end - t_begin;
+
+  // ---- shared memory carve-up (1024-byte aligned for the swizzled tiles) ----
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* base = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
+  uint8_t* sB = base;
+  uint8_t* sA = base + kBTileBytes;
+  float* w_s = reinterpret_cast<float*>(sA + kStages * kATileBytes);  // [TOK][HI] holds w / 2
+  float* c_s = w_s + kN;                                              // [TOK]  c_t = sum_j w_tj / 2
+  float* d_s = c_s + 64;                                              // [TOK]  c_t - shift_t
+  uint64_t* bars = reinterpret_cast<uint64_t*>(d_s + 64);
+  uint64_t* a_full = bars;
+  uint64_t* a_empty = bars + kStages;
+  uint64_t* b_full = bars + 2 * kStages;
+  uint64_t* t_full = b_full + 1;
+  uint64_t* t_empty = t_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(t_empty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&a_full[s], 1);
+      mbar_init(&a_empty[s], 1);
+    }
+    mbar_init(b_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&t_full[b], 1);
+      mbar_init(&t_empty[b], 8);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot))
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (warp >= 2) {
+    for (int i = threadIdx.x - 64; i < kN; i += kThreads - 64) {
+      const int t = i / HI, j = i % HI;
+      w_s[i] = (t < ntok) ? 0.5f * p.w[(int64_t)(tok0 + t) * HI + j] : 0.f;
+    }
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  if (warp >= 2) {
+    for (int t = threadIdx.x - 64; t < TOK; t += kThreads - 64) {
+      float c = 0.f;
+#pragma unroll
+      for (int j = 0; j < HI; ++j) c += w_s[t * HI + j];
+      c_s[t] = c;
+      d_s[t] = (p.shift && t < ntok) ? c - p.shift[tok0 + t] : c;
+    }
+  }
+  __syncthreads();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------ TMA producer ------------------------------------
+    if (lane == 0) {
+      mbar_arrive_expect_tx(b_full, kBTileBytes);
+      tma_load_3d(sB, &tmQ, 0, 0, tok0, b_full);
+      for (int i = 0; i < n_my; ++i) {
+        const int s = i % kStages;
+        if (!mbar_wait(&a_empty[s], ((i / kStages) & 1) ^ 1, p.err)) break;
+        mbar_arrive_expect_tx(&a_full[s], kATileBytes);
+        tma_load_2d(sA + s * kATileBytes, &tmK, 0, (t_begin + i) * kKeys, &a_full[s]);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------- MMA issuer -------------------------------------
+    if (lane == 0) {
+      bool ok = mbar_wait(b_full, 0, p.err);
+      const uint64_t bdesc0 = sw128_desc(smem_u32(sB));
+      for (int i = 0; ok && i < n_my; ++i) {
+        const int s = i % kStages, buf = i & 1;
+        if (!mbar_wait(&a_full[s], (i / kStages) & 1, p.err)) break;
+        if (!mbar_wait(&t_empty[buf], ((i >> 1) & 1) ^ 1, p.err)) break;
+        fence_after();
+        const uint64_t adesc0 = sw128_desc(smem_u32(sA + s * kATileBytes));
+#pragma unroll
+        for (int k = 0; k < kDI / 16; ++k)
+          umma(tmem + buf * kN, adesc0 + 2 * k, bdesc0 + 2 * k, k > 0 ? 1u : 0u);
+        umma_commit(&a_empty[s]);
+        umma_commit(&t_full[buf]);
+      }
+      // every MMA must have completed before TMEM is released
+      if (n_my > 0) mbar_wait(&t_full[(n_my - 1) & 1], ((n_my - 1) >> 1) & 1, p.err);
+    }
+  } else {
+    // -------------------------------------- epilogue --------------------------------------
+    const int ew = warp - 2;
+    const int quarter = warp & 3;   // TMEM lane quarter this warp may access
+    const int half = ew >> 2;       // which half of the block's tokens
+    float hb[HI];
+#pragma unroll
+    for (int j = 0; j < HI; ++j) hb[j] = 0.5f * p.bias[j];
+    float s1[TOK_HALF], s2[TOK_HALF];
+#pragma unroll
+    for (int t = 0; t < TOK_HALF; ++t) s1[t] = s2[t] = 0.f;
+    const int64_t pos0 = p.q_pos0 + tok0;
+
+    for (int i = 0; i < n_my; ++i) {
+      const int buf = i & 1;
+      if (!mbar_wait(&t_full[buf], (i >> 1) & 1, p.err)) break;
+      fence_after();
+      const int64_t key = (int64_t)(t_begin + i) * kKeys + quarter * 32 + lane;
+      const bool key_ok = key < p.Lkv;
+      // the whole tile is unmasked for every token of the block?
+      const bool tile_full = ((int64_t)(t_begin + i + 1) * kKeys <= p.Lkv) &&
+                             (!p.causal || (int64_t)(t_begin + i + 1) * kKeys - 1 <= pos0) && ntok == TOK;
+      const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + buf * kN + half * (kN / 2);
+#pragma unroll
+      for (int c = 0; c < (kN / 2) / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tbase + c * 32, r);
+        tmem_wait_ld();
+        if (c == (kN / 2) / 32 - 1) {
+          // the last load of this buffer is done: hand it back to the MMA warp
+          fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&t_empty[buf]);
+        }
+#pragma unroll
+        for (int tt = 0; tt < TOK_PER_LD; ++tt) {
+          const int tl = c * TOK_PER_LD + tt;       // token within this warp's half
+          const int ti = half * TOK_HALF + tl;      // token within the block
+          float y = 0.f;
+#pragma unroll
+          for (int j = 0; j < HI; ++j) {
+            const float z = fmaf(__uint_as_float(r[tt * HI + j]), p.half_scale, hb[j]);
+            y = fmaf(w_s[ti * HI + j], tanh_fast(z), y);
+          }
+          const bool ok = tile_full || (key_ok && ti < ntok && (!p.causal || key <= pos0 + ti));
+          if (ok) {
+            p.scores[(int64_t)(tok0 + ti) * p.ld + key] = c_s[ti] + y;
+            const float yy = d_s[ti] + y;
+            s1[tl] += yy;
+            s2[tl] = fmaf(yy, yy, s2[tl]);
+          }
+        }
+      }
+    }
+    // row statistics: reduce the 32 keys of this warp, one fp64 atomic per token and value
+    if (p.row_stats) {
+      const int64_t k_lo = (int64_t)t_begin * kKeys;
+      const int64_t k_hi = min((int64_t)t_end * kKeys, p.Lkv);
+#pragma unroll
+      for (int tl = 0; tl < TOK_HALF; ++tl) {
+        float a = s1[tl], b = s2[tl];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          a += __shfl_xor_sync(0xffffffffu, a, o);
+          b += __shfl_xor_sync(0xffffffffu, b, o);
+        }
+        const int ti = half * TOK_HALF + tl;
+        if (lane == 0 && ti < ntok) {
+          double* st = p.row_stats + (int64_t)(tok0 + ti) * 3;
+          atomicAdd(st + 0, (double)a);
+          atomicAdd(st + 1, (double)b);
+          if (quarter == 0) {
+            int64_t hi_k = p.causal ? min(k_hi, pos0 + ti + 1) : k_hi;
+            int64_t cnt = hi_k > k_lo ? hi_k - k_lo : 0;
+            atomicAdd(st + 2, (double)cnt);
+          }
+        }
+      }
+    }
+  }
+
+  fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// host side: tensor maps and launch
+// ---------------------------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+}  // namespace tc
+
+bool indexer_tc_eligible(const IdxArgs& a) {
+  const bool hi_ok = a.HI == 8 || a.HI == 4;
+  const bool al = (reinterpret_cast<uintptr_t>(a.qI) % 16 == 0) && (reinterpret_cast<uintptr_t>(a.kI) % 16 == 0) &&
+                  ((a.qi_ld * 2) % 16 == 0) && ((a.ki_ld * 2) % 16 == 0);
+  return a.dtype == GSA_DTYPE_BF16 && a.dI == tc::kDI && hi_ok && a.act == GSA_ACT_SIGMOID && al &&
+         !a.write_masked && a.Lq <= 0x7fffffffLL && a.Lkv <= 0x7fffffffLL && tc::encode_fn() != nullptr;
+}
+
+// One batch row of the indexer on the tensor cores (B = 1 slice of IdxArgs).
+int launch_indexer_tc(const IdxArgs& a, int* err, cudaStream_t stream) {
+  using namespace tc;
+  auto enc = encode_fn();
+  CUtensorMap tmK, tmQ;
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)kDI, (cuuint64_t)a.Lkv};
+    cuuint64_t strides[1] = {(cuuint64_t)a.ki_ld * 2};
+    cuuint32_t box[2] = {(cuuint32_t)kDI, (cuuint32_t)kKeys};
+    cuuint32_t es[2] = {1, 1};
+    if (enc(&tmK, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(a.kI), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return GSA_ERR_BAD_ARG;
+  }
+  const int TOK = kN / a.HI;
+  {
+    cuuint64_t dims[3] = {(cuuint64_t)kDI, (cuuint64_t)a.HI, (cuuint64_t)a.Lq};
+    cuuint64_t strides[2] = {(cuuint64_t)kDI * 2, (cuuint64_t)a.qi_ld * 2};
+    cuuint32_t box[3] = {(cuuint32_t)kDI, (cuuint32_t)a.HI, (cuuint32_t)TOK};
+    cuuint32_t es[3] = {1, 1, 1};
+    if (enc(&tmQ, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(a.qI), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return GSA_ERR_BAD_ARG;
+  }
+  Params p;
+  p.n_rows = (int)a.Lq;
+  p.Lkv = a.Lkv;
+  p.q_pos0 = a.q_pos0;
+  p.causal = a.causal;
+  p.half_scale = 0.5f * a.scale;
+  p.bias = a.bias;
+  p.w = a.w;
+  p.shift = a.shift;
+  p.scores = a.scores;
+  p.ld = a.scores_ld;
+  p.row_stats = a.row_stats;
+  p.err = err;
+  const int64_t nb = (a.Lq + TOK - 1) / TOK;
+  const int64_t key_limit = a.causal ? std::min<int64_t>(a.Lkv, a.q_pos0 + a.Lq) : a.Lkv;
+  const int64_t max_tiles = (key_limit + kKeys - 1) / kKeys;
+  const int64_t ranges = (max_tiles + kTilesPerCta - 1) / kTilesPerCta;
+  if (nb == 0 || ranges == 0) return GSA_OK;
+  if (nb > 65535 || ranges > 0x7fffffffLL) return GSA_ERR_BAD_ARG;
+  dim3 grid((unsigned)ranges, (unsigned)nb);
+  if (a.HI == 8) {
+    if (cudaFuncSetAttribute(indexer_tc_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
+        cudaSuccess)
+      return GSA_ERR_LAUNCH;
+    indexer_tc_kernel<8><<<grid, kThreads, kSmemBytes, stream>>>(tmK, tmQ, p);
+  } else {
+    if (cudaFuncSetAttribute(indexer_tc_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
+        cudaSuccess)
+      return GSA_ERR_LAUNCH;
+    indexer_tc_kernel<4><<<grid, kThreads, kSmemBytes, stream>>>(tmK, tmQ, p);
+  }
+  return cudaGetLastError() == cudaSuccess ? GSA_OK : GSA_ERR_LAUNCH;
+}
+
+}  // namespace gsa

@@ -80,6 +80,8 @@ int launch_proj_epilogue(const EpiArgs& a, cudaStream_t stream);
 int launch_apply_gate(int dtype, int act, int64_t n, const void* x, const void* logits, void* out, void* gate_out,
                       cudaStream_t stream);
 int launch_indexer_simt(const IdxArgs& a, int64_t B, cudaStream_t stream);
+bool indexer_tc_eligible(const IdxArgs& a);
+int launch_indexer_tc(const IdxArgs& a, int* err, cudaStream_t stream);
 int launch_topk_candidates(int64_t R, int64_t Lq, int64_t n_cols, int64_t q_pos0, int causal, const float* scores,
                            int64_t ld, int32_t k_eff, int32_t* cand_idx, float* cand_score, int32_t* cand_count,
                            cudaStream_t stream);

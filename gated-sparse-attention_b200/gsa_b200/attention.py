@@ -245,7 +245,7 @@ class GatedLightningIndexer(nn.Module):
             w = torch.sigmoid(self.weight_proj(hidden_states))
             causal = self.use_causal_mask and Lq == Lkv
             scores = ops.indexer_scores(self._dims(), q_idx, k_idx, w, self.bias, self.scale,
-                                        q_pos0=0, causal=causal, write_masked=True)
+                                        q_pos0=0, causal=causal)
         return scores.to(hidden_states.dtype)
 
     def get_indexer_statistics(self, hidden_states: torch.Tensor) -> dict:

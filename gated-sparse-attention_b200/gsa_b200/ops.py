@@ -88,20 +88,20 @@ def proj_epilogue(dims: Dims, layout: ProjLayout, proj: torch.Tensor, positions:
 
 def indexer_scores(dims: Dims, qI: torch.Tensor, kI: torch.Tensor, w: torch.Tensor,
                    bias: torch.Tensor, scale: float, q_pos0: int = 0, causal: bool = True,
-                   write_masked: bool = True, shift=None, row_stats=None) -> torch.Tensor:
-    """Materialised indexer scores [B, Lq, Lkv] fp32.  qI [B, Lq, H_I*d_I] and kI [B, Lkv, d_I]
-    may be row-strided views (last dim contiguous)."""
+                   shift=None, row_stats=None) -> torch.Tensor:
+    """Materialised indexer scores [B, Lq, Lkv] fp32 with -inf at causally masked entries.
+    qI [B, Lq, H_I*d_I] and kI [B, Lkv, d_I] may be row-strided views (last dim contiguous)."""
     _cuda(qI, kI, w, bias)
     B, Lq, _ = qI.shape
     Lkv = kI.shape[1]
     assert qI.stride(2) == 1 and kI.stride(2) == 1 and qI.dtype == kI.dtype
     ld = (Lkv + 3) // 4 * 4
-    fill = float("-inf") if write_masked else 0.0
-    scores = torch.full((B * Lq, ld), fill, device=qI.device, dtype=torch.float32)
+    # masked entries keep the -inf fill, so the kernels need not write them
+    scores = torch.full((B * Lq, ld), float("-inf"), device=qI.device, dtype=torch.float32)
     w = w.reshape(B * Lq, -1).float().contiguous()
     bias = bias.float().contiguous()
     _lib.call("gsa_indexer_scores", C.byref(dims), dtype_code(qI.dtype), B, Lq, Lkv, q_pos0,
-              int(causal), int(write_masked), _p(qI), qI.stride(1), qI.stride(0), _p(kI),
+              int(causal), 0, _p(qI), qI.stride(1), qI.stride(0), _p(kI),
               kI.stride(1), kI.stride(0), _p(w), _p(bias), float(scale), _p(shift), _p(scores), ld,
               _p(row_stats), _stream())
     _after("indexer_scores")

@@ -31,8 +31,9 @@ def gather_sequence(t: torch.Tensor, group, world: int) -> torch.Tensor:
     """All-gather [B, Lr, ...] shards along dim 1 into [B, world * Lr, ...] (rank order)."""
     t = t.contiguous()
     B, Lr = t.shape[0], t.shape[1]
-    buf = torch.empty((world,) + tuple(t.shape), device=t.device, dtype=t.dtype)
+    buf = torch.empty((world * B,) + tuple(t.shape[1:]), device=t.device, dtype=t.dtype)
     dist.all_gather_into_tensor(buf, t, group=group)
+    buf = buf.view((world,) + tuple(t.shape))
     if B == 1:
         return buf.view((1, world * Lr) + tuple(t.shape[2:]))
     return buf.transpose(0, 1).reshape((B, world * Lr) + tuple(t.shape[2:]))

@@ -108,13 +108,21 @@ def indexer_scores(W: dict, x_q: torch.Tensor, x_kv: torch.Tensor, n_heads: int,
     ``seq_q != seq_kv``).
     """
     B, Lq, _ = x_q.shape
-    Lkv = x_kv.shape[1]
     q_idx = F.linear(x_q, W["indexer.q_proj.weight"]).view(B, Lq, n_heads, d_idx)
     k_idx = F.linear(x_kv, W["indexer.k_proj.weight"])
     weights = torch.sigmoid(F.linear(x_q, W["indexer.weight_proj.weight"],
                                      W["indexer.weight_proj.bias"]))
+    return indexer_scores_from_proj(q_idx, k_idx, weights, W["indexer.bias"], activation, q_offset)
+
+
+def indexer_scores_from_proj(q_idx, k_idx, weights, bias_param, activation="sigmoid",
+                             q_offset: int | None = 0) -> torch.Tensor:
+    """gated_indexer.py:123-153 from the projected q^I [B,Lq,H_I,d_I], k^I [B,Lkv,d_I] and the
+    head weights sigmoid(weight_proj(h)) [B,Lq,H_I]; offset-causal as in indexer_scores."""
+    B, Lq, _, d_idx = q_idx.shape
+    Lkv = k_idx.shape[1]
     raw = torch.einsum("bqhd,bkd->bhqk", q_idx, k_idx) * (1.0 / math.sqrt(d_idx))
-    bias = W["indexer.bias"].view(1, -1, 1, 1)
+    bias = bias_param.view(1, -1, 1, 1)
     if activation == "sigmoid":
         gated = torch.sigmoid(raw + bias)
     elif activation == "relu":

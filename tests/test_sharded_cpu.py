@@ -1,0 +1,148 @@
+"""Query-sequence sharding on CPU ranks (gloo, world size 2): the decomposition the layer uses
+across GPUs (gsa_b200.sharded) -- contiguous query blocks, an all-gather of K / V / k^I, an
+offset-causal indexer and an all-reduce of the variance sum -- reproduces the unsharded layer.
+The kernels' roles are played by the CPU oracle; the sharding code is the product's.  Also:
+a rank that fails before the exchange makes the other rank's collective end with an error
+instead of waiting forever."""
+
+import datetime
+import math
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from conftest import ROOT, golden_inputs, load_golden  # noqa: F401
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _init(rank, world, port, timeout_s=60):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=timeout_s))
+
+
+def _sharded_oracle_layer(W, cfg, x_local, sp):
+    """The layer's sharded forward with oracle stand-ins for the kernels."""
+    import torch.nn.functional as F
+    import gsa_oracle as O
+
+    B, Lr, _ = x_local.shape
+    start = sp.start(Lr)
+    oc = O.OracleConfig.from_config(cfg)
+    pos = torch.arange(start, start + Lr).unsqueeze(0).expand(B, -1)
+    cos, sin = O.rope_cache(cfg.d_head, cfg.max_position_embeddings, cfg.rope_base, cfg.rope_scaling)
+    q, k, v = O.project(W, oc, x_local, pos, cos, sin)
+    q_idx = F.linear(x_local, W["indexer.q_proj.weight"]).view(B, Lr, cfg.n_indexer_heads, cfg.d_indexer)
+    k_idx = F.linear(x_local, W["indexer.k_proj.weight"])
+    wts = torch.sigmoid(F.linear(x_local, W["indexer.weight_proj.weight"], W["indexer.weight_proj.bias"]))
+    # exchange: keys of every rank, in rank order
+    k_all, v_all, kI_all = sp.gather(k), sp.gather(v), sp.gather(k_idx)
+    L = kI_all.shape[1]
+    scores = O.indexer_scores_from_proj(q_idx, kI_all, wts, W["indexer.bias"], "sigmoid", q_offset=start)
+    var, valid = O.row_variance(scores)
+    total = sp.allreduce(torch.tensor([float(var.double().sum()), float(var.numel())], dtype=torch.float64))
+    mean = torch.tensor(float(total[0]) / float(total[1]), dtype=var.dtype)
+    kv = O.adaptive_k(var, valid, mean, cfg.k_base, cfg.k_min, cfg.k_max, cfg.adaptive_k_temperature)
+    idx, msk = O.topk_select(scores, min(cfg.k_max, L), kv)
+    attn, _ = O.sparse_attention(q, k_all, v_all, idx, msk, cfg.n_heads // cfg.n_kv_heads,
+                                 1.0 / math.sqrt(cfg.d_head))
+    g = F.linear(x_local, W["output_gate.gate_proj.weight"], W["output_gate.gate_proj.bias"])
+    gated = attn * torch.sigmoid(g.view(B, Lr, cfg.n_heads, cfg.d_head))
+    return F.linear(gated.reshape(B, Lr, -1), W["o_proj.weight"]), kv
+
+
+def _worker_equivalence(rank, world, port, q):
+    import sys
+    for p in (ROOT / "gated-sparse-attention_b200", ROOT / "oracle", ROOT / "tests"):
+        sys.path.insert(0, str(p))
+    torch.set_num_threads(1)
+    from gsa_b200.sharded import QueryShards, shard_bounds
+    import gsa_oracle as O
+
+    try:
+        _init(rank, world, port)
+        _, meta = load_golden("tiny_fp32_b2_l192")
+        cfg, m, x = golden_inputs(meta)
+        W = dict(m.state_dict())
+        L = x.shape[1]
+        s0, s1 = shard_bounds(L, world, rank)
+        sp = QueryShards(dist.group.WORLD)
+        out_local, kv_local = _sharded_oracle_layer(W, cfg, x[:, s0:s1].contiguous(), sp)
+        out_full = sp.gather(out_local)
+        kv_full = sp.gather(kv_local.contiguous())
+        if rank == 0:
+            ref = O.gsa_forward(W, O.OracleConfig.from_config(cfg), x, chunk=64, keep=("k_values",))
+            err = float((out_full - ref["out"]).norm() / ref["out"].norm())
+            kdiff = int((kv_full != ref["k_values"]).sum())
+            q.put(("ok", err, kdiff))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # pragma: no cover - reported to the parent
+        q.put(("error", repr(e), -1))
+
+
+def test_query_sharded_layer_matches_unsharded():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_equivalence, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    status, err, kdiff = q.get(timeout=10)
+    assert status == "ok", err
+    assert err < 1e-5, err
+    assert kdiff == 0
+
+
+def _worker_failure(rank, world, port, q):
+    import sys
+    for p in (ROOT / "gated-sparse-attention_b200",):
+        sys.path.insert(0, str(p))
+    from gsa_b200.sharded import QueryShards
+
+    _init(rank, world, port, timeout_s=5)
+    sp = QueryShards(dist.group.WORLD)
+    if rank == 1:
+        # this rank fails before the key exchange and never joins it
+        os._exit(0)
+    try:
+        sp.gather(torch.zeros(1, 4, 2))
+        q.put("no error")
+    except Exception as e:
+        q.put("error: " + type(e).__name__)
+
+
+def test_failed_rank_surfaces_as_collective_error():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_failure, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+    msg = q.get(timeout=10)
+    assert msg.startswith("error"), msg
+
+
+def test_shard_bounds():
+    from gsa_b200.sharded import shard_bounds
+
+    assert shard_bounds(131072, 8, 7) == (114688, 131072)
+    assert shard_bounds(10, 2, 0) == (0, 5)
+    with pytest.raises(ValueError):
+        shard_bounds(10, 3, 0)
