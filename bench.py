@@ -177,7 +177,8 @@ def run_ours(args, world, rank):
     torch.cuda.synchronize()
 
     def step():
-        return m(x)[0]
+        with torch.no_grad():
+            return m(x)[0]
 
     # warm-up
     for _ in range(args.warmup):
@@ -210,7 +211,8 @@ def run_ours(args, world, rank):
     e0.record()
     for _ in range(args.steps):
         xd = x_host.to(dev, non_blocking=True)
-        out = m(xd)[0]
+        with torch.no_grad():
+            out = m(xd)[0]
         out_host.copy_(out, non_blocking=True)
     e1.record()
     torch.cuda.synchronize()
@@ -389,6 +391,25 @@ def run_reference(args, world, rank):
             "e2e": {"value": round(v, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def run_launch_list(args):
+    """N untimed forwards of the 1-GPU workload at --seq-len, for kernel profilers."""
+    from gsa_b200 import GSAConfig, GatedSparseAttention, ops
+
+    torch.cuda.set_device(0)
+    L = args.seq_len
+    cfg = GSAConfig(**WORKLOAD, max_position_embeddings=max(131072, L))
+    torch.manual_seed(0)
+    m = GatedSparseAttention(cfg).eval().to(torch.bfloat16).cuda()
+    gen = torch.Generator().manual_seed(1)
+    x = torch.randn(1, L, cfg.d_model, generator=gen).to(torch.bfloat16).cuda()
+    with torch.no_grad():
+        for _ in range(args.launch_list):
+            m(x)
+    torch.cuda.synchronize()
+    ops.check_device_error()
+    log(f"launch list: {args.launch_list} forwards at L={L} done")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -397,7 +418,11 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--seq-len", type=int, default=131072)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--launch-list", type=int, default=0, metavar="N",
+                    help="run N untimed forwards and exit (a short command for profilers)")
     args = ap.parse_args()
+    if args.launch_list:
+        return run_launch_list(args)
     args.warmup = max(args.warmup, 3)
 
     if args.impl == "reference":

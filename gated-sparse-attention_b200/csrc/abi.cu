@@ -68,7 +68,8 @@ int gsa_get_device_error(int* code_out, gsa_stream_t stream) {
 int gsa_proj_epilogue(const gsa_dims* dims, const gsa_proj_layout* layout, int dtype, int64_t T,
                       const void* proj, int64_t proj_ld, const int64_t* positions, const void* cos_tab,
                       const void* sin_tab, int tab_dtype, int64_t tab_rows, void* q_out, void* k_out,
-                      void* v_out, void* g1_out, float* w_out, float* shift_out, gsa_stream_t stream) {
+                      void* v_out, int64_t kv_ld, void* g1_out, float* w_out, float* shift_out,
+                      gsa_stream_t stream) {
   if (!dims_ok(dims) || !layout || T < 0 || (dtype != GSA_DTYPE_F32 && dtype != GSA_DTYPE_BF16) ||
       (tab_dtype != GSA_DTYPE_F32 && tab_dtype != GSA_DTYPE_BF16))
     return GSA_ERR_BAD_ARG;
@@ -77,11 +78,12 @@ int gsa_proj_epilogue(const gsa_dims* dims, const gsa_proj_layout* layout, int d
       tab_rows <= 0 || layout->q < 0 || layout->k < 0 || layout->v < 0 || layout->wi < 0)
     return GSA_ERR_BAD_ARG;
   if (dims->gate_act < GSA_ACT_SIGMOID || dims->gate_act > GSA_ACT_SILU) return GSA_ERR_UNSUPPORTED;
+  if (kv_ld < (int64_t)dims->n_kv_heads * dims->d_head) return GSA_ERR_BAD_ARG;
   DeviceInfo* di;
   int st = device_info(&di);
   if (st) return st;
   EpiArgs a{*dims, *layout, dtype, T, proj, proj_ld, positions, cos_tab, sin_tab, tab_dtype, tab_rows,
-            q_out, k_out, v_out, g1_out, w_out, shift_out, di->err};
+            q_out, k_out, v_out, kv_ld, g1_out, w_out, shift_out, di->err};
   return launch_proj_epilogue(a, reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -129,14 +131,14 @@ int gsa_row_stats(int64_t R, int64_t n_cols, const float* scores, int64_t scores
 }
 
 int gsa_topk_candidates(int64_t R, int64_t Lq, int64_t n_cols, int64_t q_pos0, int causal, const float* scores,
-                        int64_t scores_ld, int32_t k_eff, int32_t* cand_idx, float* cand_score,
-                        int32_t* cand_count, gsa_stream_t stream) {
+                        int64_t scores_ld, const float* row_center, int32_t k_eff, int32_t* cand_idx,
+                        float* cand_score, int32_t* cand_count, gsa_stream_t stream) {
   if (R < 0 || Lq <= 0 || n_cols < 0 || k_eff < 1 || scores_ld < n_cols || n_cols > 0x7fffffffLL)
     return GSA_ERR_BAD_ARG;
   if (R == 0) return GSA_OK;
   if (!scores || !cand_idx || !cand_score || !cand_count) return GSA_ERR_BAD_ARG;
-  return launch_topk_candidates(R, Lq, n_cols, q_pos0, causal, scores, scores_ld, k_eff, cand_idx, cand_score,
-                                cand_count, reinterpret_cast<cudaStream_t>(stream));
+  return launch_topk_candidates(R, Lq, n_cols, q_pos0, causal, scores, scores_ld, row_center, k_eff, cand_idx,
+                                cand_score, cand_count, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int gsa_row_variance(int64_t R, int64_t n_cols, int dtype, const double* row_stats, const float* shift,
@@ -180,20 +182,24 @@ int gsa_apply_gate(int dtype, int act, int64_t n, const void* x, const void* log
 }
 
 int gsa_sparse_sdpa(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int64_t Lkv, const void* q,
-                    const void* k, const void* v, const int32_t* sel_idx, int64_t sel_ld, const int32_t* sel_count,
-                    const void* gate, void* out, float scale, gsa_stream_t stream) {
+                    const void* k, const void* v, int64_t kv_ld, const int32_t* sel_idx, int64_t sel_ld,
+                    const int32_t* sel_count, const void* gate, void* out, float scale, gsa_stream_t stream) {
   if (!dims_ok(dims) || B < 0 || Lq < 0 || Lkv < 0 || sel_ld < 0) return GSA_ERR_BAD_ARG;
   if (B * Lq == 0) return GSA_OK;
   if (!q || !k || !v || !sel_idx || !sel_count || !out) return GSA_ERR_BAD_ARG;
+  const int64_t row_elems = (int64_t)dims->n_kv_heads * dims->d_head;
+  if (kv_ld < row_elems) return GSA_ERR_BAD_ARG;
   DeviceInfo* di;
   int st = device_info(&di);
   if (st) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == GSA_DTYPE_BF16) {
-    if (!aligned(k, 16) || !aligned(v, 16) || !aligned(q, 4)) return GSA_ERR_BAD_ARG;
+    if (!aligned(k, 16) || !aligned(v, 16) || !aligned(q, 4) || (kv_ld * 2) % 16 != 0) return GSA_ERR_BAD_ARG;
+    const bool inter = kv_ld == 2 * row_elems &&
+                       static_cast<const __nv_bfloat16*>(v) == static_cast<const __nv_bfloat16*>(k) + row_elems;
     SdpaArgs a{B, Lq, Lkv, dims->n_kv_heads,
                static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
-               static_cast<const __nv_bfloat16*>(v), sel_idx, sel_ld, sel_count,
+               static_cast<const __nv_bfloat16*>(v), kv_ld, inter ? 1 : 0, sel_idx, sel_ld, sel_count,
                static_cast<const __nv_bfloat16*>(gate), static_cast<__nv_bfloat16*>(out),
                scale * 1.4426950408889634f, 0, di->err};
     return launch_sdpa_bf16(a, dims->d_head, dims->n_heads / dims->n_kv_heads, di->num_sms, s);
@@ -201,7 +207,7 @@ int gsa_sparse_sdpa(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int6
   if (dtype == GSA_DTYPE_F32) {
     SdpaF32Args a{B, Lq, Lkv, dims->n_heads, dims->n_kv_heads, dims->d_head,
                   static_cast<const float*>(q), static_cast<const float*>(k), static_cast<const float*>(v),
-                  sel_idx, sel_ld, sel_count, static_cast<const float*>(gate), static_cast<float*>(out),
+                  kv_ld, sel_idx, sel_ld, sel_count, static_cast<const float*>(gate), static_cast<float*>(out),
                   scale, di->err};
     return launch_sdpa_f32(a, s);
   }
@@ -238,7 +244,9 @@ int gsa_indexer_select(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, i
                                   0, w + r0 * HI, bias, scale, shift ? shift + r0 : nullptr, scratch, ld,
                                   row_stats ? row_stats + r0 * 3 : nullptr, stream);
       if (st) return st;
-      st = gsa_topk_candidates(n, n, Lkv, q_pos0 + t0, causal, scratch, ld, k_eff, cand_idx + r0 * k_eff,
+      // sigmoid scores of row r lie in [0, sum_j w_rj] = [0, 2 shift_r]: the bounded-range selection
+      const float* center = (shift && dims->idx_act == GSA_ACT_SIGMOID) ? shift + r0 : nullptr;
+      st = gsa_topk_candidates(n, n, Lkv, q_pos0 + t0, causal, scratch, ld, center, k_eff, cand_idx + r0 * k_eff,
                                cand_score + r0 * k_eff, cand_count + r0, stream);
       if (st) return st;
     }

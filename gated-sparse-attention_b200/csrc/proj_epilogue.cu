@@ -53,7 +53,7 @@ __global__ void proj_epilogue_kernel(EpiArgs a) {
   for (int h = 0; h < H; ++h)
     rope_head(a, row, a.lay.q + (int64_t)h * D, cos_row, sin_row, a.q_out, (t * H + h) * D, D);
   for (int h = 0; h < Hk; ++h)
-    rope_head(a, row, a.lay.k + (int64_t)h * D, cos_row, sin_row, a.k_out, (t * Hk + h) * D, D);
+    rope_head(a, row, a.lay.k + (int64_t)h * D, cos_row, sin_row, a.k_out, t * a.kv_ld + (int64_t)h * D, D);
 
   // G2 on v, applied before RoPE and never rotated (gated_sparse_attention.py:180-186)
   for (int i = threadIdx.x; i < Hk * D; i += blockDim.x) {
@@ -62,7 +62,7 @@ __global__ void proj_epilogue_kernel(EpiArgs a) {
       float g = gate_act(load_elem(a.proj, row + a.lay.g2 + i, a.dtype), a.d.gate_act, a.dtype);
       v = fmul(v, g);
     }
-    store_elem(a.v_out, t * Hk * D + i, v, a.dtype);
+    store_elem(a.v_out, t * a.kv_ld + i, v, a.dtype);
   }
   if (a.lay.g1 >= 0 && a.g1_out) {
     for (int i = threadIdx.x; i < H * D; i += blockDim.x) {

@@ -6,9 +6,12 @@
 // [Hk, D] slice of K (and of V): 2 KiB each at 8 x 128 bf16.  The kernel is HBM-bound on
 // those gathers, so it is built around moving whole key rows:
 //
-//   * one producer warp issues one 1-D bulk copy (cp.async.bulk, TMA engine) per selected K
-//     row and per V row into a shared-memory ring of stages (16 keys per stage), completing
-//     on the stage's mbarrier; rows are padded by 16 bytes so ldmatrix reads are conflict free;
+//   * one producer warp issues 1-D bulk copies (cp.async.bulk, TMA engine) of the selected keys
+//     into a shared-memory ring of stages (16 keys per stage), completing on the stage's
+//     mbarrier.  With K and V interleaved per key in HBM ([.., Lkv, 2, Hk, D], the layer's
+//     layout) a key is ONE contiguous 4 KiB copy: the copy count, not the byte count, is what
+//     limits this engine for 2 KiB rows.  A stage slot is [K row | V row | 16 B pad]; the pad
+//     makes the ldmatrix reads of 8 consecutive keys conflict free;
 //   * one consumer warp per KV group computes S^T = K_g Q_g^T with mma.sync (keys are the M
 //     dimension, the n_rep query heads of the group the N dimension), an online softmax in
 //     registers, transposes P with movmatrix and accumulates O^T += V_g^T P^T;
@@ -22,7 +25,7 @@ namespace gsa {
 
 constexpr int kKeysPerStage = 16;
 constexpr int kMaxRowBytes = 16 * 256 * 2;
-__device__ __align__(128) uint8_t g_zero_row[kMaxRowBytes];
+__device__ __align__(128) uint8_t g_zero_row[2 * kMaxRowBytes];
 
 
 
@@ -67,8 +70,8 @@ __global__ void __launch_bounds__(17 * 32) sdpa_tc_kernel(SdpaArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int Hk = a.Hk;
   const int row_bytes = Hk * D * 2;
-  const int rs = row_bytes + 16;
-  const int stage_bytes = 2 * kKeysPerStage * rs;
+  const int rs = 2 * row_bytes + 16;  // slot: [K row | V row | pad]
+  const int stage_bytes = kKeysPerStage * rs;
   const int nst = a.nstages;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + nst;
@@ -94,8 +97,9 @@ __global__ void __launch_bounds__(17 * 32) sdpa_tc_kernel(SdpaArgs a) {
       const int64_t b = row / a.Lq;
       const int cnt = row_count(a, row);
       const int32_t* idx = a.sel_idx + row * a.sel_ld;
-      const uint8_t* kbase = reinterpret_cast<const uint8_t*>(a.k) + b * a.Lkv * row_bytes;
-      const uint8_t* vbase = reinterpret_cast<const uint8_t*>(a.v) + b * a.Lkv * row_bytes;
+      const int64_t kv_row = a.kv_ld * 2;  // bytes between consecutive keys
+      const uint8_t* kbase = reinterpret_cast<const uint8_t*>(a.k) + b * a.Lkv * kv_row;
+      const uint8_t* vbase = reinterpret_cast<const uint8_t*>(a.v) + b * a.Lkv * kv_row;
       const int nkb = (cnt + kKeysPerStage - 1) / kKeysPerStage;
       for (int kb = 0; kb < nkb; ++kb, ++it) {
         const int s = it % nst;
@@ -105,14 +109,23 @@ __global__ void __launch_bounds__(17 * 32) sdpa_tc_kernel(SdpaArgs a) {
         __syncwarp();
         const int slot = lane & 15;
         const int key = kb * kKeysPerStage + slot;
-        const uint8_t* src = g_zero_row;
+        int64_t j = -1;
         if (key < cnt) {
-          const int32_t j = idx[key];
-          if (j >= 0 && j < a.Lkv) src = (lane < 16 ? kbase : vbase) + (int64_t)j * row_bytes;
-          else set_error(a.err, GSA_ERR_INDEX);
+          j = idx[key];
+          if (j < 0 || j >= a.Lkv) {
+            set_error(a.err, GSA_ERR_INDEX);
+            j = -1;
+          }
         }
-        uint8_t* dst = stages + s * stage_bytes + (lane < 16 ? 0 : kKeysPerStage * rs) + slot * rs;
-        bulk_g2s(dst, src, (uint32_t)row_bytes, &full[s]);
+        uint8_t* dst = stages + s * stage_bytes + slot * rs;
+        if (a.interleaved) {
+          // one copy per key: K row and V row are adjacent
+          if (lane < 16) bulk_g2s(dst, j >= 0 ? kbase + j * kv_row : g_zero_row, (uint32_t)(2 * row_bytes), &full[s]);
+        } else if (lane < 16) {
+          bulk_g2s(dst, j >= 0 ? kbase + j * kv_row : g_zero_row, (uint32_t)row_bytes, &full[s]);
+        } else {
+          bulk_g2s(dst + row_bytes, j >= 0 ? vbase + j * kv_row : g_zero_row, (uint32_t)row_bytes, &full[s]);
+        }
       }
     }
     // drain: every issued copy must land before the CTA may exit
@@ -152,7 +165,7 @@ __global__ void __launch_bounds__(17 * 32) sdpa_tc_kernel(SdpaArgs a) {
       const uint32_t ph = (it / nst) & 1u;
       if (!mbar_wait(&full[s], ph, a.err)) { ok = false; break; }
       const uint8_t* Ks = stages + s * stage_bytes;
-      const uint8_t* Vs = Ks + kKeysPerStage * rs;
+      const uint8_t* Vs = Ks + row_bytes;
       float c[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
@@ -263,8 +276,8 @@ __global__ void sdpa_f32_kernel(SdpaF32Args a) {
     for (int j = 0; j < cnt; ++j) {
       int s = idx[j];
       if (s < 0 || s >= a.Lkv) { set_error(a.err, GSA_ERR_INDEX); continue; }
-      const float* kr = a.k + ((b * a.Lkv + s) * a.Hk + g) * a.D;
-      const float* vr = a.v + ((b * a.Lkv + s) * a.Hk + g) * a.D;
+      const float* kr = a.k + (b * a.Lkv + s) * a.kv_ld + (int64_t)g * a.D;
+      const float* vr = a.v + (b * a.Lkv + s) * a.kv_ld + (int64_t)g * a.D;
       float dot = 0.f;
       for (int i = 0; i < kMaxPerLane; ++i) {
         int d = lane + 32 * i;
@@ -302,7 +315,7 @@ struct SdpaCfg {
 template <int D, int NREP>
 static int launch_tc(SdpaArgs a, int num_sms, cudaStream_t stream) {
   const int row_bytes = a.Hk * D * 2;
-  const int stage_bytes = 2 * kKeysPerStage * (row_bytes + 16);
+  const int stage_bytes = kKeysPerStage * (2 * row_bytes + 16);
   const int max_smem = 227 * 1024;
   int nst = (max_smem - 256) / stage_bytes;
   if (nst > 8) nst = 8;

@@ -227,20 +227,142 @@ struct CandCol {
   __device__ int32_t operator()(int64_t i) const { return cols[i]; }
 };
 
+// ---------------------------------------------------------------------------------------------
+// Bounded-range rows: when every finite score of row r lies in [0, 2 c_r] (sigmoid indexer
+// scores: I[t,s] <= sum_j w_tj = 2 c_t), a histogram over kBins equal-width bins of that range
+// spreads the row over many bins (the fp32 bit pattern does not: the scores share two or three
+// binary exponents).  One pass finds the bin b* holding the k-th largest score; a second pass
+// compacts every score in bins >= b* (at most kCap of them) into shared memory, in column
+// order; the exact radix select then runs on that small set.  The bin map x -> floor(x * kBins
+// / 2c) is monotone, so equal scores share a bin and the top-k set lies inside bins >= b*.
+// ---------------------------------------------------------------------------------------------
+constexpr int kCap = 8192;
+
+__device__ __forceinline__ int lin_bin(float x, float scale) {
+  int b = __float2int_rd(x * scale);
+  return b < 0 ? 0 : (b >= kBins ? kBins - 1 : b);
+}
+
+__device__ void linear_histogram(const float* row, int64_t n, float scale, uint32_t* hist, uint32_t* finite) {
+  uint32_t my_finite = 0;
+  const int64_t n4 = n / 4;
+  const float4* row4 = reinterpret_cast<const float4*>(row);
+  for (int64_t i = threadIdx.x; i < n4; i += blockDim.x) {
+    const float4 v = row4[i];
+    const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (valid_key(e[j])) {
+        ++my_finite;
+        atomicAdd(&hist[lin_bin(e[j], scale)], 1u);
+      }
+    }
+  }
+  for (int64_t i = n4 * 4 + threadIdx.x; i < n; i += blockDim.x) {
+    const float x = row[i];
+    if (valid_key(x)) {
+      ++my_finite;
+      atomicAdd(&hist[lin_bin(x, scale)], 1u);
+    }
+  }
+  const uint32_t wsum = warp_sum(my_finite);
+  if ((threadIdx.x & 31) == 0) atomicAdd(finite, wsum);
+}
+
+// Ordered compaction of the finite scores with bin >= bstar into (vals, cols); returns the count.
+__device__ uint32_t compact_top_bins(const float* row, int64_t n, float scale, int bstar, float* vals,
+                                     int32_t* cols, uint32_t* ws) {
+  constexpr int PER = 4;
+  const int64_t chunk = (int64_t)blockDim.x * PER;
+  uint32_t base = 0;
+  for (int64_t c0 = 0; c0 < n; c0 += chunk) {
+    float v[PER];
+    bool f[PER];
+    uint32_t cnt = 0;
+    const int64_t i0 = c0 + (int64_t)threadIdx.x * PER;
+    if (i0 + PER <= n) {
+      const float4 q = *reinterpret_cast<const float4*>(row + i0);
+      v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < PER; ++j) v[j] = (i0 + j < n) ? row[i0 + j] : -INFINITY;
+    }
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      f[j] = valid_key(v[j]) && lin_bin(v[j], scale) >= bstar;
+      cnt += f[j];
+    }
+    uint32_t total;
+    uint32_t pos = base + block_exclusive_scan(cnt, ws, &total);
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      if (f[j]) {
+        if (pos < (uint32_t)kCap) {
+          vals[pos] = v[j];
+          cols[pos] = (int32_t)(i0 + j);
+        }
+        ++pos;
+      }
+    }
+    base += total;
+  }
+  __syncthreads();
+  return base < (uint32_t)kCap ? base : (uint32_t)kCap;
+}
+
 __global__ void __launch_bounds__(kSelThreads) topk_candidates_kernel(
     int64_t Lq, int64_t n_cols, int64_t q_pos0, int causal, const float* scores, int64_t ld,
-    int32_t k_eff, int32_t* cand_idx, float* cand_score, int32_t* cand_count) {
+    const float* row_center, int32_t k_eff, int32_t* cand_idx, float* cand_score, int32_t* cand_count) {
   __shared__ uint32_t hist[kBins];
   __shared__ uint32_t ws[48];
   __shared__ uint32_t sel[4];
+  extern __shared__ __align__(16) uint8_t topk_dyn[];  // bounded path: [kCap] vals, [kCap] cols
   const int64_t r = blockIdx.x;
   int64_t n = n_cols;
   if (causal) n = min(n_cols, q_pos0 + (r % Lq) + 1);
   if (n < 0) n = 0;
-  RowSrc src{scores + r * ld, n};
-  radix_threshold(src, (uint32_t)k_eff, hist, ws, sel);
-  uint32_t cnt = collect(src, sel[0], sel[1], sel[3] != 0, cand_idx + r * k_eff,
-                         cand_score + r * k_eff, IdentityCol{}, ws, (uint32_t)k_eff);
+  const float* row = scores + r * ld;
+  int32_t* oidx = cand_idx + r * k_eff;
+  float* osc = cand_score + r * k_eff;
+  const uint32_t K = (uint32_t)k_eff;
+  RowSrc src{row, n};
+  uint32_t cnt = 0;
+  bool done = false;
+  if (row_center) {
+    const float hi = 2.f * row_center[r];
+    if (hi > 0.f && hi < 3.0e38f) {
+      const float scale = (float)kBins / hi;
+      for (int i = threadIdx.x; i < kBins; i += blockDim.x) hist[i] = 0;
+      if (threadIdx.x == 0) sel[2] = 0;
+      __syncthreads();
+      linear_histogram(row, n, scale, hist, &sel[2]);
+      __syncthreads();
+      const uint32_t finite = sel[2];
+      if (finite <= K) {
+        cnt = collect(src, 0u, 0u, true, oidx, osc, IdentityCol{}, ws, K);
+        done = true;
+      } else {
+        uint32_t* dig = ws + 40;
+        find_digit(hist, kBins, K, ws, dig);
+        const int bstar = (int)dig[0];
+        const uint32_t C = dig[1] + hist[bstar];
+        __syncthreads();
+        if (C <= (uint32_t)kCap) {
+          float* cv = reinterpret_cast<float*>(topk_dyn);
+          int32_t* cc = reinterpret_cast<int32_t*>(topk_dyn + kCap * sizeof(float));
+          const uint32_t m = compact_top_bins(row, n, scale, bstar, cv, cc, ws);
+          RowSrc s2{cv, (int64_t)m};
+          radix_threshold(s2, K, hist, ws, sel);
+          cnt = collect(s2, sel[0], sel[1], sel[3] != 0, oidx, osc, CandCol{cc}, ws, K);
+          done = true;
+        }
+      }
+    }
+  }
+  if (!done) {
+    radix_threshold(src, K, hist, ws, sel);
+    cnt = collect(src, sel[0], sel[1], sel[3] != 0, oidx, osc, IdentityCol{}, ws, K);
+  }
   if (threadIdx.x == 0) cand_count[r] = (int32_t)cnt;
 }
 
@@ -373,12 +495,22 @@ __global__ void adaptive_k_kernel(int64_t R, int64_t n_cols, int dtype, gsa_topk
 
 // ---------------------------------------------------------------------------------------------
 int launch_topk_candidates(int64_t R, int64_t Lq, int64_t n_cols, int64_t q_pos0, int causal,
-                           const float* scores, int64_t ld, int32_t k_eff, int32_t* cand_idx,
-                           float* cand_score, int32_t* cand_count, cudaStream_t stream) {
+                           const float* scores, int64_t ld, const float* row_center, int32_t k_eff,
+                           int32_t* cand_idx, float* cand_score, int32_t* cand_count, cudaStream_t stream) {
   if (R == 0) return GSA_OK;
   if (R > 0x7fffffffLL) return GSA_ERR_BAD_ARG;
-  topk_candidates_kernel<<<(unsigned)R, kSelThreads, 0, stream>>>(Lq, n_cols, q_pos0, causal, scores, ld,
-                                                                 k_eff, cand_idx, cand_score, cand_count);
+  size_t dyn = 0;
+  if (row_center) {
+    // the float4 loads of the bounded path need 16-byte aligned rows
+    if ((reinterpret_cast<uintptr_t>(scores) % 16) != 0 || (ld % 4) != 0) return GSA_ERR_BAD_ARG;
+    dyn = 2 * kCap * sizeof(float);
+    if (cudaFuncSetAttribute(topk_candidates_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn) !=
+        cudaSuccess)
+      return GSA_ERR_LAUNCH;
+  }
+  topk_candidates_kernel<<<(unsigned)R, kSelThreads, dyn, stream>>>(Lq, n_cols, q_pos0, causal, scores, ld,
+                                                                   row_center, k_eff, cand_idx, cand_score,
+                                                                   cand_count);
   return cudaGetLastError() == cudaSuccess ? GSA_OK : GSA_ERR_LAUNCH;
 }
 

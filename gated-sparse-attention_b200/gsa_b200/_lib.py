@@ -61,15 +61,15 @@ INT = C.c_int
 SIGNATURES = {
     "gsa_get_device_error": [P, P],
     "gsa_version": [],
-    "gsa_proj_epilogue": [P, P, INT, I64, P, I64, P, P, P, INT, I64, P, P, P, P, P, P, P],
+    "gsa_proj_epilogue": [P, P, INT, I64, P, I64, P, P, P, INT, I64, P, P, P, I64, P, P, P, P],
     "gsa_indexer_scores": [P, INT, I64, I64, I64, I64, INT, INT, P, I64, I64, P, I64, I64, P, P, F32,
                            P, P, I64, P, P],
     "gsa_row_stats": [I64, I64, P, I64, P, P],
-    "gsa_topk_candidates": [I64, I64, I64, I64, INT, P, I64, I32, P, P, P, P],
+    "gsa_topk_candidates": [I64, I64, I64, I64, INT, P, I64, P, I32, P, P, P, P],
     "gsa_row_variance": [I64, I64, INT, P, P, P, P, P],
     "gsa_adaptive_k": [I64, I64, INT, P, P, P, P, P, P],
     "gsa_select_finalize": [I64, I32, P, P, P, P, P, I64, P, P, P],
-    "gsa_sparse_sdpa": [P, INT, I64, I64, I64, P, P, P, P, I64, P, P, P, F32, P],
+    "gsa_sparse_sdpa": [P, INT, I64, I64, I64, P, P, P, I64, P, I64, P, P, P, F32, P],
     "gsa_workspace_size": [I64, I64],
     "gsa_indexer_select": [P, INT, I64, I64, I64, I64, INT, P, I64, I64, P, I64, I64, P, P, F32, P,
                            I32, P, P, P, P, I64, P, I64, P],

@@ -321,9 +321,10 @@ class GSAKVCache(tuple):
     reference's cache keeps working; when it is passed back as ``past_key_value`` the indexer
     scores the new queries against every cached key."""
 
-    def __new__(cls, k, v, indexer_keys=None):
+    def __new__(cls, k, v, indexer_keys=None, kv=None):
         obj = super().__new__(cls, (k, v))
         obj.indexer_keys = indexer_keys
+        obj.kv = kv  # the interleaved [B, Lkv, 2, Hk, D] buffer k and v are views of
         return obj
 
 
@@ -486,31 +487,31 @@ class GatedSparseAttention(nn.Module):
 
         proj = torch.addmm(bvec, x.reshape(B * L, self.d_model), W.t())
         mark("proj_gemm")
-        q, k, v, g1, w, shift = ops.proj_epilogue(dims, layout, proj, positions,
-                                                  self.rotary_emb.cos_cached, self.rotary_emb.sin_cached,
-                                                  self.output_gate is not None)
+        q, kv, g1, w, shift = ops.proj_epilogue(dims, layout, proj, positions,
+                                                self.rotary_emb.cos_cached, self.rotary_emb.sin_cached,
+                                                self.output_gate is not None, return_kv=True)
         mark("proj_epilogue")
         q = q.view(B, L, H, D)
-        k = k.view(B, L, Hk, D)
-        v = v.view(B, L, Hk, D)
+        kv = kv.view(B, L, 2, Hk, D)  # k and v interleaved per token
         proj3 = proj.view(B, L, proj.shape[1])
         qI = proj3[..., layout.qi:layout.qi + HI * dI]
         kI = proj3[..., layout.ki:layout.ki + dI]
 
         indexer_keys = None
         if sp is not None:
-            # every rank needs all keys up to its last query: gather K, V and k^I in rank order
+            # every rank needs all keys up to its last query: gather K/V and k^I in rank order
             kI_all = sp.gather(kI)
-            k_all = sp.gather(k)
-            v_all = sp.gather(v)
+            kv_all = sp.gather(kv)
             q_pos0 = sp.start(L)
             indexer_keys = kI_all
         elif past_key_value is None:
-            k_all, v_all, kI_all, q_pos0 = k, v, kI, 0
+            kv_all, kI_all, q_pos0 = kv, kI, 0
             indexer_keys = kI.contiguous()
         else:
-            k_all = torch.cat([past_key_value[0], k], dim=1)
-            v_all = torch.cat([past_key_value[1], v], dim=1)
+            past_kv = getattr(past_key_value, "kv", None)
+            if past_kv is None:
+                past_kv = torch.stack([past_key_value[0], past_key_value[1]], dim=2)
+            kv_all = torch.cat([past_kv, kv], dim=1)
             past_kI = getattr(past_key_value, "indexer_keys", None)
             if past_kI is not None:
                 # scores against every cached key, offset-causal for the new rows
@@ -521,7 +522,8 @@ class GatedSparseAttention(nn.Module):
                 # a plain (k, v) cache: the reference scores the new tokens only
                 # (gated_sparse_attention.py:197-213), selecting among positions [0, L)
                 kI_all, q_pos0 = kI, 0
-        present = GSAKVCache(k_all, v_all, indexer_keys) if use_cache else None
+        k_all, v_all = kv_all[:, :, 0], kv_all[:, :, 1]
+        present = GSAKVCache(k_all, v_all, indexer_keys, kv_all) if use_cache else None
         mark("kv")
 
         n_cols = kI_all.shape[1]

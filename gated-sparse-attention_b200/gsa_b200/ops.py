@@ -62,16 +62,18 @@ def make_dims(d_model, n_heads, n_kv_heads, d_head, n_idx_heads, d_idx, gate_act
 
 
 def proj_epilogue(dims: Dims, layout: ProjLayout, proj: torch.Tensor, positions: torch.Tensor,
-                  cos_tab: torch.Tensor, sin_tab: torch.Tensor, has_g1: bool):
+                  cos_tab: torch.Tensor, sin_tab: torch.Tensor, has_g1: bool, return_kv: bool = False):
     """q, k (RoPE), v (G2), g1 gate, indexer head weights w and row shift from the fused
-    projection output ``proj`` [T, Ncat]."""
+    projection output ``proj`` [T, Ncat].  k and v are views of one interleaved [T, 2, Hk, D]
+    buffer; with ``return_kv`` that buffer is returned in their place: (q, kv, g1, w, shift)."""
     _cuda(proj, positions, cos_tab, sin_tab)
     T = proj.shape[0]
     H, Hk, D, HI = dims.n_heads, dims.n_kv_heads, dims.d_head, dims.n_idx_heads
     dt = proj.dtype
     q = torch.empty(T, H, D, device=proj.device, dtype=dt)
-    k = torch.empty(T, Hk, D, device=proj.device, dtype=dt)
-    v = torch.empty(T, Hk, D, device=proj.device, dtype=dt)
+    # K and V interleaved per token ([T, 2, Hk, D]): the sparse SDPA moves a key as one copy
+    kv = torch.empty(T, 2, Hk, D, device=proj.device, dtype=dt)
+    k, v = kv[:, 0], kv[:, 1]
     g1 = torch.empty(T, H, D, device=proj.device, dtype=dt) if has_g1 else None
     w = torch.empty(T, HI, device=proj.device, dtype=torch.float32)
     shift = torch.empty(T, device=proj.device, dtype=torch.float32)
@@ -81,8 +83,10 @@ def proj_epilogue(dims: Dims, layout: ProjLayout, proj: torch.Tensor, positions:
     sin_tab = sin_tab.contiguous()
     _lib.call("gsa_proj_epilogue", C.byref(dims), C.byref(layout), dtype_code(dt), T, _p(proj),
               proj.stride(0), _p(pos), _p(cos_tab), _p(sin_tab), dtype_code(cos_tab.dtype),
-              cos_tab.shape[0], _p(q), _p(k), _p(v), _p(g1), _p(w), _p(shift), _stream())
+              cos_tab.shape[0], _p(q), _p(k), _p(v), kv.stride(0), _p(g1), _p(w), _p(shift), _stream())
     _after("proj_epilogue")
+    if return_kv:
+        return q, kv, g1, w, shift
     return q, k, v, g1, w, shift
 
 
@@ -122,9 +126,10 @@ def row_stats(scores2d: torch.Tensor) -> torch.Tensor:
 
 
 def topk_candidates(scores2d: torch.Tensor, k_eff: int, Lq: int | None = None, q_pos0: int = 0,
-                    causal: bool = False):
+                    causal: bool = False, row_center: torch.Tensor | None = None):
     """k_eff largest finite scores per row, ascending column order (int32 idx, fp32 score,
-    int32 count).  Unfilled slots hold column 0."""
+    int32 count).  Unfilled slots hold column 0.  ``row_center`` [R]: every finite score of row
+    r lies in [0, 2 row_center[r]] (enables the two-pass bounded-range selection)."""
     _cuda(scores2d)
     s = scores2d if scores2d.dtype == torch.float32 else scores2d.float()
     if s.stride(1) != 1:
@@ -133,8 +138,10 @@ def topk_candidates(scores2d: torch.Tensor, k_eff: int, Lq: int | None = None, q
     idx = torch.zeros(R, k_eff, device=s.device, dtype=torch.int32)
     sc = torch.zeros(R, k_eff, device=s.device, dtype=torch.float32)
     cnt = torch.empty(R, device=s.device, dtype=torch.int32)
+    if row_center is not None:
+        row_center = row_center.float().contiguous()
     _lib.call("gsa_topk_candidates", R, Lq or R, n, q_pos0, int(causal), _p(s), s.stride(0),
-              int(k_eff), _p(idx), _p(sc), _p(cnt), _stream())
+              _p(row_center), int(k_eff), _p(idx), _p(sc), _p(cnt), _stream())
     _after("topk_candidates")
     return idx, sc, cnt
 
@@ -171,19 +178,30 @@ def select_finalize(cand_idx, cand_score, cand_count, k, want_mask: bool = False
     return sel, cnt, mask
 
 
+def _kv_rows(t: torch.Tensor) -> torch.Tensor:
+    """[B, Lkv, Hk, D] with unit-stride rows of Hk*D elements and batch-contiguous key rows."""
+    B, L, Hk, D = t.shape
+    if t.stride(3) != 1 or t.stride(2) != D or (B > 1 and t.stride(0) != L * t.stride(1)):
+        t = t.contiguous()
+    return t
+
+
 def sparse_sdpa(dims: Dims, q, k, v, sel_idx, sel_count, gate, scale: float) -> torch.Tensor:
-    """q [B, Lq, H, D]; k, v [B, Lkv, Hk, D]; sel [B*Lq, ld] int32; gate like q or None."""
+    """q [B, Lq, H, D]; k, v [B, Lkv, Hk, D] (separate, or views of one interleaved
+    [B, Lkv, 2, Hk, D] buffer); sel [B*Lq, ld] int32; gate like q or None."""
     _cuda(q, k, v, sel_idx, sel_count, gate)
     B, Lq = q.shape[0], q.shape[1]
     Lkv = k.shape[1]
     q = q.contiguous()
-    k = k.contiguous()
-    v = v.contiguous()
+    k = _kv_rows(k)
+    v = _kv_rows(v)
+    if k.stride(1) != v.stride(1):
+        k, v = k.contiguous(), v.contiguous()
     gate = gate.contiguous() if gate is not None else None
     out = torch.empty_like(q)
     _lib.call("gsa_sparse_sdpa", C.byref(dims), dtype_code(q.dtype), B, Lq, Lkv, _p(q), _p(k), _p(v),
-              _p(sel_idx), sel_idx.stride(0), _p(sel_count), _p(gate), _p(out), float(scale),
-              _stream())
+              k.stride(1), _p(sel_idx), sel_idx.stride(0), _p(sel_count), _p(gate), _p(out),
+              float(scale), _stream())
     _after("sparse_sdpa")
     return out
 

@@ -83,14 +83,15 @@ const char* gsa_version(void);
  *   proj          [T, proj_ld]            dtype
  *   positions     [T] int64
  *   cos_tab/sin_tab [tab_rows, d_head]    tab_dtype (the module's RoPE buffers)
- *   q_out [T, H, D], k_out [T, Hk, D], v_out [T, Hk, D], g1_out [T, H, D] (NULL if no G1),
- *   w_out [T, H_I] fp32, shift_out [T] fp32
+ *   q_out [T, H, D]; k_out, v_out: token t's [Hk, D] row at t * kv_ld (kv_ld = 2*Hk*D and
+ *   v_out = k_out + Hk*D gives the interleaved KV layout gsa_sparse_sdpa reads fastest);
+ *   g1_out [T, H, D] (NULL if no G1), w_out [T, H_I] fp32, shift_out [T] fp32
  */
 int gsa_proj_epilogue(const gsa_dims* dims, const gsa_proj_layout* layout, int dtype, int64_t T,
                       const void* proj, int64_t proj_ld, const int64_t* positions,
                       const void* cos_tab, const void* sin_tab, int tab_dtype, int64_t tab_rows,
-                      void* q_out, void* k_out, void* v_out, void* g1_out, float* w_out,
-                      float* shift_out, gsa_stream_t stream);
+                      void* q_out, void* k_out, void* v_out, int64_t kv_ld, void* g1_out,
+                      float* w_out, float* shift_out, gsa_stream_t stream);
 
 /*
  * Gated indexer scores, I[t,s] = sum_j w[t,j] * act(scale * <qI[t,j], kI[s]> + bias[j])
@@ -126,10 +127,14 @@ int gsa_row_stats(int64_t R, int64_t n_cols, const float* scores, int64_t scores
  * (the candidate set of adaptive_topk.py:174-177).  n_r = n_cols, or, with ``causal``,
  * min(n_cols, q_pos0 + (r % Lq) + 1).  cand_count[r] = min(k_eff, finite entries).
  *   scores [R, scores_ld] fp32 ; cand_idx [R, k_eff] int32 ; cand_score [R, k_eff] fp32
+ *   row_center [R] fp32 or NULL: when given, every finite score of row r must lie in
+ *     [0, 2 row_center[r]] (true of sigmoid indexer scores with row_center = the
+ *     gsa_proj_epilogue shift); the selection then takes two passes over the row instead of
+ *     four.  Requires 16-byte aligned rows (scores_ld % 4 == 0).
  */
 int gsa_topk_candidates(int64_t R, int64_t Lq, int64_t n_cols, int64_t q_pos0, int causal,
-                        const float* scores, int64_t scores_ld, int32_t k_eff,
-                        int32_t* cand_idx, float* cand_score, int32_t* cand_count,
+                        const float* scores, int64_t scores_ld, const float* row_center,
+                        int32_t k_eff, int32_t* cand_idx, float* cand_score, int32_t* cand_count,
                         gsa_stream_t stream);
 
 /*
@@ -174,13 +179,15 @@ int gsa_apply_gate(int dtype, int act, int64_t n, const void* x, const void* log
  * GQA sparse SDPA with the G1 epilogue (gated_sparse_attention.py:234-290 and
  * output_gate.py:124-126): for every row r = (b, t), softmax(scale * q K_sel^T) V_sel per
  * head over the sel_count[r] keys sel_idx[r, :] shared by all heads, times gate[r] if given.
- *   q [B, Lq, H, D] ; k, v [B, Lkv, Hk, D] (contiguous, 16-byte aligned rows) ; gate like q
- *   out [B, Lq, H, D] in dtype.  sel indices are key positions inside the batch's sequence.
+ *   q [B, Lq, H, D] ; gate like q ; out [B, Lq, H, D] in dtype
+ *   k, v: key s of batch b is the [Hk, D] row at (b * Lkv + s) * kv_ld (16-byte aligned).
+ *     The interleaved layout (kv_ld = 2*Hk*D, v = k + Hk*D) moves each selected key as one
+ *     contiguous copy.  sel indices are key positions inside the batch's sequence.
  */
 int gsa_sparse_sdpa(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int64_t Lkv,
-                    const void* q, const void* k, const void* v, const int32_t* sel_idx,
-                    int64_t sel_ld, const int32_t* sel_count, const void* gate, void* out,
-                    float scale, gsa_stream_t stream);
+                    const void* q, const void* k, const void* v, int64_t kv_ld,
+                    const int32_t* sel_idx, int64_t sel_ld, const int32_t* sel_count,
+                    const void* gate, void* out, float scale, gsa_stream_t stream);
 
 /*
  * Workspace for gsa_indexer_select: bytes needed for a query chunk of ``chunk_rows`` rows

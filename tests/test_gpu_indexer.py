@@ -123,3 +123,32 @@ def test_topk_ties_take_lower_columns(cuda_ok):
         ours = np.sort(idx[r, :int(cnt[r])].cpu().numpy())
         ref = O.topk_sets_stable(s[r:r + 1], torch.tensor([k]))[0]
         assert np.array_equal(ours, ref), r
+
+
+@pytest.mark.parametrize("n,k", [(20000, 4096), (3000, 512), (131072, 4096), (700, 4096)])
+def test_bounded_range_selection_equals_radix(cuda_ok, n, k):
+    """The two-pass bounded-range selection keeps exactly the radix select's candidates,
+    including rows that are all ties or too concentrated for the compact buffer."""
+    from gsa_b200 import ops
+
+    g = torch.Generator().manual_seed(n)
+    R = 6
+    c = torch.rand(R, generator=g) * 3 + 0.5
+    s = torch.sigmoid(torch.randn(R, n, generator=g) * 2) * (2 * c.view(-1, 1))
+    s[1] = c[1]                                  # one value: every column ties
+    s[2] = torch.round(s[2] * 8) / 8             # heavy ties at few levels
+    s[3, n // 2:] = float("-inf")                # masked tail
+    s[4] = c[4] * (1 + 1e-6 * torch.rand(n, generator=g))   # all in one bin: overflow fallback
+    s = s.contiguous()
+    sd = s.to(DEV)
+    ri, rs, rc = ops.topk_candidates(sd, k)
+    bi, bs, bc = ops.topk_candidates(sd, k, row_center=c.to(DEV))
+    torch.cuda.synchronize()
+    ops.check_device_error()
+    assert torch.equal(rc, bc)
+    valid = torch.arange(k, device=DEV).view(1, -1) < rc.view(-1, 1)
+    assert torch.equal(ri[valid], bi[valid])
+    assert torch.equal(rs[valid], bs[valid])
+    for r in range(R):
+        ref = O.topk_sets_stable(s[r:r + 1], torch.tensor([k]))[0]
+        assert np.array_equal(np.sort(bi[r, :int(bc[r])].cpu().numpy()), ref), r
