@@ -131,14 +131,14 @@ int gsa_row_stats(int64_t R, int64_t n_cols, const float* scores, int64_t scores
 }
 
 int gsa_topk_candidates(int64_t R, int64_t Lq, int64_t n_cols, int64_t q_pos0, int causal, const float* scores,
-                        int64_t scores_ld, const float* row_center, int32_t k_eff, int32_t* cand_idx,
-                        float* cand_score, int32_t* cand_count, gsa_stream_t stream) {
+                        int64_t scores_ld, const float* row_center, const double* row_stats, int32_t k_eff,
+                        int32_t* cand_idx, float* cand_score, int32_t* cand_count, gsa_stream_t stream) {
   if (R < 0 || Lq <= 0 || n_cols < 0 || k_eff < 1 || scores_ld < n_cols || n_cols > 0x7fffffffLL)
     return GSA_ERR_BAD_ARG;
   if (R == 0) return GSA_OK;
   if (!scores || !cand_idx || !cand_score || !cand_count) return GSA_ERR_BAD_ARG;
-  return launch_topk_candidates(R, Lq, n_cols, q_pos0, causal, scores, scores_ld, row_center, k_eff, cand_idx,
-                                cand_score, cand_count, reinterpret_cast<cudaStream_t>(stream));
+  return launch_topk_candidates(R, Lq, n_cols, q_pos0, causal, scores, scores_ld, row_center, row_stats, k_eff,
+                                cand_idx, cand_score, cand_count, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int gsa_row_variance(int64_t R, int64_t n_cols, int dtype, const double* row_stats, const float* shift,
@@ -246,8 +246,9 @@ int gsa_indexer_select(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, i
       if (st) return st;
       // sigmoid scores of row r lie in [0, sum_j w_rj] = [0, 2 shift_r]: the bounded-range selection
       const float* center = (shift && dims->idx_act == GSA_ACT_SIGMOID) ? shift + r0 : nullptr;
-      st = gsa_topk_candidates(n, n, Lkv, q_pos0 + t0, causal, scratch, ld, center, k_eff, cand_idx + r0 * k_eff,
-                               cand_score + r0 * k_eff, cand_count + r0, stream);
+      st = gsa_topk_candidates(n, n, Lkv, q_pos0 + t0, causal, scratch, ld, center,
+                               (center && row_stats) ? row_stats + r0 * 3 : nullptr, k_eff,
+                               cand_idx + r0 * k_eff, cand_score + r0 * k_eff, cand_count + r0, stream);
       if (st) return st;
     }
   }

@@ -18,10 +18,11 @@
 //   sigmoid(z) = 0.5 + 0.5 tanh(z / 2)  =>  I[t,s] = c_t + sum_j (w_tj / 2) tanh((scale*acc + b_j) / 2)
 // with c_t = sum_j w_tj / 2, i.e. one FFMA, one tanh.approx and one FFMA per (t, s, j).  The
 // tanh form's error (< 1e-3 relative on the score) is inside the bf16 parity bar (2e-2); the
-// fp32 layer runs on the precise CUDA-core kernel instead.
+// fp32 layer runs on the precise CUDA-core kernel instead.  The epilogue is latency-bound
+// (MUFU and TMEM-load latencies), so it runs 16 warps: four per TMEM lane quarter.
 //
-// Roles (320 threads): warp 0 = TMA producer, warp 1 = TMEM allocator + MMA issuer (one lane),
-// warps 2..9 = epilogue (two warps per TMEM lane quarter, each taking half of the tokens).
+// Roles (576 threads): warp 0 = TMA producer, warp 1 = TMEM allocator + MMA issuer (one lane),
+// warps 2..17 = epilogue (four warps per TMEM lane quarter, each taking a quarter of the tokens).
 // Work item (CTA) = one query block x a range of up to kTilesPerCta key tiles; causal tiles
 // beyond the block's last query are never visited.  Every wait is bounded.
 #include <cuda.h>
@@ -38,7 +39,8 @@ constexpr int kN = 256;             // N: (token, head) pairs per tile
 constexpr int kDI = 64;             // K: indexer dim (one 128-byte swizzle atom)
 constexpr int kStages = 6;          // kI tile ring
 constexpr int kTilesPerCta = 32;    // key tiles per work item
-constexpr int kThreads = 320;
+constexpr int kThreads = 576;
+constexpr int kEpiWarps = 16;
 constexpr int kATileBytes = kKeys * kDI * 2;  // 16 KiB
 constexpr int kBTileBytes = kN * kDI * 2;     // 32 KiB
 constexpr int kSmemBytes = 1024 + kBTileBytes + kStages * kATileBytes + kN * 4 + 2 * 64 * 4 + 256;
@@ -113,6 +115,19 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Wait for this thread's TMEM loads, with the loaded registers as operands so that no read of
+// them can be scheduled before the wait.
+__device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
+
 __device__ __forceinline__ float tanh_fast(float x) {
   float y;
   asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -123,7 +138,7 @@ template <int HI>
 __global__ void __launch_bounds__(kThreads, 1)
     indexer_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ, Params p) {
   constexpr int TOK = kN / HI;        // tokens per query block
-  constexpr int TOK_HALF = TOK / 2;   // tokens per epilogue warp
+  constexpr int TOK_Q = TOK / 4;      // tokens per epilogue warp
   constexpr int TOK_PER_LD = 32 / HI; // tokens per 32-column TMEM load
   extern __shared__ uint8_t smem_raw[];
 
@@ -166,7 +181,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(b_full, 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&t_full[b], 1);
-      mbar_init(&t_empty[b], 8);
+      mbar_init(&t_empty[b], kEpiWarps);
     }
     fence_barrier_init();
   }
@@ -232,13 +247,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     // -------------------------------------- epilogue --------------------------------------
     const int ew = warp - 2;
     const int quarter = warp & 3;   // TMEM lane quarter this warp may access
-    const int half = ew >> 2;       // which half of the block's tokens
+    const int sub = ew >> 2;        // which quarter of the block's tokens
     float hb[HI];
 #pragma unroll
     for (int j = 0; j < HI; ++j) hb[j] = 0.5f * p.bias[j];
-    float s1[TOK_HALF], s2[TOK_HALF];
+    float s1[TOK_Q], s2[TOK_Q];
 #pragma unroll
-    for (int t = 0; t < TOK_HALF; ++t) s1[t] = s2[t] = 0.f;
+    for (int t = 0; t < TOK_Q; ++t) s1[t] = s2[t] = 0.f;
     const int64_t pos0 = p.q_pos0 + tok0;
 
     for (int i = 0; i < n_my; ++i) {
@@ -250,27 +265,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       // the whole tile is unmasked for every token of the block?
       const bool tile_full = ((int64_t)(t_begin + i + 1) * kKeys <= p.Lkv) &&
                              (!p.causal || (int64_t)(t_begin + i + 1) * kKeys - 1 <= pos0) && ntok == TOK;
-      const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + buf * kN + half * (kN / 2);
+      const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + buf * kN + sub * (kN / 4);
+      static_assert((kN / 4) / 32 == 2, "two 32-column chunks per warp");
 #pragma unroll
-      for (int c = 0; c < (kN / 2) / 32; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t r[32];
         tmem_ld32(tbase + c * 32, r);
-        tmem_wait_ld();
-        if (c == (kN / 2) / 32 - 1) {
-          // the last load of this buffer is done: hand it back to the MMA warp
+        tmem_wait_ld(r);
+        if (c == 1) {
+          // every load of this buffer is done: hand it back to the MMA warp
           fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&t_empty[buf]);
         }
 #pragma unroll
         for (int tt = 0; tt < TOK_PER_LD; ++tt) {
-          const int tl = c * TOK_PER_LD + tt;       // token within this warp's half
-          const int ti = half * TOK_HALF + tl;      // token within the block
+          const int tl = c * TOK_PER_LD + tt;       // token within this warp's quarter
+          const int ti = sub * TOK_Q + tl;          // token within the block
+          float th[HI];
+#pragma unroll
+          for (int j = 0; j < HI; ++j) th[j] = tanh_fast(fmaf(__uint_as_float(r[tt * HI + j]), p.half_scale, hb[j]));
+          const float4* w4 = reinterpret_cast<const float4*>(w_s + ti * HI);
           float y = 0.f;
 #pragma unroll
-          for (int j = 0; j < HI; ++j) {
-            const float z = fmaf(__uint_as_float(r[tt * HI + j]), p.half_scale, hb[j]);
-            y = fmaf(w_s[ti * HI + j], tanh_fast(z), y);
+          for (int j4 = 0; j4 < HI / 4; ++j4) {
+            const float4 w = w4[j4];
+            y = fmaf(w.x, th[4 * j4 + 0], y);
+            y = fmaf(w.y, th[4 * j4 + 1], y);
+            y = fmaf(w.z, th[4 * j4 + 2], y);
+            y = fmaf(w.w, th[4 * j4 + 3], y);
           }
           const bool ok = tile_full || (key_ok && ti < ntok && (!p.causal || key <= pos0 + ti));
           if (ok) {
@@ -287,14 +310,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t k_lo = (int64_t)t_begin * kKeys;
       const int64_t k_hi = min((int64_t)t_end * kKeys, p.Lkv);
 #pragma unroll
-      for (int tl = 0; tl < TOK_HALF; ++tl) {
+      for (int tl = 0; tl < TOK_Q; ++tl) {
         float a = s1[tl], b = s2[tl];
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
           a += __shfl_xor_sync(0xffffffffu, a, o);
           b += __shfl_xor_sync(0xffffffffu, b, o);
         }
-        const int ti = half * TOK_HALF + tl;
+        const int ti = sub * TOK_Q + tl;
         if (lane == 0 && ti < ntok) {
           double* st = p.row_stats + (int64_t)(tok0 + ti) * 3;
           atomicAdd(st + 0, (double)a);

@@ -238,65 +238,52 @@ struct CandCol {
 // ---------------------------------------------------------------------------------------------
 constexpr int kCap = 8192;
 
-__device__ __forceinline__ int lin_bin(float x, float scale) {
-  int b = __float2int_rd(x * scale);
-  return b < 0 ? 0 : (b >= kBins ? kBins - 1 : b);
+// Bin of x in [0, 2c] -> [0, kBins): the saturating float->uint conversion maps negatives,
+// NaN and -inf to 0 and +inf to the top, so the map is monotone on every input.
+__device__ __forceinline__ uint32_t lin_bin(float x, float scale) {
+  return min(__float2uint_rz(x * scale), (uint32_t)(kBins - 1));
 }
 
-__device__ void linear_histogram(const float* row, int64_t n, float scale, uint32_t* hist, uint32_t* finite) {
-  uint32_t my_finite = 0;
-  const int64_t n4 = n / 4;
+// Histogram of the first n scores of a 16-byte aligned row (8 per thread per iteration).
+__device__ void linear_histogram(const float* row, int64_t n, float scale, uint32_t* hist) {
+  const int64_t n8 = n / 8;
   const float4* row4 = reinterpret_cast<const float4*>(row);
-  for (int64_t i = threadIdx.x; i < n4; i += blockDim.x) {
-    const float4 v = row4[i];
-    const float e[4] = {v.x, v.y, v.z, v.w};
+  for (int64_t i = threadIdx.x; i < n8; i += blockDim.x) {
+    const float4 a = row4[2 * i], b = row4[2 * i + 1];
+    const float e[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      if (valid_key(e[j])) {
-        ++my_finite;
-        atomicAdd(&hist[lin_bin(e[j], scale)], 1u);
-      }
-    }
+    for (int j = 0; j < 8; ++j) atomicAdd(&hist[lin_bin(e[j], scale)], 1u);
   }
-  for (int64_t i = n4 * 4 + threadIdx.x; i < n; i += blockDim.x) {
-    const float x = row[i];
-    if (valid_key(x)) {
-      ++my_finite;
-      atomicAdd(&hist[lin_bin(x, scale)], 1u);
-    }
-  }
-  const uint32_t wsum = warp_sum(my_finite);
-  if ((threadIdx.x & 31) == 0) atomicAdd(finite, wsum);
+  for (int64_t i = n8 * 8 + threadIdx.x; i < n; i += blockDim.x) atomicAdd(&hist[lin_bin(row[i], scale)], 1u);
 }
 
-// Ordered compaction of the finite scores with bin >= bstar into (vals, cols); returns the count.
-__device__ uint32_t compact_top_bins(const float* row, int64_t n, float scale, int bstar, float* vals,
-                                     int32_t* cols, uint32_t* ws) {
-  constexpr int PER = 4;
+// Ordered compaction of the finite scores that satisfy `keep` into (vals, cols), 8 consecutive
+// scores per thread.  Writes at most kCap of them and returns the full count.
+template <typename Keep>
+__device__ uint32_t compact_row(const float* row, int64_t n, Keep keep, float* vals, int32_t* cols, uint32_t* ws) {
+  constexpr int PER = 8;
   const int64_t chunk = (int64_t)blockDim.x * PER;
   uint32_t base = 0;
   for (int64_t c0 = 0; c0 < n; c0 += chunk) {
     float v[PER];
-    bool f[PER];
-    uint32_t cnt = 0;
     const int64_t i0 = c0 + (int64_t)threadIdx.x * PER;
     if (i0 + PER <= n) {
-      const float4 q = *reinterpret_cast<const float4*>(row + i0);
-      v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+      const float4 a = *reinterpret_cast<const float4*>(row + i0);
+      const float4 b = *reinterpret_cast<const float4*>(row + i0 + 4);
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
     } else {
 #pragma unroll
       for (int j = 0; j < PER; ++j) v[j] = (i0 + j < n) ? row[i0 + j] : -INFINITY;
     }
+    uint32_t flags = 0;
 #pragma unroll
-    for (int j = 0; j < PER; ++j) {
-      f[j] = valid_key(v[j]) && lin_bin(v[j], scale) >= bstar;
-      cnt += f[j];
-    }
+    for (int j = 0; j < PER; ++j)
+      if (keep(v[j]) && valid_key(v[j])) flags |= 1u << j;
     uint32_t total;
-    uint32_t pos = base + block_exclusive_scan(cnt, ws, &total);
+    uint32_t pos = base + block_exclusive_scan((uint32_t)__popc(flags), ws, &total);
 #pragma unroll
     for (int j = 0; j < PER; ++j) {
-      if (f[j]) {
+      if (flags & (1u << j)) {
         if (pos < (uint32_t)kCap) {
           vals[pos] = v[j];
           cols[pos] = (int32_t)(i0 + j);
@@ -307,12 +294,122 @@ __device__ uint32_t compact_top_bins(const float* row, int64_t n, float scale, i
     base += total;
   }
   __syncthreads();
-  return base < (uint32_t)kCap ? base : (uint32_t)kCap;
+  return base;
 }
+
+// ---------------------------------------------------------------------------------------------
+// Exact top-K of a small shared-memory set (the survivors of a row, or a row's candidates):
+// vals[0..m) finite, in column order.  A 2048-bin histogram over [min, max] finds the bin b* of
+// the K-th largest; every value above b* is kept; inside b* the values are ranked exactly
+// (value descending, then position) -- b* holds few values unless the set is tie-heavy, in
+// which case the 3-pass radix select takes over.  Kept positions are flagged in take[m].
+// Returns false if the caller must use the radix select.
+// ---------------------------------------------------------------------------------------------
+constexpr int kRankCap = 1024;
+
+__device__ bool flag_top_smem(const float* vals, uint32_t m, uint32_t K, uint32_t* hist, uint32_t* ws,
+                              uint8_t* take, uint32_t* list, float* red) {
+  // min / max
+  float lo = INFINITY, hi = -INFINITY;
+  for (uint32_t i = threadIdx.x; i < m; i += blockDim.x) {
+    lo = fminf(lo, vals[i]);
+    hi = fmaxf(hi, vals[i]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+    hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+  }
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if (lane == 0) { red[wid] = lo; red[32 + wid] = hi; }
+  for (int i = threadIdx.x; i < kBins; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  lo = red[0];
+  hi = red[32];
+  for (int w = 1; w < nw; ++w) { lo = fminf(lo, red[w]); hi = fmaxf(hi, red[32 + w]); }
+  if (!(hi > lo)) {
+    // one value: the first K positions
+    for (uint32_t i = threadIdx.x; i < m; i += blockDim.x) take[i] = i < K;
+    __syncthreads();
+    return true;
+  }
+  const float scale = (float)kBins / (hi - lo);
+  auto bin = [&](float x) { return min(__float2uint_rz((x - lo) * scale), (uint32_t)(kBins - 1)); };
+  for (uint32_t i = threadIdx.x; i < m; i += blockDim.x) atomicAdd(&hist[bin(vals[i])], 1u);
+  __syncthreads();
+  uint32_t* dig = ws + 40;
+  find_digit(hist, kBins, K, ws, dig);
+  const uint32_t bstar = dig[0];
+  const uint32_t need = K - dig[1];
+  const uint32_t e = hist[bstar];
+  __syncthreads();
+  if (e > (uint32_t)kRankCap) return false;
+  // flag everything above b*; list the b* members in position order
+  uint32_t base = 0;
+  for (uint32_t c0 = 0; c0 < m; c0 += blockDim.x) {
+    const uint32_t i = c0 + threadIdx.x;
+    uint32_t b = 0, in = 0;
+    if (i < m) {
+      b = bin(vals[i]);
+      take[i] = b > bstar;
+      in = b == bstar;
+    }
+    uint32_t total;
+    const uint32_t pos = base + block_exclusive_scan(in, ws, &total);
+    if (in) list[pos] = i;
+    base += total;
+  }
+  __syncthreads();
+  // rank inside b*: value descending, then position ascending
+  for (uint32_t a = threadIdx.x; a < e; a += blockDim.x) {
+    const uint32_t ia = list[a];
+    const float va = vals[ia];
+    uint32_t rank = 0;
+    for (uint32_t b = 0; b < e; ++b) {
+      const float vb = vals[list[b]];
+      rank += (vb > va) || (vb == va && b < a);
+    }
+    if (rank < need) take[ia] = 1;
+  }
+  __syncthreads();
+  return true;
+}
+
+// Ordered compaction of the flagged positions: writes out_idx (through col map), out_score and
+// out_mask (by position); returns the count.
+template <typename ColMap>
+__device__ uint32_t collect_flagged(const float* vals, uint32_t m, const uint8_t* take, int32_t* out_idx,
+                                    float* out_score, ColMap out_col, uint8_t* out_mask, uint32_t cap, uint32_t* ws) {
+  uint32_t base = 0;
+  for (uint32_t c0 = 0; c0 < m; c0 += blockDim.x) {
+    const uint32_t i = c0 + threadIdx.x;
+    const uint32_t t = (i < m) ? take[i] : 0u;
+    uint32_t total;
+    const uint32_t pos = base + block_exclusive_scan(t, ws, &total);
+    if (t && pos < cap) {
+      out_idx[pos] = out_col(i);
+      if (out_score) out_score[pos] = vals[i];
+      if (out_mask) out_mask[i] = 1;
+    }
+    base += total;
+  }
+  return base < cap ? base : cap;
+}
+
+struct KeepBins {
+  float scale;
+  uint32_t bstar;
+  __device__ bool operator()(float x) const { return lin_bin(x, scale) >= bstar; }
+};
+struct KeepAbove {
+  float tau;
+  __device__ bool operator()(float x) const { return x >= tau; }
+};
 
 __global__ void __launch_bounds__(kSelThreads) topk_candidates_kernel(
     int64_t Lq, int64_t n_cols, int64_t q_pos0, int causal, const float* scores, int64_t ld,
-    const float* row_center, int32_t k_eff, int32_t* cand_idx, float* cand_score, int32_t* cand_count) {
+    const float* row_center, const double* row_stats, int32_t k_eff, int32_t* cand_idx, float* cand_score,
+    int32_t* cand_count) {
   __shared__ uint32_t hist[kBins];
   __shared__ uint32_t ws[48];
   __shared__ uint32_t sel[4];
@@ -330,32 +427,64 @@ __global__ void __launch_bounds__(kSelThreads) topk_candidates_kernel(
   bool done = false;
   if (row_center) {
     const float hi = 2.f * row_center[r];
-    if (hi > 0.f && hi < 3.0e38f) {
-      const float scale = (float)kBins / hi;
-      for (int i = threadIdx.x; i < kBins; i += blockDim.x) hist[i] = 0;
-      if (threadIdx.x == 0) sel[2] = 0;
-      __syncthreads();
-      linear_histogram(row, n, scale, hist, &sel[2]);
-      __syncthreads();
-      const uint32_t finite = sel[2];
-      if (finite <= K) {
-        cnt = collect(src, 0u, 0u, true, oidx, osc, IdentityCol{}, ws, K);
-        done = true;
-      } else {
+    float* cv = reinterpret_cast<float*>(topk_dyn);
+    int32_t* cc = reinterpret_cast<int32_t*>(topk_dyn + kCap * sizeof(float));
+    int64_t m = -1;  // number of scores compacted into (cv, cc), -1 = none
+    if (n <= (int64_t)K) {
+      // every finite score is a candidate
+      cnt = collect(src, 0u, 0u, true, oidx, osc, IdentityCol{}, ws, K);
+      done = true;
+    } else {
+      if (row_stats && row_stats[r * 3 + 2] > 0.0) {
+        // One pass: a threshold from the row's mean and spread (the indexer's statistics,
+        // taken relative to row_center) at the normal quantile of 1.5 K / n.  Retried lower or
+        // higher if fewer than K or more than kCap scores pass it.
+        const double* st = row_stats + r * 3;
+        const double mu_y = st[0] / st[2];
+        const double var = st[1] / st[2] - mu_y * mu_y;
+        const float sd = (float)sqrt(var > 0.0 ? var : 0.0);
+        const float mean = row_center[r] + (float)mu_y;
+        const float pt = 1.5f * (float)K / (float)n;
+        float tau = pt >= 1.f ? -INFINITY : mean + sd * 1.41421356f * erfinvf(1.f - 2.f * pt);
+        for (int attempt = 0; attempt < 3; ++attempt) {
+          const uint32_t C = compact_row(row, n, KeepAbove{tau}, cv, cc, ws);
+          if (C >= K && C <= (uint32_t)kCap) {
+            m = C;
+            break;
+          }
+          if (C < K) tau = attempt == 0 ? tau - sd : -INFINITY;
+          else tau = tau + 0.25f * sd;
+        }
+      }
+      if (m < 0 && hi > 0.f && hi < 3.0e38f) {
+        // two passes: a histogram over the bounded range finds the bin of the K-th score
+        const float scale = (float)kBins / hi;
+        for (int i = threadIdx.x; i < kBins; i += blockDim.x) hist[i] = 0;
+        __syncthreads();
+        linear_histogram(row, n, scale, hist);
+        __syncthreads();
         uint32_t* dig = ws + 40;
         find_digit(hist, kBins, K, ws, dig);
-        const int bstar = (int)dig[0];
+        const uint32_t bstar = dig[0];
         const uint32_t C = dig[1] + hist[bstar];
         __syncthreads();
-        if (C <= (uint32_t)kCap) {
-          float* cv = reinterpret_cast<float*>(topk_dyn);
-          int32_t* cc = reinterpret_cast<int32_t*>(topk_dyn + kCap * sizeof(float));
-          const uint32_t m = compact_top_bins(row, n, scale, bstar, cv, cc, ws);
-          RowSrc s2{cv, (int64_t)m};
+        if (C <= (uint32_t)kCap) m = compact_row(row, n, KeepBins{scale, bstar}, cv, cc, ws);
+      }
+      if (m >= 0 && m <= kCap) {
+        uint8_t* take = reinterpret_cast<uint8_t*>(topk_dyn + 2 * kCap * sizeof(float));
+        uint32_t* list = reinterpret_cast<uint32_t*>(take + kCap);
+        __shared__ float red[64];
+        if ((uint32_t)m <= K) {
+          RowSrc s2{cv, m};
+          cnt = collect(s2, 0u, 0u, true, oidx, osc, CandCol{cc}, ws, K);
+        } else if (flag_top_smem(cv, (uint32_t)m, K, hist, ws, take, list, red)) {
+          cnt = collect_flagged(cv, (uint32_t)m, take, oidx, osc, CandCol{cc}, nullptr, K, ws);
+        } else {
+          RowSrc s2{cv, m};
           radix_threshold(s2, K, hist, ws, sel);
           cnt = collect(s2, sel[0], sel[1], sel[3] != 0, oidx, osc, CandCol{cc}, ws, K);
-          done = true;
         }
+        done = true;
       }
     }
   }
@@ -368,36 +497,62 @@ __global__ void __launch_bounds__(kSelThreads) topk_candidates_kernel(
 
 __global__ void __launch_bounds__(kSelThreads) select_finalize_kernel(
     int32_t k_eff, const int32_t* cand_idx, const float* cand_score, const int32_t* cand_count,
-    const int32_t* k, int32_t* sel_idx, int64_t sel_ld, int32_t* sel_count, uint8_t* sel_mask) {
+    const int32_t* k, int32_t* sel_idx, int64_t sel_ld, int32_t* sel_count, uint8_t* sel_mask, int stage) {
   __shared__ uint32_t hist[kBins];
   __shared__ uint32_t ws[48];
   __shared__ uint32_t sel[4];
+  extern __shared__ __align__(16) uint8_t fin_dyn[];  // staged candidates: [k_eff] scores, [k_eff] cols
   const int64_t r = blockIdx.x;
   int32_t c = cand_count[r];
   int32_t kr = k[r];
   if (kr < 0) kr = 0;
   if (c < 0) c = 0;
   if (c > k_eff) c = k_eff;
-  RowSrc src{cand_score + r * k_eff, c};
+  const float* vals = cand_score + r * k_eff;
+  const int32_t* cols = cand_idx + r * k_eff;
   uint8_t* mrow = sel_mask ? sel_mask + r * k_eff : nullptr;
-  if (mrow) {
+  if (mrow)
     for (int i = threadIdx.x; i < k_eff; i += blockDim.x) mrow[i] = 0;
-    __syncthreads();
+  const bool radix = kr > 0 && kr < c;
+  if (radix && stage) {
+    // the radix passes re-read the candidates: stage them in shared memory once
+    float* sv = reinterpret_cast<float*>(fin_dyn);
+    int32_t* si = reinterpret_cast<int32_t*>(fin_dyn + (size_t)k_eff * sizeof(float));
+    for (int i = threadIdx.x; i < c; i += blockDim.x) {
+      sv[i] = vals[i];
+      si[i] = cols[i];
+    }
+    vals = sv;
+    cols = si;
   }
+  __syncthreads();
   uint32_t cnt;
   if (kr == 0 || c == 0) {
     cnt = 0;
   } else if (kr >= c) {
     // every candidate is kept: copy in order
     for (int i = threadIdx.x; i < c; i += blockDim.x) {
-      sel_idx[r * sel_ld + i] = cand_idx[r * k_eff + i];
+      sel_idx[r * sel_ld + i] = cols[i];
       if (mrow) mrow[i] = 1;
     }
     cnt = (uint32_t)c;
   } else {
-    radix_threshold(src, (uint32_t)kr, hist, ws, sel);
-    cnt = collect(src, sel[0], sel[1], sel[3] != 0, sel_idx + r * sel_ld, nullptr,
-                  CandCol{cand_idx + r * k_eff}, ws, (uint32_t)kr, mrow);
+    bool flagged = false;
+    if (stage) {
+      __shared__ float red[64];
+      uint8_t* take = fin_dyn + (size_t)k_eff * 8;
+      uint32_t* list = reinterpret_cast<uint32_t*>(take + ((k_eff + 15) / 16) * 16);
+      flagged = flag_top_smem(vals, (uint32_t)c, (uint32_t)kr, hist, ws, take, list, red);
+      if (flagged)
+        cnt = collect_flagged(vals, (uint32_t)c, take, sel_idx + r * sel_ld, nullptr, CandCol{cols}, mrow,
+                              (uint32_t)kr, ws);
+    }
+    if (!flagged) {
+      RowSrc src{vals, c};
+      radix_threshold(src, (uint32_t)kr, hist, ws, sel);
+      cnt = collect(src, sel[0], sel[1], sel[3] != 0, sel_idx + r * sel_ld, nullptr, CandCol{cols}, ws,
+                    (uint32_t)kr, mrow);
+    }
   }
   if (threadIdx.x == 0) sel_count[r] = (int32_t)cnt;
 }
@@ -495,22 +650,23 @@ __global__ void adaptive_k_kernel(int64_t R, int64_t n_cols, int dtype, gsa_topk
 
 // ---------------------------------------------------------------------------------------------
 int launch_topk_candidates(int64_t R, int64_t Lq, int64_t n_cols, int64_t q_pos0, int causal,
-                           const float* scores, int64_t ld, const float* row_center, int32_t k_eff,
-                           int32_t* cand_idx, float* cand_score, int32_t* cand_count, cudaStream_t stream) {
+                           const float* scores, int64_t ld, const float* row_center, const double* row_stats,
+                           int32_t k_eff, int32_t* cand_idx, float* cand_score, int32_t* cand_count,
+                           cudaStream_t stream) {
   if (R == 0) return GSA_OK;
   if (R > 0x7fffffffLL) return GSA_ERR_BAD_ARG;
   size_t dyn = 0;
   if (row_center) {
     // the float4 loads of the bounded path need 16-byte aligned rows
     if ((reinterpret_cast<uintptr_t>(scores) % 16) != 0 || (ld % 4) != 0) return GSA_ERR_BAD_ARG;
-    dyn = 2 * kCap * sizeof(float);
+    dyn = 2 * kCap * sizeof(float) + kCap + kRankCap * sizeof(uint32_t);
     if (cudaFuncSetAttribute(topk_candidates_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn) !=
         cudaSuccess)
       return GSA_ERR_LAUNCH;
   }
   topk_candidates_kernel<<<(unsigned)R, kSelThreads, dyn, stream>>>(Lq, n_cols, q_pos0, causal, scores, ld,
-                                                                   row_center, k_eff, cand_idx, cand_score,
-                                                                   cand_count);
+                                                                   row_center, row_stats, k_eff, cand_idx,
+                                                                   cand_score, cand_count);
   return cudaGetLastError() == cudaSuccess ? GSA_OK : GSA_ERR_LAUNCH;
 }
 
@@ -518,8 +674,15 @@ int launch_select_finalize(int64_t R, int32_t k_eff, const int32_t* cand_idx, co
                            const int32_t* cand_count, const int32_t* k, int32_t* sel_idx, int64_t sel_ld,
                            int32_t* sel_count, uint8_t* sel_mask, cudaStream_t stream) {
   if (R == 0) return GSA_OK;
-  select_finalize_kernel<<<(unsigned)R, kSelThreads, 0, stream>>>(k_eff, cand_idx, cand_score, cand_count,
-                                                                 k, sel_idx, sel_ld, sel_count, sel_mask);
+  const size_t dyn = (size_t)k_eff * 8 + ((size_t)(k_eff + 15) / 16) * 16 + kRankCap * sizeof(uint32_t);
+  const int stage = dyn <= 112 * 1024 ? 1 : 0;
+  // static + dynamic shared memory exceeds the 48 KiB default: opt in
+  if (stage &&
+      cudaFuncSetAttribute(select_finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn) !=
+          cudaSuccess)
+    return GSA_ERR_LAUNCH;
+  select_finalize_kernel<<<(unsigned)R, kSelThreads, stage ? dyn : 0, stream>>>(
+      k_eff, cand_idx, cand_score, cand_count, k, sel_idx, sel_ld, sel_count, sel_mask, stage);
   return cudaGetLastError() == cudaSuccess ? GSA_OK : GSA_ERR_LAUNCH;
 }
 

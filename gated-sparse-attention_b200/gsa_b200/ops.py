@@ -126,7 +126,8 @@ def row_stats(scores2d: torch.Tensor) -> torch.Tensor:
 
 
 def topk_candidates(scores2d: torch.Tensor, k_eff: int, Lq: int | None = None, q_pos0: int = 0,
-                    causal: bool = False, row_center: torch.Tensor | None = None):
+                    causal: bool = False, row_center: torch.Tensor | None = None,
+                    row_stats: torch.Tensor | None = None):
     """k_eff largest finite scores per row, ascending column order (int32 idx, fp32 score,
     int32 count).  Unfilled slots hold column 0.  ``row_center`` [R]: every finite score of row
     r lies in [0, 2 row_center[r]] (enables the two-pass bounded-range selection)."""
@@ -141,7 +142,7 @@ def topk_candidates(scores2d: torch.Tensor, k_eff: int, Lq: int | None = None, q
     if row_center is not None:
         row_center = row_center.float().contiguous()
     _lib.call("gsa_topk_candidates", R, Lq or R, n, q_pos0, int(causal), _p(s), s.stride(0),
-              _p(row_center), int(k_eff), _p(idx), _p(sc), _p(cnt), _stream())
+              _p(row_center), _p(row_stats), int(k_eff), _p(idx), _p(sc), _p(cnt), _stream())
     _after("topk_candidates")
     return idx, sc, cnt
 

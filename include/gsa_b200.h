@@ -131,11 +131,15 @@ int gsa_row_stats(int64_t R, int64_t n_cols, const float* scores, int64_t scores
  *     [0, 2 row_center[r]] (true of sigmoid indexer scores with row_center = the
  *     gsa_proj_epilogue shift); the selection then takes two passes over the row instead of
  *     four.  Requires 16-byte aligned rows (scores_ld % 4 == 0).
+ *   row_stats [R, 3] fp64 or NULL (needs row_center): the row statistics gsa_indexer_scores
+ *     produced for these rows with shift = row_center; the selection then usually takes one
+ *     pass (a threshold at the row's estimated (1 - 1.5 k_eff / n) quantile).  The result is
+ *     the same with or without it.
  */
 int gsa_topk_candidates(int64_t R, int64_t Lq, int64_t n_cols, int64_t q_pos0, int causal,
                         const float* scores, int64_t scores_ld, const float* row_center,
-                        int32_t k_eff, int32_t* cand_idx, float* cand_score, int32_t* cand_count,
-                        gsa_stream_t stream);
+                        const double* row_stats, int32_t k_eff, int32_t* cand_idx,
+                        float* cand_score, int32_t* cand_count, gsa_stream_t stream);
 
 /*
  * Per-row variance over all N_r = n_cols entries with masked entries counted as 0, unbiased

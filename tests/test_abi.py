@@ -50,10 +50,10 @@ def test_bad_arguments_are_rejected_before_any_launch():
 
     lib = _lib.lib()
     # negative sizes / null pointers
-    assert lib.gsa_topk_candidates(-1, 1, 10, 0, 0, None, 10, None, 4, None, None, None, None) == 1
-    assert lib.gsa_topk_candidates(4, 4, 10, 0, 0, None, 10, None, 0, None, None, None, None) == 1
+    assert lib.gsa_topk_candidates(-1, 1, 10, 0, 0, None, 10, None, None, 4, None, None, None, None) == 1
+    assert lib.gsa_topk_candidates(4, 4, 10, 0, 0, None, 10, None, None, 0, None, None, None, None) == 1
     assert lib.gsa_select_finalize(4, 8, None, None, None, None, None, 4, None, None, None) == 1
     assert lib.gsa_row_stats(4, 10, None, 5, None, None) == 1
     assert lib.gsa_apply_gate(7, 0, 10, None, None, None, None, None) == 1
     # empty work is a no-op success
-    assert lib.gsa_topk_candidates(0, 1, 10, 0, 0, None, 10, None, 4, None, None, None, None) == 0
+    assert lib.gsa_topk_candidates(0, 1, 10, 0, 0, None, 10, None, None, 4, None, None, None, None) == 0

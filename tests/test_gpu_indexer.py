@@ -142,13 +142,18 @@ def test_bounded_range_selection_equals_radix(cuda_ok, n, k):
     s = s.contiguous()
     sd = s.to(DEV)
     ri, rs, rc = ops.topk_candidates(sd, k)
-    bi, bs, bc = ops.topk_candidates(sd, k, row_center=c.to(DEV))
-    torch.cuda.synchronize()
-    ops.check_device_error()
-    assert torch.equal(rc, bc)
-    valid = torch.arange(k, device=DEV).view(1, -1) < rc.view(-1, 1)
-    assert torch.equal(ri[valid], bi[valid])
-    assert torch.equal(rs[valid], bs[valid])
-    for r in range(R):
-        ref = O.topk_sets_stable(s[r:r + 1], torch.tensor([k]))[0]
-        assert np.array_equal(np.sort(bi[r, :int(bc[r])].cpu().numpy()), ref), r
+    # row statistics relative to the centre, as the indexer produces them
+    fin = torch.isfinite(s)
+    y = torch.where(fin, s.double() - c.double().view(-1, 1), torch.zeros_like(s, dtype=torch.float64))
+    stats = torch.stack([y.sum(-1), (y * y).sum(-1), fin.sum(-1).double()], -1).to(DEV)
+    for st in (None, stats):
+        bi, bs, bc = ops.topk_candidates(sd, k, row_center=c.to(DEV), row_stats=st)
+        torch.cuda.synchronize()
+        ops.check_device_error()
+        assert torch.equal(rc, bc)
+        valid = torch.arange(k, device=DEV).view(1, -1) < rc.view(-1, 1)
+        assert torch.equal(ri[valid], bi[valid])
+        assert torch.equal(rs[valid], bs[valid])
+        for r in range(R):
+            ref = O.topk_sets_stable(s[r:r + 1], torch.tensor([k]))[0]
+            assert np.array_equal(np.sort(bi[r, :int(bc[r])].cpu().numpy()), ref), r
