@@ -261,16 +261,18 @@ __device__ void linear_histogram(const float* row, int64_t n, float scale, uint3
 // scores per thread.  Writes at most kCap of them and returns the full count.
 template <typename Keep>
 __device__ uint32_t compact_row(const float* row, int64_t n, Keep keep, float* vals, int32_t* cols, uint32_t* ws) {
-  constexpr int PER = 8;
+  constexpr int PER = 16;
   const int64_t chunk = (int64_t)blockDim.x * PER;
   uint32_t base = 0;
   for (int64_t c0 = 0; c0 < n; c0 += chunk) {
     float v[PER];
     const int64_t i0 = c0 + (int64_t)threadIdx.x * PER;
     if (i0 + PER <= n) {
-      const float4 a = *reinterpret_cast<const float4*>(row + i0);
-      const float4 b = *reinterpret_cast<const float4*>(row + i0 + 4);
-      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+#pragma unroll
+      for (int q = 0; q < PER / 4; ++q) {
+        const float4 a = *reinterpret_cast<const float4*>(row + i0 + 4 * q);
+        v[4 * q] = a.x; v[4 * q + 1] = a.y; v[4 * q + 2] = a.z; v[4 * q + 3] = a.w;
+      }
     } else {
 #pragma unroll
       for (int j = 0; j < PER; ++j) v[j] = (i0 + j < n) ? row[i0 + j] : -INFINITY;
@@ -344,19 +346,25 @@ __device__ bool flag_top_smem(const float* vals, uint32_t m, uint32_t K, uint32_
   const uint32_t e = hist[bstar];
   __syncthreads();
   if (e > (uint32_t)kRankCap) return false;
-  // flag everything above b*; list the b* members in position order
+  // flag everything above b*; list the b* members in position order (8 positions per thread)
   uint32_t base = 0;
-  for (uint32_t c0 = 0; c0 < m; c0 += blockDim.x) {
-    const uint32_t i = c0 + threadIdx.x;
-    uint32_t b = 0, in = 0;
-    if (i < m) {
-      b = bin(vals[i]);
-      take[i] = b > bstar;
-      in = b == bstar;
+  for (uint32_t c0 = 0; c0 < m; c0 += blockDim.x * 8) {
+    const uint32_t i0 = c0 + threadIdx.x * 8;
+    uint32_t in = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t i = i0 + j;
+      if (i < m) {
+        const uint32_t b = bin(vals[i]);
+        take[i] = b > bstar;
+        in |= (uint32_t)(b == bstar) << j;
+      }
     }
     uint32_t total;
-    const uint32_t pos = base + block_exclusive_scan(in, ws, &total);
-    if (in) list[pos] = i;
+    uint32_t pos = base + block_exclusive_scan((uint32_t)__popc(in), ws, &total);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (in & (1u << j)) list[pos++] = i0 + j;
     base += total;
   }
   __syncthreads();
@@ -381,15 +389,25 @@ template <typename ColMap>
 __device__ uint32_t collect_flagged(const float* vals, uint32_t m, const uint8_t* take, int32_t* out_idx,
                                     float* out_score, ColMap out_col, uint8_t* out_mask, uint32_t cap, uint32_t* ws) {
   uint32_t base = 0;
-  for (uint32_t c0 = 0; c0 < m; c0 += blockDim.x) {
-    const uint32_t i = c0 + threadIdx.x;
-    const uint32_t t = (i < m) ? take[i] : 0u;
+  for (uint32_t c0 = 0; c0 < m; c0 += blockDim.x * 8) {
+    const uint32_t i0 = c0 + threadIdx.x * 8;
+    uint32_t t = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (i0 + j < m && take[i0 + j]) t |= 1u << j;
     uint32_t total;
-    const uint32_t pos = base + block_exclusive_scan(t, ws, &total);
-    if (t && pos < cap) {
-      out_idx[pos] = out_col(i);
-      if (out_score) out_score[pos] = vals[i];
-      if (out_mask) out_mask[i] = 1;
+    uint32_t pos = base + block_exclusive_scan((uint32_t)__popc(t), ws, &total);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (t & (1u << j)) {
+        const uint32_t i = i0 + j;
+        if (pos < cap) {
+          out_idx[pos] = out_col(i);
+          if (out_score) out_score[pos] = vals[i];
+          if (out_mask) out_mask[i] = 1;
+        }
+        ++pos;
+      }
     }
     base += total;
   }
