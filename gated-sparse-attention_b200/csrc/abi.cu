@@ -201,7 +201,7 @@ int gsa_sparse_sdpa(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int6
                static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
                static_cast<const __nv_bfloat16*>(v), kv_ld, inter ? 1 : 0, sel_idx, sel_ld, sel_count,
                static_cast<const __nv_bfloat16*>(gate), static_cast<__nv_bfloat16*>(out),
-               scale * 1.4426950408889634f, 0, di->err};
+               scale * 1.4426950408889634f, 0, 2, di->err};
     return launch_sdpa_bf16(a, dims->d_head, dims->n_heads / dims->n_kv_heads, di->num_sms, s);
   }
   if (dtype == GSA_DTYPE_F32) {

@@ -61,6 +61,7 @@ struct SdpaArgs {
   __nv_bfloat16* out;
   float scale_log2;
   int nstages;
+  int nprod;          // producer warps
   int* err;
 };
 

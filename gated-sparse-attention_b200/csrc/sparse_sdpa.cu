@@ -24,7 +24,7 @@
 namespace gsa {
 
 constexpr int kKeysPerStage = 16;
-constexpr int kProducers = 2;
+constexpr int kMaxProducers = 3;
 constexpr int kMaxRowBytes = 16 * 256 * 2;
 __device__ __align__(128) uint8_t g_zero_row[2 * kMaxRowBytes];
 
@@ -66,7 +66,7 @@ __device__ __forceinline__ int row_count(const SdpaArgs& a, int64_t row) {
 }
 
 template <int D, int NREP>
-__global__ void __launch_bounds__(18 * 32) sdpa_tc_kernel(SdpaArgs a) {
+__global__ void __launch_bounds__(19 * 32) sdpa_tc_kernel(SdpaArgs a) {
   static_assert(D % 16 == 0 && NREP >= 1 && NREP <= 8, "tile shape");
   extern __shared__ __align__(128) uint8_t smem[];
   const int Hk = a.Hk;
@@ -92,8 +92,12 @@ __global__ void __launch_bounds__(18 * 32) sdpa_tc_kernel(SdpaArgs a) {
 
   if (warp >= Hk) {
     // ---------------------------- producer warps ----------------------------
-    // kProducers warps issue alternate stages: one warp's per-lane bulk-copy issue is the
-    // limit of a single producer, two raise the gather rate by ~9%.
+    // a.nprod warps issue stages round-robin: one warp's per-lane bulk-copy issue is the limit
+    // of a single producer.  nprod <= nstages keeps the parity waits unambiguous: before a
+    // producer waits on a stage's empty barrier, its own previous wait (nprod iterations
+    // earlier) guarantees the releases up to 2 * nstages iterations back, so the barrier is at
+    // most one phase behind the phase it waits for.
+    const int kProducers = a.nprod;
     const int pw = warp - Hk;
     uint32_t it = 0;
     bool ok = true;
@@ -332,7 +336,8 @@ static int launch_tc(SdpaArgs a, int num_sms, cudaStream_t stream) {
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return GSA_ERR_LAUNCH;
   int per_sm = 0;
-  const int threads = (a.Hk + kProducers) * 32;
+  a.nprod = nst < kMaxProducers ? nst : kMaxProducers;  // nprod <= nstages (see the producer loop)
+  const int threads = (a.Hk + a.nprod) * 32;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem) != cudaSuccess || per_sm < 1)
     return GSA_ERR_LAUNCH;
   const int64_t R = a.B * a.Lq;
