@@ -3,9 +3,10 @@
 Workload (one "step"): one GatedSparseAttention forward, d_model 4096, 32 query / 8 KV heads of
 128, 8 indexer heads of 64, k_base 2048 (k_min 256, k_max 4096, adaptive), value and output gates
 on, bf16, batch 1 x 131072 tokens, x ~ N(0,1), weights from the default init with seed 0.
-With N > 1 GPUs (torchrun) the query sequence is sharded: rank r owns a contiguous block of
-131072 / N tokens, K / V / indexer keys are all-gathered over NCCL and the adaptive-k variance
-sum is all-reduced; ``value`` is 131072 / (max over ranks of the step time).
+With N > 1 GPUs (torchrun) the query sequence is sharded: it is cut into 2N segments and rank r
+owns segments r and 2N-1-r (equal causal work per rank); K / V / indexer keys are all-gathered
+over NCCL and the adaptive-k variance sum is all-reduced; ``value`` is 131072 / (max over ranks
+of the step time).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--seq-len L]
 
@@ -156,7 +157,7 @@ def sdpa_algorithmic_bytes(cfg, cnt: torch.Tensor) -> float:
 
 def run_ours(args, world, rank):
     from gsa_b200 import GSAConfig, GatedSparseAttention, ops
-    from gsa_b200.sharded import enable_query_sharding
+    from gsa_b200.sharded import enable_query_sharding, zigzag_slice
 
     dev = torch.device("cuda", torch.cuda.current_device())
     L = args.seq_len
@@ -166,12 +167,14 @@ def run_ours(args, world, rank):
     if world > 1:
         import torch.distributed as dist
 
-        enable_query_sharding(m, dist.group.WORLD)
-    assert L % world == 0
+        # zigzag: rank r owns segments r and 2P-1-r of 2P, so causal indexer work is balanced
+        enable_query_sharding(m, dist.group.WORLD, layout="zigzag")
+    assert L % (2 * world) == 0
     Lr = L // world
     gen = torch.Generator().manual_seed(1)
     x_full = torch.randn(1, L, cfg.d_model, generator=gen, dtype=torch.float32)
-    x_host = x_full[:, rank * Lr:(rank + 1) * Lr].to(torch.bfloat16).contiguous().pin_memory()
+    x_host = (zigzag_slice(x_full, world, rank) if world > 1 else x_full).to(torch.bfloat16)
+    x_host = x_host.contiguous().pin_memory()
     del x_full
     x = x_host.to(dev)
     torch.cuda.synchronize()
@@ -284,7 +287,8 @@ def run_ours(args, world, rank):
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: x ~ N(0,1) seed 1, default-init weights seed 0",
         "config": {"workload": f"GSA layer fwd B=1 L={L} d4096 h32/8x128 idx8x64 k2048[256,4096] bf16",
-                   "batch": 1, "seq_len": L, "parallelism": f"query-sequence shards x{world}",
+                   "batch": 1, "seq_len": L,
+                   "parallelism": f"query-sequence shards x{world}" + (" (zigzag)" if world > 1 else ""),
                    "l2": "inputs larger than L2 (x 1 GiB, K/V 256 MiB each)"},
         "e2e": e2e, "roofline": roofline, "gpu_launches": launches_per_step * args.steps,
         "stages_ms": stages, "clocks": clocks,

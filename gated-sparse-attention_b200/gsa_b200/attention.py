@@ -472,11 +472,14 @@ class GatedSparseAttention(nn.Module):
         if sp is not None and past_key_value is not None:
             raise NotImplementedError("query-sharded layers run prefill without a KV cache")
         past_len = past_key_value[0].shape[1] if past_key_value is not None else 0
-        if sp is not None:
-            past_len = sp.start(L)  # absolute position of this rank's first token
+        # (local row start, rows, absolute position of the first row) of each query segment
+        segs = sp.segments(L) if sp is not None else [(0, L, past_len)]
+        if sp is not None and len(segs) > 1 and B != 1:
+            raise NotImplementedError("zigzag query sharding takes one sequence per call")
         if positions is None:
-            positions = torch.arange(past_len, past_len + L, device=x.device).unsqueeze(0).expand(B, -1)
-            max_pos = past_len + L - 1
+            positions = torch.cat([torch.arange(p0, p0 + n, device=x.device) for _, n, p0 in segs])
+            positions = positions.unsqueeze(0).expand(B, -1)
+            max_pos = max(p0 + n - 1 for _, n, p0 in segs)
         else:
             max_pos = int(positions.max().item())  # the reference syncs here too (rope.py:133-134)
         self.rotary_emb.ensure(max_pos + 1)
@@ -499,10 +502,10 @@ class GatedSparseAttention(nn.Module):
 
         indexer_keys = None
         if sp is not None:
-            # every rank needs all keys up to its last query: gather K/V and k^I in rank order
+            # every rank needs all keys up to its last query: gather K/V and k^I in sequence order
             kI_all = sp.gather(kI)
             kv_all = sp.gather(kv)
-            q_pos0 = sp.start(L)
+            q_pos0 = segs[0][2]
             indexer_keys = kI_all
         elif past_key_value is None:
             kv_all, kI_all, q_pos0 = kv, kI, 0
@@ -528,9 +531,23 @@ class GatedSparseAttention(nn.Module):
 
         n_cols = kI_all.shape[1]
         k_eff = min(cfg.k_max, n_cols) if cfg.use_adaptive_k else min(cfg.k_base, n_cols)
-        cand_idx, cand_score, cand_count, stats = ops.indexer_select(
-            dims, qI, kI_all, w, self.indexer.bias, self.indexer.scale, shift, k_eff,
-            q_pos0=q_pos0, causal=True)
+        if len(segs) == 1:
+            cand_idx, cand_score, cand_count, stats = ops.indexer_select(
+                dims, qI, kI_all, w, self.indexer.bias, self.indexer.scale, shift, k_eff,
+                q_pos0=q_pos0, causal=True)
+        else:
+            # one indexer pass per query segment, each with its own causal offset
+            R = B * L
+            cand_idx = torch.zeros(R, k_eff, device=x.device, dtype=torch.int32)
+            cand_score = torch.empty(R, k_eff, device=x.device, dtype=torch.float32)
+            cand_count = torch.empty(R, device=x.device, dtype=torch.int32)
+            stats = torch.zeros(R, 3, device=x.device, dtype=torch.float64)
+            wv = w.view(L, HI)
+            for l0, n, p0 in segs:
+                ops.indexer_select(dims, qI[:, l0:l0 + n], kI_all, wv[l0:l0 + n], self.indexer.bias,
+                                   self.indexer.scale, shift[l0:l0 + n], k_eff, q_pos0=p0, causal=True,
+                                   row_stats=stats[l0:l0 + n],
+                                   out=(cand_idx[l0:l0 + n], cand_score[l0:l0 + n], cand_count[l0:l0 + n]))
         mark("indexer_topk")
         if cfg.use_adaptive_k:
             var, total = ops.row_variance(stats, n_cols, dt, shift)

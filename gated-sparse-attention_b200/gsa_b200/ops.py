@@ -226,11 +226,12 @@ def workspace_bytes(chunk_rows: int, n_cols: int) -> int:
 
 def indexer_select(dims: Dims, qI, kI, w, bias, scale: float, shift, k_eff: int, q_pos0: int = 0,
                    causal: bool = True, chunk_rows: int | None = None, row_stats=None,
-                   workspace=None):
+                   workspace=None, out=None):
     """Indexer + top-k candidates for all rows, chunk by chunk (no [Lq, Lkv] score matrix).
 
     qI [B, Lq, H_I*d_I], kI [B, Lkv, d_I] (row-strided views allowed).  Returns
-    (cand_idx, cand_score, cand_count, row_stats) with rows = B*Lq."""
+    (cand_idx, cand_score, cand_count, row_stats) with rows = B*Lq; ``out`` may supply the first
+    three (row-contiguous) to be filled in place."""
     _cuda(qI, kI, w, bias)
     B, Lq, _ = qI.shape
     Lkv = kI.shape[1]
@@ -244,9 +245,13 @@ def indexer_select(dims: Dims, qI, kI, w, bias, scale: float, shift, k_eff: int,
     need = workspace_bytes(chunk_rows, Lkv)
     if workspace is None or workspace.numel() < need:
         workspace = torch.empty(need, device=dev, dtype=torch.uint8)
-    cand_idx = torch.zeros(R, k_eff, device=dev, dtype=torch.int32)
-    cand_score = torch.empty(R, k_eff, device=dev, dtype=torch.float32)
-    cand_count = torch.empty(R, device=dev, dtype=torch.int32)
+    if out is not None:
+        cand_idx, cand_score, cand_count = out
+        assert cand_idx.is_contiguous() and cand_score.is_contiguous() and cand_count.is_contiguous()
+    else:
+        cand_idx = torch.zeros(R, k_eff, device=dev, dtype=torch.int32)
+        cand_score = torch.empty(R, k_eff, device=dev, dtype=torch.float32)
+        cand_count = torch.empty(R, device=dev, dtype=torch.int32)
     if row_stats is None:
         row_stats = torch.zeros(R, 3, device=dev, dtype=torch.float64)
     w = w.reshape(R, -1).float().contiguous()

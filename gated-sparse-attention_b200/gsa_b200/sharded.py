@@ -45,25 +45,67 @@ def allreduce_sum(t: torch.Tensor, group) -> torch.Tensor:
 
 
 class QueryShards:
-    """The layer's view of its process group."""
+    """The layer's view of its process group and of its share of the query sequence.
 
-    def __init__(self, group):
+    ``layout="contiguous"``: rank r owns tokens [r*n, (r+1)*n) (n = the local length).
+    ``layout="zigzag"``: the sequence is cut into 2P equal segments and rank r owns segments r and
+    2P-1-r, in that order, so every rank gets the same number of causal (query, key) pairs --
+    with contiguous blocks the last rank does (2P-1)/P^2 of the indexer work.  Zigzag takes a
+    single sequence per call (batch 1)."""
+
+    def __init__(self, group, layout: str = "contiguous"):
+        if layout not in ("contiguous", "zigzag"):
+            raise ValueError(f"unknown layout {layout!r}")
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
+        self.layout = layout
+
+    def segments(self, L_local: int):
+        """[(local_start, length, absolute_position_of_first_token)] of this rank's tokens."""
+        if self.layout == "contiguous":
+            return [(0, L_local, self.rank * L_local)]
+        if L_local % 2:
+            raise ValueError("zigzag sharding needs an even number of local tokens")
+        S = L_local // 2
+        return [(0, S, self.rank * S), (S, S, (2 * self.world - 1 - self.rank) * S)]
+
+    def positions(self, L_local: int, device) -> torch.Tensor:
+        return torch.cat([torch.arange(p0, p0 + n, device=device) for _, n, p0 in self.segments(L_local)])
 
     def start(self, L_local: int) -> int:
-        return self.rank * L_local
+        return self.segments(L_local)[0][2]
 
-    def gather(self, t):
-        return gather_sequence(t, self.group, self.world)
+    def gather(self, t: torch.Tensor) -> torch.Tensor:
+        """All-gather every rank's [B, L_local, ...] tokens into [B, L_total, ...] in sequence order."""
+        g = gather_sequence(t, self.group, self.world)
+        if self.layout == "contiguous":
+            return g
+        B, Ll = t.shape[0], t.shape[1]
+        S = Ll // 2
+        rest = tuple(t.shape[2:])
+        blocks = g.view((B, self.world, 2, S) + rest)
+        first = blocks[:, :, 0].reshape((B, self.world * S) + rest)            # segments 0..P-1
+        second = blocks[:, :, 1].flip(1).reshape((B, self.world * S) + rest)   # segments P..2P-1
+        return torch.cat([first, second], dim=1)
 
     def allreduce(self, t):
         return allreduce_sum(t, self.group)
 
 
-def enable_query_sharding(layer, group=None):
+def zigzag_slice(x: torch.Tensor, world: int, rank: int) -> torch.Tensor:
+    """This rank's tokens of a full [B, L, ...] sequence under the zigzag layout."""
+    L = x.shape[1]
+    if L % (2 * world):
+        raise ValueError(f"sequence length {L} does not split into {2 * world} segments")
+    S = L // (2 * world)
+    a, b = rank, 2 * world - 1 - rank
+    return torch.cat([x[:, a * S:(a + 1) * S], x[:, b * S:(b + 1) * S]], dim=1)
+
+
+def enable_query_sharding(layer, group=None, layout: str = "contiguous"):
     """Make ``layer`` (a GatedSparseAttention) run query-sharded over ``group``: its input is
-    this rank's block of tokens and its output the same block."""
-    layer.query_shards = QueryShards(group if group is not None else dist.group.WORLD)
+    this rank's tokens (a contiguous block, or for ``layout="zigzag"`` the two segments given by
+    :func:`zigzag_slice`) and its output the same tokens."""
+    layer.query_shards = QueryShards(group if group is not None else dist.group.WORLD, layout)
     return layer

@@ -24,12 +24,12 @@ def _port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, layout, q):
     import sys
     sys.path.insert(0, str(ROOT / "gated-sparse-attention_b200"))
     import torch.distributed as dist
     from gsa_b200 import GSAConfig, GatedSparseAttention
-    from gsa_b200.sharded import enable_query_sharding, gather_sequence
+    from gsa_b200.sharded import enable_query_sharding, zigzag_slice
 
     try:
         os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -45,10 +45,11 @@ def _worker(rank, world, port, q):
         x = torch.randn(1, L, cfg.d_model, generator=gen).to(torch.bfloat16).cuda()
         with torch.no_grad():
             ref = m(x)[0] if rank == 0 else None
-            enable_query_sharding(m, dist.group.WORLD)
+            enable_query_sharding(m, dist.group.WORLD, layout)
             Lr = L // world
-            out = m(x[:, rank * Lr:(rank + 1) * Lr].contiguous())[0]
-            full = gather_sequence(out, dist.group.WORLD, world)
+            x_local = zigzag_slice(x, world, rank) if layout == "zigzag" else x[:, rank * Lr:(rank + 1) * Lr]
+            out = m(x_local.contiguous())[0]
+            full = m.query_shards.gather(out)
         torch.cuda.synchronize()
         if rank == 0:
             err = float((full.double() - ref.double()).norm() / ref.double().norm())
@@ -59,13 +60,14 @@ def _worker(rank, world, port, q):
         q.put(("error", repr(e)))
 
 
-def test_two_gpu_query_sharding_matches_single_gpu():
+@pytest.mark.parametrize("layout", ["contiguous", "zigzag"])
+def test_two_gpu_query_sharding_matches_single_gpu(layout):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, layout, q)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:

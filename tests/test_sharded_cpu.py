@@ -37,18 +37,20 @@ def _sharded_oracle_layer(W, cfg, x_local, sp):
     import gsa_oracle as O
 
     B, Lr, _ = x_local.shape
-    start = sp.start(Lr)
+    segs = sp.segments(Lr)
     oc = O.OracleConfig.from_config(cfg)
-    pos = torch.arange(start, start + Lr).unsqueeze(0).expand(B, -1)
+    pos = sp.positions(Lr, "cpu").unsqueeze(0).expand(B, -1)
     cos, sin = O.rope_cache(cfg.d_head, cfg.max_position_embeddings, cfg.rope_base, cfg.rope_scaling)
     q, k, v = O.project(W, oc, x_local, pos, cos, sin)
     q_idx = F.linear(x_local, W["indexer.q_proj.weight"]).view(B, Lr, cfg.n_indexer_heads, cfg.d_indexer)
     k_idx = F.linear(x_local, W["indexer.k_proj.weight"])
     wts = torch.sigmoid(F.linear(x_local, W["indexer.weight_proj.weight"], W["indexer.weight_proj.bias"]))
-    # exchange: keys of every rank, in rank order
+    # exchange: keys of every rank, in sequence order
     k_all, v_all, kI_all = sp.gather(k), sp.gather(v), sp.gather(k_idx)
     L = kI_all.shape[1]
-    scores = O.indexer_scores_from_proj(q_idx, kI_all, wts, W["indexer.bias"], "sigmoid", q_offset=start)
+    scores = torch.cat([O.indexer_scores_from_proj(q_idx[:, l0:l0 + n], kI_all, wts[:, l0:l0 + n],
+                                                   W["indexer.bias"], "sigmoid", q_offset=p0)
+                        for l0, n, p0 in segs], dim=1)
     var, valid = O.row_variance(scores)
     total = sp.allreduce(torch.tensor([float(var.double().sum()), float(var.numel())], dtype=torch.float64))
     mean = torch.tensor(float(total[0]) / float(total[1]), dtype=var.dtype)
@@ -61,23 +63,28 @@ def _sharded_oracle_layer(W, cfg, x_local, sp):
     return F.linear(gated.reshape(B, Lr, -1), W["o_proj.weight"]), kv
 
 
-def _worker_equivalence(rank, world, port, q):
+def _worker_equivalence(rank, world, port, layout, q):
     import sys
     for p in (ROOT / "gated-sparse-attention_b200", ROOT / "oracle", ROOT / "tests"):
         sys.path.insert(0, str(p))
     torch.set_num_threads(1)
-    from gsa_b200.sharded import QueryShards, shard_bounds
+    from gsa_b200.sharded import QueryShards, shard_bounds, zigzag_slice
     import gsa_oracle as O
 
     try:
         _init(rank, world, port)
         _, meta = load_golden("tiny_fp32_b2_l192")
         cfg, m, x = golden_inputs(meta)
+        x = x[:1]  # one sequence (the zigzag layout takes one per call)
         W = dict(m.state_dict())
         L = x.shape[1]
-        s0, s1 = shard_bounds(L, world, rank)
-        sp = QueryShards(dist.group.WORLD)
-        out_local, kv_local = _sharded_oracle_layer(W, cfg, x[:, s0:s1].contiguous(), sp)
+        sp = QueryShards(dist.group.WORLD, layout)
+        if layout == "zigzag":
+            x_local = zigzag_slice(x, world, rank)
+        else:
+            s0, s1 = shard_bounds(L, world, rank)
+            x_local = x[:, s0:s1]
+        out_local, kv_local = _sharded_oracle_layer(W, cfg, x_local.contiguous(), sp)
         out_full = sp.gather(out_local)
         kv_full = sp.gather(kv_local.contiguous())
         if rank == 0:
@@ -91,11 +98,12 @@ def _worker_equivalence(rank, world, port, q):
         q.put(("error", repr(e), -1))
 
 
-def test_query_sharded_layer_matches_unsharded():
+@pytest.mark.parametrize("layout", ["contiguous", "zigzag"])
+def test_query_sharded_layer_matches_unsharded(layout):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker_equivalence, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker_equivalence, args=(r, 2, port, layout, q)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
@@ -140,7 +148,11 @@ def test_failed_rank_surfaces_as_collective_error():
 
 
 def test_shard_bounds():
-    from gsa_b200.sharded import shard_bounds
+    from gsa_b200.sharded import shard_bounds, zigzag_slice
+
+    x = torch.arange(16).view(1, 16)
+    assert zigzag_slice(x, 2, 0).tolist() == [[0, 1, 2, 3, 12, 13, 14, 15]]
+    assert zigzag_slice(x, 2, 1).tolist() == [[4, 5, 6, 7, 8, 9, 10, 11]]
 
     assert shard_bounds(131072, 8, 7) == (114688, 131072)
     assert shard_bounds(10, 2, 0) == (0, 5)
