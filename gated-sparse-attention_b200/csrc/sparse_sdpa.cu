@@ -6,9 +6,11 @@
 // [Hk, D] slice of K (and of V): 2 KiB each at 8 x 128 bf16.  The kernel is HBM-bound on
 // those gathers, so it is built around moving whole key rows:
 //
-//   * one producer warp issues 1-D bulk copies (cp.async.bulk, TMA engine) of the selected keys
+//   * producer warps issue 1-D bulk copies (cp.async.bulk, TMA engine) of the selected keys
 //     into a shared-memory ring of stages (16 keys per stage), completing on the stage's
-//     mbarrier.  With K and V interleaved per key in HBM ([.., Lkv, 2, Hk, D], the layer's
+//     mbarrier; three groups of two warps take the stages round-robin, each warp issuing half a
+//     stage (a single warp's serial per-lane issue was the limit: 1 -> 2 -> 6 warps took the
+//     gather from 7.8 to 12.5 TB/s at 128K tokens, most of it served by L2).  With K and V interleaved per key in HBM ([.., Lkv, 2, Hk, D], the layer's
 //     layout) a key is ONE contiguous 4 KiB copy: the copy count, not the byte count, is what
 //     limits this engine for 2 KiB rows.  A stage slot is [K row | V row | 16 B pad]; the pad
 //     makes the ldmatrix reads of 8 consecutive keys conflict free;
@@ -24,7 +26,7 @@
 namespace gsa {
 
 constexpr int kKeysPerStage = 16;
-constexpr int kMaxProducers = 3;
+constexpr int kMaxGroups = 3;  // producer groups of two warps
 constexpr int kMaxRowBytes = 16 * 256 * 2;
 __device__ __align__(128) uint8_t g_zero_row[2 * kMaxRowBytes];
 
@@ -66,7 +68,7 @@ __device__ __forceinline__ int row_count(const SdpaArgs& a, int64_t row) {
 }
 
 template <int D, int NREP>
-__global__ void __launch_bounds__(19 * 32) sdpa_tc_kernel(SdpaArgs a) {
+__global__ void __launch_bounds__(22 * 32) sdpa_tc_kernel(SdpaArgs a) {
   static_assert(D % 16 == 0 && NREP >= 1 && NREP <= 8, "tile shape");
   extern __shared__ __align__(128) uint8_t smem[];
   const int Hk = a.Hk;
@@ -83,7 +85,7 @@ __global__ void __launch_bounds__(19 * 32) sdpa_tc_kernel(SdpaArgs a) {
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < nst; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], 2);  // the two producer warps of the stage's group each arrive once
       mbar_init(&empty[s], (uint32_t)Hk);
     }
     fence_barrier_init();
@@ -92,13 +94,15 @@ __global__ void __launch_bounds__(19 * 32) sdpa_tc_kernel(SdpaArgs a) {
 
   if (warp >= Hk) {
     // ---------------------------- producer warps ----------------------------
-    // a.nprod warps issue stages round-robin: one warp's per-lane bulk-copy issue is the limit
-    // of a single producer.  nprod <= nstages keeps the parity waits unambiguous: before a
-    // producer waits on a stage's empty barrier, its own previous wait (nprod iterations
+    // a.nprod / 2 producer groups take stages round-robin; the two warps of a group each issue
+    // half of a stage's copies.  The bulk-copy issue of one warp (one lane per copy, serially)
+    // is what limits a single producer.  Groups <= nstages keeps the parity waits unambiguous:
+    // before a group waits on a stage's empty barrier, its own previous wait (groups iterations
     // earlier) guarantees the releases up to 2 * nstages iterations back, so the barrier is at
     // most one phase behind the phase it waits for.
-    const int kProducers = a.nprod;
+    const int groups = a.nprod / 2;
     const int pw = warp - Hk;
+    const int grp = pw >> 1, half = pw & 1;
     uint32_t it = 0;
     bool ok = true;
     for (int64_t row = blockIdx.x; row < R && ok; row += gridDim.x) {
@@ -110,13 +114,14 @@ __global__ void __launch_bounds__(19 * 32) sdpa_tc_kernel(SdpaArgs a) {
       const uint8_t* vbase = reinterpret_cast<const uint8_t*>(a.v) + b * a.Lkv * kv_row;
       const int nkb = (cnt + kKeysPerStage - 1) / kKeysPerStage;
       for (int kb = 0; kb < nkb; ++kb, ++it) {
-        if ((int)(it % kProducers) != pw) continue;
+        if ((int)(it % groups) != grp) continue;
         const int s = it % nst;
         const uint32_t ph = (it / nst) & 1u;
         if (!mbar_wait(&empty[s], ph ^ 1u, a.err)) { ok = false; break; }
-        if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(2 * kKeysPerStage * row_bytes));
+        if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(kKeysPerStage * row_bytes));
         __syncwarp();
-        const int slot = lane & 15;
+        // this warp's 8 slots of the stage; with separate K and V, lanes 8-15 copy the V rows
+        const int slot = half * 8 + (lane & 7);
         const int key = kb * kKeysPerStage + slot;
         int64_t j = -1;
         if (key < cnt) {
@@ -129,10 +134,10 @@ __global__ void __launch_bounds__(19 * 32) sdpa_tc_kernel(SdpaArgs a) {
         uint8_t* dst = stages + s * stage_bytes + slot * rs;
         if (a.interleaved) {
           // one copy per key: K row and V row are adjacent
-          if (lane < 16) bulk_g2s(dst, j >= 0 ? kbase + j * kv_row : g_zero_row, (uint32_t)(2 * row_bytes), &full[s]);
-        } else if (lane < 16) {
+          if (lane < 8) bulk_g2s(dst, j >= 0 ? kbase + j * kv_row : g_zero_row, (uint32_t)(2 * row_bytes), &full[s]);
+        } else if (lane < 8) {
           bulk_g2s(dst, j >= 0 ? kbase + j * kv_row : g_zero_row, (uint32_t)row_bytes, &full[s]);
-        } else {
+        } else if (lane < 16) {
           bulk_g2s(dst + row_bytes, j >= 0 ? vbase + j * kv_row : g_zero_row, (uint32_t)row_bytes, &full[s]);
         }
       }
@@ -140,7 +145,7 @@ __global__ void __launch_bounds__(19 * 32) sdpa_tc_kernel(SdpaArgs a) {
     // drain: every copy this warp issued must land before the CTA may exit
     const uint32_t first = it > (uint32_t)nst ? it - (uint32_t)nst : 0u;
     for (uint32_t i = first; i < it; ++i)
-      if ((int)(i % kProducers) == pw) mbar_wait(&full[i % nst], (i / nst) & 1u, a.err);
+      if ((int)(i % groups) == grp) mbar_wait(&full[i % nst], (i / nst) & 1u, a.err);
     return;
   }
 
@@ -336,7 +341,7 @@ static int launch_tc(SdpaArgs a, int num_sms, cudaStream_t stream) {
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return GSA_ERR_LAUNCH;
   int per_sm = 0;
-  a.nprod = nst < kMaxProducers ? nst : kMaxProducers;  // nprod <= nstages (see the producer loop)
+  a.nprod = 2 * (nst < kMaxGroups ? nst : kMaxGroups);  // groups <= nstages (see the producer loop)
   const int threads = (a.Hk + a.nprod) * 32;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem) != cudaSuccess || per_sm < 1)
     return GSA_ERR_LAUNCH;
