@@ -134,6 +134,21 @@ __device__ __forceinline__ float tanh_fast(float x) {
   return y;
 }
 
+// Packed pairs of fp32 for the f32x2 FMA (two lanes of arithmetic per instruction).
+__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack2(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
 template <int HI>
 __global__ void __launch_bounds__(kThreads, 1)
     indexer_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ, Params p) {
@@ -248,9 +263,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int ew = warp - 2;
     const int quarter = warp & 3;   // TMEM lane quarter this warp may access
     const int sub = ew >> 2;        // which quarter of the block's tokens
-    float hb[HI];
+    uint64_t hb2[HI / 2];
 #pragma unroll
-    for (int j = 0; j < HI; ++j) hb[j] = 0.5f * p.bias[j];
+    for (int j = 0; j < HI / 2; ++j) hb2[j] = pack2(0.5f * p.bias[2 * j], 0.5f * p.bias[2 * j + 1]);
+    const uint64_t hs2 = pack2(p.half_scale, p.half_scale);
     float s1[TOK_Q], s2[TOK_Q];
 #pragma unroll
     for (int t = 0; t < TOK_Q; ++t) s1[t] = s2[t] = 0.f;
@@ -282,19 +298,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int tt = 0; tt < TOK_PER_LD; ++tt) {
           const int tl = c * TOK_PER_LD + tt;       // token within this warp's quarter
           const int ti = sub * TOK_Q + tl;          // token within the block
+          // z = (scale * acc + b_j) / 2 and y = sum_j (w_j / 2) tanh(z), two heads per f32x2 FMA
           float th[HI];
 #pragma unroll
-          for (int j = 0; j < HI; ++j) th[j] = tanh_fast(fmaf(__uint_as_float(r[tt * HI + j]), p.half_scale, hb[j]));
+          for (int j = 0; j < HI / 2; ++j) {
+            const uint64_t z2 = ffma2(pack2(__uint_as_float(r[tt * HI + 2 * j]), __uint_as_float(r[tt * HI + 2 * j + 1])),
+                                      hs2, hb2[j]);
+            float z0, z1;
+            unpack2(z2, z0, z1);
+            th[2 * j] = tanh_fast(z0);
+            th[2 * j + 1] = tanh_fast(z1);
+          }
           const float4* w4 = reinterpret_cast<const float4*>(w_s + ti * HI);
-          float y = 0.f;
+          uint64_t y2 = pack2(0.f, 0.f);
 #pragma unroll
           for (int j4 = 0; j4 < HI / 4; ++j4) {
             const float4 w = w4[j4];
-            y = fmaf(w.x, th[4 * j4 + 0], y);
-            y = fmaf(w.y, th[4 * j4 + 1], y);
-            y = fmaf(w.z, th[4 * j4 + 2], y);
-            y = fmaf(w.w, th[4 * j4 + 3], y);
+            y2 = ffma2(pack2(w.x, w.y), pack2(th[4 * j4 + 0], th[4 * j4 + 1]), y2);
+            y2 = ffma2(pack2(w.z, w.w), pack2(th[4 * j4 + 2], th[4 * j4 + 3]), y2);
           }
+          float ya, yb;
+          unpack2(y2, ya, yb);
+          const float y = ya + yb;
           const bool ok = tile_full || (key_ok && ti < ntok && (!p.causal || key <= pos0 + ti));
           if (ok) {
             p.scores[(int64_t)(tok0 + ti) * p.ld + key] = c_s[ti] + y;
