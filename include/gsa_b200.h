@@ -213,6 +213,31 @@ int gsa_indexer_select(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, i
                        int32_t* cand_count, double* row_stats, int64_t chunk_rows,
                        void* workspace, int64_t workspace_bytes, gsa_stream_t stream);
 
+/*
+ * gsa_indexer_select without a workspace argument: it allocates no device memory.  No
+ * counterpart in the reference (whose indexer materialises the score matrix with torch).
+ *
+ * For callers that cannot provide or allocate scratch at call time: serving runtimes that
+ * reserve all device memory for their own pools up front, and host code with no device
+ * allocator of its own.  The chunk scores live in a buffer of GSA_STATIC_SCRATCH_BYTES that
+ * the library holds per device, so a chunk is GSA_STATIC_SCRATCH_BYTES / (4 * round4(Lkv))
+ * query rows and Lkv may be at most 16,777,216; a longer key length returns
+ * GSA_ERR_WORKSPACE.  row_stats (if given) is zeroed by the call itself, on ``stream``.
+ *
+ * The first call on each device performs set-up (it looks up the buffer's device address with
+ * that device current); make that first call before any stream capture.  All calls on a device
+ * share the buffer: calls that overlap in time on one device (two streams or two host threads)
+ * race on it, so the caller serialises them.
+ */
+#define GSA_STATIC_SCRATCH_BYTES (64LL << 20)
+int gsa_indexer_select_static(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq,
+                              int64_t Lkv, int64_t q_pos0, int causal, const void* qI,
+                              int64_t qi_ld, int64_t qi_bstride, const void* kI, int64_t ki_ld,
+                              int64_t ki_bstride, const float* w, const float* bias, float scale,
+                              const float* shift, int32_t k_eff, int32_t* cand_idx,
+                              float* cand_score, int32_t* cand_count, double* row_stats,
+                              gsa_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
