@@ -67,8 +67,8 @@ __device__ __forceinline__ int row_count(const SdpaArgs& a, int64_t row) {
   return c;
 }
 
-template <int D, int NREP>
-__global__ void __launch_bounds__(22 * 32) sdpa_tc_kernel(SdpaArgs a) {
+template <int D, int NREP, int MAXW>
+__global__ void __launch_bounds__(MAXW * 32) sdpa_tc_kernel(SdpaArgs a) {
   static_assert(D % 16 == 0 && NREP >= 1 && NREP <= 8, "tile shape");
   extern __shared__ __align__(128) uint8_t smem[];
   const int Hk = a.Hk;
@@ -181,15 +181,32 @@ __global__ void __launch_bounds__(22 * 32) sdpa_tc_kernel(SdpaArgs a) {
       if (!mbar_wait(&full[s], ph, a.err)) { ok = false; break; }
       const uint8_t* Ks = stages + s * stage_bytes;
       const uint8_t* Vs = Ks + row_bytes;
-      float c[4] = {0.f, 0.f, 0.f, 0.f};
+      // Stage the group's K and V tiles in registers and hand the slot back at once: the copy
+      // ring then keeps (almost) all of its stages in flight while this warp computes.
+      uint32_t kf[D / 16][4], vf[D / 16][4];
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
         const int key = r8 + ((mi & 1) ? 8 : 0);
         const int dim = kk * 16 + ((mi & 2) ? 8 : 0);
-        uint32_t a0, a1, a2, a3;
-        ldsm_x4(smem_u32(Ks + key * rs + (g * D + dim) * 2), a0, a1, a2, a3);
-        mma_bf16(c, a0, a1, a2, a3, qf[kk][0], qf[kk][1]);
+        ldsm_x4(smem_u32(Ks + key * rs + (g * D + dim) * 2), kf[kk][0], kf[kk][1], kf[kk][2], kf[kk][3]);
       }
+#pragma unroll
+      for (int mt = 0; mt < D / 16; ++mt) {
+        const int key = r8 + ((mi & 2) ? 8 : 0);
+        const int dim = mt * 16 + ((mi & 1) ? 8 : 0);
+        ldsm_x4_t(smem_u32(Vs + key * rs + (g * D + dim) * 2), vf[mt][0], vf[mt][1], vf[mt][2], vf[mt][3]);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      // S^T = K Q^T with two independent accumulation chains
+      float c[4] = {0.f, 0.f, 0.f, 0.f}, c2[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int kk = 0; kk < D / 16; kk += 2) {
+        mma_bf16(c, kf[kk][0], kf[kk][1], kf[kk][2], kf[kk][3], qf[kk][0], qf[kk][1]);
+        mma_bf16(c2, kf[kk + 1][0], kf[kk + 1][1], kf[kk + 1][2], kf[kk + 1][3], qf[kk + 1][0], qf[kk + 1][1]);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) c[e] += c2[e];
       const int valid = cnt - kb * kKeysPerStage;
       const bool v0 = grp < valid, v1 = grp + 8 < valid;
       float x0 = v0 ? c[0] * a.scale_log2 : -INFINITY;
@@ -220,15 +237,7 @@ __global__ void __launch_bounds__(22 * 32) sdpa_tc_kernel(SdpaArgs a) {
       const uint32_t b0 = movm_t(pack_bf16(p0, p1));
       const uint32_t b1 = movm_t(pack_bf16(p2, p3));
 #pragma unroll
-      for (int mt = 0; mt < D / 16; ++mt) {
-        const int key = r8 + ((mi & 2) ? 8 : 0);
-        const int dim = mt * 16 + ((mi & 1) ? 8 : 0);
-        uint32_t a0, a1, a2, a3;
-        ldsm_x4_t(smem_u32(Vs + key * rs + (g * D + dim) * 2), a0, a1, a2, a3);
-        mma_bf16(o[mt], a0, a1, a2, a3, b0, b1);
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
+      for (int mt = 0; mt < D / 16; ++mt) mma_bf16(o[mt], vf[mt][0], vf[mt][1], vf[mt][2], vf[mt][3], b0, b1);
     }
     if (!ok) return;
 #pragma unroll
@@ -327,8 +336,8 @@ struct SdpaCfg {
   size_t smem;
 };
 
-template <int D, int NREP>
-static int launch_tc(SdpaArgs a, int num_sms, cudaStream_t stream) {
+template <int D, int NREP, int MAXW>
+static int launch_tc_w(SdpaArgs a, int num_sms, cudaStream_t stream) {
   const int row_bytes = a.Hk * D * 2;
   const int stage_bytes = kKeysPerStage * (2 * row_bytes + 16);
   const int max_smem = 227 * 1024;
@@ -337,12 +346,13 @@ static int launch_tc(SdpaArgs a, int num_sms, cudaStream_t stream) {
   if (nst < 2) return GSA_ERR_UNSUPPORTED;
   a.nstages = nst;
   const size_t smem = 256 + (size_t)nst * stage_bytes;
-  auto kern = sdpa_tc_kernel<D, NREP>;
+  auto kern = sdpa_tc_kernel<D, NREP, MAXW>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return GSA_ERR_LAUNCH;
   int per_sm = 0;
   a.nprod = 2 * (nst < kMaxGroups ? nst : kMaxGroups);  // groups <= nstages (see the producer loop)
   const int threads = (a.Hk + a.nprod) * 32;
+  if (threads > MAXW * 32) return GSA_ERR_UNSUPPORTED;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem) != cudaSuccess || per_sm < 1)
     return GSA_ERR_LAUNCH;
   const int64_t R = a.B * a.Lq;
@@ -350,6 +360,14 @@ static int launch_tc(SdpaArgs a, int num_sms, cudaStream_t stream) {
   if (grid > R) grid = R;
   kern<<<(unsigned)grid, threads, smem, stream>>>(a);
   return cudaGetLastError() == cudaSuccess ? GSA_OK : GSA_ERR_LAUNCH;
+}
+
+// The register-staged consumers want more than the 93 registers a 22-warp block leaves, so
+// groups of up to 8 KV heads (8 consumer + 6 producer warps) get a 14-warp build.
+template <int D, int NREP>
+static int launch_tc(SdpaArgs a, int num_sms, cudaStream_t stream) {
+  if (a.Hk + 2 * kMaxGroups <= 14) return launch_tc_w<D, NREP, 14>(a, num_sms, stream);
+  return launch_tc_w<D, NREP, 22>(a, num_sms, stream);
 }
 
 template <int D>
