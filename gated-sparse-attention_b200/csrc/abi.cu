@@ -165,7 +165,7 @@ int gsa_adaptive_k(int64_t R, int64_t n_cols, int dtype, const gsa_topk_params* 
 int gsa_select_finalize(int64_t R, int32_t k_eff, const int32_t* cand_idx, const float* cand_score,
                         const int32_t* cand_count, const int32_t* k, int32_t* sel_idx, int64_t sel_ld,
                         int32_t* sel_count, uint8_t* sel_mask, gsa_stream_t stream) {
-  if (R < 0 || k_eff < 1 || sel_ld < k_eff) return GSA_ERR_BAD_ARG;
+  if (R < 0 || k_eff < 1 || sel_ld < 1) return GSA_ERR_BAD_ARG;
   if (R == 0) return GSA_OK;
   if (!cand_idx || !cand_score || !cand_count || !k || !sel_idx || !sel_count) return GSA_ERR_BAD_ARG;
   return launch_select_finalize(R, k_eff, cand_idx, cand_score, cand_count, k, sel_idx, sel_ld, sel_count,
@@ -249,6 +249,58 @@ int gsa_indexer_select(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, i
       st = gsa_topk_candidates(n, n, Lkv, q_pos0 + t0, causal, scratch, ld, center,
                                (center && row_stats) ? row_stats + r0 * 3 : nullptr, k_eff,
                                cand_idx + r0 * k_eff, cand_score + r0 * k_eff, cand_count + r0, stream);
+      if (st) return st;
+    }
+  }
+  return GSA_OK;
+}
+
+static int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
+
+int64_t gsa_survivors_workspace_size(int64_t chunk_rows, int64_t n_cols) {
+  if (chunk_rows <= 0 || n_cols <= 0) return 0;
+  return align256(gsa_workspace_size(chunk_rows, n_cols)) + align256(chunk_rows * 4) + 256;
+}
+
+int gsa_indexer_survivors(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int64_t Lkv, int64_t q_pos0,
+                          int causal, const void* qI, int64_t qi_ld, int64_t qi_bstride, const void* kI,
+                          int64_t ki_ld, int64_t ki_bstride, const float* w, const float* bias, float scale,
+                          const float* shift, int32_t k_eff, int32_t cap, int32_t* cand_idx, float* cand_score,
+                          int32_t* cand_count, double* row_stats, int64_t chunk_rows, void* workspace,
+                          int64_t workspace_bytes, gsa_stream_t stream) {
+  if (!dims_ok(dims) || B < 0 || Lq < 0 || Lkv < 0 || chunk_rows <= 0 || k_eff < 1 || cap < k_eff)
+    return GSA_ERR_BAD_ARG;
+  if (B * Lq == 0 || Lkv == 0) return GSA_OK;
+  if (!shift || !row_stats || !cand_idx || !cand_score || !cand_count || !w || !bias || !qI || !kI)
+    return GSA_ERR_BAD_ARG;
+  // sigmoid scores (the threshold statistics are relative to the row centre) and room above
+  // the 1.5 k_eff survivors the threshold aims at
+  if (dims->idx_act != GSA_ACT_SIGMOID || 2 * (int64_t)cap < 3 * (int64_t)k_eff + 2048) return GSA_ERR_UNSUPPORTED;
+  if (!workspace || !aligned(workspace, 256) || workspace_bytes < gsa_survivors_workspace_size(chunk_rows, Lkv))
+    return GSA_ERR_WORKSPACE;
+  DeviceInfo* di;
+  int st = device_info(&di);
+  if (st) return st;
+  const int64_t ld = (Lkv + 3) / 4 * 4;
+  uint8_t* wsb = static_cast<uint8_t*>(workspace);
+  float* scratch = reinterpret_cast<float*>(wsb);
+  int32_t* fail_list = reinterpret_cast<int32_t*>(wsb + align256(gsa_workspace_size(chunk_rows, Lkv)));
+  int32_t* fail_count = fail_list + align256(chunk_rows * 4) / 4;
+  const size_t esz = dtype == GSA_DTYPE_BF16 ? 2 : 4;
+  const int HI = dims->n_idx_heads;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  for (int64_t b = 0; b < B; ++b) {
+    for (int64_t t0 = 0; t0 < Lq; t0 += chunk_rows) {
+      const int64_t n = (Lq - t0) < chunk_rows ? (Lq - t0) : chunk_rows;
+      const int64_t r0 = b * Lq + t0;
+      const void* q_ptr = static_cast<const char*>(qI) + (b * qi_bstride + t0 * qi_ld) * (int64_t)esz;
+      const void* k_ptr = static_cast<const char*>(kI) + (b * ki_bstride) * (int64_t)esz;
+      st = gsa_indexer_scores(dims, dtype, 1, n, Lkv, q_pos0 + t0, causal, 0, q_ptr, qi_ld, 0, k_ptr, ki_ld, 0,
+                              w + r0 * HI, bias, scale, shift + r0, scratch, ld, row_stats + r0 * 3, stream);
+      if (st) return st;
+      st = launch_threshold_candidates(n, n, Lkv, q_pos0 + t0, causal, scratch, ld, shift + r0, row_stats + r0 * 3,
+                                       k_eff, cap, cand_idx + r0 * cap, cand_score + r0 * cap, cand_count + r0,
+                                       fail_list, fail_count, di->num_sms, di->err, s);
       if (st) return st;
     }
   }

@@ -424,21 +424,21 @@ struct KeepAbove {
   __device__ bool operator()(float x) const { return x >= tau; }
 };
 
-__global__ void __launch_bounds__(kSelThreads) topk_candidates_kernel(
-    int64_t Lq, int64_t n_cols, int64_t q_pos0, int causal, const float* scores, int64_t ld,
-    const float* row_center, const double* row_stats, int32_t k_eff, int32_t* cand_idx, float* cand_score,
-    int32_t* cand_count) {
+// The k_eff best candidates of row r (one CTA of kSelThreads threads).  topk_dyn: the dynamic
+// shared memory of the bounded path ([kCap] vals, [kCap] cols, flags, tie list).
+__device__ void topk_row(int64_t r, int64_t Lq, int64_t n_cols, int64_t q_pos0, int causal, const float* scores,
+                         int64_t ld, const float* row_center, const double* row_stats, int32_t k_eff,
+                         int64_t out_ld, int32_t* cand_idx, float* cand_score, int32_t* cand_count,
+                         uint8_t* topk_dyn) {
   __shared__ uint32_t hist[kBins];
   __shared__ uint32_t ws[48];
   __shared__ uint32_t sel[4];
-  extern __shared__ __align__(16) uint8_t topk_dyn[];  // bounded path: [kCap] vals, [kCap] cols
-  const int64_t r = blockIdx.x;
   int64_t n = n_cols;
   if (causal) n = min(n_cols, q_pos0 + (r % Lq) + 1);
   if (n < 0) n = 0;
   const float* row = scores + r * ld;
-  int32_t* oidx = cand_idx + r * k_eff;
-  float* osc = cand_score + r * k_eff;
+  int32_t* oidx = cand_idx + r * out_ld;
+  float* osc = cand_score + r * out_ld;
   const uint32_t K = (uint32_t)k_eff;
   RowSrc src{row, n};
   uint32_t cnt = 0;
@@ -513,6 +513,15 @@ __global__ void __launch_bounds__(kSelThreads) topk_candidates_kernel(
   if (threadIdx.x == 0) cand_count[r] = (int32_t)cnt;
 }
 
+__global__ void __launch_bounds__(kSelThreads) topk_candidates_kernel(
+    int64_t Lq, int64_t n_cols, int64_t q_pos0, int causal, const float* scores, int64_t ld,
+    const float* row_center, const double* row_stats, int32_t k_eff, int32_t* cand_idx, float* cand_score,
+    int32_t* cand_count) {
+  extern __shared__ __align__(16) uint8_t topk_dyn[];
+  topk_row(blockIdx.x, Lq, n_cols, q_pos0, causal, scores, ld, row_center, row_stats, k_eff, k_eff, cand_idx,
+           cand_score, cand_count, topk_dyn);
+}
+
 __global__ void __launch_bounds__(kSelThreads) select_finalize_kernel(
     int32_t k_eff, const int32_t* cand_idx, const float* cand_score, const int32_t* cand_count,
     const int32_t* k, int32_t* sel_idx, int64_t sel_ld, int32_t* sel_count, uint8_t* sel_mask, int stage) {
@@ -524,6 +533,7 @@ __global__ void __launch_bounds__(kSelThreads) select_finalize_kernel(
   int32_t c = cand_count[r];
   int32_t kr = k[r];
   if (kr < 0) kr = 0;
+  if (kr > sel_ld) kr = (int32_t)sel_ld;  // a row of sel holds at most sel_ld keys
   if (c < 0) c = 0;
   if (c > k_eff) c = k_eff;
   const float* vals = cand_score + r * k_eff;
@@ -573,6 +583,227 @@ __global__ void __launch_bounds__(kSelThreads) select_finalize_kernel(
     }
   }
   if (threadIdx.x == 0) sel_count[r] = (int32_t)cnt;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Streaming threshold compaction (the layer's candidate pass).  Every score of row r at or above
+// the threshold tau_r -- the row's normal quantile of 1.5 K / n_r from its statistics, the same
+// threshold as the first attempt of topk_row -- is a survivor; rows of n_r <= cap keep every
+// score.  Survivors are written in ascending column order to cand[r, 0..cap).  A row whose
+// survivors are fewer than min(K, n_r) or more than cap goes to fail_list and is selected
+// exactly by topk_fallback_kernel.  Either way the row's candidates hold its K best scores, in
+// ascending column order, which is all the final selection needs.
+//
+// Persistent CTAs: one producer warp streams each row in 16 KiB chunks through a 4-stage
+// shared-memory ring with 1-D bulk copies (the rows are contiguous), continuing across rows,
+// so the scores arrive at HBM rate while 8 consumer warps compact.  A chunk's survivors are
+// compacted into shared memory first and then copied out with consecutive threads writing
+// consecutive positions (scattered per-thread stores cost ~9 sectors per request).  Consumers
+// synchronise on a named barrier that excludes the producer.  All waits are bounded.
+// ---------------------------------------------------------------------------------------------
+constexpr int kCmpConsumers = 256;
+constexpr int kCmpThreads = kCmpConsumers + 32;
+constexpr int kCmpPer = 16;                              // scores per consumer thread per chunk
+constexpr int kCmpChunk = kCmpConsumers * kCmpPer;       // 4096 scores = 16 KiB
+constexpr int kCmpStages = 4;
+constexpr int kCmpSmem = 256 + kCmpStages * kCmpChunk * 4 + kCmpChunk * 8;  // ring + survivor staging
+
+struct CmpArgs {
+  int64_t R, Lq, n_cols, q_pos0;
+  int causal;
+  const float* scores;
+  int64_t ld;
+  const float* center;
+  const double* stats;
+  int32_t K, cap;
+  int32_t* idx;
+  float* score;
+  int32_t* count;
+  int32_t* fail_list;
+  int32_t* fail_count;
+  int* err;
+};
+
+__device__ __forceinline__ int64_t cmp_row_cols(const CmpArgs& a, int64_t r) {
+  int64_t n = a.n_cols;
+  if (a.causal) n = min(a.n_cols, a.q_pos0 + (r % a.Lq) + 1);
+  return n < 0 ? 0 : n;
+}
+
+__device__ __forceinline__ float cmp_threshold(const CmpArgs& a, int64_t r, int64_t n) {
+  if (n <= a.cap) return -INFINITY;
+  const double* st = a.stats + r * 3;
+  if (!(st[2] > 0.0)) return -INFINITY;  // no statistics: overflows cap, selected exactly
+  const double mu_y = st[0] / st[2];
+  const double var = st[1] / st[2] - mu_y * mu_y;
+  const float sd = (float)sqrt(var > 0.0 ? var : 0.0);
+  const float mean = a.center[r] + (float)mu_y;
+  const float pt = 1.5f * (float)a.K / (float)n;
+  return pt >= 1.f ? -INFINITY : mean + sd * 1.41421356f * erfinvf(1.f - 2.f * pt);
+}
+
+__device__ __forceinline__ void cmp_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kCmpConsumers) : "memory"); }
+
+// Exclusive scan over the consumer threads (two scratch buffers alternate, so two barriers).
+__device__ __forceinline__ uint32_t cmp_scan(uint32_t v, uint32_t* ws, uint32_t* total) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  uint32_t x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) ws[wid] = x;
+  cmp_bar();
+  uint32_t off = 0, tot = 0;
+#pragma unroll
+  for (int w = 0; w < kCmpConsumers / 32; ++w) {
+    const uint32_t c = ws[w];
+    if (w < wid) off += c;
+    tot += c;
+  }
+  *total = tot;
+  return off + x - v;
+}
+
+__global__ void __launch_bounds__(kCmpThreads) threshold_compact_kernel(CmpArgs a) {
+  extern __shared__ __align__(128) uint8_t cmp_smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(cmp_smem);
+  uint64_t* empty = full + kCmpStages;
+  uint32_t* wsb = reinterpret_cast<uint32_t*>(empty + kCmpStages);  // 2 x 8 words
+  float* stage = reinterpret_cast<float*>(cmp_smem + 256);
+  int32_t* keep_col = reinterpret_cast<int32_t*>(stage + kCmpStages * kCmpChunk);  // [kCmpChunk]
+  float* keep_val = reinterpret_cast<float*>(keep_col + kCmpChunk);                // [kCmpChunk]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kCmpStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kCmpConsumers / 32);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == kCmpConsumers / 32) {
+    // ------------------------------ producer ------------------------------
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int64_t r = blockIdx.x; r < a.R && ok; r += gridDim.x) {
+        const int64_t n = cmp_row_cols(a, r);
+        const float* row = a.scores + r * a.ld;
+        for (int64_t c0 = 0; c0 < n; c0 += kCmpChunk, ++it) {
+          const int s = it % kCmpStages;
+          if (!mbar_wait(&empty[s], ((it / kCmpStages) & 1u) ^ 1u, a.err)) { ok = false; break; }
+          const int64_t cnt = min((int64_t)kCmpChunk, n - c0);
+          const uint32_t bytes = (uint32_t)((cnt + 3) / 4 * 16);
+          mbar_arrive_expect_tx(&full[s], bytes);
+          bulk_g2s(stage + s * kCmpChunk, row + c0, bytes, &full[s]);
+        }
+      }
+      // every copy issued must land before the CTA exits
+      const uint32_t first = it > (uint32_t)kCmpStages ? it - (uint32_t)kCmpStages : 0u;
+      for (uint32_t i = first; i < it; ++i) mbar_wait(&full[i % kCmpStages], (i / kCmpStages) & 1u, a.err);
+    }
+    return;
+  }
+
+  // ------------------------------ consumers ------------------------------
+  uint32_t it = 0, parity = 0;
+  bool ok = true;
+  for (int64_t r = blockIdx.x; r < a.R; r += gridDim.x) {
+    const int64_t n = cmp_row_cols(a, r);
+    const float tau = cmp_threshold(a, r, n);
+    int32_t* oi = a.idx + r * a.cap;
+    float* os = a.score + r * a.cap;
+    uint32_t base = 0;
+    for (int64_t c0 = 0; c0 < n; c0 += kCmpChunk, ++it) {
+      const int s = it % kCmpStages;
+      // after a failed wait the warp keeps its place in every barrier but stops waiting
+      if (ok && !mbar_wait(&full[s], (it / kCmpStages) & 1u, a.err)) ok = false;
+      const float4* src = reinterpret_cast<const float4*>(stage + s * kCmpChunk + threadIdx.x * kCmpPer);
+      float v[kCmpPer];
+#pragma unroll
+      for (int q = 0; q < kCmpPer / 4; ++q) {
+        const float4 f = src[q];
+        v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      const int64_t i0 = c0 + threadIdx.x * kCmpPer;
+      uint32_t flags = 0;
+#pragma unroll
+      for (int j = 0; j < kCmpPer; ++j)
+        if (i0 + j < n && valid_key(v[j]) && v[j] >= tau) flags |= 1u << j;
+      uint32_t total;
+      uint32_t pos = cmp_scan((uint32_t)__popc(flags), wsb + (parity & 1u) * 8, &total);
+      parity ^= 1u;
+#pragma unroll
+      for (int j = 0; j < kCmpPer; ++j) {
+        if (flags & (1u << j)) {
+          keep_col[pos] = (int32_t)(i0 + j);
+          keep_val[pos] = v[j];
+          ++pos;
+        }
+      }
+      cmp_bar();
+      // the chunk's survivors go to positions base .. base + total of the row (up to cap)
+      const uint32_t lim = base >= (uint32_t)a.cap ? 0u : min(total, (uint32_t)a.cap - base);
+      if (ok)
+        for (uint32_t i = threadIdx.x; i < lim; i += kCmpConsumers) {
+          oi[base + i] = keep_col[i];
+          os[base + i] = keep_val[i];
+        }
+      base += total;
+    }
+    if (threadIdx.x == 0) {
+      const int64_t need = min((int64_t)a.K, n);
+      if ((int64_t)base > a.cap || (int64_t)base < need) a.fail_list[atomicAdd(a.fail_count, 1)] = (int32_t)r;
+      a.count[r] = (int32_t)min(base, (uint32_t)a.cap);
+    }
+  }
+}
+
+// Exact selection (topk_row) of the rows the compaction could not settle.
+__global__ void __launch_bounds__(kSelThreads) topk_fallback_kernel(CmpArgs a) {
+  extern __shared__ __align__(16) uint8_t topk_dyn[];
+  const int32_t nf = *a.fail_count;
+  for (int32_t i = blockIdx.x; i < nf; i += gridDim.x) {
+    const int64_t r = a.fail_list[i];
+    topk_row(r, a.Lq, a.n_cols, a.q_pos0, a.causal, a.scores, a.ld, a.center, a.stats, a.K, a.cap, a.idx,
+             a.score, a.count, topk_dyn);
+    __syncthreads();
+  }
+}
+
+int launch_threshold_candidates(int64_t R, int64_t Lq, int64_t n_cols, int64_t q_pos0, int causal,
+                                const float* scores, int64_t ld, const float* center, const double* stats,
+                                int32_t K, int32_t cap, int32_t* cand_idx, float* cand_score, int32_t* cand_count,
+                                int32_t* fail_list, int32_t* fail_count, int num_sms, int* err,
+                                cudaStream_t stream) {
+  if (R == 0) return GSA_OK;
+  if (R > 0x7fffffffLL || ld % 4 != 0 || (reinterpret_cast<uintptr_t>(scores) % 16) != 0) return GSA_ERR_BAD_ARG;
+  CmpArgs a{R, Lq, n_cols, q_pos0, causal, scores, ld, center, stats, K, cap, cand_idx, cand_score, cand_count,
+            fail_list, fail_count, err};
+  if (cudaMemsetAsync(fail_count, 0, sizeof(int32_t), stream) != cudaSuccess) return GSA_ERR_CUDA;
+  if (cudaFuncSetAttribute(threshold_compact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kCmpSmem) !=
+      cudaSuccess)
+    return GSA_ERR_LAUNCH;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, threshold_compact_kernel, kCmpThreads, kCmpSmem) !=
+          cudaSuccess ||
+      per_sm < 1)
+    return GSA_ERR_LAUNCH;
+  int64_t grid = (int64_t)num_sms * per_sm;
+  if (grid > R) grid = R;
+  threshold_compact_kernel<<<(unsigned)grid, kCmpThreads, kCmpSmem, stream>>>(a);
+  if (cudaGetLastError() != cudaSuccess) return GSA_ERR_LAUNCH;
+  const size_t dyn = 2 * kCap * sizeof(float) + kCap + kRankCap * sizeof(uint32_t);
+  if (cudaFuncSetAttribute(topk_fallback_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn) !=
+      cudaSuccess)
+    return GSA_ERR_LAUNCH;
+  topk_fallback_kernel<<<(unsigned)num_sms, kSelThreads, dyn, stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? GSA_OK : GSA_ERR_LAUNCH;
 }
 
 // Row statistics of a materialised score matrix: sum, sum of squares, finite count (fp64).

@@ -74,10 +74,14 @@ SIGNATURES = {
     "gsa_indexer_select": [P, INT, I64, I64, I64, I64, INT, P, I64, I64, P, I64, I64, P, P, F32, P,
                            I32, P, P, P, P, I64, P, I64, P],
     "gsa_apply_gate": [INT, INT, I64, P, P, P, P, P],
+    "gsa_survivors_workspace_size": [I64, I64],
+    "gsa_indexer_survivors": [P, INT, I64, I64, I64, I64, INT, P, I64, I64, P, I64, I64, P, P, F32, P,
+                              I32, I32, P, P, P, P, I64, P, I64, P],
     "gsa_indexer_select_static": [P, INT, I64, I64, I64, I64, INT, P, I64, I64, P, I64, I64, P, P, F32,
                                   P, I32, P, P, P, P, P],
 }
-_RESTYPES = {"gsa_version": C.c_char_p, "gsa_workspace_size": C.c_int64}
+_RESTYPES = {"gsa_version": C.c_char_p, "gsa_workspace_size": C.c_int64,
+             "gsa_survivors_workspace_size": C.c_int64}
 
 _lib = None
 _lock = threading.Lock()

@@ -353,6 +353,10 @@ class GatedSparseAttention(nn.Module):
         self.d_head = config.d_head
         self.n_rep = self.n_heads // self.n_kv_heads
         self.scale = 1.0 / math.sqrt(self.d_head)
+        # candidate pass: "auto" takes the threshold-survivor pass where it applies (sigmoid
+        # indexer), "exact" always selects each row's k_eff best first; the keys finally
+        # selected are the same
+        self.selection_path = "auto"
 
         self.q_proj = nn.Linear(self.d_model, self.n_heads * self.d_head, bias=False)
         self.k_proj = nn.Linear(self.d_model, self.n_kv_heads * self.d_head, bias=False)
@@ -531,23 +535,29 @@ class GatedSparseAttention(nn.Module):
 
         n_cols = kI_all.shape[1]
         k_eff = min(cfg.k_max, n_cols) if cfg.use_adaptive_k else min(cfg.k_base, n_cols)
+        # the candidates of a row: its k_eff best keys (exact) or its threshold survivors, a
+        # superset in the same ascending order; the final selection takes k_t from either
+        survivors = (self.selection_path == "auto" and not output_attentions
+                     and ops.survivors_eligible(dims, k_eff, True))
+        select_fn = ops.indexer_survivors if survivors else ops.indexer_select
+        cand_ld = ops.SURVIVOR_CAP if survivors else k_eff
         if len(segs) == 1:
-            cand_idx, cand_score, cand_count, stats = ops.indexer_select(
+            cand_idx, cand_score, cand_count, stats = select_fn(
                 dims, qI, kI_all, w, self.indexer.bias, self.indexer.scale, shift, k_eff,
                 q_pos0=q_pos0, causal=True)
         else:
             # one indexer pass per query segment, each with its own causal offset
             R = B * L
-            cand_idx = torch.zeros(R, k_eff, device=x.device, dtype=torch.int32)
-            cand_score = torch.empty(R, k_eff, device=x.device, dtype=torch.float32)
+            cand_idx = torch.zeros(R, cand_ld, device=x.device, dtype=torch.int32)
+            cand_score = torch.empty(R, cand_ld, device=x.device, dtype=torch.float32)
             cand_count = torch.empty(R, device=x.device, dtype=torch.int32)
             stats = torch.zeros(R, 3, device=x.device, dtype=torch.float64)
             wv = w.view(L, HI)
             for l0, n, p0 in segs:
-                ops.indexer_select(dims, qI[:, l0:l0 + n], kI_all, wv[l0:l0 + n], self.indexer.bias,
-                                   self.indexer.scale, shift[l0:l0 + n], k_eff, q_pos0=p0, causal=True,
-                                   row_stats=stats[l0:l0 + n],
-                                   out=(cand_idx[l0:l0 + n], cand_score[l0:l0 + n], cand_count[l0:l0 + n]))
+                select_fn(dims, qI[:, l0:l0 + n], kI_all, wv[l0:l0 + n], self.indexer.bias,
+                          self.indexer.scale, shift[l0:l0 + n], k_eff, q_pos0=p0, causal=True,
+                          row_stats=stats[l0:l0 + n],
+                          out=(cand_idx[l0:l0 + n], cand_score[l0:l0 + n], cand_count[l0:l0 + n]))
         mark("indexer_topk")
         if cfg.use_adaptive_k:
             var, total = ops.row_variance(stats, n_cols, dt, shift)
@@ -557,7 +567,8 @@ class GatedSparseAttention(nn.Module):
             var = total = None
         kt = ops.adaptive_k(stats, var, total, n_cols, dt, cfg.k_base, cfg.k_min, cfg.k_max,
                             cfg.use_adaptive_k, cfg.adaptive_k_temperature)
-        sel, cnt, mask = ops.select_finalize(cand_idx, cand_score, cand_count, kt, want_mask=output_attentions)
+        sel, cnt, mask = ops.select_finalize(cand_idx, cand_score, cand_count, kt, want_mask=output_attentions,
+                                             sel_ld=k_eff)
         mark("adaptive_k_select")
         attn = ops.sparse_sdpa(dims, q, k_all, v_all, sel, cnt, g1, self.scale)
         mark("sparse_sdpa")
@@ -565,7 +576,7 @@ class GatedSparseAttention(nn.Module):
         mark("o_proj")
         if capture is not None:
             capture.update(dims=dims, q=q, k=k_all, v=v_all, sel=sel, cnt=cnt, gate=g1, k_t=kt,
-                           n_chunks=ops.last_chunk_count)
+                           n_chunks=ops.last_chunk_count, candidate_path="survivors" if survivors else "exact")
 
         weights = None
         if output_attentions:

@@ -168,13 +168,15 @@ def adaptive_k(stats, var, total, n_cols: int, dt: torch.dtype, k_base: int, k_m
     return k
 
 
-def select_finalize(cand_idx, cand_score, cand_count, k, want_mask: bool = False):
+def select_finalize(cand_idx, cand_score, cand_count, k, want_mask: bool = False, sel_ld: int | None = None):
+    """The k[r] best candidates of each row, ascending column order: (sel [R, sel_ld], count [R],
+    mask [R, cand_ld] or None).  sel_ld defaults to the candidate row length."""
     R, k_eff = cand_idx.shape
-    sel = torch.empty(R, k_eff, device=cand_idx.device, dtype=torch.int32)
+    sel = torch.empty(R, sel_ld or k_eff, device=cand_idx.device, dtype=torch.int32)
     cnt = torch.empty(R, device=cand_idx.device, dtype=torch.int32)
     mask = torch.empty(R, k_eff, device=cand_idx.device, dtype=torch.uint8) if want_mask else None
     _lib.call("gsa_select_finalize", R, k_eff, _p(cand_idx), _p(cand_score), _p(cand_count), _p(k),
-              _p(sel), k_eff, _p(cnt), _p(mask), _stream())
+              _p(sel), sel.stride(0), _p(cnt), _p(mask), _stream())
     _after("select_finalize")
     return sel, cnt, mask
 
@@ -262,4 +264,50 @@ def indexer_select(dims: Dims, qI, kI, w, bias, scale: float, shift, k_eff: int,
               _p(cand_idx), _p(cand_score), _p(cand_count), _p(row_stats), chunk_rows,
               _p(workspace), workspace.numel(), _stream())
     _after("indexer_select")
+    return cand_idx, cand_score, cand_count, row_stats
+
+
+SURVIVOR_CAP = 8192
+
+
+def survivors_eligible(dims: Dims, k_eff: int, has_shift: bool) -> bool:
+    """Whether gsa_indexer_survivors applies: sigmoid indexer with its row centre, and
+    2 cap >= 3 k_eff + 2048."""
+    return has_shift and dims.idx_act == ACT["sigmoid"] and 2 * SURVIVOR_CAP >= 3 * k_eff + 2048
+
+
+def indexer_survivors(dims: Dims, qI, kI, w, bias, scale: float, shift, k_eff: int, q_pos0: int = 0,
+                      causal: bool = True, chunk_rows: int | None = None, row_stats=None, out=None):
+    """Indexer + threshold survivors for all rows, chunk by chunk.  Returns (cand_idx [R, cap],
+    cand_score [R, cap], cand_count [R], row_stats): each row's candidates hold its k_eff best
+    scores (and usually more), in ascending column order."""
+    _cuda(qI, kI, w, bias, shift)
+    B, Lq, _ = qI.shape
+    Lkv = kI.shape[1]
+    R = B * Lq
+    dev = qI.device
+    cap = SURVIVOR_CAP
+    if chunk_rows is None:
+        # bound the score scratch to ~1 GiB
+        chunk_rows = max(1, min(Lq, (1 << 30) // (4 * ((Lkv + 3) // 4 * 4))))
+    global last_chunk_count
+    last_chunk_count = B * ((Lq + chunk_rows - 1) // chunk_rows)
+    ws_bytes = _lib.lib().gsa_survivors_workspace_size(chunk_rows, Lkv)
+    workspace = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+    if out is not None:
+        cand_idx, cand_score, cand_count = out
+        assert cand_idx.is_contiguous() and cand_score.is_contiguous() and cand_count.is_contiguous()
+    else:
+        cand_idx = torch.empty(R, cap, device=dev, dtype=torch.int32)
+        cand_score = torch.empty(R, cap, device=dev, dtype=torch.float32)
+        cand_count = torch.empty(R, device=dev, dtype=torch.int32)
+    if row_stats is None:
+        row_stats = torch.zeros(R, 3, device=dev, dtype=torch.float64)
+    w = w.reshape(R, -1).float().contiguous()
+    bias = bias.float().contiguous()
+    _lib.call("gsa_indexer_survivors", C.byref(dims), dtype_code(qI.dtype), B, Lq, Lkv, q_pos0, int(causal),
+              _p(qI), qI.stride(1), qI.stride(0), _p(kI), kI.stride(1), kI.stride(0), _p(w), _p(bias),
+              float(scale), _p(shift), int(k_eff), cap, _p(cand_idx), _p(cand_score), _p(cand_count),
+              _p(row_stats), chunk_rows, _p(workspace), ws_bytes, _stream())
+    _after("indexer_survivors")
     return cand_idx, cand_score, cand_count, row_stats

@@ -161,7 +161,8 @@ int gsa_adaptive_k(int64_t R, int64_t n_cols, int dtype, const gsa_topk_params* 
 
 /*
  * Final selection: the top k[r] of each row's candidates (ties lower column first), in
- * ascending column order, into sel_idx[R, sel_ld]; sel_count[r] = min(k[r], cand_count[r]).
+ * ascending column order, into sel_idx[R, sel_ld]; sel_count[r] = min(k[r], cand_count[r],
+ * sel_ld).  The candidates are cand_idx / cand_score [R, k_eff] with cand_count[r] <= k_eff.
  * Reproduces the mask p < k_t of adaptive_topk.py:181-189.  If sel_mask [R, k_eff] (uint8)
  * is given, sel_mask[r, p] = 1 iff candidate p of row r is selected (the reference's
  * (indices, mask) pair with indices = the candidates).
@@ -212,6 +213,29 @@ int gsa_indexer_select(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, i
                        int32_t k_eff, int32_t* cand_idx, float* cand_score,
                        int32_t* cand_count, double* row_stats, int64_t chunk_rows,
                        void* workspace, int64_t workspace_bytes, gsa_stream_t stream);
+
+/*
+ * Indexer + threshold survivors, chunk by chunk (the layer's selection path for the sigmoid
+ * indexer; gated_indexer.py:106-155 with the candidate stage of adaptive_topk.py:138-177).
+ * Like gsa_indexer_select, but each row's candidates are its survivors: every score at or
+ * above the row's estimated (1 - 1.5 k_eff / n_r) quantile (from the row statistics the
+ * indexer accumulates), in ascending column order, up to ``cap`` per row.  Rows of n_r <= cap
+ * keep every score; a row whose survivors are fewer than min(k_eff, n_r) or more than cap is
+ * selected exactly (its k_eff best).  The candidates of every row therefore contain its k_eff
+ * best scores, and gsa_select_finalize (with k_eff := cap) takes the final k_t from them.
+ *   cand_idx / cand_score [B*Lq, cap]; cand_count [B*Lq]; row_stats [B*Lq, 3] (caller zeroes)
+ *   shift (the row centre of gsa_proj_epilogue) is required; 2 cap >= 3 k_eff + 2048.
+ *   workspace: gsa_survivors_workspace_size(chunk_rows, Lkv) bytes, 256-byte aligned.
+ * The score pass streams each chunk once at HBM rate, instead of a per-row selection.
+ */
+int64_t gsa_survivors_workspace_size(int64_t chunk_rows, int64_t n_cols);
+int gsa_indexer_survivors(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int64_t Lkv,
+                          int64_t q_pos0, int causal, const void* qI, int64_t qi_ld,
+                          int64_t qi_bstride, const void* kI, int64_t ki_ld, int64_t ki_bstride,
+                          const float* w, const float* bias, float scale, const float* shift,
+                          int32_t k_eff, int32_t cap, int32_t* cand_idx, float* cand_score,
+                          int32_t* cand_count, double* row_stats, int64_t chunk_rows,
+                          void* workspace, int64_t workspace_bytes, gsa_stream_t stream);
 
 /*
  * gsa_indexer_select without a workspace argument: it allocates no device memory.  No
