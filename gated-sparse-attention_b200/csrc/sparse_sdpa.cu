@@ -196,8 +196,17 @@ __global__ void __launch_bounds__(MAXW * 32) sdpa_tc_kernel(SdpaArgs a) {
         const int dim = mt * 16 + ((mi & 1) ? 8 : 0);
         ldsm_x4_t(smem_u32(Vs + key * rs + (g * D + dim) * 2), vf[mt][0], vf[mt][1], vf[mt][2], vf[mt][3]);
       }
+      // Hand the slot back only after every ldmatrix of this warp has returned its data: the
+      // next bulk copy into the slot must not overtake a shared-memory read in flight.  A value
+      // built from one register of each load (the four registers of an ldmatrix arrive
+      // together) makes the release wait for them.
+      uint32_t dep = 0;
+#pragma unroll
+      for (int i = 0; i < D / 16; ++i) dep ^= kf[i][0] ^ vf[i][0];
+      uint32_t zero;
+      asm volatile("and.b32 %0, %1, 0;" : "=r"(zero) : "r"(dep));
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
+      if (lane == 0) mbar_arrive(reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(&empty[s]) + zero));
       // S^T = K Q^T with two independent accumulation chains
       float c[4] = {0.f, 0.f, 0.f, 0.f}, c2[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll

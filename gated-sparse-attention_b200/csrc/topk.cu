@@ -586,10 +586,9 @@ __global__ void __launch_bounds__(kSelThreads) select_finalize_kernel(
 }
 
 // ---------------------------------------------------------------------------------------------
-// Streaming threshold compaction (the layer's candidate pass).  Every score of row r at or above
-// the threshold tau_r -- the row's normal quantile of 1.5 K / n_r from its statistics, the same
-// threshold as the first attempt of topk_row -- is a survivor; rows of n_r <= cap keep every
-// score.  Survivors are written in ascending column order to cand[r, 0..cap).  A row whose
+// Streaming threshold compaction (the layer's candidate pass).  Every finite score of row r at
+// or above the threshold tau_r -- the row's normal quantile of 1.25 K / n_r from its
+// statistics -- is a survivor; rows of n_r <= cap keep every score.  Survivors are written in ascending column order to cand[r, 0..cap).  A row whose
 // survivors are fewer than min(K, n_r) or more than cap goes to fail_list and is selected
 // exactly by topk_fallback_kernel.  Either way the row's candidates hold its K best scores, in
 // ascending column order, which is all the final selection needs.
@@ -606,6 +605,7 @@ constexpr int kCmpThreads = kCmpConsumers + 32;
 constexpr int kCmpPer = 16;                              // scores per consumer thread per chunk
 constexpr int kCmpChunk = kCmpConsumers * kCmpPer;       // 4096 scores = 16 KiB
 constexpr int kCmpStages = 4;
+constexpr float kSurvivorFactor = 1.25f;                 // survivors aimed at per needed key
 constexpr int kCmpSmem = 256 + kCmpStages * kCmpChunk * 4 + kCmpChunk * 8;  // ring + survivor staging
 
 struct CmpArgs {
@@ -638,7 +638,7 @@ __device__ __forceinline__ float cmp_threshold(const CmpArgs& a, int64_t r, int6
   const double var = st[1] / st[2] - mu_y * mu_y;
   const float sd = (float)sqrt(var > 0.0 ? var : 0.0);
   const float mean = a.center[r] + (float)mu_y;
-  const float pt = 1.5f * (float)a.K / (float)n;
+  const float pt = kSurvivorFactor * (float)a.K / (float)n;
   return pt >= 1.f ? -INFINITY : mean + sd * 1.41421356f * erfinvf(1.f - 2.f * pt);
 }
 
@@ -672,8 +672,8 @@ __global__ void __launch_bounds__(kCmpThreads) threshold_compact_kernel(CmpArgs 
   uint64_t* empty = full + kCmpStages;
   uint32_t* wsb = reinterpret_cast<uint32_t*>(empty + kCmpStages);  // 2 x 8 words
   float* stage = reinterpret_cast<float*>(cmp_smem + 256);
-  int32_t* keep_col = reinterpret_cast<int32_t*>(stage + kCmpStages * kCmpChunk);  // [kCmpChunk]
-  float* keep_val = reinterpret_cast<float*>(keep_col + kCmpChunk);                // [kCmpChunk]
+  // a chunk's survivors as (column, score bits) pairs, in column order
+  uint2* keep = reinterpret_cast<uint2*>(stage + kCmpStages * kCmpChunk);  // [kCmpChunk]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kCmpStages; ++s) {
@@ -728,21 +728,23 @@ __global__ void __launch_bounds__(kCmpThreads) threshold_compact_kernel(CmpArgs 
         const float4 f = src[q];
         v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
-      const int64_t i0 = c0 + threadIdx.x * kCmpPer;
+      const int32_t i0 = (int32_t)c0 + (int32_t)threadIdx.x * kCmpPer;
+      const int32_t nn = (int32_t)n;
       uint32_t flags = 0;
 #pragma unroll
       for (int j = 0; j < kCmpPer; ++j)
-        if (i0 + j < n && valid_key(v[j]) && v[j] >= tau) flags |= 1u << j;
+        if (i0 + j < nn && v[j] >= tau && v[j] > -INFINITY) flags |= 1u << j;  // NaN fails both
+      // release the slot only once every lane's loads have returned (the flags consume them):
+      // the next bulk copy into it must not overtake a shared-memory read still in flight
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
       uint32_t total;
       uint32_t pos = cmp_scan((uint32_t)__popc(flags), wsb + (parity & 1u) * 8, &total);
       parity ^= 1u;
 #pragma unroll
       for (int j = 0; j < kCmpPer; ++j) {
         if (flags & (1u << j)) {
-          keep_col[pos] = (int32_t)(i0 + j);
-          keep_val[pos] = v[j];
+          keep[pos] = make_uint2((uint32_t)(i0 + j), __float_as_uint(v[j]));
           ++pos;
         }
       }
@@ -751,8 +753,9 @@ __global__ void __launch_bounds__(kCmpThreads) threshold_compact_kernel(CmpArgs 
       const uint32_t lim = base >= (uint32_t)a.cap ? 0u : min(total, (uint32_t)a.cap - base);
       if (ok)
         for (uint32_t i = threadIdx.x; i < lim; i += kCmpConsumers) {
-          oi[base + i] = keep_col[i];
-          os[base + i] = keep_val[i];
+          const uint2 e = keep[i];
+          oi[base + i] = (int32_t)e.x;
+          os[base + i] = __uint_as_float(e.y);
         }
       base += total;
     }

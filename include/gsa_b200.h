@@ -218,13 +218,14 @@ int gsa_indexer_select(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, i
  * Indexer + threshold survivors, chunk by chunk (the layer's selection path for the sigmoid
  * indexer; gated_indexer.py:106-155 with the candidate stage of adaptive_topk.py:138-177).
  * Like gsa_indexer_select, but each row's candidates are its survivors: every score at or
- * above the row's estimated (1 - 1.5 k_eff / n_r) quantile (from the row statistics the
+ * above the row's estimated (1 - 1.25 k_eff / n_r) quantile (from the row statistics the
  * indexer accumulates), in ascending column order, up to ``cap`` per row.  Rows of n_r <= cap
  * keep every score; a row whose survivors are fewer than min(k_eff, n_r) or more than cap is
  * selected exactly (its k_eff best).  The candidates of every row therefore contain its k_eff
  * best scores, and gsa_select_finalize (with k_eff := cap) takes the final k_t from them.
  *   cand_idx / cand_score [B*Lq, cap]; cand_count [B*Lq]; row_stats [B*Lq, 3] (caller zeroes)
- *   shift (the row centre of gsa_proj_epilogue) is required; 2 cap >= 3 k_eff + 2048.
+ *   shift (the row centre of gsa_proj_epilogue) is required; 2 cap >= 3 k_eff + 2048 (room
+ *   above the threshold's aim).
  *   workspace: gsa_survivors_workspace_size(chunk_rows, Lkv) bytes, 256-byte aligned.
  * The score pass streams each chunk once at HBM rate, instead of a per-row selection.
  */

@@ -94,3 +94,21 @@ def test_layer_candidate_paths_agree(cuda_ok):
     assert cap_s["candidate_path"] == "survivors" and cap_e["candidate_path"] == "exact"
     assert torch.equal(cap_s["cnt"], cap_e["cnt"])
     assert torch.equal(out_s, out_e)
+
+
+def test_layer_forward_is_deterministic(cuda_ok):
+    """Repeated bf16 forwards give bit-identical outputs: no shared-memory slot is refilled while a
+    read of it is still in flight (compaction ring, SDPA ring), and fp64 statistic sums that
+    differ in their last bits do not change the selection."""
+    from gsa_b200 import GatedSparseAttention, GSAConfig
+
+    cfg = GSAConfig(d_model=1024, n_heads=8, n_kv_heads=2, d_indexer=64, n_indexer_heads=8, k_base=2048,
+                    k_min=256, k_max=4096, max_position_embeddings=16384)
+    torch.manual_seed(0)
+    m = GatedSparseAttention(cfg).to(DEV).to(torch.bfloat16).eval()
+    x = torch.randn(1, 10000, 1024, generator=torch.Generator().manual_seed(1)).to(DEV, torch.bfloat16)
+    with torch.no_grad():
+        outs = [m(x)[0] for _ in range(6)]
+    torch.cuda.synchronize()
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
