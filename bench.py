@@ -118,6 +118,8 @@ def dist_setup(n_gpus):
         import datetime
         import torch.distributed as dist
 
+        # keep NCCL's version banner off stdout, where the result line goes
+        os.environ.setdefault("NCCL_DEBUG", "WARN")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
@@ -244,8 +246,12 @@ def run_ours(args, world, rank):
     for name, ev in marks:
         stages[name] = round(prev.elapsed_time(ev), 3)
         prev = ev
+    # our kernels per forward: the projection epilogue; per query chunk the indexer and the
+    # candidate pass (survivor compaction + exact fallback, or the exact top-k); row variance
+    # (2) and adaptive k; the final selection; the SDPA
     n_chunks = cap["n_chunks"]
-    launches_per_step = 1 + 2 * n_chunks + (3 if cfg.use_adaptive_k else 1) + 1 + 1
+    per_chunk = 3 if cap.get("candidate_path") == "survivors" else 2
+    launches_per_step = 1 + per_chunk * n_chunks + (3 if cfg.use_adaptive_k else 1) + 1 + 1
     sdpa_bytes = sdpa_algorithmic_bytes(cfg, cap["cnt"])
     reps = 3
     s0 = torch.cuda.Event(enable_timing=True)
