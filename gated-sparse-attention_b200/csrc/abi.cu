@@ -168,6 +168,14 @@ int gsa_select_finalize(int64_t R, int32_t k_eff, const int32_t* cand_idx, const
   if (R < 0 || k_eff < 1 || sel_ld < 1) return GSA_ERR_BAD_ARG;
   if (R == 0) return GSA_OK;
   if (!cand_idx || !cand_score || !cand_count || !k || !sel_idx || !sel_count) return GSA_ERR_BAD_ARG;
+  if (!sel_mask) {
+    // one warp per row (the selection mask needs the per-row CTA kernel)
+    DeviceInfo* di;
+    int st = device_info(&di);
+    if (st) return st;
+    return launch_select_finalize_warp(R, k_eff, cand_idx, cand_score, cand_count, k, sel_idx, sel_ld, sel_count,
+                                       di->num_sms, reinterpret_cast<cudaStream_t>(stream));
+  }
   return launch_select_finalize(R, k_eff, cand_idx, cand_score, cand_count, k, sel_idx, sel_ld, sel_count,
                                 sel_mask, reinterpret_cast<cudaStream_t>(stream));
 }

@@ -95,6 +95,9 @@ int launch_threshold_candidates(int64_t R, int64_t Lq, int64_t n_cols, int64_t q
                                 int32_t K, int32_t cap, int32_t* cand_idx, float* cand_score, int32_t* cand_count,
                                 int32_t* fail_list, int32_t* fail_count, int num_sms, int* err,
                                 cudaStream_t stream);
+int launch_select_finalize_warp(int64_t R, int32_t cand_ld, const int32_t* cand_idx, const float* cand_score,
+                                const int32_t* cand_count, const int32_t* k, int32_t* sel_idx, int64_t sel_ld,
+                                int32_t* sel_count, int num_sms, cudaStream_t stream);
 int launch_select_finalize(int64_t R, int32_t k_eff, const int32_t* cand_idx, const float* cand_score,
                            const int32_t* cand_count, const int32_t* k, int32_t* sel_idx, int64_t sel_ld,
                            int32_t* sel_count, uint8_t* sel_mask, cudaStream_t stream);

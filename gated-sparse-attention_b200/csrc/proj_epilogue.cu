@@ -81,9 +81,142 @@ __global__ void proj_epilogue_kernel(EpiArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// bf16 fast path: the same ops and roundings, 8 elements per thread with 16-byte accesses.  A
+// RoPE task takes elements i..i+7 of a head's first half together with their rotate-half
+// partners i+D/2..i+D/2+7, so every loaded element is used once.
+// ---------------------------------------------------------------------------------------------
+struct Vec8 {
+  float f[8];
+};
+
+__device__ __forceinline__ Vec8 ld8_bf16(const __nv_bfloat16* p) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  Vec8 v;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    v.f[2 * k] = __uint_as_float(w[k] << 16);
+    v.f[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
+  }
+  return v;
+}
+
+__device__ __forceinline__ Vec8 ld8_tab(const __nv_bfloat16* p) { return ld8_bf16(p); }
+__device__ __forceinline__ Vec8 ld8_tab(const float* p) {
+  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+  Vec8 v;
+  v.f[0] = a.x; v.f[1] = a.y; v.f[2] = a.z; v.f[3] = a.w;
+  v.f[4] = b.x; v.f[5] = b.y; v.f[6] = b.z; v.f[7] = b.w;
+  return v;
+}
+
+// store rounds each value to bf16 (round to nearest even), as store_elem does
+__device__ __forceinline__ void st8_bf16(__nv_bfloat16* p, const Vec8& v) {
+  uint32_t w[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(v.f[2 * k], v.f[2 * k + 1]);
+    w[k] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+template <typename TabT>
+__global__ void __launch_bounds__(256) proj_epilogue_bf16_kernel(EpiArgs a) {
+  const int64_t t = blockIdx.x;
+  if (t >= a.T) return;
+  constexpr int dt = GSA_DTYPE_BF16;
+  const int H = a.d.n_heads, Hk = a.d.n_kv_heads, D = a.d.d_head, HI = a.d.n_idx_heads;
+  const int half = D / 2, vh = half / 8;
+  const __nv_bfloat16* prow = reinterpret_cast<const __nv_bfloat16*>(a.proj) + t * a.proj_ld;
+  int64_t pos = a.positions[t];
+  if (pos < 0 || pos >= a.tab_rows) {
+    set_error(a.err, GSA_ERR_INDEX);
+    pos = pos < 0 ? 0 : a.tab_rows - 1;
+  }
+  const TabT* cr = reinterpret_cast<const TabT*>(a.cos_tab) + pos * D;
+  const TabT* sr = reinterpret_cast<const TabT*>(a.sin_tab) + pos * D;
+  __nv_bfloat16* qo = reinterpret_cast<__nv_bfloat16*>(a.q_out);
+  __nv_bfloat16* ko = reinterpret_cast<__nv_bfloat16*>(a.k_out);
+  __nv_bfloat16* vo = reinterpret_cast<__nv_bfloat16*>(a.v_out);
+  __nv_bfloat16* go = reinterpret_cast<__nv_bfloat16*>(a.g1_out);
+  const int nq = H * vh, nk = Hk * vh, nv = Hk * D / 8;
+  const int ng = (a.lay.g1 >= 0 && a.g1_out) ? H * D / 8 : 0;
+  const int ntask = nq + nk + nv + ng;
+  for (int task = threadIdx.x; task < ntask; task += blockDim.x) {
+    if (task < nq + nk) {
+      const bool isq = task < nq;
+      const int tt = isq ? task : task - nq;
+      const int h = tt / vh, i = (tt % vh) * 8;
+      const __nv_bfloat16* src = prow + (isq ? a.lay.q : a.lay.k) + (int64_t)h * D;
+      const Vec8 x1 = ld8_bf16(src + i), x2 = ld8_bf16(src + i + half);
+      const Vec8 c1 = ld8_tab(cr + i), c2 = ld8_tab(cr + i + half);
+      const Vec8 s1 = ld8_tab(sr + i), s2 = ld8_tab(sr + i + half);
+      Vec8 o1, o2;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        // (x * cos) + (rotate_half(x) * sin), rotate_half = cat(-x2, x1); each op rounded
+        o1.f[e] = fadd(rnd(fmul(x1.f[e], c1.f[e]), dt), rnd(fmul(-x2.f[e], s1.f[e]), dt));
+        o2.f[e] = fadd(rnd(fmul(x2.f[e], c2.f[e]), dt), rnd(fmul(x1.f[e], s2.f[e]), dt));
+      }
+      __nv_bfloat16* dst = isq ? qo + (t * H + h) * D : ko + t * a.kv_ld + (int64_t)h * D;
+      st8_bf16(dst + i, o1);
+      st8_bf16(dst + i + half, o2);
+    } else if (task < nq + nk + nv) {
+      const int i = (task - nq - nk) * 8;
+      Vec8 v = ld8_bf16(prow + a.lay.v + i);
+      if (a.lay.g2 >= 0) {
+        const Vec8 g = ld8_bf16(prow + a.lay.g2 + i);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v.f[e] = fmul(v.f[e], gate_act(g.f[e], a.d.gate_act, dt));
+      }
+      st8_bf16(vo + t * a.kv_ld + i, v);
+    } else {
+      const int i = (task - nq - nk - nv) * 8;
+      Vec8 g = ld8_bf16(prow + a.lay.g1 + i);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) g.f[e] = gate_act(g.f[e], a.d.gate_act, dt);
+      st8_bf16(go + t * (int64_t)H * D + i, g);
+    }
+  }
+  if (threadIdx.x == 0) {
+    float sum = 0.f;
+    for (int j = 0; j < HI; ++j) {
+      float w = rnd(sigmoid_precise(__bfloat162float(prow[a.lay.wi + j])), dt);
+      a.w_out[t * HI + j] = w;
+      sum += w;
+    }
+    a.shift_out[t] = 0.5f * sum;
+  }
+}
+
+static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) % 16) == 0; }
+
+// The vector path needs every row segment it touches to start on a 16-byte boundary.
+static bool epilogue_vec_ok(const EpiArgs& a) {
+  const int D = a.d.d_head;
+  auto el = [](int64_t x) { return (x * 2) % 16 == 0; };
+  bool ok = a.dtype == GSA_DTYPE_BF16 && D % 16 == 0 && al16(a.proj) && el(a.proj_ld) && el(a.lay.q) &&
+            el(a.lay.k) && el(a.lay.v) && (a.lay.g2 < 0 || el(a.lay.g2)) && al16(a.q_out) && al16(a.k_out) &&
+            al16(a.v_out) && el(a.kv_ld);
+  if (a.lay.g1 >= 0 && a.g1_out) ok = ok && el(a.lay.g1) && al16(a.g1_out);
+  const size_t tab_el = a.tab_dtype == GSA_DTYPE_BF16 ? 2 : 4;
+  ok = ok && al16(a.cos_tab) && al16(a.sin_tab) && ((int64_t)D * tab_el) % 16 == 0;
+  return ok;
+}
+
 int launch_proj_epilogue(const EpiArgs& a, cudaStream_t stream) {
   if (a.T == 0) return GSA_OK;
-  proj_epilogue_kernel<<<(unsigned)a.T, 128, 0, stream>>>(a);
+  if (a.T > 0x7fffffffLL) return GSA_ERR_BAD_ARG;
+  if (epilogue_vec_ok(a)) {
+    if (a.tab_dtype == GSA_DTYPE_BF16)
+      proj_epilogue_bf16_kernel<__nv_bfloat16><<<(unsigned)a.T, 256, 0, stream>>>(a);
+    else
+      proj_epilogue_bf16_kernel<float><<<(unsigned)a.T, 256, 0, stream>>>(a);
+  } else {
+    proj_epilogue_kernel<<<(unsigned)a.T, 128, 0, stream>>>(a);
+  }
   return cudaGetLastError() == cudaSuccess ? GSA_OK : GSA_ERR_LAUNCH;
 }
 

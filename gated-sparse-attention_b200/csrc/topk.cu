@@ -809,6 +809,232 @@ int launch_threshold_candidates(int64_t R, int64_t Lq, int64_t n_cols, int64_t q
   return cudaGetLastError() == cudaSuccess ? GSA_OK : GSA_ERR_LAUNCH;
 }
 
+// ---------------------------------------------------------------------------------------------
+// Final selection, one warp per row (used when no selection mask is asked for).  The k_t best
+// of a row's m candidates (ascending columns), ties lower column first, written in ascending
+// column order:
+//   1. min / max of the scores;
+//   2. a 1024-bin histogram over [min, max] in the warp's shared memory: the bin b* holding the
+//      k_t-th score; every candidate in a higher bin is kept;
+//   3. the cut inside b*: the need-th member under (score desc, position asc), as (v_cut, p_cut).
+//      Few members (<= kWarpListCap): ranked exactly from a shared list.  Tie-heavy bins: a radix
+//      select over the members' fp32 keys (4 x 8 bits) gives v_cut, an ordered pass p_cut;
+//   4. one ordered pass keeps bin > b*, or bin == b* and (v > v_cut, or v == v_cut and position
+//      <= p_cut), ranks the kept candidates of each 32 by ballot and stores them coalesced.
+// Only warp collectives: no block barriers, 32 rows in flight per SM.
+// ---------------------------------------------------------------------------------------------
+constexpr int kWarpBins = 1024;
+constexpr int kWarpListCap = 256;
+constexpr int kWarpSelWarps = 8;
+constexpr int kWarpSelSmem = kWarpSelWarps * (kWarpBins * 4 + kWarpListCap * 8);
+
+__device__ __forceinline__ float key_float(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+// Finds, among hist[0..nb) scanned from the top, the bin where the count from the top reaches K
+// (count(bins above) < K <= count(bins >= it)); returns it and the count above it.  nb is a
+// multiple of 32; every lane gets the result.
+__device__ __forceinline__ void warp_find_bin(const uint32_t* hist, int nb, uint32_t K, uint32_t& bin_out,
+                                              uint32_t& above_out) {
+  const int lane = threadIdx.x & 31;
+  const int per = nb / 32;
+  const int top = nb - per * lane - 1;
+  uint32_t own = 0;
+  for (int j = 0; j < per; ++j) own += hist[top - j];
+  uint32_t incl = own;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  const uint32_t excl = incl - own;
+  const uint32_t crossing = __ballot_sync(0xffffffffu, excl < K && incl >= K);
+  const int src = crossing ? __ffs(crossing) - 1 : 31;
+  uint32_t b = 0, above = 0;
+  if (lane == src) {
+    uint32_t acc = excl;
+    for (int j = 0; j < per; ++j) {
+      const uint32_t c = hist[top - j];
+      b = (uint32_t)(top - j);
+      above = acc;
+      if (acc + c >= K) break;
+      acc += c;
+    }
+  }
+  bin_out = __shfl_sync(0xffffffffu, b, src);
+  above_out = __shfl_sync(0xffffffffu, above, src);
+}
+
+__global__ void __launch_bounds__(kWarpSelWarps * 32) select_finalize_warp_kernel(
+    int64_t R, int32_t cand_ld, const int32_t* cand_idx, const float* cand_score, const int32_t* cand_count,
+    const int32_t* k, int32_t* sel_idx, int64_t sel_ld, int32_t* sel_count) {
+  extern __shared__ __align__(16) uint8_t wsel_smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint32_t* hist = reinterpret_cast<uint32_t*>(wsel_smem) + warp * kWarpBins;
+  float* lval = reinterpret_cast<float*>(wsel_smem + kWarpSelWarps * kWarpBins * 4) + warp * 2 * kWarpListCap;
+  uint32_t* lpos = reinterpret_cast<uint32_t*>(lval + kWarpListCap);
+  const uint32_t lt = (1u << lane) - 1u;
+  for (int64_t r = (int64_t)blockIdx.x * kWarpSelWarps + warp; r < R; r += (int64_t)gridDim.x * kWarpSelWarps) {
+    int32_t m = cand_count[r];
+    m = m < 0 ? 0 : (m > cand_ld ? cand_ld : m);
+    int32_t K = k[r];
+    K = K < 0 ? 0 : K;
+    if ((int64_t)K > sel_ld) K = (int32_t)sel_ld;
+    const float* vals = cand_score + r * cand_ld;
+    const int32_t* cols = cand_idx + r * cand_ld;
+    int32_t* out = sel_idx + r * sel_ld;
+    if (K == 0 || m == 0) {
+      if (lane == 0) sel_count[r] = 0;
+      continue;
+    }
+    if (K >= m) {
+      for (int i = lane; i < m; i += 32) out[i] = cols[i];
+      if (lane == 0) sel_count[r] = m;
+      continue;
+    }
+    // 1. range
+    float lo = INFINITY, hi = -INFINITY;
+    for (int i = lane; i < m; i += 32) {
+      const float v = vals[i];
+      lo = fminf(lo, v);
+      hi = fmaxf(hi, v);
+    }
+    lo = -warp_max(-lo);
+    hi = warp_max(hi);
+    float scale = (float)kWarpBins / (hi - lo);
+    if (!(hi > lo) || !(scale < INFINITY) || !(scale > 0.f)) scale = 0.f;  // one bin: the cut decides
+    auto bin = [&](float x) { return min(__float2uint_rz((x - lo) * scale), (uint32_t)(kWarpBins - 1)); };
+    // 2. histogram and the bin of the K-th score
+    for (int b = lane; b < kWarpBins; b += 32) hist[b] = 0u;
+    __syncwarp();
+    for (int i = lane; i < m; i += 32) atomicAdd(&hist[bin(vals[i])], 1u);
+    __syncwarp();
+    uint32_t bstar, above;
+    warp_find_bin(hist, kWarpBins, (uint32_t)K, bstar, above);
+    const uint32_t need = (uint32_t)K - above;  // >= 1
+    const uint32_t e = hist[bstar];
+    __syncwarp();
+    // 3. the cut inside b*
+    float vc = 0.f;
+    uint32_t pc = 0;
+    if (e <= (uint32_t)kWarpListCap) {
+      uint32_t nl = 0;
+      for (int i0 = 0; i0 < m; i0 += 32) {
+        const int i = i0 + lane;
+        float v = 0.f;
+        bool in = false;
+        if (i < m) {
+          v = vals[i];
+          in = bin(v) == bstar;
+        }
+        const uint32_t bal = __ballot_sync(0xffffffffu, in);
+        if (in) {
+          const uint32_t p = nl + (uint32_t)__popc(bal & lt);
+          lval[p] = v;
+          lpos[p] = (uint32_t)i;
+        }
+        nl += (uint32_t)__popc(bal);
+      }
+      __syncwarp();
+      bool found = false;
+      for (uint32_t a = lane; a < nl; a += 32) {
+        const float va = lval[a];
+        const uint32_t pa = lpos[a];
+        uint32_t rank = 0;
+        for (uint32_t b = 0; b < nl; ++b) {
+          const float vb = lval[b];
+          rank += (vb > va) || (vb == va && lpos[b] < pa);
+        }
+        if (rank == need - 1) {
+          vc = va;
+          pc = pa;
+          found = true;
+        }
+      }
+      const int src = __ffs(__ballot_sync(0xffffffffu, found)) - 1;
+      vc = __shfl_sync(0xffffffffu, vc, src < 0 ? 0 : src);
+      pc = __shfl_sync(0xffffffffu, pc, src < 0 ? 0 : src);
+    } else {
+      // radix select over the members' keys: the need-th largest value among them
+      uint32_t prefix = 0, want = need;
+      for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int b = lane; b < 256; b += 32) hist[b] = 0u;
+        __syncwarp();
+        const uint32_t pmask = shift == 24 ? 0u : (0xffffffffu << (shift + 8));
+        for (int i = lane; i < m; i += 32) {
+          const float v = vals[i];
+          if (bin(v) != bstar) continue;
+          const uint32_t key = float_key(v);
+          if ((key & pmask) == (prefix & pmask)) atomicAdd(&hist[(key >> shift) & 0xffu], 1u);
+        }
+        __syncwarp();
+        uint32_t d, ab;
+        warp_find_bin(hist, 256, want, d, ab);
+        prefix |= d << shift;
+        want -= ab;
+        __syncwarp();
+      }
+      vc = key_float(prefix);
+      // the want-th member equal to v_cut, in position order
+      uint32_t seen = 0;
+      for (int i0 = 0; i0 < m; i0 += 32) {
+        const int i = i0 + lane;
+        const bool eq = i < m && vals[i] == vc && bin(vals[i]) == bstar;
+        const uint32_t bal = __ballot_sync(0xffffffffu, eq);
+        const uint32_t c = (uint32_t)__popc(bal);
+        if (seen + c >= want) {
+          // the (want - seen)-th set bit of bal
+          uint32_t bb = bal;
+          for (uint32_t j = 1; j < want - seen; ++j) bb &= bb - 1u;
+          pc = (uint32_t)(i0 + __ffs(bb) - 1);
+          break;
+        }
+        seen += c;
+      }
+    }
+    __syncwarp();
+    // 4. ordered output
+    uint32_t base = 0;
+    for (int i0 = 0; i0 < m; i0 += 32) {
+      const int i = i0 + lane;
+      bool keep = false;
+      if (i < m) {
+        const float v = vals[i];
+        const uint32_t b = bin(v);
+        keep = b > bstar || (b == bstar && (v > vc || (v == vc && (uint32_t)i <= pc)));
+      }
+      const uint32_t bal = __ballot_sync(0xffffffffu, keep);
+      if (keep) {
+        const uint32_t p = base + (uint32_t)__popc(bal & lt);
+        if (p < (uint32_t)K) out[p] = cols[i];
+      }
+      base += (uint32_t)__popc(bal);
+    }
+    if (lane == 0) sel_count[r] = (int32_t)min(base, (uint32_t)K);
+  }
+}
+
+int launch_select_finalize_warp(int64_t R, int32_t cand_ld, const int32_t* cand_idx, const float* cand_score,
+                                const int32_t* cand_count, const int32_t* k, int32_t* sel_idx, int64_t sel_ld,
+                                int32_t* sel_count, int num_sms, cudaStream_t stream) {
+  if (R == 0) return GSA_OK;
+  if (cudaFuncSetAttribute(select_finalize_warp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           kWarpSelSmem) != cudaSuccess)
+    return GSA_ERR_LAUNCH;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, select_finalize_warp_kernel, kWarpSelWarps * 32,
+                                                    kWarpSelSmem) != cudaSuccess ||
+      per_sm < 1)
+    return GSA_ERR_LAUNCH;
+  int64_t grid = (int64_t)num_sms * per_sm;
+  const int64_t need = (R + kWarpSelWarps - 1) / kWarpSelWarps;
+  if (grid > need) grid = need;
+  select_finalize_warp_kernel<<<(unsigned)grid, kWarpSelWarps * 32, kWarpSelSmem, stream>>>(
+      R, cand_ld, cand_idx, cand_score, cand_count, k, sel_idx, sel_ld, sel_count);
+  return cudaGetLastError() == cudaSuccess ? GSA_OK : GSA_ERR_LAUNCH;
+}
+
 // Row statistics of a materialised score matrix: sum, sum of squares, finite count (fp64).
 __global__ void row_stats_kernel(int64_t n_cols, const float* scores, int64_t ld, double* stats) {
   const int64_t r = blockIdx.x;
