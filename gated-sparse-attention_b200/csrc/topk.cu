@@ -827,6 +827,7 @@ constexpr int kWarpBins = 1024;
 constexpr int kWarpListCap = 256;
 constexpr int kWarpSelWarps = 8;
 constexpr int kWarpSelSmem = kWarpSelWarps * (kWarpBins * 4 + kWarpListCap * 8);
+constexpr int kWarpUnroll = 8;  // loads in flight per lane: each pass walks tiles of 8 x 32 scores
 
 __device__ __forceinline__ float key_float(uint32_t k) {
   return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
@@ -895,10 +896,18 @@ __global__ void __launch_bounds__(kWarpSelWarps * 32) select_finalize_warp_kerne
     }
     // 1. range
     float lo = INFINITY, hi = -INFINITY;
-    for (int i = lane; i < m; i += 32) {
-      const float v = vals[i];
-      lo = fminf(lo, v);
-      hi = fmaxf(hi, v);
+    for (int i0 = 0; i0 < m; i0 += 32 * kWarpUnroll) {
+      float v[kWarpUnroll];
+#pragma unroll
+      for (int j = 0; j < kWarpUnroll; ++j) {
+        const int i = i0 + j * 32 + lane;
+        v[j] = i < m ? vals[i] : vals[0];
+      }
+#pragma unroll
+      for (int j = 0; j < kWarpUnroll; ++j) {
+        lo = fminf(lo, v[j]);
+        hi = fmaxf(hi, v[j]);
+      }
     }
     lo = -warp_max(-lo);
     hi = warp_max(hi);
@@ -908,7 +917,17 @@ __global__ void __launch_bounds__(kWarpSelWarps * 32) select_finalize_warp_kerne
     // 2. histogram and the bin of the K-th score
     for (int b = lane; b < kWarpBins; b += 32) hist[b] = 0u;
     __syncwarp();
-    for (int i = lane; i < m; i += 32) atomicAdd(&hist[bin(vals[i])], 1u);
+    for (int i0 = 0; i0 < m; i0 += 32 * kWarpUnroll) {
+      float v[kWarpUnroll];
+#pragma unroll
+      for (int j = 0; j < kWarpUnroll; ++j) {
+        const int i = i0 + j * 32 + lane;
+        v[j] = i < m ? vals[i] : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < kWarpUnroll; ++j)
+        if (i0 + j * 32 + lane < m) atomicAdd(&hist[bin(v[j])], 1u);
+    }
     __syncwarp();
     uint32_t bstar, above;
     warp_find_bin(hist, kWarpBins, (uint32_t)K, bstar, above);
@@ -920,21 +939,25 @@ __global__ void __launch_bounds__(kWarpSelWarps * 32) select_finalize_warp_kerne
     uint32_t pc = 0;
     if (e <= (uint32_t)kWarpListCap) {
       uint32_t nl = 0;
-      for (int i0 = 0; i0 < m; i0 += 32) {
-        const int i = i0 + lane;
-        float v = 0.f;
-        bool in = false;
-        if (i < m) {
-          v = vals[i];
-          in = bin(v) == bstar;
+      for (int i0 = 0; i0 < m; i0 += 32 * kWarpUnroll) {
+        float v[kWarpUnroll];
+#pragma unroll
+        for (int j = 0; j < kWarpUnroll; ++j) {
+          const int i = i0 + j * 32 + lane;
+          v[j] = i < m ? vals[i] : 0.f;
         }
-        const uint32_t bal = __ballot_sync(0xffffffffu, in);
-        if (in) {
-          const uint32_t p = nl + (uint32_t)__popc(bal & lt);
-          lval[p] = v;
-          lpos[p] = (uint32_t)i;
+#pragma unroll
+        for (int j = 0; j < kWarpUnroll; ++j) {
+          const int i = i0 + j * 32 + lane;
+          const bool in = i < m && bin(v[j]) == bstar;
+          const uint32_t bal = __ballot_sync(0xffffffffu, in);
+          if (in) {
+            const uint32_t p = nl + (uint32_t)__popc(bal & lt);
+            lval[p] = v[j];
+            lpos[p] = (uint32_t)i;
+          }
+          nl += (uint32_t)__popc(bal);
         }
-        nl += (uint32_t)__popc(bal);
       }
       __syncwarp();
       bool found = false;
@@ -994,22 +1017,32 @@ __global__ void __launch_bounds__(kWarpSelWarps * 32) select_finalize_warp_kerne
       }
     }
     __syncwarp();
-    // 4. ordered output
+    // 4. ordered output (tiles in order, and chunks of 32 in order within a tile)
     uint32_t base = 0;
-    for (int i0 = 0; i0 < m; i0 += 32) {
-      const int i = i0 + lane;
-      bool keep = false;
-      if (i < m) {
-        const float v = vals[i];
-        const uint32_t b = bin(v);
-        keep = b > bstar || (b == bstar && (v > vc || (v == vc && (uint32_t)i <= pc)));
+    for (int i0 = 0; i0 < m; i0 += 32 * kWarpUnroll) {
+      float v[kWarpUnroll];
+      int32_t c[kWarpUnroll];
+#pragma unroll
+      for (int j = 0; j < kWarpUnroll; ++j) {
+        const int i = i0 + j * 32 + lane;
+        v[j] = i < m ? vals[i] : 0.f;
+        c[j] = i < m ? cols[i] : 0;
       }
-      const uint32_t bal = __ballot_sync(0xffffffffu, keep);
-      if (keep) {
-        const uint32_t p = base + (uint32_t)__popc(bal & lt);
-        if (p < (uint32_t)K) out[p] = cols[i];
+#pragma unroll
+      for (int j = 0; j < kWarpUnroll; ++j) {
+        const int i = i0 + j * 32 + lane;
+        bool keep = false;
+        if (i < m) {
+          const uint32_t b = bin(v[j]);
+          keep = b > bstar || (b == bstar && (v[j] > vc || (v[j] == vc && (uint32_t)i <= pc)));
+        }
+        const uint32_t bal = __ballot_sync(0xffffffffu, keep);
+        if (keep) {
+          const uint32_t p = base + (uint32_t)__popc(bal & lt);
+          if (p < (uint32_t)K) out[p] = c[j];
+        }
+        base += (uint32_t)__popc(bal);
       }
-      base += (uint32_t)__popc(bal);
     }
     if (lane == 0) sel_count[r] = (int32_t)min(base, (uint32_t)K);
   }
