@@ -18,6 +18,9 @@ from ._lib import ACT, DTYPE_BF16, DTYPE_F32, Dims, ProjLayout, TopkParams
 DEBUG = os.environ.get("GSA_DEBUG", "0") == "1"
 # number of (indexer, top-k) chunk launches of the last indexer_select call
 last_chunk_count = 0
+# bound of the chunk score scratch of the layer's indexer pass (fewer, larger chunks amortise
+# each launch's tail; the scratch lives only during the call)
+SCORE_CHUNK_BYTES = 4 << 30
 
 
 def _p(t):
@@ -240,8 +243,7 @@ def indexer_select(dims: Dims, qI, kI, w, bias, scale: float, shift, k_eff: int,
     R = B * Lq
     dev = qI.device
     if chunk_rows is None:
-        # bound the score scratch to ~1 GiB
-        chunk_rows = max(1, min(Lq, (1 << 30) // (4 * ((Lkv + 3) // 4 * 4))))
+        chunk_rows = max(1, min(Lq, SCORE_CHUNK_BYTES // (4 * ((Lkv + 3) // 4 * 4))))
     global last_chunk_count
     last_chunk_count = B * ((Lq + chunk_rows - 1) // chunk_rows)
     need = workspace_bytes(chunk_rows, Lkv)
@@ -288,8 +290,7 @@ def indexer_survivors(dims: Dims, qI, kI, w, bias, scale: float, shift, k_eff: i
     dev = qI.device
     cap = SURVIVOR_CAP
     if chunk_rows is None:
-        # bound the score scratch to ~1 GiB
-        chunk_rows = max(1, min(Lq, (1 << 30) // (4 * ((Lkv + 3) // 4 * 4))))
+        chunk_rows = max(1, min(Lq, SCORE_CHUNK_BYTES // (4 * ((Lkv + 3) // 4 * 4))))
     global last_chunk_count
     last_chunk_count = B * ((Lq + chunk_rows - 1) // chunk_rows)
     ws_bytes = _lib.lib().gsa_survivors_workspace_size(chunk_rows, Lkv)
