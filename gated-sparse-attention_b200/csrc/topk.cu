@@ -644,21 +644,23 @@ __device__ __forceinline__ float cmp_threshold(const CmpArgs& a, int64_t r, int6
 
 __device__ __forceinline__ void cmp_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kCmpConsumers) : "memory"); }
 
-// Exclusive scan over the consumer threads (two scratch buffers alternate, so two barriers).
-__device__ __forceinline__ uint32_t cmp_scan(uint32_t v, uint32_t* ws, uint32_t* total) {
+// Exclusive scan over the consumer threads of four 16-bit counts packed in one 64-bit word (no
+// field's total exceeds 16 bits); the scratch alternates between two buffers by the caller.
+__device__ __forceinline__ unsigned long long cmp_scan4(unsigned long long v, unsigned long long* ws,
+                                                        unsigned long long* total) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  uint32_t x = v;
+  unsigned long long x = v;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+    const unsigned long long y = __shfl_up_sync(0xffffffffu, x, o);
     if (lane >= o) x += y;
   }
   if (lane == 31) ws[wid] = x;
   cmp_bar();
-  uint32_t off = 0, tot = 0;
+  unsigned long long off = 0, tot = 0;
 #pragma unroll
   for (int w = 0; w < kCmpConsumers / 32; ++w) {
-    const uint32_t c = ws[w];
+    const unsigned long long c = ws[w];
     if (w < wid) off += c;
     tot += c;
   }
@@ -670,7 +672,7 @@ __global__ void __launch_bounds__(kCmpThreads) threshold_compact_kernel(CmpArgs 
   extern __shared__ __align__(128) uint8_t cmp_smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(cmp_smem);
   uint64_t* empty = full + kCmpStages;
-  uint32_t* wsb = reinterpret_cast<uint32_t*>(empty + kCmpStages);  // 2 x 8 words
+  unsigned long long* wsb = reinterpret_cast<unsigned long long*>(empty + kCmpStages);  // 2 x 8
   float* stage = reinterpret_cast<float*>(cmp_smem + 256);
   // a chunk's survivors as (column, score bits) pairs, in column order
   uint2* keep = reinterpret_cast<uint2*>(stage + kCmpStages * kCmpChunk);  // [kCmpChunk]
@@ -721,32 +723,51 @@ __global__ void __launch_bounds__(kCmpThreads) threshold_compact_kernel(CmpArgs 
       const int s = it % kCmpStages;
       // after a failed wait the warp keeps its place in every barrier but stops waiting
       if (ok && !mbar_wait(&full[s], (it / kCmpStages) & 1u, a.err)) ok = false;
-      const float4* src = reinterpret_cast<const float4*>(stage + s * kCmpChunk + threadIdx.x * kCmpPer);
+      // Group q of the chunk is columns [q * 1024, (q + 1) * 1024); thread t takes columns
+      // 4t .. 4t + 3 of each group, so every float4 read of a warp is 512 contiguous bytes
+      // (no bank conflicts).  Column order is (group, thread, element).
+      const float4* src = reinterpret_cast<const float4*>(stage + s * kCmpChunk);
       float v[kCmpPer];
 #pragma unroll
       for (int q = 0; q < kCmpPer / 4; ++q) {
-        const float4 f = src[q];
+        const float4 f = src[q * kCmpConsumers + threadIdx.x];
         v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
       }
-      const int32_t i0 = (int32_t)c0 + (int32_t)threadIdx.x * kCmpPer;
       const int32_t nn = (int32_t)n;
       uint32_t flags = 0;
+      unsigned long long counts = 0;
 #pragma unroll
-      for (int j = 0; j < kCmpPer; ++j)
-        if (i0 + j < nn && v[j] >= tau && v[j] > -INFINITY) flags |= 1u << j;  // NaN fails both
+      for (int q = 0; q < kCmpPer / 4; ++q) {
+        const int32_t col0 = (int32_t)c0 + q * 4 * kCmpConsumers + 4 * (int32_t)threadIdx.x;
+        uint32_t fq = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float x = v[4 * q + e];
+          if (col0 + e < nn && x >= tau && x > -INFINITY) fq |= 1u << e;  // NaN fails both
+        }
+        flags |= fq << (4 * q);
+        counts |= (unsigned long long)__popc(fq) << (16 * q);
+      }
       // release the slot only once every lane's loads have returned (the flags consume them):
       // the next bulk copy into it must not overtake a shared-memory read still in flight
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
-      uint32_t total;
-      uint32_t pos = cmp_scan((uint32_t)__popc(flags), wsb + (parity & 1u) * 8, &total);
+      unsigned long long tot4;
+      const unsigned long long pre4 = cmp_scan4(counts, wsb + (parity & 1u) * 8, &tot4);
       parity ^= 1u;
+      uint32_t total = 0;
 #pragma unroll
-      for (int j = 0; j < kCmpPer; ++j) {
-        if (flags & (1u << j)) {
-          keep[pos] = make_uint2((uint32_t)(i0 + j), __float_as_uint(v[j]));
-          ++pos;
+      for (int q = 0; q < kCmpPer / 4; ++q) {
+        uint32_t pos = total + (uint32_t)((pre4 >> (16 * q)) & 0xffffu);
+        const int32_t col0 = (int32_t)c0 + q * 4 * kCmpConsumers + 4 * (int32_t)threadIdx.x;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          if (flags & (1u << (4 * q + e))) {
+            keep[pos] = make_uint2((uint32_t)(col0 + e), __float_as_uint(v[4 * q + e]));
+            ++pos;
+          }
         }
+        total += (uint32_t)((tot4 >> (16 * q)) & 0xffffu);
       }
       cmp_bar();
       // the chunk's survivors go to positions base .. base + total of the row (up to cap)
