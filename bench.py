@@ -32,6 +32,7 @@ sys.path.insert(0, str(ROOT / "gated-sparse-attention_b200"))
 
 import torch  # noqa: E402
 
+ZIGZAG_FOLDS = 4  # query layout across ranks (gsa_b200.sharded): 2 x folds segments per rank
 WORKLOAD = dict(d_model=4096, n_heads=32, n_kv_heads=8, d_indexer=64, n_indexer_heads=8,
                 k_base=2048, k_min=256, k_max=4096)
 METRIC = "GSA layer fwd tokens/sec at 128K ctx (1/2/4/8 B200); % HBM / tensor roofline"
@@ -169,13 +170,14 @@ def run_ours(args, world, rank):
     if world > 1:
         import torch.distributed as dist
 
-        # zigzag: rank r owns segments r and 2P-1-r of 2P, so causal indexer work is balanced
-        enable_query_sharding(m, dist.group.WORLD, layout="zigzag")
-    assert L % (2 * world) == 0
+        # zigzag with 4 folds: 8 segments per rank dealt in alternating sweeps, which balances the
+        # causal indexer work exactly and the SDPA work (k_t grows with the position) to ~2%
+        enable_query_sharding(m, dist.group.WORLD, layout="zigzag", folds=ZIGZAG_FOLDS)
+    assert L % (2 * ZIGZAG_FOLDS * world) == 0
     Lr = L // world
     gen = torch.Generator().manual_seed(1)
     x_full = torch.randn(1, L, cfg.d_model, generator=gen, dtype=torch.float32)
-    x_host = (zigzag_slice(x_full, world, rank) if world > 1 else x_full).to(torch.bfloat16)
+    x_host = (zigzag_slice(x_full, world, rank, ZIGZAG_FOLDS) if world > 1 else x_full).to(torch.bfloat16)
     x_host = x_host.contiguous().pin_memory()
     del x_full
     x = x_host.to(dev)
@@ -294,7 +296,8 @@ def run_ours(args, world, rank):
         "data": "synthetic: x ~ N(0,1) seed 1, default-init weights seed 0",
         "config": {"workload": f"GSA layer fwd B=1 L={L} d4096 h32/8x128 idx8x64 k2048[256,4096] bf16",
                    "batch": 1, "seq_len": L,
-                   "parallelism": f"query-sequence shards x{world}" + (" (zigzag)" if world > 1 else ""),
+                   "parallelism": f"query-sequence shards x{world}" +
+                                  (f" (zigzag, {ZIGZAG_FOLDS} folds)" if world > 1 else ""),
                    "l2": "inputs larger than L2 (x 1 GiB, K/V 256 MiB each)"},
         "e2e": e2e, "roofline": roofline, "gpu_launches": launches_per_step * args.steps,
         "stages_ms": stages, "clocks": clocks,

@@ -48,27 +48,35 @@ class QueryShards:
     """The layer's view of its process group and of its share of the query sequence.
 
     ``layout="contiguous"``: rank r owns tokens [r*n, (r+1)*n) (n = the local length).
-    ``layout="zigzag"``: the sequence is cut into 2P equal segments and rank r owns segments r and
-    2P-1-r, in that order, so every rank gets the same number of causal (query, key) pairs --
-    with contiguous blocks the last rank does (2P-1)/P^2 of the indexer work.  Zigzag takes a
-    single sequence per call (batch 1)."""
+    ``layout="zigzag"``: the sequence is cut into 2·P·folds equal segments, dealt to the ranks in
+    sweeps that alternate direction (0..P-1, P-1..0, 0..P-1, ...); rank r owns its 2·folds
+    segments in sequence order.  With folds = 1 rank r owns segments r and 2P-1-r: every rank gets
+    the same number of causal (query, key) pairs, where contiguous blocks give the last rank
+    (2P-1)/P^2 of the indexer work.  More folds also even out costs that grow non-linearly along
+    the sequence -- the adaptive k_t, hence the SDPA work, rises with the position (at 128K tokens
+    on 8 ranks the busiest rank's SDPA keys are 1.15x the mean with 1 fold, 1.02x with 4).  Zigzag
+    takes a single sequence per call (batch 1)."""
 
-    def __init__(self, group, layout: str = "contiguous"):
+    def __init__(self, group, layout: str = "contiguous", folds: int = 1):
         if layout not in ("contiguous", "zigzag"):
             raise ValueError(f"unknown layout {layout!r}")
+        if folds < 1:
+            raise ValueError("folds must be >= 1")
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         self.layout = layout
+        self.folds = folds
 
     def segments(self, L_local: int):
         """[(local_start, length, absolute_position_of_first_token)] of this rank's tokens."""
         if self.layout == "contiguous":
             return [(0, L_local, self.rank * L_local)]
-        if L_local % 2:
-            raise ValueError("zigzag sharding needs an even number of local tokens")
-        S = L_local // 2
-        return [(0, S, self.rank * S), (S, S, (2 * self.world - 1 - self.rank) * S)]
+        nseg = 2 * self.folds
+        if L_local % nseg:
+            raise ValueError(f"zigzag sharding needs a multiple of {nseg} local tokens")
+        S = L_local // nseg
+        return [(k * S, S, zigzag_block(k, self.world, self.rank) * S) for k in range(nseg)]
 
     def positions(self, L_local: int, device) -> torch.Tensor:
         return torch.cat([torch.arange(p0, p0 + n, device=device) for _, n, p0 in self.segments(L_local)])
@@ -82,30 +90,37 @@ class QueryShards:
         if self.layout == "contiguous":
             return g
         B, Ll = t.shape[0], t.shape[1]
-        S = Ll // 2
+        nseg = 2 * self.folds
+        S = Ll // nseg
         rest = tuple(t.shape[2:])
-        blocks = g.view((B, self.world, 2, S) + rest)
-        first = blocks[:, :, 0].reshape((B, self.world * S) + rest)            # segments 0..P-1
-        second = blocks[:, :, 1].flip(1).reshape((B, self.world * S) + rest)   # segments P..2P-1
-        return torch.cat([first, second], dim=1)
+        blocks = g.view((B, self.world, nseg, S) + rest)
+        # sweep k holds sequence segments k*P .. k*P+P-1, owned by ranks 0..P-1 (even k) or P-1..0
+        sweeps = [blocks[:, :, k] if k % 2 == 0 else blocks[:, :, k].flip(1) for k in range(nseg)]
+        return torch.cat([sw.reshape((B, self.world * S) + rest) for sw in sweeps], dim=1)
 
     def allreduce(self, t):
         return allreduce_sum(t, self.group)
 
 
-def zigzag_slice(x: torch.Tensor, world: int, rank: int) -> torch.Tensor:
+def zigzag_block(k: int, world: int, rank: int) -> int:
+    """Sequence index of rank's k-th zigzag segment (segments of L / (2 * world * folds) tokens)."""
+    return k * world + (rank if k % 2 == 0 else world - 1 - rank)
+
+
+def zigzag_slice(x: torch.Tensor, world: int, rank: int, folds: int = 1) -> torch.Tensor:
     """This rank's tokens of a full [B, L, ...] sequence under the zigzag layout."""
     L = x.shape[1]
-    if L % (2 * world):
-        raise ValueError(f"sequence length {L} does not split into {2 * world} segments")
-    S = L // (2 * world)
-    a, b = rank, 2 * world - 1 - rank
-    return torch.cat([x[:, a * S:(a + 1) * S], x[:, b * S:(b + 1) * S]], dim=1)
+    nseg = 2 * folds
+    if L % (nseg * world):
+        raise ValueError(f"sequence length {L} does not split into {nseg * world} segments")
+    S = L // (nseg * world)
+    return torch.cat([x[:, zigzag_block(k, world, rank) * S:(zigzag_block(k, world, rank) + 1) * S]
+                      for k in range(nseg)], dim=1)
 
 
-def enable_query_sharding(layer, group=None, layout: str = "contiguous"):
+def enable_query_sharding(layer, group=None, layout: str = "contiguous", folds: int = 1):
     """Make ``layer`` (a GatedSparseAttention) run query-sharded over ``group``: its input is
-    this rank's tokens (a contiguous block, or for ``layout="zigzag"`` the two segments given by
-    :func:`zigzag_slice`) and its output the same tokens."""
-    layer.query_shards = QueryShards(group if group is not None else dist.group.WORLD, layout)
+    this rank's tokens (a contiguous block, or for ``layout="zigzag"`` the segments given by
+    :func:`zigzag_slice` with the same ``folds``) and its output the same tokens."""
+    layer.query_shards = QueryShards(group if group is not None else dist.group.WORLD, layout, folds)
     return layer

@@ -24,7 +24,7 @@ def _port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, layout, q):
+def _worker(rank, world, port, layout, folds, q):
     import sys
     sys.path.insert(0, str(ROOT / "gated-sparse-attention_b200"))
     import torch.distributed as dist
@@ -45,9 +45,9 @@ def _worker(rank, world, port, layout, q):
         x = torch.randn(1, L, cfg.d_model, generator=gen).to(torch.bfloat16).cuda()
         with torch.no_grad():
             ref = m(x)[0] if rank == 0 else None
-            enable_query_sharding(m, dist.group.WORLD, layout)
+            enable_query_sharding(m, dist.group.WORLD, layout, folds)
             Lr = L // world
-            x_local = zigzag_slice(x, world, rank) if layout == "zigzag" else x[:, rank * Lr:(rank + 1) * Lr]
+            x_local = zigzag_slice(x, world, rank, folds) if layout == "zigzag" else x[:, rank * Lr:(rank + 1) * Lr]
             out = m(x_local.contiguous())[0]
             full = m.query_shards.gather(out)
         torch.cuda.synchronize()
@@ -60,14 +60,14 @@ def _worker(rank, world, port, layout, q):
         q.put(("error", repr(e)))
 
 
-@pytest.mark.parametrize("layout", ["contiguous", "zigzag"])
-def test_two_gpu_query_sharding_matches_single_gpu(layout):
+@pytest.mark.parametrize("layout,folds", [("contiguous", 1), ("zigzag", 1), ("zigzag", 4)])
+def test_two_gpu_query_sharding_matches_single_gpu(layout, folds):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, layout, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, layout, folds, q)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:

@@ -63,7 +63,7 @@ def _sharded_oracle_layer(W, cfg, x_local, sp):
     return F.linear(gated.reshape(B, Lr, -1), W["o_proj.weight"]), kv
 
 
-def _worker_equivalence(rank, world, port, layout, q):
+def _worker_equivalence(rank, world, port, layout, folds, q):
     import sys
     for p in (ROOT / "gated-sparse-attention_b200", ROOT / "oracle", ROOT / "tests"):
         sys.path.insert(0, str(p))
@@ -78,9 +78,9 @@ def _worker_equivalence(rank, world, port, layout, q):
         x = x[:1]  # one sequence (the zigzag layout takes one per call)
         W = dict(m.state_dict())
         L = x.shape[1]
-        sp = QueryShards(dist.group.WORLD, layout)
+        sp = QueryShards(dist.group.WORLD, layout, folds)
         if layout == "zigzag":
-            x_local = zigzag_slice(x, world, rank)
+            x_local = zigzag_slice(x, world, rank, folds)
         else:
             s0, s1 = shard_bounds(L, world, rank)
             x_local = x[:, s0:s1]
@@ -98,12 +98,12 @@ def _worker_equivalence(rank, world, port, layout, q):
         q.put(("error", repr(e), -1))
 
 
-@pytest.mark.parametrize("layout", ["contiguous", "zigzag"])
-def test_query_sharded_layer_matches_unsharded(layout):
+@pytest.mark.parametrize("layout,folds", [("contiguous", 1), ("zigzag", 1), ("zigzag", 3)])
+def test_query_sharded_layer_matches_unsharded(layout, folds):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker_equivalence, args=(r, 2, port, layout, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker_equivalence, args=(r, 2, port, layout, folds, q)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
@@ -153,6 +153,9 @@ def test_shard_bounds():
     x = torch.arange(16).view(1, 16)
     assert zigzag_slice(x, 2, 0).tolist() == [[0, 1, 2, 3, 12, 13, 14, 15]]
     assert zigzag_slice(x, 2, 1).tolist() == [[4, 5, 6, 7, 8, 9, 10, 11]]
+    # two folds: 8 segments of 2 dealt 0 1 | 1 0 | 0 1 | 1 0
+    assert zigzag_slice(x, 2, 0, folds=2).tolist() == [[0, 1, 6, 7, 8, 9, 14, 15]]
+    assert zigzag_slice(x, 2, 1, folds=2).tolist() == [[2, 3, 4, 5, 10, 11, 12, 13]]
 
     assert shard_bounds(131072, 8, 7) == (114688, 131072)
     assert shard_bounds(10, 2, 0) == (0, 5)
