@@ -149,6 +149,40 @@ __device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
   return d;
 }
 
+// One (token, key) of the epilogue: y = sum_j (w_j / 2) tanh((scale * acc_j + b_j) / 2), two heads
+// per f32x2 FMA; the score c + y is stored and (y + c - shift) enters the row statistics.  FULL:
+// the tile is unmasked for every token, so no per-token check.
+template <int HI, bool FULL>
+__device__ __forceinline__ void epi_token(const uint32_t* r, uint64_t hs2, const uint64_t* hb2, const float* w_t,
+                                          float2 cd, bool ok, float* dst, float& s1, float& s2) {
+  float th[HI];
+#pragma unroll
+  for (int j = 0; j < HI / 2; ++j) {
+    const uint64_t z2 = ffma2(pack2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])), hs2, hb2[j]);
+    float z0, z1;
+    unpack2(z2, z0, z1);
+    th[2 * j] = tanh_fast(z0);
+    th[2 * j + 1] = tanh_fast(z1);
+  }
+  const float4* w4 = reinterpret_cast<const float4*>(w_t);
+  uint64_t y2 = pack2(0.f, 0.f);
+#pragma unroll
+  for (int j4 = 0; j4 < HI / 4; ++j4) {
+    const float4 w = w4[j4];
+    y2 = ffma2(pack2(w.x, w.y), pack2(th[4 * j4 + 0], th[4 * j4 + 1]), y2);
+    y2 = ffma2(pack2(w.z, w.w), pack2(th[4 * j4 + 2], th[4 * j4 + 3]), y2);
+  }
+  float ya, yb;
+  unpack2(y2, ya, yb);
+  const float y = ya + yb;
+  if (FULL || ok) {
+    *dst = cd.x + y;
+    const float yy = cd.y + y;
+    s1 += yy;
+    s2 = fmaf(yy, yy, s2);
+  }
+}
+
 template <int HI>
 __global__ void __launch_bounds__(kThreads, 1)
     indexer_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ, Params p) {
@@ -176,9 +210,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sB = base;
   uint8_t* sA = base + kBTileBytes;
   float* w_s = reinterpret_cast<float*>(sA + kStages * kATileBytes);  // [TOK][HI] holds w / 2
-  float* c_s = w_s + kN;                                              // [TOK]  c_t = sum_j w_tj / 2
-  float* d_s = c_s + 64;                                              // [TOK]  c_t - shift_t
-  uint64_t* bars = reinterpret_cast<uint64_t*>(d_s + 64);
+  float2* cd_s = reinterpret_cast<float2*>(w_s + kN);                // [TOK]  (c_t = sum_j w_tj / 2, c_t - shift_t)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(cd_s + 64);
   uint64_t* a_full = bars;
   uint64_t* a_empty = bars + kStages;
   uint64_t* b_full = bars + 2 * kStages;
@@ -219,8 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float c = 0.f;
 #pragma unroll
       for (int j = 0; j < HI; ++j) c += w_s[t * HI + j];
-      c_s[t] = c;
-      d_s[t] = (p.shift && t < ntok) ? c - p.shift[tok0 + t] : c;
+      cd_s[t] = make_float2(c, (p.shift && t < ntok) ? c - p.shift[tok0 + t] : c);
     }
   }
   __syncthreads();
@@ -294,38 +326,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&t_empty[buf]);
         }
+        float* srow = p.scores + (int64_t)(tok0 + sub * TOK_Q + c * TOK_PER_LD) * p.ld + key;
+        // (H_I = 4 keeps the one generic loop: eight tokens per load leave no registers for two)
+        if (HI == 8 && tile_full) {
 #pragma unroll
-        for (int tt = 0; tt < TOK_PER_LD; ++tt) {
-          const int tl = c * TOK_PER_LD + tt;       // token within this warp's quarter
-          const int ti = sub * TOK_Q + tl;          // token within the block
-          // z = (scale * acc + b_j) / 2 and y = sum_j (w_j / 2) tanh(z), two heads per f32x2 FMA
-          float th[HI];
-#pragma unroll
-          for (int j = 0; j < HI / 2; ++j) {
-            const uint64_t z2 = ffma2(pack2(__uint_as_float(r[tt * HI + 2 * j]), __uint_as_float(r[tt * HI + 2 * j + 1])),
-                                      hs2, hb2[j]);
-            float z0, z1;
-            unpack2(z2, z0, z1);
-            th[2 * j] = tanh_fast(z0);
-            th[2 * j + 1] = tanh_fast(z1);
+          for (int tt = 0; tt < TOK_PER_LD; ++tt) {
+            const int tl = c * TOK_PER_LD + tt;  // token within this warp's quarter
+            const int ti = sub * TOK_Q + tl;     // token within the block
+            epi_token<HI, true>(r + tt * HI, hs2, hb2, w_s + ti * HI, cd_s[ti], true, srow + tt * p.ld, s1[tl],
+                                s2[tl]);
           }
-          const float4* w4 = reinterpret_cast<const float4*>(w_s + ti * HI);
-          uint64_t y2 = pack2(0.f, 0.f);
+        } else {
 #pragma unroll
-          for (int j4 = 0; j4 < HI / 4; ++j4) {
-            const float4 w = w4[j4];
-            y2 = ffma2(pack2(w.x, w.y), pack2(th[4 * j4 + 0], th[4 * j4 + 1]), y2);
-            y2 = ffma2(pack2(w.z, w.w), pack2(th[4 * j4 + 2], th[4 * j4 + 3]), y2);
-          }
-          float ya, yb;
-          unpack2(y2, ya, yb);
-          const float y = ya + yb;
-          const bool ok = tile_full || (key_ok && ti < ntok && (!p.causal || key <= pos0 + ti));
-          if (ok) {
-            p.scores[(int64_t)(tok0 + ti) * p.ld + key] = c_s[ti] + y;
-            const float yy = d_s[ti] + y;
-            s1[tl] += yy;
-            s2[tl] = fmaf(yy, yy, s2[tl]);
+          for (int tt = 0; tt < TOK_PER_LD; ++tt) {
+            const int tl = c * TOK_PER_LD + tt;
+            const int ti = sub * TOK_Q + tl;
+            const bool ok = key_ok && ti < ntok && (!p.causal || key <= pos0 + ti);
+            epi_token<HI, false>(r + tt * HI, hs2, hb2, w_s + ti * HI, cd_s[ti], ok, srow + tt * p.ld, s1[tl],
+                                 s2[tl]);
           }
         }
       }
