@@ -505,10 +505,14 @@ class GatedSparseAttention(nn.Module):
         kI = proj3[..., layout.ki:layout.ki + dI]
 
         indexer_keys = None
+        kv_finish = None
         if sp is not None:
-            # every rank needs all keys up to its last query: gather K/V and k^I in sequence order
+            # every rank needs all keys up to its last query, in sequence order: k^I now (the
+            # indexer reads it), K/V asynchronously (only the SDPA reads them), so that their
+            # transfer overlaps the indexer
             kI_all = sp.gather(kI)
-            kv_all = sp.gather(kv)
+            kv_finish = sp.gather_async(kv)
+            kv_all = None
             q_pos0 = segs[0][2]
             indexer_keys = kI_all
         elif past_key_value is None:
@@ -529,8 +533,9 @@ class GatedSparseAttention(nn.Module):
                 # a plain (k, v) cache: the reference scores the new tokens only
                 # (gated_sparse_attention.py:197-213), selecting among positions [0, L)
                 kI_all, q_pos0 = kI, 0
-        k_all, v_all = kv_all[:, :, 0], kv_all[:, :, 1]
-        present = GSAKVCache(k_all, v_all, indexer_keys, kv_all) if use_cache else None
+        if kv_finish is None:
+            k_all, v_all = kv_all[:, :, 0], kv_all[:, :, 1]
+            present = GSAKVCache(k_all, v_all, indexer_keys, kv_all) if use_cache else None
         mark("kv")
 
         n_cols = kI_all.shape[1]
@@ -570,6 +575,10 @@ class GatedSparseAttention(nn.Module):
         sel, cnt, mask = ops.select_finalize(cand_idx, cand_score, cand_count, kt, want_mask=output_attentions,
                                              sel_ld=k_eff)
         mark("adaptive_k_select")
+        if kv_finish is not None:
+            kv_all = kv_finish()
+            k_all, v_all = kv_all[:, :, 0], kv_all[:, :, 1]
+            present = GSAKVCache(k_all, v_all, indexer_keys, kv_all) if use_cache else None
         attn = ops.sparse_sdpa(dims, q, k_all, v_all, sel, cnt, g1, self.scale)
         mark("sparse_sdpa")
         out = F.linear(attn.view(B, L, H * D), self.o_proj.weight)

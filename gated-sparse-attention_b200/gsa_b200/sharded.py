@@ -27,16 +27,21 @@ def shard_bounds(L_total: int, world: int, rank: int):
     return rank * n, (rank + 1) * n
 
 
+def _rank_major(buf: torch.Tensor, shape, world: int) -> torch.Tensor:
+    """[world * B, Lr, ...] gathered shards as [B, world * Lr, ...] (rank order)."""
+    B, Lr = shape[0], shape[1]
+    buf = buf.view((world,) + tuple(shape))
+    if B == 1:
+        return buf.view((1, world * Lr) + tuple(shape[2:]))
+    return buf.transpose(0, 1).reshape((B, world * Lr) + tuple(shape[2:]))
+
+
 def gather_sequence(t: torch.Tensor, group, world: int) -> torch.Tensor:
     """All-gather [B, Lr, ...] shards along dim 1 into [B, world * Lr, ...] (rank order)."""
     t = t.contiguous()
-    B, Lr = t.shape[0], t.shape[1]
-    buf = torch.empty((world * B,) + tuple(t.shape[1:]), device=t.device, dtype=t.dtype)
+    buf = torch.empty((world * t.shape[0],) + tuple(t.shape[1:]), device=t.device, dtype=t.dtype)
     dist.all_gather_into_tensor(buf, t, group=group)
-    buf = buf.view((world,) + tuple(t.shape))
-    if B == 1:
-        return buf.view((1, world * Lr) + tuple(t.shape[2:]))
-    return buf.transpose(0, 1).reshape((B, world * Lr) + tuple(t.shape[2:]))
+    return _rank_major(buf, t.shape, world)
 
 
 def allreduce_sum(t: torch.Tensor, group) -> torch.Tensor:
@@ -86,7 +91,23 @@ class QueryShards:
 
     def gather(self, t: torch.Tensor) -> torch.Tensor:
         """All-gather every rank's [B, L_local, ...] tokens into [B, L_total, ...] in sequence order."""
-        g = gather_sequence(t, self.group, self.world)
+        return self._sequence_order(gather_sequence(t, self.group, self.world), t)
+
+    def gather_async(self, t: torch.Tensor):
+        """Start the all-gather of :meth:`gather` and return ``finish()``, which makes the current
+        stream wait for it and returns the same tensor.  The collective runs on NCCL's stream
+        meanwhile, so work queued in between (the indexer, for K and V) overlaps the transfer."""
+        t = t.contiguous()
+        buf = torch.empty((self.world * t.shape[0],) + tuple(t.shape[1:]), device=t.device, dtype=t.dtype)
+        work = dist.all_gather_into_tensor(buf, t, group=self.group, async_op=True)
+
+        def finish():
+            work.wait()
+            return self._sequence_order(_rank_major(buf, t.shape, self.world), t)
+
+        return finish
+
+    def _sequence_order(self, g: torch.Tensor, t: torch.Tensor) -> torch.Tensor:
         if self.layout == "contiguous":
             return g
         B, Ll = t.shape[0], t.shape[1]

@@ -11,7 +11,6 @@ Analysis: GatedLightningIndexer.get_indexer_statistics and
 AdaptiveTopKSelector.get_selection_statistics against the same statistics computed from the
 oracle's scores and k values (gated_indexer.py:157-175, adaptive_topk.py:195-211)."""
 
-
 import pytest
 import torch
 

@@ -114,6 +114,42 @@ def test_query_sharded_layer_matches_unsharded(layout, folds):
     assert kdiff == 0
 
 
+def _worker_async_gather(rank, world, port, q):
+    import sys
+    for p in (ROOT / "gated-sparse-attention_b200",):
+        sys.path.insert(0, str(p))
+    from gsa_b200.sharded import QueryShards
+
+    try:
+        _init(rank, world, port)
+        ok = True
+        for layout, folds in (("contiguous", 1), ("zigzag", 1), ("zigzag", 2)):
+            sp = QueryShards(dist.group.WORLD, layout, folds)
+            t = torch.arange(2 * 8 * 3, dtype=torch.float32).view(2, 8, 3) + 1000 * rank
+            t = t[:1] if layout == "zigzag" else t
+            finish = sp.gather_async(t)
+            ok = ok and torch.equal(finish(), sp.gather(t))
+        q.put(("ok", ok) if rank == 0 else ("rank", ok))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # pragma: no cover - reported to the parent
+        q.put(("error", repr(e)))
+
+
+def test_async_gather_equals_gather():
+    """The asynchronous all-gather the layer uses for K/V returns what the blocking one returns."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_async_gather, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    results = [q.get(timeout=10) for _ in range(2)]
+    assert all(r[0] in ("ok", "rank") and r[1] is True for r in results), results
+
+
 def _worker_failure(rank, world, port, q):
     import sys
     for p in (ROOT / "gated-sparse-attention_b200",):
