@@ -158,6 +158,69 @@ def sdpa_algorithmic_bytes(cfg, cnt: torch.Tensor) -> float:
     return sum_k * (2 * Hk * D * 2 + 4) + rows * 3 * H * D * 2
 
 
+def causal_pairs(first: int, m: int, n_keys: int) -> int:
+    """Sum over query positions first .. first + m - 1 of the keys each sees, min(n_keys, pos + 1)."""
+    m1 = min(m, max(0, n_keys - first))          # rows not yet clipped by n_keys
+    return m1 * (first + 1) + m1 * (m1 - 1) // 2 + (m - m1) * n_keys
+
+
+def indexer_roofline(cap, cfg, pk, chunk_bytes=4 << 30, reps=2):
+    """The tensor-core indexer timed alone over this rank's query segments (the forward's own
+    q^I, k^I, w), chunked like the layer, scores into one reused scratch: algorithmic flops
+    2*H_I*d_I per causal (query, key) pair against the measured bf16 GEMM peak, and its sigmoid
+    (tanh) rate against the MUFU pipe's 16 results / clock / SM at the maximum SM clock."""
+    import ctypes as C
+    from gsa_b200 import _lib, ops
+
+    qI, kI, w, shift = cap["qI"], cap["kI"], cap["w"], cap["shift"]
+    dims, HI, dI = cap["dims"], cfg.n_indexer_heads, cfg.d_indexer
+    B, Lkv = qI.shape[0], kI.shape[1]
+    ld = (Lkv + 3) // 4 * 4
+    rows_max = max(1, chunk_bytes // (4 * ld))
+    scratch = torch.empty(min(rows_max, max(n for _, n, _ in cap["idx_segments"])) * ld, device=qI.device,
+                          dtype=torch.float32)
+    wv = w.reshape(-1, HI).float().contiguous()
+    bias = cap["bias"].float().contiguous()
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    pairs = 0
+    launches = []
+    for l0, n, p0 in cap["idx_segments"]:
+        for t0 in range(0, n, rows_max):
+            m = min(rows_max, n - t0)
+            q = qI[:, l0 + t0:l0 + t0 + m]
+            launches.append((q, m, p0 + t0, l0 + t0))
+            pairs += causal_pairs(p0 + t0, m, Lkv)
+    pairs = pairs * B
+
+    def run():
+        for q, m, qpos, r0 in launches:
+            _lib.call("gsa_indexer_scores", C.byref(dims), ops.dtype_code(q.dtype), 1, m, Lkv, qpos, 1, 0,
+                      C.c_void_p(q.data_ptr()), q.stride(1), 0, C.c_void_p(kI.data_ptr()), kI.stride(1), 0,
+                      C.c_void_p(wv[r0:].data_ptr()), C.c_void_p(bias.data_ptr()), float(cap["idx_scale"]),
+                      C.c_void_p(shift[r0:].data_ptr()), C.c_void_p(scratch.data_ptr()), ld, None, stream)
+
+    run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    flops = 2.0 * HI * dI * pairs
+    achieved = flops / (ms / 1e3) / 1e12
+    tanh_peak = 148 * 16 * pk.get("sm_max_mhz", 1965.0) * 1e6
+    tanh_rate = HI * pairs / (ms / 1e3)
+    return {"kernel": "gsa::tc::indexer_tc_kernel<8>", "bound": "tensor", "achieved": round(achieved, 1),
+            "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": round(achieved / pk["bf16_tflops"], 4),
+            "algorithmic_flops": flops, "kernel_ms": round(ms, 3), "launches": len(launches),
+            "epilogue": {"bound": "mufu", "tanh_per_s": tanh_rate, "peak_tanh_per_s": tanh_peak,
+                         "frac": round(tanh_rate / tanh_peak, 4),
+                         "note": "H_I sigmoids per pair, one tanh.approx each; 16 per clock per SM at the "
+                                 "maximum SM clock"}}
+
+
 def run_ours(args, world, rank):
     from gsa_b200 import GSAConfig, GatedSparseAttention, ops
     from gsa_b200.sharded import enable_query_sharding, zigzag_slice
@@ -288,6 +351,7 @@ def run_ours(args, world, rank):
                 "algorithmic_bytes": sdpa_bytes,
                 "kernel_ms": round(sdpa_ms, 3), "mean_k": float(cap["cnt"].double().mean().item())}
 
+    roofline_indexer = indexer_roofline(cap, cfg, pk)
     clocks = clk.summary()
     res = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
@@ -299,7 +363,8 @@ def run_ours(args, world, rank):
                    "parallelism": f"query-sequence shards x{world}" +
                                   (f" (zigzag, {ZIGZAG_FOLDS} folds)" if world > 1 else ""),
                    "l2": "inputs larger than L2 (x 1 GiB, K/V 256 MiB each)"},
-        "e2e": e2e, "roofline": roofline, "gpu_launches": launches_per_step * args.steps,
+        "e2e": e2e, "roofline": roofline, "roofline_indexer": roofline_indexer,
+        "gpu_launches": launches_per_step * args.steps,
         "stages_ms": stages, "clocks": clocks,
     }
     return res

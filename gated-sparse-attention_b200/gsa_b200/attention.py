@@ -584,6 +584,10 @@ class GatedSparseAttention(nn.Module):
         out = F.linear(attn.view(B, L, H * D), self.o_proj.weight)
         mark("o_proj")
         if capture is not None:
+            # the indexer's inputs and its query segments (local start, rows, first position)
+            capture.update(qI=qI, kI=kI_all, w=w, shift=shift, bias=self.indexer.bias,
+                           idx_scale=self.indexer.scale,
+                           idx_segments=list(segs) if len(segs) > 1 else [(0, L, q_pos0)])
             capture.update(dims=dims, q=q, k=k_all, v=v_all, sel=sel, cnt=cnt, gate=g1, k_t=kt,
                            n_chunks=ops.last_chunk_count, candidate_path="survivors" if survivors else "exact")
 
