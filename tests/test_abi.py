@@ -57,3 +57,36 @@ def test_bad_arguments_are_rejected_before_any_launch():
     assert lib.gsa_apply_gate(7, 0, 10, None, None, None, None, None) == 1
     # empty work is a no-op success
     assert lib.gsa_topk_candidates(0, 1, 10, 0, 0, None, 10, None, None, 4, None, None, None, None) == 0
+
+
+def test_survivor_entry_points_validate_before_any_launch():
+    """gsa_indexer_survivors / gsa_survivors_workspace_size / gsa_select_finalize reject bad
+    arguments without touching the device (CPU only)."""
+    import ctypes as C
+
+    from gsa_b200 import _lib, ops
+
+    lib = _lib.lib()
+    ld = (1000 + 3) // 4 * 4
+    assert lib.gsa_survivors_workspace_size(16, 1000) == ((16 * ld * 4 + 255) // 256) * 256 + 256 + 256
+    assert lib.gsa_survivors_workspace_size(0, 1000) == 0
+    dims = ops.make_dims(4096, 32, 8, 128, 8, 64)
+    relu = ops.make_dims(4096, 32, 8, 128, 8, 64, idx_act="relu")
+    p = C.c_void_p(16)  # a stand-in pointer: every case below returns before using it
+
+    def call(d, k_eff, cap, shift=p, ws_bytes=1 << 40, chunk=16):
+        return lib.gsa_indexer_survivors(C.byref(d), 1, 1, 100, 1000, 0, 1, p, 512, 0, p, 64, 0, p, p, 0.125,
+                                         shift, k_eff, cap, p, p, p, p, chunk, p, ws_bytes, None)
+
+    assert call(dims, 0, 8192) == 1                 # k_eff < 1
+    assert call(dims, 4096, 1024) == 1              # cap < k_eff
+    assert call(dims, 64, 8192, shift=None) == 1    # the row centre is required
+    assert call(dims, 64, 8192, chunk=0) == 1       # no chunk rows
+    assert call(relu, 64, 8192) == 2                # thresholds need the sigmoid indexer
+    assert call(dims, 6000, 8192) == 2              # no room above 1.5 k_eff in the cap
+    assert call(dims, 64, 8192, ws_bytes=100) == 3  # workspace too small
+    # empty work is a no-op success
+    assert lib.gsa_indexer_survivors(C.byref(dims), 1, 1, 0, 1000, 0, 1, p, 512, 0, p, 64, 0, p, p, 0.125, p,
+                                     64, 8192, p, p, p, p, 16, p, 1 << 40, None) == 0
+    assert lib.gsa_select_finalize(4, 0, p, p, p, p, p, 4, p, None, None) == 1   # k_eff < 1
+    assert lib.gsa_select_finalize(4, 8, p, p, p, p, p, 0, p, None, None) == 1   # sel_ld < 1
