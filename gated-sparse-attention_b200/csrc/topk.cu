@@ -604,7 +604,7 @@ constexpr int kCmpConsumers = 256;
 constexpr int kCmpThreads = kCmpConsumers + 32;
 constexpr int kCmpPer = 16;                              // scores per consumer thread per chunk
 constexpr int kCmpChunk = kCmpConsumers * kCmpPer;       // 4096 scores = 16 KiB
-constexpr int kCmpStages = 4;
+constexpr int kCmpStages = 5;
 constexpr float kSurvivorFactor = 1.25f;                 // survivors aimed at per needed key
 constexpr int kCmpSmem = 256 + kCmpStages * kCmpChunk * 4 + kCmpChunk * 8;  // ring + survivor staging
 
