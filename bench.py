@@ -371,6 +371,191 @@ def run_ours(args, world, rank):
 
 
 # ---------------------------------------------------------------------------------------------
+# decode workload: 64 sequences x 65,536 cached tokens, one new token each per step
+# ---------------------------------------------------------------------------------------------
+DECODE_SEQS = 64
+DECODE_CACHED = 65536
+DECODE_METRIC = "GSA layer decode tokens/sec, 64 seqs x 1 new token vs 65,536 cached (B200)"
+
+
+def decode_step_bytes(cfg, n_seqs: int, n_keys: int, cnt: torch.Tensor) -> dict:
+    """Bytes one decode step must move from HBM: the layer's weights (fused projection and
+    o_proj, bf16), every cached indexer key (d_I bf16 per key), the selected K and V rows
+    (Hk*D bf16 each) with their int32 indices, and the per-token vectors (x, q, gate, out)."""
+    H, Hk, D, dI = cfg.n_heads, cfg.n_kv_heads, cfg.d_head, cfg.d_indexer
+    n_cat = H * D + 3 * Hk * D + H * D + cfg.n_indexer_heads * dI + dI + cfg.n_indexer_heads
+    weights = (n_cat + H * D) * cfg.d_model * 2
+    ki = n_seqs * n_keys * dI * 2
+    sum_k = float(cnt.double().sum().item())
+    kv = sum_k * (2 * Hk * D * 2 + 4)
+    vec = n_seqs * (2 * cfg.d_model + 3 * H * D) * 2
+    return {"weights": weights, "indexer_keys": ki, "kv_rows": kv, "vectors": vec,
+            "total": weights + ki + kv + vec}
+
+
+def run_decode(args, world, rank):
+    from gsa_b200 import GSAConfig, GatedSparseAttention, ops
+    from gsa_b200.sharded import enable_sequence_sharding
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    n_cached = args.cached
+    if DECODE_SEQS % world:
+        raise SystemExit(f"{DECODE_SEQS} sequences do not divide over {world} ranks")
+    B = DECODE_SEQS // world
+    total_steps = args.warmup + 2 * args.steps + 2
+    cfg = GSAConfig(**WORKLOAD, max_position_embeddings=n_cached + total_steps + 1)
+    torch.manual_seed(0)
+    m = GatedSparseAttention(cfg).eval().to(torch.bfloat16).to(dev)
+    if world > 1:
+        import torch.distributed as dist
+
+        enable_sequence_sharding(m, dist.group.WORLD)
+    # the cache: N(0,1) K, V and indexer keys (seed 2; this rank's sequences), room for every step
+    cache = m.allocate_cache(B, n_cached + total_steps)
+    g = torch.Generator(device=dev).manual_seed(2 + rank)
+    st = cache.store
+    for b in range(B):
+        st.kv[b, :n_cached].normal_(generator=g)
+        st.ki[b, :n_cached].normal_(generator=g)
+    st.filled = n_cached
+    cache = st.view(n_cached)
+    gen = torch.Generator().manual_seed(1 + rank)
+    x_host = torch.randn(total_steps, B, 1, cfg.d_model, generator=gen).to(torch.bfloat16).pin_memory()
+    xs = x_host.to(dev)
+    torch.cuda.synchronize()
+    it = [0]
+
+    def step(c, x=None):
+        x = xs[it[0]] if x is None else x
+        it[0] += 1
+        with torch.no_grad():
+            out, c, _ = m(x, past_key_value=c, use_cache=True)
+        return out, c
+
+    for _ in range(args.warmup):
+        _, cache = step(cache)
+    torch.cuda.synchronize()
+    ops.check_device_error()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index if world == 1 else int(os.environ.get("LOCAL_RANK", "0"))) as clk:
+        barrier(world)
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(args.steps):
+            _, cache = step(cache)
+        end.record()
+        torch.cuda.synchronize()
+        barrier(world)
+    ms = max_over_ranks(start.elapsed_time(end) / args.steps, world)
+    value = DECODE_SEQS / (ms / 1e3)
+
+    # end to end: each step's token copied from pinned host memory, its output read back
+    out_host = torch.empty(B, 1, cfg.d_model, dtype=torch.bfloat16).pin_memory()
+    barrier(world)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        xd = x_host[it[0]].to(dev, non_blocking=True)
+        out, cache = step(cache, xd)
+        out_host.copy_(out, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    e2e = {"value": DECODE_SEQS / (e2e_ms / 1e3), "unit": "tokens/s",
+           "h2d_bytes_per_step": out_host.numel() * 2 * world, "d2h_bytes_per_step": out_host.numel() * 2 * world,
+           "ms_per_step": e2e_ms}
+
+    # one more step with stage marks and captured selections; kernels timed alone
+    cap, marks = {}, []
+
+    def mark(name):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        marks.append((name, ev))
+
+    n_keys = cache[0].shape[1] + 1
+    with torch.no_grad():
+        e_start = torch.cuda.Event(enable_timing=True)
+        e_start.record()
+        m._forward_impl(xs[it[0]], None, cache, False, False, mark=mark, capture=cap)
+    torch.cuda.synchronize()
+    stages, prev = {}, e_start
+    for name, ev in marks:
+        stages[name] = round(prev.elapsed_time(ev), 4)
+        prev = ev
+    pk, pk_kind = peaks()
+    nbytes = decode_step_bytes(cfg, B, n_keys, cap["cnt"])
+    reps = 20
+
+    def timed(fn):
+        fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps
+
+    import ctypes as C
+    from gsa_b200 import _lib
+
+    qI, kI, w, shift = cap["qI"], cap["kI"], cap["w"], cap["shift"]
+    ld = (n_keys + 3) // 4 * 4
+    scratch = torch.empty(B * ld, device=dev, dtype=torch.float32)
+    wv = w.reshape(-1, cfg.n_indexer_heads).float().contiguous()
+    bias = cap["bias"].float().contiguous()
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def indexer():
+        _lib.call("gsa_indexer_scores", C.byref(cap["dims"]), ops.dtype_code(qI.dtype), B, 1, n_keys, n_keys - 1, 1,
+                  0, C.c_void_p(qI.data_ptr()), qI.stride(1), qI.stride(0), C.c_void_p(kI.data_ptr()), kI.stride(1),
+                  kI.stride(0), C.c_void_p(wv.data_ptr()), C.c_void_p(bias.data_ptr()), float(cap["idx_scale"]),
+                  C.c_void_p(shift.data_ptr()), C.c_void_p(scratch.data_ptr()), ld, None, stream)
+
+    def sdpa():
+        ops.sparse_sdpa(cap["dims"], cap["q"], cap["k"], cap["v"], cap["sel"], cap["cnt"], cap["gate"], m.scale)
+
+    with torch.no_grad():
+        idx_ms = timed(indexer)
+        sdpa_ms = timed(sdpa)
+    hbm = pk["hbm_gbs"]
+
+    def rl(name, b, t_ms):
+        a = b / (t_ms / 1e3) / 1e9
+        return {"kernel": name, "bound": "hbm", "achieved": round(a, 1), "peak": hbm, "unit": "GB/s",
+                "frac": round(a / hbm, 4), "peak_kind": pk_kind, "algorithmic_bytes": b, "kernel_ms": round(t_ms, 4)}
+
+    roofline = rl("decode step (all kernels and GEMMs, device time per step)", nbytes["total"], ms)
+    roofline["traffic"] = None
+    roofline["bytes"] = nbytes
+    parts = {"indexer": rl("gsa::dec::indexer_decode_kernel<8,1,4>", nbytes["indexer_keys"], idx_ms),
+             "sdpa": rl("gsa::sdpa_tc_kernel<128,4>", nbytes["kv_rows"] + B * 3 * cfg.n_heads * cfg.d_head * 2,
+                        sdpa_ms)}
+    # our kernels per step (one gsa_decode_attend call): projection epilogue, decode indexer,
+    # survivor compaction + exact fallback, row variance (2) + adaptive k, final selection, split
+    # SDPA + merge
+    launches_per_step = 1 + 1 + 2 + (3 if cfg.use_adaptive_k else 1) + 1 + 2
+    return {
+        "metric": DECODE_METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: cache K, V, k^I ~ N(0,1) seed 2, new tokens x ~ N(0,1) seed 1, default-init weights seed 0",
+        "config": {"workload": f"GSA layer decode {DECODE_SEQS} seqs x 1 token vs {n_cached}+ cached "
+                               "d4096 h32/8x128 idx8x64 k2048[256,4096] bf16",
+                   "batch": DECODE_SEQS, "cached": n_cached, "parallelism": f"sequence shards x{world}",
+                   "l2": "inputs larger than L2 (cache 17 GB)"},
+        "e2e": e2e, "roofline": roofline, "roofline_kernels": parts, "mean_k": float(cap["cnt"].double().mean()),
+        "gpu_launches": launches_per_step * args.steps, "stages_ms": stages, "clocks": clk.summary(),
+    }
+
+
+# ---------------------------------------------------------------------------------------------
 # CPU path of the reference algorithm (oracle restatement), sampled and extrapolated
 # ---------------------------------------------------------------------------------------------
 def cpu_reference_estimate(L: int, proj_rows: int, chunk_rows: int, n_chunks: int, seed: int = 0):
@@ -450,8 +635,79 @@ def cpu_reference_estimate(L: int, proj_rows: int, chunk_rows: int, n_chunks: in
     return est, desc
 
 
+def cpu_decode_estimate(n_cached: int, n_sample: int = 4, seed: int = 0):
+    """Seconds for one step of the 64-sequence decode workload on the host cores, timed with the
+    oracle's restatement of the reference's torch ops (bf16, torch.no_grad): the projections,
+    gates and o_proj for all 64 new tokens; the indexer over every cached key, the variance,
+    top-k and sparse attention for ``n_sample`` sequences, scaled by 64 / n_sample.
+    Returns (seconds, description)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import torch.nn.functional as F
+
+    import gsa_oracle as O
+
+    torch.set_num_threads(len(os.sched_getaffinity(0)))
+    from gsa_b200 import GSAConfig, GatedSparseAttention
+
+    cfg = GSAConfig(**WORKLOAD, max_position_embeddings=n_cached + 8)
+    torch.manual_seed(seed)
+    m = GatedSparseAttention(cfg).eval().to(torch.bfloat16)
+    W = {k: v for k, v in m.state_dict().items()}
+    oc = O.OracleConfig.from_config(cfg)
+    gen = torch.Generator().manual_seed(2)
+    dt = torch.bfloat16
+    H, Hk, D, HI, dI = cfg.n_heads, cfg.n_kv_heads, cfg.d_head, cfg.n_indexer_heads, cfg.d_indexer
+    S, n = n_sample, n_cached + 1
+    with torch.no_grad():
+        K = torch.randn(S, n, Hk, D, generator=gen).to(dt)
+        V = torch.randn(S, n, Hk, D, generator=gen).to(dt)
+        kI = torch.randn(S, n, dI, generator=gen).to(dt)
+        x = torch.randn(DECODE_SEQS, 1, cfg.d_model, generator=gen).to(dt)
+        pos = torch.full((DECODE_SEQS, 1), n_cached)
+        t0 = time.perf_counter()
+        q, k, v = O.project(W, oc, x, pos, m.rotary_emb.cos_cached, m.rotary_emb.sin_cached)
+        q_idx = F.linear(x, W["indexer.q_proj.weight"]).view(DECODE_SEQS, 1, HI, dI)
+        k_new = F.linear(x, W["indexer.k_proj.weight"])
+        wts = torch.sigmoid(F.linear(x, W["indexer.weight_proj.weight"], W["indexer.weight_proj.bias"]))
+        g1 = O.gate_activation(F.linear(x, W["output_gate.gate_proj.weight"],
+                                        W["output_gate.gate_proj.bias"]).view(DECODE_SEQS, 1, H, D), "sigmoid")
+        F.linear((q * g1).reshape(DECODE_SEQS, 1, -1), W["o_proj.weight"])
+        t_dense = time.perf_counter() - t0
+        t1 = time.perf_counter()
+        K[:, -1:], V[:, -1:], kI[:, -1:] = k[:S], v[:S], k_new[:S]
+        sc = O.indexer_scores_from_proj(q_idx[:S], kI, wts[:S], W["indexer.bias"], "sigmoid", q_offset=n_cached)
+        var, valid = O.row_variance(sc)
+        k_t = O.adaptive_k(var, valid, var.mean(), cfg.k_base, cfg.k_min, cfg.k_max, 1.0)
+        idx, msk = O.topk_select(sc, min(cfg.k_max, n), k_t)
+        O.sparse_attention(q[:S], K, V, idx, msk, H // Hk, 1.0 / math.sqrt(D))
+        t_seq = (time.perf_counter() - t1) * DECODE_SEQS / S
+    desc = (f"projections/gates/o_proj for all {DECODE_SEQS} tokens; indexer over {n} keys, variance, "
+            f"top-k and sparse attention for {S} sequences x {DECODE_SEQS}/{S}")
+    return t_dense + t_seq, desc
+
+
 def run_reference(args, world, rank):
     """Reference arm: the reference algorithm's CPU path, timed on this box's host cores."""
+    if args.workload == "decode":
+        samples, desc = [], ""
+        for i in range(args.warmup + args.steps):
+            sec, desc = cpu_decode_estimate(args.cached)
+            if i >= args.warmup:
+                samples.append(sec)
+        sec = statistics.median(samples)
+        v = DECODE_SEQS / sec
+        cores = len(os.sched_getaffinity(0))
+        return {"metric": DECODE_METRIC, "value": round(v, 3), "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 1),
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic: cache ~ N(0,1), x ~ N(0,1), default-init weights seed 0",
+                "config": {"workload": f"GSA layer decode {DECODE_SEQS} seqs x 1 token vs {args.cached} cached "
+                                       "d4096 h32/8x128 idx8x64 k2048[256,4096] bf16",
+                           "batch": DECODE_SEQS, "cached": args.cached, "parallelism": "host CPU"},
+                "impl": "reference",
+                "cpu_baseline": {"value": round(v, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
+                                 "sample": desc},
+                "e2e": {"value": round(v, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     L = args.seq_len
     samples = []
     desc = ""
@@ -475,10 +731,31 @@ def run_reference(args, world, rank):
 
 
 def run_launch_list(args):
-    """N untimed forwards of the 1-GPU workload at --seq-len, for kernel profilers."""
+    """N untimed forwards of the 1-GPU workload at --seq-len (or N decode steps against
+    --cached tokens), for kernel profilers."""
     from gsa_b200 import GSAConfig, GatedSparseAttention, ops
 
     torch.cuda.set_device(0)
+    if args.workload == "decode":
+        cfg = GSAConfig(**WORKLOAD, max_position_embeddings=args.cached + args.launch_list + 1)
+        torch.manual_seed(0)
+        m = GatedSparseAttention(cfg).eval().to(torch.bfloat16).cuda()
+        cache = m.allocate_cache(DECODE_SEQS, args.cached + args.launch_list)
+        st = cache.store
+        g = torch.Generator(device="cuda").manual_seed(2)
+        st.kv[:, :args.cached].normal_(generator=g)
+        st.ki[:, :args.cached].normal_(generator=g)
+        st.filled = args.cached
+        cache = st.view(args.cached)
+        x = torch.randn(DECODE_SEQS, 1, cfg.d_model, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16)
+        x = x.cuda()
+        with torch.no_grad():
+            for _ in range(args.launch_list):
+                _, cache, _ = m(x, past_key_value=cache, use_cache=True)
+        torch.cuda.synchronize()
+        ops.check_device_error()
+        log(f"launch list: {args.launch_list} decode steps against {args.cached} cached tokens done")
+        return
     L = args.seq_len
     cfg = GSAConfig(**WORKLOAD, max_position_embeddings=max(131072, L))
     torch.manual_seed(0)
@@ -503,6 +780,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--launch-list", type=int, default=0, metavar="N",
                     help="run N untimed forwards and exit (a short command for profilers)")
+    ap.add_argument("--workload", default="prefill", choices=["prefill", "decode"],
+                    help="prefill: one 131072-token sequence; decode: 64 sequences x 1 token vs 65,536 cached")
+    ap.add_argument("--cached", type=int, default=DECODE_CACHED, help="decode: cached tokens per sequence")
     args = ap.parse_args()
     if args.launch_list:
         return run_launch_list(args)
@@ -520,6 +800,15 @@ def main():
 
     world, rank, local = dist_setup(args.gpus)
     try:
+        if args.workload == "decode":
+            res = run_decode(args, world, rank)
+            if rank == 0 and world == 1 and not args.no_cpu_baseline:
+                sec, desc = cpu_decode_estimate(args.cached)
+                res["cpu_baseline"] = {"value": round(DECODE_SEQS / sec, 3), "unit": "tokens/s",
+                                       "cores": len(os.sched_getaffinity(0)), "kind": "port", "sample": desc}
+            if rank == 0:
+                print(json.dumps(res))
+            return
         res = run_ours(args, world, rank)
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             est, desc = cpu_reference_estimate(args.seq_len, proj_rows=128, chunk_rows=16, n_chunks=2)

@@ -39,6 +39,39 @@ static int device_info(DeviceInfo** out) {
 
 static bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// Query chunks of at most ``rows`` rows for the indexer passes.  Lq <= rows: whole sequences,
+// nb of them from sequence b0 (n = Lq rows each), so that short rows (decode) of many sequences
+// share one launch; otherwise rows [t0, t0 + n) of the single sequence b0 (nb = 1).
+struct ChunkIter {
+  int64_t B, Lq, rows;
+  int64_t b0 = 0, nb = 0, t0 = 0, n = 0;
+  bool started = false;
+  ChunkIter(int64_t B_, int64_t Lq_, int64_t rows_) : B(B_), Lq(Lq_), rows(rows_) {}
+  bool next() {
+    if (Lq <= rows) {
+      if (started) b0 += nb;
+      started = true;
+      if (b0 >= B) return false;
+      nb = std::min(rows / Lq, B - b0);
+      t0 = 0;
+      n = Lq;
+      return true;
+    }
+    if (started) {
+      t0 += n;
+      if (t0 >= Lq) {
+        t0 = 0;
+        ++b0;
+      }
+    }
+    started = true;
+    if (b0 >= B) return false;
+    nb = 1;
+    n = std::min(rows, Lq - t0);
+    return true;
+  }
+};
+
 static bool dims_ok(const gsa_dims* d) {
   return d && d->d_model > 0 && d->n_heads > 0 && d->n_kv_heads > 0 && d->n_heads % d->n_kv_heads == 0 &&
          d->d_head > 0 && d->d_head % 2 == 0 && d->n_idx_heads > 0 && d->d_idx > 0;
@@ -87,6 +120,30 @@ int gsa_proj_epilogue(const gsa_dims* dims, const gsa_proj_layout* layout, int d
   return launch_proj_epilogue(a, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int gsa_proj_epilogue_cache(const gsa_dims* dims, const gsa_proj_layout* layout, int dtype, int64_t B, int64_t L,
+                            const void* proj, int64_t proj_ld, const int64_t* positions, const void* cos_tab,
+                            const void* sin_tab, int tab_dtype, int64_t tab_rows, void* q_out, void* k_out,
+                            void* v_out, int64_t kv_ld, int64_t kv_bstride, void* ki_out, int64_t ki_ld,
+                            int64_t ki_bstride, void* g1_out, float* w_out, float* shift_out, gsa_stream_t stream) {
+  if (!dims_ok(dims) || !layout || B < 0 || L < 0 || (dtype != GSA_DTYPE_F32 && dtype != GSA_DTYPE_BF16) ||
+      (tab_dtype != GSA_DTYPE_F32 && tab_dtype != GSA_DTYPE_BF16))
+    return GSA_ERR_BAD_ARG;
+  if (B * L == 0) return GSA_OK;
+  if (!proj || !positions || !cos_tab || !sin_tab || !q_out || !k_out || !v_out || !w_out || !shift_out ||
+      tab_rows <= 0 || layout->q < 0 || layout->k < 0 || layout->v < 0 || layout->wi < 0)
+    return GSA_ERR_BAD_ARG;
+  if (dims->gate_act < GSA_ACT_SIGMOID || dims->gate_act > GSA_ACT_SILU) return GSA_ERR_UNSUPPORTED;
+  if (kv_ld < (int64_t)dims->n_kv_heads * dims->d_head || kv_bstride < L * kv_ld) return GSA_ERR_BAD_ARG;
+  if (ki_out && (layout->ki < 0 || ki_ld < dims->d_idx || ki_bstride < L * ki_ld)) return GSA_ERR_BAD_ARG;
+  DeviceInfo* di;
+  int st = device_info(&di);
+  if (st) return st;
+  EpiArgs a{*dims, *layout, dtype, B * L, proj, proj_ld, positions, cos_tab, sin_tab, tab_dtype, tab_rows,
+            q_out, k_out, v_out, kv_ld, g1_out, w_out, shift_out, di->err, L, kv_bstride, ki_out, ki_ld,
+            ki_bstride};
+  return launch_proj_epilogue(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
 int gsa_indexer_scores(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int64_t Lkv, int64_t q_pos0,
                        int causal, int write_masked, const void* qI, int64_t qi_ld, int64_t qi_bstride,
                        const void* kI, int64_t ki_ld, int64_t ki_bstride, const float* w, const float* bias,
@@ -100,6 +157,13 @@ int gsa_indexer_scores(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, i
   IdxArgs a{dtype, Lq, Lkv, q_pos0, causal, write_masked, dims->n_idx_heads, dims->d_idx, dims->idx_act,
             qI, qi_ld, qi_bstride, kI, ki_ld, ki_bstride, w, bias, scale, shift, scores, scores_ld, row_stats};
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (indexer_decode_eligible(a, B)) {
+    // a few tokens per sequence (decode): every sequence in one launch, streaming k^I once
+    DeviceInfo* di;
+    int st = device_info(&di);
+    if (st) return st;
+    return launch_indexer_decode(a, B, di->num_sms, s);
+  }
   if (indexer_tc_eligible(a)) {
     // tensor-core kernel: bf16, d_I = 64, H_I in {4, 8}, sigmoid; one launch per batch row
     DeviceInfo* di;
@@ -169,12 +233,15 @@ int gsa_select_finalize(int64_t R, int32_t k_eff, const int32_t* cand_idx, const
   if (R == 0) return GSA_OK;
   if (!cand_idx || !cand_score || !cand_count || !k || !sel_idx || !sel_count) return GSA_ERR_BAD_ARG;
   if (!sel_mask) {
-    // one warp per row (the selection mask needs the per-row CTA kernel)
+    // one warp per row when the rows fill the GPU; few rows (decode) take a CTA each, since a
+    // row's passes over its candidates are latency-bound on one warp (the selection mask needs
+    // the per-row CTA kernel as well)
     DeviceInfo* di;
     int st = device_info(&di);
     if (st) return st;
-    return launch_select_finalize_warp(R, k_eff, cand_idx, cand_score, cand_count, k, sel_idx, sel_ld, sel_count,
-                                       di->num_sms, reinterpret_cast<cudaStream_t>(stream));
+    if (R >= 2LL * di->num_sms)
+      return launch_select_finalize_warp(R, k_eff, cand_idx, cand_score, cand_count, k, sel_idx, sel_ld, sel_count,
+                                         di->num_sms, reinterpret_cast<cudaStream_t>(stream));
   }
   return launch_select_finalize(R, k_eff, cand_idx, cand_score, cand_count, k, sel_idx, sel_ld, sel_count,
                                 sel_mask, reinterpret_cast<cudaStream_t>(stream));
@@ -192,31 +259,53 @@ int gsa_apply_gate(int dtype, int act, int64_t n, const void* x, const void* log
 int gsa_sparse_sdpa(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int64_t Lkv, const void* q,
                     const void* k, const void* v, int64_t kv_ld, const int32_t* sel_idx, int64_t sel_ld,
                     const int32_t* sel_count, const void* gate, void* out, float scale, gsa_stream_t stream) {
+  return gsa_sparse_sdpa_strided(dims, dtype, B, Lq, Lkv, q, k, v, kv_ld, Lkv * kv_ld, sel_idx, sel_ld, sel_count,
+                                 gate, out, scale, nullptr, 0, stream);
+}
+
+int64_t gsa_sdpa_workspace_size(const gsa_dims* dims, int64_t B, int64_t Lq) {
+  if (!dims_ok(dims) || B <= 0 || Lq <= 0) return 0;
+  DeviceInfo* di;
+  if (device_info(&di)) return 0;
+  const int64_t R = B * Lq, slots = 2LL * di->num_sms;
+  if (R >= slots) return 0;
+  const int64_t splits = std::min<int64_t>(slots / R, 8);
+  if (splits < 2) return 0;
+  return R * splits * (int64_t)dims->n_heads * (dims->d_head + 1) * (int64_t)sizeof(float);
+}
+
+int gsa_sparse_sdpa_strided(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int64_t Lkv, const void* q,
+                            const void* k, const void* v, int64_t kv_ld, int64_t kv_bstride, const int32_t* sel_idx,
+                            int64_t sel_ld, const int32_t* sel_count, const void* gate, void* out, float scale,
+                            void* workspace, int64_t workspace_bytes, gsa_stream_t stream) {
   if (!dims_ok(dims) || B < 0 || Lq < 0 || Lkv < 0 || sel_ld < 0) return GSA_ERR_BAD_ARG;
   if (B * Lq == 0) return GSA_OK;
   if (!q || !k || !v || !sel_idx || !sel_count || !out) return GSA_ERR_BAD_ARG;
   const int64_t row_elems = (int64_t)dims->n_kv_heads * dims->d_head;
-  if (kv_ld < row_elems) return GSA_ERR_BAD_ARG;
+  if (kv_ld < row_elems || kv_bstride < Lkv * kv_ld) return GSA_ERR_BAD_ARG;
   DeviceInfo* di;
   int st = device_info(&di);
   if (st) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == GSA_DTYPE_BF16) {
-    if (!aligned(k, 16) || !aligned(v, 16) || !aligned(q, 4) || (kv_ld * 2) % 16 != 0) return GSA_ERR_BAD_ARG;
+    if (!aligned(k, 16) || !aligned(v, 16) || !aligned(q, 4) || (kv_ld * 2) % 16 != 0 || (kv_bstride * 2) % 16 != 0)
+      return GSA_ERR_BAD_ARG;
     const bool inter = kv_ld == 2 * row_elems &&
                        static_cast<const __nv_bfloat16*>(v) == static_cast<const __nv_bfloat16*>(k) + row_elems;
     SdpaArgs a{B, Lq, Lkv, dims->n_kv_heads,
                static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
                static_cast<const __nv_bfloat16*>(v), kv_ld, inter ? 1 : 0, sel_idx, sel_ld, sel_count,
                static_cast<const __nv_bfloat16*>(gate), static_cast<__nv_bfloat16*>(out),
-               scale * 1.4426950408889634f, 0, 2, di->err};
+               scale * 1.4426950408889634f, 0, 2, di->err, kv_bstride, 1,
+               (workspace && aligned(workspace, 16)) ? static_cast<float*>(workspace) : nullptr,
+               workspace ? workspace_bytes / (int64_t)sizeof(float) : 0};
     return launch_sdpa_bf16(a, dims->d_head, dims->n_heads / dims->n_kv_heads, di->num_sms, s);
   }
   if (dtype == GSA_DTYPE_F32) {
     SdpaF32Args a{B, Lq, Lkv, dims->n_heads, dims->n_kv_heads, dims->d_head,
                   static_cast<const float*>(q), static_cast<const float*>(k), static_cast<const float*>(v),
                   kv_ld, sel_idx, sel_ld, sel_count, static_cast<const float*>(gate), static_cast<float*>(out),
-                  scale, di->err};
+                  scale, di->err, kv_bstride};
     return launch_sdpa_f32(a, s);
   }
   return GSA_ERR_BAD_ARG;
@@ -242,23 +331,20 @@ int gsa_indexer_select(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, i
   float* scratch = static_cast<float*>(workspace);
   const size_t esz = dtype == GSA_DTYPE_BF16 ? 2 : 4;
   const int HI = dims->n_idx_heads;
-  for (int64_t b = 0; b < B; ++b) {
-    for (int64_t t0 = 0; t0 < Lq; t0 += chunk_rows) {
-      const int64_t n = (Lq - t0) < chunk_rows ? (Lq - t0) : chunk_rows;
-      const int64_t r0 = b * Lq + t0;
-      const void* q_ptr = static_cast<const char*>(qI) + (b * qi_bstride + t0 * qi_ld) * (int64_t)esz;
-      const void* k_ptr = static_cast<const char*>(kI) + (b * ki_bstride) * (int64_t)esz;
-      int st = gsa_indexer_scores(dims, dtype, 1, n, Lkv, q_pos0 + t0, causal, 0, q_ptr, qi_ld, 0, k_ptr, ki_ld,
-                                  0, w + r0 * HI, bias, scale, shift ? shift + r0 : nullptr, scratch, ld,
-                                  row_stats ? row_stats + r0 * 3 : nullptr, stream);
-      if (st) return st;
-      // sigmoid scores of row r lie in [0, sum_j w_rj] = [0, 2 shift_r]: the bounded-range selection
-      const float* center = (shift && dims->idx_act == GSA_ACT_SIGMOID) ? shift + r0 : nullptr;
-      st = gsa_topk_candidates(n, n, Lkv, q_pos0 + t0, causal, scratch, ld, center,
-                               (center && row_stats) ? row_stats + r0 * 3 : nullptr, k_eff,
-                               cand_idx + r0 * k_eff, cand_score + r0 * k_eff, cand_count + r0, stream);
-      if (st) return st;
-    }
+  for (ChunkIter c(B, Lq, chunk_rows); c.next();) {
+    const int64_t r0 = c.b0 * Lq + c.t0, n = c.nb * c.n;
+    const void* q_ptr = static_cast<const char*>(qI) + (c.b0 * qi_bstride + c.t0 * qi_ld) * (int64_t)esz;
+    const void* k_ptr = static_cast<const char*>(kI) + (c.b0 * ki_bstride) * (int64_t)esz;
+    int st = gsa_indexer_scores(dims, dtype, c.nb, c.n, Lkv, q_pos0 + c.t0, causal, 0, q_ptr, qi_ld, qi_bstride,
+                                k_ptr, ki_ld, ki_bstride, w + r0 * HI, bias, scale, shift ? shift + r0 : nullptr,
+                                scratch, ld, row_stats ? row_stats + r0 * 3 : nullptr, stream);
+    if (st) return st;
+    // sigmoid scores of row r lie in [0, sum_j w_rj] = [0, 2 shift_r]: the bounded-range selection
+    const float* center = (shift && dims->idx_act == GSA_ACT_SIGMOID) ? shift + r0 : nullptr;
+    st = gsa_topk_candidates(n, c.n, Lkv, q_pos0 + c.t0, causal, scratch, ld, center,
+                             (center && row_stats) ? row_stats + r0 * 3 : nullptr, k_eff,
+                             cand_idx + r0 * k_eff, cand_score + r0 * k_eff, cand_count + r0, stream);
+    if (st) return st;
   }
   return GSA_OK;
 }
@@ -297,21 +383,157 @@ int gsa_indexer_survivors(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq
   const size_t esz = dtype == GSA_DTYPE_BF16 ? 2 : 4;
   const int HI = dims->n_idx_heads;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  for (int64_t b = 0; b < B; ++b) {
-    for (int64_t t0 = 0; t0 < Lq; t0 += chunk_rows) {
-      const int64_t n = (Lq - t0) < chunk_rows ? (Lq - t0) : chunk_rows;
-      const int64_t r0 = b * Lq + t0;
-      const void* q_ptr = static_cast<const char*>(qI) + (b * qi_bstride + t0 * qi_ld) * (int64_t)esz;
-      const void* k_ptr = static_cast<const char*>(kI) + (b * ki_bstride) * (int64_t)esz;
-      st = gsa_indexer_scores(dims, dtype, 1, n, Lkv, q_pos0 + t0, causal, 0, q_ptr, qi_ld, 0, k_ptr, ki_ld, 0,
-                              w + r0 * HI, bias, scale, shift + r0, scratch, ld, row_stats + r0 * 3, stream);
-      if (st) return st;
-      st = launch_threshold_candidates(n, n, Lkv, q_pos0 + t0, causal, scratch, ld, shift + r0, row_stats + r0 * 3,
-                                       k_eff, cap, cand_idx + r0 * cap, cand_score + r0 * cap, cand_count + r0,
-                                       fail_list, fail_count, di->num_sms, di->err, s);
-      if (st) return st;
-    }
+  for (ChunkIter c(B, Lq, chunk_rows); c.next();) {
+    const int64_t r0 = c.b0 * Lq + c.t0, n = c.nb * c.n;
+    const void* q_ptr = static_cast<const char*>(qI) + (c.b0 * qi_bstride + c.t0 * qi_ld) * (int64_t)esz;
+    const void* k_ptr = static_cast<const char*>(kI) + (c.b0 * ki_bstride) * (int64_t)esz;
+    st = gsa_indexer_scores(dims, dtype, c.nb, c.n, Lkv, q_pos0 + c.t0, causal, 0, q_ptr, qi_ld, qi_bstride, k_ptr,
+                            ki_ld, ki_bstride, w + r0 * HI, bias, scale, shift + r0, scratch, ld, row_stats + r0 * 3,
+                            stream);
+    if (st) return st;
+    st = launch_threshold_candidates(n, c.n, Lkv, q_pos0 + c.t0, causal, scratch, ld, shift + r0, row_stats + r0 * 3,
+                                     k_eff, cap, cand_idx + r0 * cap, cand_score + r0 * cap, cand_count + r0,
+                                     fail_list, fail_count, di->num_sms, di->err, s);
+    if (st) return st;
   }
+  return GSA_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// One decode step between the two GEMMs
+// ---------------------------------------------------------------------------------------------
+namespace gsa {
+
+constexpr int32_t kSurvivorCap = 8192;  // candidate row of the threshold-survivor pass
+
+// Byte offsets of the scratch tensors of gsa_decode_attend inside its workspace.
+struct DecodeLayout {
+  int64_t q, g1, w, shift, stats, var, total, kt, cidx, cscore, ccount, idx_ws, idx_ws_bytes, sel, scount,
+      sdpa_ws, sdpa_ws_bytes, bytes;
+  int32_t k_eff, cand_ld;
+  bool survivors;
+};
+
+static DecodeLayout decode_layout(const gsa_dims* d, const gsa_topk_params* tp, int dtype, int64_t B, int64_t L,
+                                  int64_t n_keys) {
+  DecodeLayout o;
+  const int64_t R = B * L, H = d->n_heads, D = d->d_head, HI = d->n_idx_heads;
+  const int64_t esz = dtype == GSA_DTYPE_BF16 ? 2 : 4;
+  int64_t k_eff = std::min<int64_t>(tp->use_adaptive ? tp->k_max : tp->k_base, n_keys);
+  if (k_eff < 1) k_eff = 1;
+  o.k_eff = (int32_t)k_eff;
+  o.survivors = d->idx_act == GSA_ACT_SIGMOID && 2LL * kSurvivorCap >= 3 * k_eff + 2048;
+  o.cand_ld = o.survivors ? kSurvivorCap : o.k_eff;
+  int64_t off = 0;
+  auto take = [&](int64_t bytes) {
+    const int64_t p = off;
+    off += align256(bytes);
+    return p;
+  };
+  o.q = take(R * H * D * esz);
+  o.g1 = take(R * H * D * esz);
+  o.w = take(R * HI * 4);
+  o.shift = take(R * 4);
+  o.stats = take(R * 3 * 8);
+  o.var = take(R * 4);
+  o.total = take(16);
+  o.kt = take(R * 4);
+  o.cidx = take(R * o.cand_ld * 4);
+  o.cscore = take(R * o.cand_ld * 4);
+  o.ccount = take(R * 4);
+  o.idx_ws_bytes = o.survivors ? gsa_survivors_workspace_size(R, n_keys) : gsa_workspace_size(R, n_keys);
+  o.idx_ws = take(o.idx_ws_bytes);
+  o.sel = take(R * k_eff * 4);
+  o.scount = take(R * 4);
+  o.sdpa_ws_bytes = dtype == GSA_DTYPE_BF16 ? gsa_sdpa_workspace_size(d, B, L) : 0;
+  o.sdpa_ws = take(o.sdpa_ws_bytes);
+  o.bytes = off;
+  return o;
+}
+
+}  // namespace gsa
+
+extern "C" {
+
+int64_t gsa_decode_workspace_size(const gsa_dims* dims, const gsa_topk_params* tp, int dtype, int64_t B, int64_t L,
+                                  int64_t n_keys) {
+  if (!dims_ok(dims) || !tp || B <= 0 || L <= 0 || n_keys < L || (dtype != GSA_DTYPE_F32 && dtype != GSA_DTYPE_BF16))
+    return 0;
+  return decode_layout(dims, tp, dtype, B, L, n_keys).bytes;
+}
+
+int gsa_decode_attend(const gsa_dims* dims, const gsa_proj_layout* layout, const gsa_topk_params* tp, int dtype,
+                      int64_t B, int64_t L, int64_t past, const void* proj, int64_t proj_ld,
+                      const int64_t* positions, const void* cos_tab, const void* sin_tab, int tab_dtype,
+                      int64_t tab_rows, void* kv_store, int64_t kv_bstride, void* ki_store, int64_t ki_bstride,
+                      const float* idx_bias, float idx_scale, float attn_scale, void* attn_out, int32_t* k_out,
+                      void* workspace, int64_t workspace_bytes, gsa_stream_t stream) {
+  if (!dims_ok(dims) || !layout || !tp || B < 0 || L < 0 || past < 0 ||
+      (dtype != GSA_DTYPE_F32 && dtype != GSA_DTYPE_BF16) || (tab_dtype != GSA_DTYPE_F32 && tab_dtype != GSA_DTYPE_BF16))
+    return GSA_ERR_BAD_ARG;
+  if (B * L == 0) return GSA_OK;
+  if (!proj || !cos_tab || !sin_tab || !kv_store || !ki_store || !idx_bias || !attn_out || tab_rows <= 0 ||
+      layout->q < 0 || layout->k < 0 || layout->v < 0 || layout->qi < 0 || layout->ki < 0 || layout->wi < 0)
+    return GSA_ERR_BAD_ARG;
+  if (dims->gate_act < GSA_ACT_SIGMOID || dims->gate_act > GSA_ACT_SILU) return GSA_ERR_UNSUPPORTED;
+  const int64_t R = B * L, n = past + L;
+  const int64_t row = (int64_t)dims->n_kv_heads * dims->d_head, kv_ld = 2 * row, dI = dims->d_idx;
+  if (kv_bstride < n * kv_ld || ki_bstride < n * dI) return GSA_ERR_BAD_ARG;
+  const DecodeLayout o = decode_layout(dims, tp, dtype, B, L, n);
+  if (!workspace || !aligned(workspace, 256) || workspace_bytes < o.bytes) return GSA_ERR_WORKSPACE;
+  DeviceInfo* di;
+  int st = device_info(&di);
+  if (st) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const size_t esz = dtype == GSA_DTYPE_BF16 ? 2 : 4;
+  uint8_t* kvb = static_cast<uint8_t*>(kv_store);
+  uint8_t* kib = static_cast<uint8_t*>(ki_store);
+  void* q = ws + o.q;
+  void* g1 = layout->g1 >= 0 ? ws + o.g1 : nullptr;
+  float* w = reinterpret_cast<float*>(ws + o.w);
+  float* shift = reinterpret_cast<float*>(ws + o.shift);
+  double* stats = reinterpret_cast<double*>(ws + o.stats);
+  float* var = reinterpret_cast<float*>(ws + o.var);
+  double* total = reinterpret_cast<double*>(ws + o.total);
+  int32_t* kt = reinterpret_cast<int32_t*>(ws + o.kt);
+  int32_t* cidx = reinterpret_cast<int32_t*>(ws + o.cidx);
+  float* cscore = reinterpret_cast<float*>(ws + o.cscore);
+  int32_t* ccount = reinterpret_cast<int32_t*>(ws + o.ccount);
+  int32_t* sel = reinterpret_cast<int32_t*>(ws + o.sel);
+  int32_t* scount = reinterpret_cast<int32_t*>(ws + o.scount);
+
+  // 1. RoPE / gates / head weights; K, V and k^I of the new tokens into slots past .. past+L-1
+  EpiArgs ea{*dims, *layout, dtype, R, proj, proj_ld, positions, cos_tab, sin_tab, tab_dtype, tab_rows,
+             q, kvb + past * kv_ld * esz, kvb + (past * kv_ld + row) * esz, kv_ld, g1, w, shift, di->err, L,
+             kv_bstride, kib + past * dI * esz, dI, ki_bstride, past};
+  if ((st = launch_proj_epilogue(ea, s))) return st;
+  // 2. indexer over every cached key + the candidates of each row
+  if (cudaMemsetAsync(stats, 0, R * 3 * sizeof(double), s) != cudaSuccess) return GSA_ERR_CUDA;
+  const void* qI = static_cast<const uint8_t*>(proj) + layout->qi * esz;
+  if (o.survivors)
+    st = gsa_indexer_survivors(dims, dtype, B, L, n, past, 1, qI, proj_ld, L * proj_ld, ki_store, dI, ki_bstride, w,
+                               idx_bias, idx_scale, shift, o.k_eff, o.cand_ld, cidx, cscore, ccount, stats, R,
+                               ws + o.idx_ws, o.idx_ws_bytes, stream);
+  else
+    st = gsa_indexer_select(dims, dtype, B, L, n, past, 1, qI, proj_ld, L * proj_ld, ki_store, dI, ki_bstride, w,
+                            idx_bias, idx_scale, shift, o.k_eff, cidx, cscore, ccount, stats, R, ws + o.idx_ws,
+                            o.idx_ws_bytes, stream);
+  if (st) return st;
+  // 3. adaptive k (variance mean over the B * L rows of this call), final selection
+  if (tp->use_adaptive && (st = gsa_row_variance(R, n, dtype, stats, shift, var, total, stream))) return st;
+  if ((st = gsa_adaptive_k(R, n, dtype, tp, var, total, stats, kt, stream))) return st;
+  if ((st = gsa_select_finalize(R, o.cand_ld, cidx, cscore, ccount, kt, sel, o.k_eff, scount, nullptr, stream)))
+    return st;
+  // 4. sparse SDPA with the G1 gate
+  if ((st = gsa_sparse_sdpa_strided(dims, dtype, B, L, n, q, kv_store, kvb + row * esz, kv_ld, kv_bstride, sel,
+                                    o.k_eff, scount, g1, attn_out, attn_scale, ws + o.sdpa_ws, o.sdpa_ws_bytes,
+                                    stream)))
+    return st;
+  if (k_out && cudaMemcpyAsync(k_out, kt, R * sizeof(int32_t), cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+    return GSA_ERR_CUDA;
   return GSA_OK;
 }
 

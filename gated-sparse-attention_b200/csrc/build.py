@@ -22,7 +22,7 @@ OUT_DIR = PKG_ROOT / "gsa_b200"
 LIB = OUT_DIR / "libgsa_b200.so"
 OBJ_DIR = PKG_ROOT / "_build"
 
-SOURCES = ["abi.cu", "proj_epilogue.cu", "indexer_simt.cu", "indexer_tc.cu", "topk.cu",
+SOURCES = ["abi.cu", "proj_epilogue.cu", "indexer_simt.cu", "indexer_tc.cu", "indexer_decode.cu", "topk.cu",
            "sparse_sdpa.cu", "select_static.cu"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -26,7 +26,24 @@ struct EpiArgs {
   float* w_out;
   float* shift_out;
   int* err;
+  // cache layout (gsa_proj_epilogue_cache): token t = b * L + i of k_out/v_out at
+  // b * kv_bstride + i * kv_ld, its k^I at b * ki_bstride + i * ki_ld; L = 0: t * kv_ld, no k^I
+  int64_t L;
+  int64_t kv_bstride;
+  void* ki_out;
+  int64_t ki_ld, ki_bstride;
+  int64_t pos0;       // positions == NULL: token t = b * L + i sits at position pos0 + i
 };
+
+// RoPE position of the epilogue's token t.
+__device__ __forceinline__ int64_t epi_position(const EpiArgs& a, int64_t t) {
+  return a.positions ? a.positions[t] : a.pos0 + (a.L ? t % a.L : t);
+}
+
+// Offset of token t's K (or V) row in an epilogue's k_out / v_out.
+__host__ __device__ __forceinline__ int64_t epi_kv_off(const EpiArgs& a, int64_t t) {
+  return a.L ? (t / a.L) * a.kv_bstride + (t % a.L) * a.kv_ld : t * a.kv_ld;
+}
 
 struct IdxArgs {
   int dtype;
@@ -63,6 +80,13 @@ struct SdpaArgs {
   int nstages;
   int nprod;          // producer warps
   int* err;
+  int64_t kv_bstride; // elements between batches of k and of v (>= Lkv * kv_ld)
+  // key splits per row (few rows: each row's selected keys are cut into `splits` ranges taken by
+  // different CTAs; partial outputs o [R*splits, H, D] fp32 and their log2-sum-exp [R*splits, H]
+  // in `part`, merged by a second kernel).  1: no split.
+  int splits;
+  float* part;
+  int64_t part_floats; // capacity of part
 };
 
 struct SdpaF32Args {
@@ -79,6 +103,7 @@ struct SdpaF32Args {
   float* out;
   float scale;
   int* err;
+  int64_t kv_bstride;
 };
 
 int launch_proj_epilogue(const EpiArgs& a, cudaStream_t stream);
@@ -87,6 +112,8 @@ int launch_apply_gate(int dtype, int act, int64_t n, const void* x, const void* 
 int launch_indexer_simt(const IdxArgs& a, int64_t B, cudaStream_t stream);
 bool indexer_tc_eligible(const IdxArgs& a);
 int launch_indexer_tc(const IdxArgs& a, int* err, cudaStream_t stream);
+bool indexer_decode_eligible(const IdxArgs& a, int64_t B);
+int launch_indexer_decode(const IdxArgs& a, int64_t B, int num_sms, cudaStream_t stream);
 int launch_topk_candidates(int64_t R, int64_t Lq, int64_t n_cols, int64_t q_pos0, int causal, const float* scores,
                            int64_t ld, const float* row_center, const double* row_stats, int32_t k_eff,
                            int32_t* cand_idx, float* cand_score, int32_t* cand_count, cudaStream_t stream);

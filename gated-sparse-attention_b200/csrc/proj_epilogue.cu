@@ -37,7 +37,7 @@ __global__ void proj_epilogue_kernel(EpiArgs a) {
   if (t >= a.T) return;
   const int H = a.d.n_heads, Hk = a.d.n_kv_heads, D = a.d.d_head, HI = a.d.n_idx_heads;
   const int64_t row = t * a.proj_ld;
-  int64_t pos = a.positions[t];
+  int64_t pos = epi_position(a, t);
   if (pos < 0 || pos >= a.tab_rows) {
     set_error(a.err, GSA_ERR_INDEX);
     pos = pos < 0 ? 0 : a.tab_rows - 1;
@@ -52,8 +52,9 @@ __global__ void proj_epilogue_kernel(EpiArgs a) {
 
   for (int h = 0; h < H; ++h)
     rope_head(a, row, a.lay.q + (int64_t)h * D, cos_row, sin_row, a.q_out, (t * H + h) * D, D);
+  const int64_t kv_off = epi_kv_off(a, t);
   for (int h = 0; h < Hk; ++h)
-    rope_head(a, row, a.lay.k + (int64_t)h * D, cos_row, sin_row, a.k_out, t * a.kv_ld + (int64_t)h * D, D);
+    rope_head(a, row, a.lay.k + (int64_t)h * D, cos_row, sin_row, a.k_out, kv_off + (int64_t)h * D, D);
 
   // G2 on v, applied before RoPE and never rotated (gated_sparse_attention.py:180-186)
   for (int i = threadIdx.x; i < Hk * D; i += blockDim.x) {
@@ -62,7 +63,12 @@ __global__ void proj_epilogue_kernel(EpiArgs a) {
       float g = gate_act(load_elem(a.proj, row + a.lay.g2 + i, a.dtype), a.d.gate_act, a.dtype);
       v = fmul(v, g);
     }
-    store_elem(a.v_out, t * a.kv_ld + i, v, a.dtype);
+    store_elem(a.v_out, kv_off + i, v, a.dtype);
+  }
+  if (a.ki_out) {
+    const int64_t ki_off = (t / a.L) * a.ki_bstride + (t % a.L) * a.ki_ld;
+    for (int i = threadIdx.x; i < a.d.d_idx; i += blockDim.x)
+      store_elem(a.ki_out, ki_off + i, load_elem(a.proj, row + a.lay.ki + i, a.dtype), a.dtype);
   }
   if (a.lay.g1 >= 0 && a.g1_out) {
     for (int i = threadIdx.x; i < H * D; i += blockDim.x) {
@@ -130,7 +136,7 @@ __global__ void __launch_bounds__(256) proj_epilogue_bf16_kernel(EpiArgs a) {
   const int H = a.d.n_heads, Hk = a.d.n_kv_heads, D = a.d.d_head, HI = a.d.n_idx_heads;
   const int half = D / 2, vh = half / 8;
   const __nv_bfloat16* prow = reinterpret_cast<const __nv_bfloat16*>(a.proj) + t * a.proj_ld;
-  int64_t pos = a.positions[t];
+  int64_t pos = epi_position(a, t);
   if (pos < 0 || pos >= a.tab_rows) {
     set_error(a.err, GSA_ERR_INDEX);
     pos = pos < 0 ? 0 : a.tab_rows - 1;
@@ -143,7 +149,9 @@ __global__ void __launch_bounds__(256) proj_epilogue_bf16_kernel(EpiArgs a) {
   __nv_bfloat16* go = reinterpret_cast<__nv_bfloat16*>(a.g1_out);
   const int nq = H * vh, nk = Hk * vh, nv = Hk * D / 8;
   const int ng = (a.lay.g1 >= 0 && a.g1_out) ? H * D / 8 : 0;
-  const int ntask = nq + nk + nv + ng;
+  const int nki = a.ki_out ? a.d.d_idx / 8 : 0;
+  const int ntask = nq + nk + nv + ng + nki;
+  const int64_t kv_off = epi_kv_off(a, t);
   for (int task = threadIdx.x; task < ntask; task += blockDim.x) {
     if (task < nq + nk) {
       const bool isq = task < nq;
@@ -160,7 +168,7 @@ __global__ void __launch_bounds__(256) proj_epilogue_bf16_kernel(EpiArgs a) {
         o1.f[e] = fadd(rnd(fmul(x1.f[e], c1.f[e]), dt), rnd(fmul(-x2.f[e], s1.f[e]), dt));
         o2.f[e] = fadd(rnd(fmul(x2.f[e], c2.f[e]), dt), rnd(fmul(x1.f[e], s2.f[e]), dt));
       }
-      __nv_bfloat16* dst = isq ? qo + (t * H + h) * D : ko + t * a.kv_ld + (int64_t)h * D;
+      __nv_bfloat16* dst = isq ? qo + (t * H + h) * D : ko + kv_off + (int64_t)h * D;
       st8_bf16(dst + i, o1);
       st8_bf16(dst + i + half, o2);
     } else if (task < nq + nk + nv) {
@@ -171,7 +179,13 @@ __global__ void __launch_bounds__(256) proj_epilogue_bf16_kernel(EpiArgs a) {
 #pragma unroll
         for (int e = 0; e < 8; ++e) v.f[e] = fmul(v.f[e], gate_act(g.f[e], a.d.gate_act, dt));
       }
-      st8_bf16(vo + t * a.kv_ld + i, v);
+      st8_bf16(vo + kv_off + i, v);
+    } else if (task >= nq + nk + nv + ng) {
+      // k^I into the cache: a plain 16-byte copy (already bf16)
+      const int i = (task - nq - nk - nv - ng) * 8;
+      __nv_bfloat16* kio = reinterpret_cast<__nv_bfloat16*>(a.ki_out) + (t / a.L) * a.ki_bstride +
+                           (t % a.L) * a.ki_ld;
+      *reinterpret_cast<uint4*>(kio + i) = *reinterpret_cast<const uint4*>(prow + a.lay.ki + i);
     } else {
       const int i = (task - nq - nk - nv) * 8;
       Vec8 g = ld8_bf16(prow + a.lay.g1 + i);
@@ -201,6 +215,8 @@ static bool epilogue_vec_ok(const EpiArgs& a) {
             el(a.lay.k) && el(a.lay.v) && (a.lay.g2 < 0 || el(a.lay.g2)) && al16(a.q_out) && al16(a.k_out) &&
             al16(a.v_out) && el(a.kv_ld);
   if (a.lay.g1 >= 0 && a.g1_out) ok = ok && el(a.lay.g1) && al16(a.g1_out);
+  if (a.L) ok = ok && el(a.kv_bstride);
+  if (a.ki_out) ok = ok && a.d.d_idx % 8 == 0 && el(a.lay.ki) && al16(a.ki_out) && el(a.ki_ld) && el(a.ki_bstride);
   const size_t tab_el = a.tab_dtype == GSA_DTYPE_BF16 ? 2 : 4;
   ok = ok && al16(a.cos_tab) && al16(a.sin_tab) && ((int64_t)D * tab_el) % 16 == 0;
   return ok;

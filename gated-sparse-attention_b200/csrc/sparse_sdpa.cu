@@ -27,6 +27,7 @@ namespace gsa {
 
 constexpr int kKeysPerStage = 16;
 constexpr int kMaxGroups = 3;  // producer groups of two warps
+constexpr int kMaxSplits = 8;  // key ranges per row when rows are fewer than CTAs
 constexpr int kMaxRowBytes = 16 * 256 * 2;
 __device__ __align__(128) uint8_t g_zero_row[2 * kMaxRowBytes];
 
@@ -60,6 +61,14 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// Key blocks [lo, hi) of split sp of a row with cnt selected keys (blocks of kKeysPerStage).
+__device__ __forceinline__ void split_range(int cnt, int sp, int splits, int& lo, int& hi) {
+  const int nkb = (cnt + kKeysPerStage - 1) / kKeysPerStage;
+  const int per = (nkb + splits - 1) / splits;
+  lo = min(nkb, sp * per);
+  hi = min(nkb, lo + per);
+}
+
 __device__ __forceinline__ int row_count(const SdpaArgs& a, int64_t row) {
   int c = a.sel_count[row];
   if (c < 0) c = 0;
@@ -81,6 +90,7 @@ __global__ void __launch_bounds__(MAXW * 32) sdpa_tc_kernel(SdpaArgs a) {
   uint8_t* stages = smem + 256;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t R = a.B * a.Lq;
+  const int64_t NW = R * a.splits;  // work items: (row, key range)
   const int H = Hk * NREP;
 
   if (threadIdx.x == 0) {
@@ -105,15 +115,17 @@ __global__ void __launch_bounds__(MAXW * 32) sdpa_tc_kernel(SdpaArgs a) {
     const int grp = pw >> 1, half = pw & 1;
     uint32_t it = 0;
     bool ok = true;
-    for (int64_t row = blockIdx.x; row < R && ok; row += gridDim.x) {
+    for (int64_t wi = blockIdx.x; wi < NW && ok; wi += gridDim.x) {
+      const int64_t row = wi / a.splits;
       const int64_t b = row / a.Lq;
       const int cnt = row_count(a, row);
       const int32_t* idx = a.sel_idx + row * a.sel_ld;
       const int64_t kv_row = a.kv_ld * 2;  // bytes between consecutive keys
-      const uint8_t* kbase = reinterpret_cast<const uint8_t*>(a.k) + b * a.Lkv * kv_row;
-      const uint8_t* vbase = reinterpret_cast<const uint8_t*>(a.v) + b * a.Lkv * kv_row;
-      const int nkb = (cnt + kKeysPerStage - 1) / kKeysPerStage;
-      for (int kb = 0; kb < nkb; ++kb, ++it) {
+      const uint8_t* kbase = reinterpret_cast<const uint8_t*>(a.k) + b * a.kv_bstride * 2;
+      const uint8_t* vbase = reinterpret_cast<const uint8_t*>(a.v) + b * a.kv_bstride * 2;
+      int kb_lo, kb_hi;
+      split_range(cnt, (int)(wi % a.splits), a.splits, kb_lo, kb_hi);
+      for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
         if ((int)(it % groups) != grp) continue;
         const int s = it % nst;
         const uint32_t ph = (it / nst) & 1u;
@@ -154,7 +166,8 @@ __global__ void __launch_bounds__(MAXW * 32) sdpa_tc_kernel(SdpaArgs a) {
   const int grp = lane >> 2, tq = lane & 3;
   const int mi = lane >> 3, r8 = lane & 7;
   uint32_t it = 0;
-  for (int64_t row = blockIdx.x; row < R; row += gridDim.x) {
+  for (int64_t wi = blockIdx.x; wi < NW; wi += gridDim.x) {
+    const int64_t row = wi / a.splits;
     const int cnt = row_count(a, row);
     const __nv_bfloat16* qrow = a.q + (row * H + (int64_t)g * NREP) * D;
     uint32_t qf[D / 16][2];
@@ -173,9 +186,10 @@ __global__ void __launch_bounds__(MAXW * 32) sdpa_tc_kernel(SdpaArgs a) {
 #pragma unroll
     for (int mt = 0; mt < D / 16; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
 
-    const int nkb = (cnt + kKeysPerStage - 1) / kKeysPerStage;
+    int kb_lo, kb_hi;
+    split_range(cnt, (int)(wi % a.splits), a.splits, kb_lo, kb_hi);
     bool ok = true;
-    for (int kb = 0; kb < nkb; ++kb, ++it) {
+    for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
       const int s = it % nst;
       const uint32_t ph = (it / nst) & 1u;
       if (!mbar_wait(&full[s], ph, a.err)) { ok = false; break; }
@@ -257,6 +271,25 @@ __global__ void __launch_bounds__(MAXW * 32) sdpa_tc_kernel(SdpaArgs a) {
     const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f;
     const float inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
     const int h0 = tq * 2, h1 = tq * 2 + 1;
+    if (a.splits > 1) {
+      // partial of this key range: o / l in fp32 and log2(sum exp) = m + log2(l) per head
+      float* po = a.part + (wi * H + g * NREP) * D;
+      float* pl = a.part + NW * H * D + wi * H + g * NREP;
+#pragma unroll
+      for (int mt = 0; mt < D / 16; ++mt) {
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const int dim = mt * 16 + grp + half * 8;
+          if (h0 < NREP) po[h0 * D + dim] = o[mt][half * 2 + 0] * inv0;
+          if (h1 < NREP) po[h1 * D + dim] = o[mt][half * 2 + 1] * inv1;
+        }
+      }
+      if (grp == 0) {
+        if (h0 < NREP) pl[h0] = l0 > 0.f ? m0 + log2f(l0) : -INFINITY;
+        if (h1 < NREP) pl[h1] = l1 > 0.f ? m1 + log2f(l1) : -INFINITY;
+      }
+      continue;
+    }
 #pragma unroll
     for (int mt = 0; mt < D / 16; ++mt) {
 #pragma unroll
@@ -309,8 +342,8 @@ __global__ void sdpa_f32_kernel(SdpaF32Args a) {
     for (int j = 0; j < cnt; ++j) {
       int s = idx[j];
       if (s < 0 || s >= a.Lkv) { set_error(a.err, GSA_ERR_INDEX); continue; }
-      const float* kr = a.k + (b * a.Lkv + s) * a.kv_ld + (int64_t)g * a.D;
-      const float* vr = a.v + (b * a.Lkv + s) * a.kv_ld + (int64_t)g * a.D;
+      const float* kr = a.k + b * a.kv_bstride + s * a.kv_ld + (int64_t)g * a.D;
+      const float* vr = a.v + b * a.kv_bstride + s * a.kv_ld + (int64_t)g * a.D;
       float dot = 0.f;
       for (int i = 0; i < kMaxPerLane; ++i) {
         int d = lane + 32 * i;
@@ -336,6 +369,32 @@ __global__ void sdpa_f32_kernel(SdpaF32Args a) {
         a.out[off] = y;
       }
     }
+  }
+}
+
+// Merge the key-range partials of each row: out = bf16(sum_s 2^(lse_s - M) o_s / sum_s 2^(lse_s - M)),
+// times the G1 gate (the unsplit epilogue's roundings).  One CTA per row.
+__global__ void sdpa_combine_kernel(int64_t R, int H, int D, int splits, const float* part,
+                                    const __nv_bfloat16* gate, __nv_bfloat16* out) {
+  const int64_t row = blockIdx.x;
+  const int64_t NW = R * splits;
+  const float* lse = part + NW * H * D + row * splits * H;
+  for (int e = threadIdx.x; e < H * D; e += blockDim.x) {
+    const int h = e / D;
+    float M = -INFINITY;
+    for (int s = 0; s < splits; ++s) M = fmaxf(M, lse[s * H + h]);
+    float num = 0.f, den = 0.f;
+    if (M > -INFINITY) {
+      for (int s = 0; s < splits; ++s) {
+        const float w = exp2f(lse[s * H + h] - M);
+        num = fmaf(w, part[((row * splits + s) * H) * D + e], num);
+        den += w;
+      }
+    }
+    const int64_t off = row * H * D + e;
+    float y = __bfloat162float(__float2bfloat16_rn(den > 0.f ? num / den : 0.f));
+    if (gate) y *= __bfloat162float(gate[off]);
+    out[off] = __float2bfloat16_rn(y);
   }
 }
 
@@ -365,10 +424,25 @@ static int launch_tc_w(SdpaArgs a, int num_sms, cudaStream_t stream) {
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem) != cudaSuccess || per_sm < 1)
     return GSA_ERR_LAUNCH;
   const int64_t R = a.B * a.Lq;
+  const int H = a.Hk * NREP;
   int64_t grid = (int64_t)num_sms * per_sm;
-  if (grid > R) grid = R;
+  // fewer rows than resident CTAs: cut each row's keys into ranges (as many as the partials
+  // buffer holds) so that every CTA streams keys
+  a.splits = 1;
+  if (a.part && R < grid) {
+    int64_t sp = std::min<int64_t>(grid / R, kMaxSplits);
+    while (sp > 1 && R * sp * H * (D + 1) > a.part_floats) --sp;
+    a.splits = (int)sp;
+  }
+  const int64_t items = R * a.splits;
+  if (grid > items) grid = items;
   kern<<<(unsigned)grid, threads, smem, stream>>>(a);
-  return cudaGetLastError() == cudaSuccess ? GSA_OK : GSA_ERR_LAUNCH;
+  if (cudaGetLastError() != cudaSuccess) return GSA_ERR_LAUNCH;
+  if (a.splits > 1) {
+    sdpa_combine_kernel<<<(unsigned)R, 256, 0, stream>>>(R, H, D, a.splits, a.part, a.gate, a.out);
+    if (cudaGetLastError() != cudaSuccess) return GSA_ERR_LAUNCH;
+  }
+  return GSA_OK;
 }
 
 // The register-staged consumers want more than the 93 registers a 22-warp block leaves, so

@@ -62,6 +62,8 @@ SIGNATURES = {
     "gsa_get_device_error": [P, P],
     "gsa_version": [],
     "gsa_proj_epilogue": [P, P, INT, I64, P, I64, P, P, P, INT, I64, P, P, P, I64, P, P, P, P],
+    "gsa_proj_epilogue_cache": [P, P, INT, I64, I64, P, I64, P, P, P, INT, I64, P, P, P, I64, I64, P, I64, I64,
+                                P, P, P, P],
     "gsa_indexer_scores": [P, INT, I64, I64, I64, I64, INT, INT, P, I64, I64, P, I64, I64, P, P, F32,
                            P, P, I64, P, P],
     "gsa_row_stats": [I64, I64, P, I64, P, P],
@@ -70,6 +72,11 @@ SIGNATURES = {
     "gsa_adaptive_k": [I64, I64, INT, P, P, P, P, P, P],
     "gsa_select_finalize": [I64, I32, P, P, P, P, P, I64, P, P, P],
     "gsa_sparse_sdpa": [P, INT, I64, I64, I64, P, P, P, I64, P, I64, P, P, P, F32, P],
+    "gsa_sparse_sdpa_strided": [P, INT, I64, I64, I64, P, P, P, I64, I64, P, I64, P, P, P, F32, P, I64, P],
+    "gsa_sdpa_workspace_size": [P, I64, I64],
+    "gsa_decode_workspace_size": [P, P, INT, I64, I64, I64],
+    "gsa_decode_attend": [P, P, P, INT, I64, I64, I64, P, I64, P, P, P, INT, I64, P, I64, P, I64, P, F32, F32, P, P,
+                          P, I64, P],
     "gsa_workspace_size": [I64, I64],
     "gsa_indexer_select": [P, INT, I64, I64, I64, I64, INT, P, I64, I64, P, I64, I64, P, P, F32, P,
                            I32, P, P, P, P, I64, P, I64, P],
@@ -81,7 +88,8 @@ SIGNATURES = {
                                   P, I32, P, P, P, P, P],
 }
 _RESTYPES = {"gsa_version": C.c_char_p, "gsa_workspace_size": C.c_int64,
-             "gsa_survivors_workspace_size": C.c_int64}
+             "gsa_survivors_workspace_size": C.c_int64, "gsa_sdpa_workspace_size": C.c_int64,
+             "gsa_decode_workspace_size": C.c_int64}
 
 _lib = None
 _lock = threading.Lock()

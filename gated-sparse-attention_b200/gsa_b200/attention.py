@@ -315,17 +315,71 @@ class AdaptiveTopKSelector(nn.Module):
 # ---------------------------------------------------------------------------------------------
 # KV cache
 # ---------------------------------------------------------------------------------------------
+class KVCacheStore:
+    """Preallocated buffers of one layer's KV cache: K and V interleaved per token
+    [B, capacity, 2, Hk, D] (the layout the sparse SDPA reads) and the indexer keys
+    [B, capacity, d_I].  ``filled`` is the number of leading tokens some cache handed out holds;
+    a cache of exactly that length may append in place, any other length copies first, so that
+    two continuations of one cache never write the same slots.  The store also keeps the
+    scratch of the native step (sized for its capacity), so that a decode loop allocates
+    nothing per step."""
+
+    def __init__(self, batch: int, capacity: int, n_kv_heads: int, d_head: int, d_idx: int,
+                 dtype: torch.dtype, device):
+        self.kv = torch.empty(batch, capacity, 2, n_kv_heads, d_head, dtype=dtype, device=device)
+        self.ki = torch.empty(batch, capacity, d_idx, dtype=dtype, device=device)
+        self.filled = 0
+        self._scratch = {}
+
+    def scratch(self, key, nbytes: int) -> torch.Tensor:
+        t = self._scratch.get(key)
+        if t is None or t.numel() < nbytes:
+            t = torch.empty(nbytes, dtype=torch.uint8, device=self.kv.device)
+            self._scratch[key] = t
+        return t
+
+    @property
+    def capacity(self) -> int:
+        return self.kv.shape[1]
+
+    def fits(self, batch: int, length: int, dtype, device) -> bool:
+        return (self.kv.shape[0] == batch and length <= self.capacity and self.kv.dtype == dtype
+                and self.kv.device == device)
+
+    def view(self, n: int) -> "GSAKVCache":
+        kv = self.kv[:, :n]
+        return GSAKVCache(kv[:, :, 0], kv[:, :, 1], self.ki[:, :n], kv, self)
+
+
+def _grown_capacity(n: int) -> int:
+    """Capacity of a new cache store for n tokens: a quarter (at least 256 tokens) of headroom,
+    rounded up to 256, so that a decode loop reallocates O(log) times."""
+    return (n + max(n // 4, 256) + 255) // 256 * 256
+
+
 class GSAKVCache(tuple):
     """The (k, v) cache pair of the reference (post-RoPE k, post-G2 v, [B, Lkv, Hk, D]) that
     also carries the indexer keys k^I [B, Lkv, d_I].  It is a 2-tuple, so code written for the
     reference's cache keeps working; when it is passed back as ``past_key_value`` the indexer
-    scores the new queries against every cached key."""
+    scores the new queries against every cached key.
 
-    def __new__(cls, k, v, indexer_keys=None, kv=None):
+    A cache returned by the layer is a view of a :class:`KVCacheStore` with room for more
+    tokens: passing it back appends the new tokens' K, V and k^I in place (the reference
+    concatenates the whole cache every step, gated_sparse_attention.py:188-192); when the store
+    is full, or when this cache is not the longest view of its store, the layer moves to a new,
+    larger store first.  ``GatedSparseAttention.allocate_cache`` preallocates one."""
+
+    def __new__(cls, k, v, indexer_keys=None, kv=None, store=None):
         obj = super().__new__(cls, (k, v))
         obj.indexer_keys = indexer_keys
         obj.kv = kv  # the interleaved [B, Lkv, 2, Hk, D] buffer k and v are views of
+        obj.store = store
         return obj
+
+    @property
+    def capacity(self) -> int:
+        """Tokens this cache can hold before the layer moves it to a larger store."""
+        return self.store.capacity if self.store is not None else self[0].shape[1]
 
 
 class _ForwardOnly(torch.autograd.Function):
@@ -380,6 +434,24 @@ class GatedSparseAttention(nn.Module):
         self._fused = None
         # set by gsa_b200.sharded.enable_query_sharding: this rank's share of the query sequence
         self.query_shards = None
+        # set by gsa_b200.sharded.enable_sequence_sharding: the process group whose ranks hold
+        # the other sequences of the batch (the adaptive k's variance mean spans them)
+        self.sequence_shards = None
+        # steps that write into a KV cache store run everything between the two GEMMs as one
+        # native call (gsa_decode_attend); False runs the same kernels one by one from Python
+        self.native_step = True
+        self._static = None
+
+    def allocate_cache(self, batch_size: int, capacity: int, dtype: Optional[torch.dtype] = None,
+                       device=None) -> "GSAKVCache":
+        """An empty KV cache (length 0) with room for ``capacity`` tokens of each of
+        ``batch_size`` sequences.  Pass it as ``past_key_value`` of the prefill (with
+        ``use_cache=True``); the prefill and every decode step then write K, V and the indexer
+        keys into it in place."""
+        w = self.q_proj.weight
+        store = KVCacheStore(batch_size, capacity, self.n_kv_heads, self.d_head, self.config.d_indexer,
+                             dtype or w.dtype, device or w.device)
+        return store.view(0)
 
     def _init_weights(self):
         for module in [self.q_proj, self.k_proj, self.v_proj]:
@@ -441,6 +513,18 @@ class GatedSparseAttention(nn.Module):
                              (self.output_gate.activation if self.output_gate is not None else "sigmoid"),
                              self.indexer.activation)
 
+    def _step_constants(self):
+        """(dims, top-k parameters, fp32 indexer bias) of the native step, rebuilt when the
+        indexer bias changes."""
+        b = self.indexer.bias
+        key = (b.data_ptr(), b._version, b.dtype)
+        if self._static is None or self._static[0] != key:
+            cfg = self.config
+            tp = ops.TopkParams(cfg.k_base, cfg.k_min, cfg.k_max, int(cfg.use_adaptive_k),
+                                float(cfg.adaptive_k_temperature))
+            self._static = (key, self._dims(), tp, b.detach().float().contiguous())
+        return self._static[1:]
+
     # -- forward ----------------------------------------------------------------------------
     def forward(self, hidden_states: torch.Tensor, positions: Optional[torch.Tensor] = None,
                 attention_mask: Optional[torch.Tensor] = None,
@@ -464,7 +548,9 @@ class GatedSparseAttention(nn.Module):
     def _forward_impl(self, x, positions, past_key_value, use_cache, output_attentions,
                       mark=None, capture=None):
         """The forward computation.  ``mark(name)`` (optional) is called after each stage and
-        ``capture`` (optional dict) receives the SDPA inputs; both are for measurement."""
+        ``capture`` (optional dict) receives the SDPA inputs; both are for measurement (and
+        keep the stages apart, one call each)."""
+        mark_fn = mark
         mark = mark or (lambda name: None)
         B, L, _ = x.shape
         dt = x.dtype
@@ -480,9 +566,8 @@ class GatedSparseAttention(nn.Module):
         segs = sp.segments(L) if sp is not None else [(0, L, past_len)]
         if sp is not None and len(segs) > 1 and B != 1:
             raise NotImplementedError("zigzag query sharding takes one sequence per call")
+        positions_given = positions is not None
         if positions is None:
-            positions = torch.cat([torch.arange(p0, p0 + n, device=x.device) for _, n, p0 in segs])
-            positions = positions.unsqueeze(0).expand(B, -1)
             max_pos = max(p0 + n - 1 for _, n, p0 in segs)
         else:
             max_pos = int(positions.max().item())  # the reference syncs here too (rope.py:133-134)
@@ -490,13 +575,49 @@ class GatedSparseAttention(nn.Module):
         W, bvec, layout = self.fused_projection()
         if W.dtype != dt:
             raise RuntimeError(f"layer parameters are {W.dtype} but the input is {dt}")
-        dims = self._dims()
+        dims = self._step_constants()[0]
+
+        # the KV cache store the new tokens' K, V and k^I are written into (None: a fresh
+        # [B, L, 2, Hk, D] buffer), and whether the returned cache may claim them
+        store = None
+        if sp is None and (past_key_value is None or getattr(past_key_value, "indexer_keys", None) is not None):
+            old = getattr(past_key_value, "store", None) if past_key_value is not None else None
+            if old is not None and old.filled == past_len and old.fits(B, past_len + L, dt, x.device):
+                store = old
+            elif past_key_value is not None or use_cache:
+                store = KVCacheStore(B, _grown_capacity(past_len + L), Hk, D, dI, dt, x.device)
+                if past_len:
+                    store.kv[:, :past_len, 0] = past_key_value[0]
+                    store.kv[:, :past_len, 1] = past_key_value[1]
+                    store.ki[:, :past_len] = past_key_value.indexer_keys
+                store.filled = past_len
 
         proj = torch.addmm(bvec, x.reshape(B * L, self.d_model), W.t())
+        n_all = past_len + L
+        if (store is not None and self.native_step and self.selection_path == "auto" and mark_fn is None
+                and capture is None and not output_attentions and self.sequence_shards is None
+                and B * L * ((n_all + 3) // 4 * 4) * 4 <= ops.SCORE_CHUNK_BYTES):
+            # everything between the two GEMMs in one native call, scratch kept on the store
+            dims, tp, idx_bias = self._step_constants()
+            nbytes = ops.decode_workspace_bytes(dims, tp, dt, B, L, store.capacity)
+            attn = ops.decode_attend(dims, layout, tp, proj, B, L, past_len, positions if positions_given else None,
+                                     self.rotary_emb.cos_cached, self.rotary_emb.sin_cached, store.kv, store.ki,
+                                     idx_bias, self.indexer.scale, self.scale, store.scratch((B, L), nbytes))
+            out = F.linear(attn.view(B, L, H * D), self.o_proj.weight)
+            present = None
+            if use_cache:
+                store.filled = n_all
+                present = store.view(n_all)
+            return out, present, None
+        if not positions_given:
+            positions = torch.cat([torch.arange(p0, p0 + n, device=x.device) for _, n, p0 in segs])
+            positions = positions.unsqueeze(0).expand(B, -1)
         mark("proj_gemm")
-        q, kv, g1, w, shift = ops.proj_epilogue(dims, layout, proj, positions,
-                                                self.rotary_emb.cos_cached, self.rotary_emb.sin_cached,
-                                                self.output_gate is not None, return_kv=True)
+        q, kv, g1, w, shift = ops.proj_epilogue(
+            dims, layout, proj, positions, self.rotary_emb.cos_cached, self.rotary_emb.sin_cached,
+            self.output_gate is not None, return_kv=True,
+            kv_out=store.kv[:, past_len:past_len + L] if store is not None else None,
+            ki_out=store.ki[:, past_len:past_len + L] if store is not None else None)
         mark("proj_epilogue")
         q = q.view(B, L, H, D)
         kv = kv.view(B, L, 2, Hk, D)  # k and v interleaved per token
@@ -506,7 +627,16 @@ class GatedSparseAttention(nn.Module):
 
         indexer_keys = None
         kv_finish = None
-        if sp is not None:
+        present = None
+        if store is not None:
+            # K, V and k^I of every cached and new token, in place in the store
+            n = past_len + L
+            kv_all, kI_all, q_pos0 = store.kv[:, :n], store.ki[:, :n], past_len
+            indexer_keys = kI_all
+            if use_cache:
+                store.filled = n
+                present = store.view(n)
+        elif sp is not None:
             # every rank needs all keys up to its last query, in sequence order: k^I now (the
             # indexer reads it), K/V asynchronously (only the SDPA reads them), so that their
             # transfer overlaps the indexer
@@ -516,26 +646,19 @@ class GatedSparseAttention(nn.Module):
             q_pos0 = segs[0][2]
             indexer_keys = kI_all
         elif past_key_value is None:
+            # no cache kept
             kv_all, kI_all, q_pos0 = kv, kI, 0
-            indexer_keys = kI.contiguous()
         else:
-            past_kv = getattr(past_key_value, "kv", None)
-            if past_kv is None:
-                past_kv = torch.stack([past_key_value[0], past_key_value[1]], dim=2)
+            # a plain (k, v) cache (no indexer keys): the reference concatenates it and scores
+            # the new tokens only (gated_sparse_attention.py:188-213), selecting among
+            # positions [0, L)
+            past_kv = torch.stack([past_key_value[0], past_key_value[1]], dim=2)
             kv_all = torch.cat([past_kv, kv], dim=1)
-            past_kI = getattr(past_key_value, "indexer_keys", None)
-            if past_kI is not None:
-                # scores against every cached key, offset-causal for the new rows
-                kI_all = torch.cat([past_kI, kI.contiguous()], dim=1)
-                q_pos0 = past_len
-                indexer_keys = kI_all
-            else:
-                # a plain (k, v) cache: the reference scores the new tokens only
-                # (gated_sparse_attention.py:197-213), selecting among positions [0, L)
-                kI_all, q_pos0 = kI, 0
+            kI_all, q_pos0 = kI, 0
         if kv_finish is None:
             k_all, v_all = kv_all[:, :, 0], kv_all[:, :, 1]
-            present = GSAKVCache(k_all, v_all, indexer_keys, kv_all) if use_cache else None
+            if use_cache and present is None:
+                present = GSAKVCache(k_all, v_all, indexer_keys, kv_all)
         mark("kv")
 
         n_cols = kI_all.shape[1]
@@ -568,6 +691,8 @@ class GatedSparseAttention(nn.Module):
             var, total = ops.row_variance(stats, n_cols, dt, shift)
             if sp is not None:
                 total = sp.allreduce(total)
+            elif self.sequence_shards is not None:
+                total = self.sequence_shards.allreduce(total)
         else:
             var = total = None
         kt = ops.adaptive_k(stats, var, total, n_cols, dt, cfg.k_base, cfg.k_min, cfg.k_max,

@@ -65,18 +65,19 @@ def make_dims(d_model, n_heads, n_kv_heads, d_head, n_idx_heads, d_idx, gate_act
 
 
 def proj_epilogue(dims: Dims, layout: ProjLayout, proj: torch.Tensor, positions: torch.Tensor,
-                  cos_tab: torch.Tensor, sin_tab: torch.Tensor, has_g1: bool, return_kv: bool = False):
+                  cos_tab: torch.Tensor, sin_tab: torch.Tensor, has_g1: bool, return_kv: bool = False,
+                  kv_out: torch.Tensor | None = None, ki_out: torch.Tensor | None = None):
     """q, k (RoPE), v (G2), g1 gate, indexer head weights w and row shift from the fused
     projection output ``proj`` [T, Ncat].  k and v are views of one interleaved [T, 2, Hk, D]
-    buffer; with ``return_kv`` that buffer is returned in their place: (q, kv, g1, w, shift)."""
+    buffer; with ``return_kv`` that buffer is returned in their place: (q, kv, g1, w, shift).
+
+    ``kv_out`` [B, L, 2, Hk, D] (T = B*L; a view into a KV cache with a larger batch stride) and
+    ``ki_out`` [B, L, d_I] receive K/V and the indexer keys directly; kv_out is then the returned kv."""
     _cuda(proj, positions, cos_tab, sin_tab)
     T = proj.shape[0]
     H, Hk, D, HI = dims.n_heads, dims.n_kv_heads, dims.d_head, dims.n_idx_heads
     dt = proj.dtype
     q = torch.empty(T, H, D, device=proj.device, dtype=dt)
-    # K and V interleaved per token ([T, 2, Hk, D]): the sparse SDPA moves a key as one copy
-    kv = torch.empty(T, 2, Hk, D, device=proj.device, dtype=dt)
-    k, v = kv[:, 0], kv[:, 1]
     g1 = torch.empty(T, H, D, device=proj.device, dtype=dt) if has_g1 else None
     w = torch.empty(T, HI, device=proj.device, dtype=torch.float32)
     shift = torch.empty(T, device=proj.device, dtype=torch.float32)
@@ -84,9 +85,28 @@ def proj_epilogue(dims: Dims, layout: ProjLayout, proj: torch.Tensor, positions:
     assert proj.stride(1) == 1 and pos.numel() == T
     cos_tab = cos_tab.contiguous()
     sin_tab = sin_tab.contiguous()
-    _lib.call("gsa_proj_epilogue", C.byref(dims), C.byref(layout), dtype_code(dt), T, _p(proj),
-              proj.stride(0), _p(pos), _p(cos_tab), _p(sin_tab), dtype_code(cos_tab.dtype),
-              cos_tab.shape[0], _p(q), _p(k), _p(v), kv.stride(0), _p(g1), _p(w), _p(shift), _stream())
+    if kv_out is None:
+        # K and V interleaved per token ([T, 2, Hk, D]): the sparse SDPA moves a key as one copy
+        kv = torch.empty(T, 2, Hk, D, device=proj.device, dtype=dt)
+        k, v = kv[:, 0], kv[:, 1]
+        _lib.call("gsa_proj_epilogue", C.byref(dims), C.byref(layout), dtype_code(dt), T, _p(proj),
+                  proj.stride(0), _p(pos), _p(cos_tab), _p(sin_tab), dtype_code(cos_tab.dtype),
+                  cos_tab.shape[0], _p(q), _p(k), _p(v), kv.stride(0), _p(g1), _p(w), _p(shift), _stream())
+    else:
+        _cuda(kv_out, ki_out)
+        B, L = kv_out.shape[0], kv_out.shape[1]
+        assert B * L == T and kv_out.dtype == dt and tuple(kv_out.shape[2:]) == (2, Hk, D)
+        assert kv_out.stride(4) == 1 and kv_out.stride(3) == D and kv_out.stride(2) == Hk * D
+        kv = kv_out
+        k, v = kv[:, :, 0], kv[:, :, 1]
+        ki_ld = ki_bs = 0
+        if ki_out is not None:
+            assert ki_out.shape == (B, L, dims.d_idx) and ki_out.stride(2) == 1 and ki_out.dtype == dt
+            ki_ld, ki_bs = ki_out.stride(1), ki_out.stride(0)
+        _lib.call("gsa_proj_epilogue_cache", C.byref(dims), C.byref(layout), dtype_code(dt), B, L, _p(proj),
+                  proj.stride(0), _p(pos), _p(cos_tab), _p(sin_tab), dtype_code(cos_tab.dtype),
+                  cos_tab.shape[0], _p(q), _p(k), _p(v), kv.stride(1), kv.stride(0), _p(ki_out), ki_ld, ki_bs,
+                  _p(g1), _p(w), _p(shift), _stream())
     _after("proj_epilogue")
     if return_kv:
         return q, kv, g1, w, shift
@@ -171,6 +191,28 @@ def adaptive_k(stats, var, total, n_cols: int, dt: torch.dtype, k_base: int, k_m
     return k
 
 
+def decode_workspace_bytes(dims: Dims, tp: TopkParams, dt: torch.dtype, B: int, L: int, n_keys: int) -> int:
+    return int(_lib.lib().gsa_decode_workspace_size(C.byref(dims), C.byref(tp), dtype_code(dt), B, L, n_keys))
+
+
+def decode_attend(dims: Dims, layout: ProjLayout, tp: TopkParams, proj: torch.Tensor, B: int, L: int, past: int,
+                  positions, cos_tab, sin_tab, kv_store: torch.Tensor, ki_store: torch.Tensor, idx_bias: torch.Tensor,
+                  idx_scale: float, attn_scale: float, workspace: torch.Tensor) -> torch.Tensor:
+    """The attention of one step between its two GEMMs in one native call (gsa_decode_attend):
+    the new tokens' K, V, k^I appended to the stores at slot ``past``, the indexer over all
+    past + L keys, the selection and the gated SDPA.  Returns attn [B*L, H*D]."""
+    dt = proj.dtype
+    attn = torch.empty(B * L, dims.n_heads * dims.d_head, device=proj.device, dtype=dt)
+    if positions is not None:
+        positions = positions.reshape(-1).to(torch.int64).contiguous()
+    _lib.call("gsa_decode_attend", C.byref(dims), C.byref(layout), C.byref(tp), dtype_code(dt), B, L, past,
+              _p(proj), proj.stride(0), _p(positions), _p(cos_tab), _p(sin_tab), dtype_code(cos_tab.dtype),
+              cos_tab.shape[0], _p(kv_store), kv_store.stride(0), _p(ki_store), ki_store.stride(0), _p(idx_bias),
+              float(idx_scale), float(attn_scale), _p(attn), None, _p(workspace), workspace.numel(), _stream())
+    _after("decode_attend")
+    return attn
+
+
 def select_finalize(cand_idx, cand_score, cand_count, k, want_mask: bool = False, sel_ld: int | None = None):
     """The k[r] best candidates of each row, ascending column order: (sel [R, sel_ld], count [R],
     mask [R, cand_ld] or None).  sel_ld defaults to the candidate row length."""
@@ -185,11 +227,16 @@ def select_finalize(cand_idx, cand_score, cand_count, k, want_mask: bool = False
 
 
 def _kv_rows(t: torch.Tensor) -> torch.Tensor:
-    """[B, Lkv, Hk, D] with unit-stride rows of Hk*D elements and batch-contiguous key rows."""
+    """[B, Lkv, Hk, D] with unit-stride rows of Hk*D elements and a batch stride that holds the
+    Lkv key rows (a KV cache may hold room for more)."""
     B, L, Hk, D = t.shape
-    if t.stride(3) != 1 or t.stride(2) != D or (B > 1 and t.stride(0) != L * t.stride(1)):
+    if t.stride(3) != 1 or t.stride(2) != D or (B > 1 and (t.stride(0) < L * t.stride(1) or t.stride(0) % 8)):
         t = t.contiguous()
     return t
+
+
+def _kv_bstride(t: torch.Tensor) -> int:
+    return t.stride(0) if t.shape[0] > 1 else t.shape[1] * t.stride(1)
 
 
 def sparse_sdpa(dims: Dims, q, k, v, sel_idx, sel_count, gate, scale: float) -> torch.Tensor:
@@ -201,13 +248,16 @@ def sparse_sdpa(dims: Dims, q, k, v, sel_idx, sel_count, gate, scale: float) -> 
     q = q.contiguous()
     k = _kv_rows(k)
     v = _kv_rows(v)
-    if k.stride(1) != v.stride(1):
+    if k.stride(1) != v.stride(1) or _kv_bstride(k) != _kv_bstride(v):
         k, v = k.contiguous(), v.contiguous()
     gate = gate.contiguous() if gate is not None else None
     out = torch.empty_like(q)
-    _lib.call("gsa_sparse_sdpa", C.byref(dims), dtype_code(q.dtype), B, Lq, Lkv, _p(q), _p(k), _p(v),
-              k.stride(1), _p(sel_idx), sel_idx.stride(0), _p(sel_count), _p(gate), _p(out),
-              float(scale), _stream())
+    # few rows (decode): room for per-key-range partials, so that every CTA streams keys
+    ws_bytes = int(_lib.lib().gsa_sdpa_workspace_size(C.byref(dims), B, Lq)) if q.dtype == torch.bfloat16 else 0
+    ws = torch.empty(ws_bytes, device=q.device, dtype=torch.uint8) if ws_bytes else None
+    _lib.call("gsa_sparse_sdpa_strided", C.byref(dims), dtype_code(q.dtype), B, Lq, Lkv, _p(q), _p(k), _p(v),
+              k.stride(1), _kv_bstride(k), _p(sel_idx), sel_idx.stride(0), _p(sel_count), _p(gate), _p(out),
+              float(scale), _p(ws), ws_bytes, _stream())
     _after("sparse_sdpa")
     return out
 
@@ -223,6 +273,18 @@ def apply_gate(x: torch.Tensor, logits: torch.Tensor, act: str, want_gate: bool 
               _p(gate), _stream())
     _after("apply_gate")
     return out, gate
+
+
+def _chunking(B: int, Lq: int, Lkv: int, chunk_rows: int | None):
+    """(rows per indexer chunk, number of chunks).  Chunks hold whole sequences when a sequence's
+    rows fit (so the short rows of many sequences share a launch), else rows of one sequence."""
+    if chunk_rows is None:
+        cap = max(1, SCORE_CHUNK_BYTES // (4 * ((Lkv + 3) // 4 * 4)))
+        chunk_rows = min(B, cap // Lq) * Lq if cap >= Lq else cap
+    if chunk_rows >= Lq:
+        per = chunk_rows // Lq
+        return chunk_rows, (B + per - 1) // per
+    return chunk_rows, B * ((Lq + chunk_rows - 1) // chunk_rows)
 
 
 def workspace_bytes(chunk_rows: int, n_cols: int) -> int:
@@ -242,10 +304,8 @@ def indexer_select(dims: Dims, qI, kI, w, bias, scale: float, shift, k_eff: int,
     Lkv = kI.shape[1]
     R = B * Lq
     dev = qI.device
-    if chunk_rows is None:
-        chunk_rows = max(1, min(Lq, SCORE_CHUNK_BYTES // (4 * ((Lkv + 3) // 4 * 4))))
     global last_chunk_count
-    last_chunk_count = B * ((Lq + chunk_rows - 1) // chunk_rows)
+    chunk_rows, last_chunk_count = _chunking(B, Lq, Lkv, chunk_rows)
     need = workspace_bytes(chunk_rows, Lkv)
     if workspace is None or workspace.numel() < need:
         workspace = torch.empty(need, device=dev, dtype=torch.uint8)
@@ -289,10 +349,8 @@ def indexer_survivors(dims: Dims, qI, kI, w, bias, scale: float, shift, k_eff: i
     R = B * Lq
     dev = qI.device
     cap = SURVIVOR_CAP
-    if chunk_rows is None:
-        chunk_rows = max(1, min(Lq, SCORE_CHUNK_BYTES // (4 * ((Lkv + 3) // 4 * 4))))
     global last_chunk_count
-    last_chunk_count = B * ((Lq + chunk_rows - 1) // chunk_rows)
+    chunk_rows, last_chunk_count = _chunking(B, Lq, Lkv, chunk_rows)
     ws_bytes = _lib.lib().gsa_survivors_workspace_size(chunk_rows, Lkv)
     workspace = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
     if out is not None:

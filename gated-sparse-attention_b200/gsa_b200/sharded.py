@@ -123,6 +123,28 @@ class QueryShards:
         return allreduce_sum(t, self.group)
 
 
+class SequenceShards:
+    """The layer's view of a process group whose ranks each hold different sequences of the
+    batch (decode with the KV cache sharded by sequence).  Nothing is exchanged but the
+    adaptive k's two fp64 numbers: its variance mean runs over every (batch, query) row of the
+    call (adaptive_topk.py:93-96), so over all ranks' sequences."""
+
+    def __init__(self, group):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+
+    def allreduce(self, t):
+        return allreduce_sum(t, self.group)
+
+
+def enable_sequence_sharding(layer, group=None):
+    """Make ``layer`` run its batch sharded by sequence over ``group``: each rank passes its own
+    sequences (and their KV cache); the selections equal those of one call over all sequences."""
+    layer.sequence_shards = SequenceShards(group if group is not None else dist.group.WORLD)
+    return layer
+
+
 def zigzag_block(k: int, world: int, rank: int) -> int:
     """Sequence index of rank's k-th zigzag segment (segments of L / (2 * world * folds) tokens)."""
     return k * world + (rank if k % 2 == 0 else world - 1 - rank)

@@ -94,6 +94,25 @@ int gsa_proj_epilogue(const gsa_dims* dims, const gsa_proj_layout* layout, int d
                       float* w_out, float* shift_out, gsa_stream_t stream);
 
 /*
+ * gsa_proj_epilogue writing K, V and the indexer keys k^I straight into a KV cache that holds
+ * room for more tokens than it has (the append-in-place cache of GatedSparseAttention).  The
+ * T = B * L rows of ``proj`` are L new tokens of each of B sequences; token t of sequence b goes to
+ *   k_out, v_out at b * kv_bstride + t * kv_ld    (kv_bstride >= L * kv_ld; pass the cache
+ *                                                  pointers already offset to the first new slot)
+ *   ki_out       at b * ki_bstride + t * ki_ld    (d_I elements copied from proj's k^I columns;
+ *                                                  NULL: not written)
+ * q_out, g1_out, w_out and shift_out are dense [T, ...] as in gsa_proj_epilogue.  Replaces the
+ * torch.cat of gated_sparse_attention.py:188-192 (the reference has no k^I cache).
+ */
+int gsa_proj_epilogue_cache(const gsa_dims* dims, const gsa_proj_layout* layout, int dtype,
+                            int64_t B, int64_t L, const void* proj, int64_t proj_ld,
+                            const int64_t* positions, const void* cos_tab, const void* sin_tab,
+                            int tab_dtype, int64_t tab_rows, void* q_out, void* k_out, void* v_out,
+                            int64_t kv_ld, int64_t kv_bstride, void* ki_out, int64_t ki_ld,
+                            int64_t ki_bstride, void* g1_out, float* w_out, float* shift_out,
+                            gsa_stream_t stream);
+
+/*
  * Gated indexer scores, I[t,s] = sum_j w[t,j] * act(scale * <qI[t,j], kI[s]> + bias[j])
  * (gated_indexer.py:106-145), for query rows t in [0, Lq) of each batch against keys
  * s in [0, Lkv).  With ``causal`` set, key s is masked for query row t when
@@ -195,6 +214,21 @@ int gsa_sparse_sdpa(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int6
                     const void* gate, void* out, float scale, gsa_stream_t stream);
 
 /*
+ * gsa_sparse_sdpa over a KV cache with room beyond its Lkv tokens: key s of batch b is the
+ * [Hk, D] row at b * kv_bstride + s * kv_ld (kv_bstride >= Lkv * kv_ld, a multiple of 8
+ * elements).  With fewer rows B*Lq than the GPU holds CTAs (decode), a workspace of
+ * gsa_sdpa_workspace_size bytes (16-byte aligned; NULL or smaller: not used) lets each row's
+ * selected keys be split over several CTAs, whose partial softmax results a second kernel
+ * merges.  gsa_sparse_sdpa is this call with kv_bstride = Lkv * kv_ld and no workspace.
+ */
+int64_t gsa_sdpa_workspace_size(const gsa_dims* dims, int64_t B, int64_t Lq);
+int gsa_sparse_sdpa_strided(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int64_t Lkv,
+                            const void* q, const void* k, const void* v, int64_t kv_ld,
+                            int64_t kv_bstride, const int32_t* sel_idx, int64_t sel_ld,
+                            const int32_t* sel_count, const void* gate, void* out, float scale,
+                            void* workspace, int64_t workspace_bytes, gsa_stream_t stream);
+
+/*
  * Workspace for gsa_indexer_select: bytes needed for a query chunk of ``chunk_rows`` rows
  * against n_cols keys.
  */
@@ -262,6 +296,35 @@ int gsa_indexer_select_static(const gsa_dims* dims, int dtype, int64_t B, int64_
                               const float* shift, int32_t k_eff, int32_t* cand_idx,
                               float* cand_score, int32_t* cand_count, double* row_stats,
                               gsa_stream_t stream);
+
+/*
+ * The attention of one decode step between its two GEMMs, in one call: B sequences of L new
+ * tokens each, whose K/V and k^I caches hold ``past`` tokens in stores with room for the new ones
+ * (GatedSparseAttention.forward, gated_sparse_attention.py:175-230, after the fused projection
+ * GEMM and before o_proj; the reference concatenates the caches at :188-192 and has no k^I cache):
+ *   gsa_proj_epilogue_cache (K, V, k^I of the new tokens into slots past .. past+L-1)
+ *   -> gsa_indexer_survivors (gsa_indexer_select where the survivor pass does not apply) over
+ *      the past+L keys, offset-causal -> gsa_row_variance -> gsa_adaptive_k (variance mean over
+ *      the B*L rows of the call) -> gsa_select_finalize -> gsa_sparse_sdpa_strided.
+ *   proj       [B*L, proj_ld] dtype: x . Wcat^T + b (the layout of gsa_proj_layout)
+ *   positions  [B*L] int64, or NULL: token t of a sequence at position past + t
+ *   kv_store   [B, cap, 2, Hk, D] dtype (K and V interleaved), batch stride kv_bstride elements
+ *   ki_store   [B, cap, d_I] dtype, batch stride ki_bstride elements
+ *   idx_bias   [H_I] fp32 (GatedLightningIndexer.bias); idx_scale = 1/sqrt(d_I); attn_scale = 1/sqrt(D)
+ *   attn_out   [B*L, H*D] dtype: the gated attention output (o_proj's input)
+ *   k_out      [B*L] int32 or NULL: each row's k_t
+ *   workspace  gsa_decode_workspace_size(dims, tp, dtype, B, L, n_keys) bytes with n_keys >= past + L
+ *              (size it once for the cache capacity), 256-byte aligned.
+ */
+int64_t gsa_decode_workspace_size(const gsa_dims* dims, const gsa_topk_params* tp, int dtype,
+                                  int64_t B, int64_t L, int64_t n_keys);
+int gsa_decode_attend(const gsa_dims* dims, const gsa_proj_layout* layout, const gsa_topk_params* tp,
+                      int dtype, int64_t B, int64_t L, int64_t past, const void* proj, int64_t proj_ld,
+                      const int64_t* positions, const void* cos_tab, const void* sin_tab, int tab_dtype,
+                      int64_t tab_rows, void* kv_store, int64_t kv_bstride, void* ki_store,
+                      int64_t ki_bstride, const float* idx_bias, float idx_scale, float attn_scale,
+                      void* attn_out, int32_t* k_out, void* workspace, int64_t workspace_bytes,
+                      gsa_stream_t stream);
 
 #ifdef __cplusplus
 }

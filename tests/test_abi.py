@@ -90,3 +90,34 @@ def test_survivor_entry_points_validate_before_any_launch():
                                      64, 8192, p, p, p, p, 16, p, 1 << 40, None) == 0
     assert lib.gsa_select_finalize(4, 0, p, p, p, p, p, 4, p, None, None) == 1   # k_eff < 1
     assert lib.gsa_select_finalize(4, 8, p, p, p, p, p, 0, p, None, None) == 1   # sel_ld < 1
+
+
+def test_cache_entry_points_validate_before_any_launch():
+    """gsa_proj_epilogue_cache and gsa_sparse_sdpa_strided reject a batch stride that cannot
+    hold the sequence, without touching the device (CPU only)."""
+    import ctypes as C
+
+    from gsa_b200 import _lib, ops
+
+    lib = _lib.lib()
+    dims = ops.make_dims(4096, 32, 8, 128, 8, 64)
+    lay = _lib.ProjLayout(0, 4096, 5120, 6144, 7168, 11264, 11776, 11840)
+    p = C.c_void_p(16)  # a stand-in pointer: every case below returns before using it
+    kv_ld = 2 * 8 * 128
+
+    def epi(B, L, kv_bstride, ki=None, ki_ld=64, ki_bstride=1 << 30):
+        return lib.gsa_proj_epilogue_cache(C.byref(dims), C.byref(lay), 1, B, L, p, 15936, p, p, p, 1, 4096, p, p,
+                                           p, kv_ld, kv_bstride, ki, ki_ld, ki_bstride, p, p, p, None)
+
+    assert epi(2, 10, 9 * kv_ld) == 1                            # batch stride below L rows
+    assert epi(2, 10, 10 * kv_ld, ki=p, ki_ld=32) == 1           # k^I rows narrower than d_I
+    assert epi(2, 10, 10 * kv_ld, ki=p, ki_bstride=9 * 64) == 1  # k^I batch stride below L rows
+    assert epi(2, 0, 0) == 0 and epi(0, 10, 0) == 0              # empty work is a no-op success
+
+    def sdpa(Lkv, kv_bstride):
+        return lib.gsa_sparse_sdpa_strided(C.byref(dims), 1, 2, 1, Lkv, p, p, p, kv_ld, kv_bstride, p, 16, p, None,
+                                           p, 0.1, None, 0, None)
+
+    assert sdpa(100, 99 * kv_ld) == 1
+    assert lib.gsa_sparse_sdpa_strided(C.byref(dims), 1, 0, 1, 100, p, p, p, kv_ld, 100 * kv_ld, p, 16, p, None, p,
+                                       0.1, None, 0, None) == 0
