@@ -267,6 +267,8 @@ int64_t gsa_sdpa_workspace_size(const gsa_dims* dims, int64_t B, int64_t Lq) {
   if (!dims_ok(dims) || B <= 0 || Lq <= 0) return 0;
   DeviceInfo* di;
   if (device_info(&di)) return 0;
+  // room for the most key ranges the launch may choose (one per resident CTA, at most 8 per
+  // row; at most two resident CTAs per SM)
   const int64_t R = B * Lq, slots = 2LL * di->num_sms;
   if (R >= slots) return 0;
   const int64_t splits = std::min<int64_t>(slots / R, 8);
@@ -353,7 +355,9 @@ static int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
 
 int64_t gsa_survivors_workspace_size(int64_t chunk_rows, int64_t n_cols) {
   if (chunk_rows <= 0 || n_cols <= 0) return 0;
-  return align256(gsa_workspace_size(chunk_rows, n_cols)) + align256(chunk_rows * 4) + 256;
+  // score scratch, failed-row list, its count, per-row segment counts (few-row compaction)
+  return align256(gsa_workspace_size(chunk_rows, n_cols)) + align256(chunk_rows * 4) + 256 +
+         align256(chunk_rows * 16 * 4);
 }
 
 int gsa_indexer_survivors(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int64_t Lkv, int64_t q_pos0,
@@ -380,6 +384,7 @@ int gsa_indexer_survivors(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq
   float* scratch = reinterpret_cast<float*>(wsb);
   int32_t* fail_list = reinterpret_cast<int32_t*>(wsb + align256(gsa_workspace_size(chunk_rows, Lkv)));
   int32_t* fail_count = fail_list + align256(chunk_rows * 4) / 4;
+  int32_t* seg_count = fail_count + 256 / 4;
   const size_t esz = dtype == GSA_DTYPE_BF16 ? 2 : 4;
   const int HI = dims->n_idx_heads;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
@@ -393,7 +398,7 @@ int gsa_indexer_survivors(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq
     if (st) return st;
     st = launch_threshold_candidates(n, c.n, Lkv, q_pos0 + c.t0, causal, scratch, ld, shift + r0, row_stats + r0 * 3,
                                      k_eff, cap, cand_idx + r0 * cap, cand_score + r0 * cap, cand_count + r0,
-                                     fail_list, fail_count, di->num_sms, di->err, s);
+                                     fail_list, fail_count, seg_count, di->num_sms, di->err, s);
     if (st) return st;
   }
   return GSA_OK;
@@ -469,9 +474,11 @@ int gsa_decode_attend(const gsa_dims* dims, const gsa_proj_layout* layout, const
                       const int64_t* positions, const void* cos_tab, const void* sin_tab, int tab_dtype,
                       int64_t tab_rows, void* kv_store, int64_t kv_bstride, void* ki_store, int64_t ki_bstride,
                       const float* idx_bias, float idx_scale, float attn_scale, void* attn_out, int32_t* k_out,
-                      void* workspace, int64_t workspace_bytes, gsa_stream_t stream) {
+                      double* var_total, int phase, void* workspace, int64_t workspace_bytes, gsa_stream_t stream) {
   if (!dims_ok(dims) || !layout || !tp || B < 0 || L < 0 || past < 0 ||
       (dtype != GSA_DTYPE_F32 && dtype != GSA_DTYPE_BF16) || (tab_dtype != GSA_DTYPE_F32 && tab_dtype != GSA_DTYPE_BF16))
+    return GSA_ERR_BAD_ARG;
+  if (phase < GSA_DECODE_ALL || phase > GSA_DECODE_ATTEND || (phase != GSA_DECODE_ALL && !var_total))
     return GSA_ERR_BAD_ARG;
   if (B * L == 0) return GSA_OK;
   if (!proj || !cos_tab || !sin_tab || !kv_store || !ki_store || !idx_bias || !attn_out || tab_rows <= 0 ||
@@ -497,7 +504,7 @@ int gsa_decode_attend(const gsa_dims* dims, const gsa_proj_layout* layout, const
   float* shift = reinterpret_cast<float*>(ws + o.shift);
   double* stats = reinterpret_cast<double*>(ws + o.stats);
   float* var = reinterpret_cast<float*>(ws + o.var);
-  double* total = reinterpret_cast<double*>(ws + o.total);
+  double* total = var_total ? var_total : reinterpret_cast<double*>(ws + o.total);
   int32_t* kt = reinterpret_cast<int32_t*>(ws + o.kt);
   int32_t* cidx = reinterpret_cast<int32_t*>(ws + o.cidx);
   float* cscore = reinterpret_cast<float*>(ws + o.cscore);
@@ -505,6 +512,8 @@ int gsa_decode_attend(const gsa_dims* dims, const gsa_proj_layout* layout, const
   int32_t* sel = reinterpret_cast<int32_t*>(ws + o.sel);
   int32_t* scount = reinterpret_cast<int32_t*>(ws + o.scount);
 
+  if (phase == GSA_DECODE_ATTEND) goto attend;
+  {
   // 1. RoPE / gates / head weights; K, V and k^I of the new tokens into slots past .. past+L-1
   EpiArgs ea{*dims, *layout, dtype, R, proj, proj_ld, positions, cos_tab, sin_tab, tab_dtype, tab_rows,
              q, kvb + past * kv_ld * esz, kvb + (past * kv_ld + row) * esz, kv_ld, g1, w, shift, di->err, L,
@@ -522,12 +531,21 @@ int gsa_decode_attend(const gsa_dims* dims, const gsa_proj_layout* layout, const
                             idx_bias, idx_scale, shift, o.k_eff, cidx, cscore, ccount, stats, R, ws + o.idx_ws,
                             o.idx_ws_bytes, stream);
   if (st) return st;
-  // 3. adaptive k (variance mean over the B * L rows of this call), final selection
-  if (tp->use_adaptive && (st = gsa_row_variance(R, n, dtype, stats, shift, var, total, stream))) return st;
+  // 3. per-row variances and their sum (all-reduced between the phases when the sequences of
+  // the batch are spread over several GPUs)
+  if (tp->use_adaptive) {
+    if ((st = gsa_row_variance(R, n, dtype, stats, shift, var, total, stream))) return st;
+  } else if (var_total && cudaMemsetAsync(var_total, 0, 2 * sizeof(double), s) != cudaSuccess) {
+    return GSA_ERR_CUDA;
+  }
+  if (phase == GSA_DECODE_SCORE) return GSA_OK;
+  }
+attend:
+  // 4. adaptive k (variance mean over every row of the batch), final selection
   if ((st = gsa_adaptive_k(R, n, dtype, tp, var, total, stats, kt, stream))) return st;
   if ((st = gsa_select_finalize(R, o.cand_ld, cidx, cscore, ccount, kt, sel, o.k_eff, scount, nullptr, stream)))
     return st;
-  // 4. sparse SDPA with the G1 gate
+  // 5. sparse SDPA with the G1 gate
   if ((st = gsa_sparse_sdpa_strided(dims, dtype, B, L, n, q, kv_store, kvb + row * esz, kv_ld, kv_bstride, sel,
                                     o.k_eff, scount, g1, attn_out, attn_scale, ws + o.sdpa_ws, o.sdpa_ws_bytes,
                                     stream)))

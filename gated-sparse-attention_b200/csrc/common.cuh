@@ -124,6 +124,11 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gsrc, uint3
       : "memory");
 }
 
+// Prefetch a global range into L2 through the bulk-copy engine (16-byte aligned, multiple of 16).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* gsrc, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gsrc), "r"(bytes) : "memory");
+}
+
 // ---------------------------------------------------------------------------------------------
 // Block-wide helpers.
 // ---------------------------------------------------------------------------------------------

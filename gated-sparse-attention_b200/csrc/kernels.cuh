@@ -87,6 +87,7 @@ struct SdpaArgs {
   int splits;
   float* part;
   int64_t part_floats; // capacity of part
+  int prefetch;        // stages ahead whose keys the producers prefetch into L2 (0: none)
 };
 
 struct SdpaF32Args {
@@ -120,7 +121,7 @@ int launch_topk_candidates(int64_t R, int64_t Lq, int64_t n_cols, int64_t q_pos0
 int launch_threshold_candidates(int64_t R, int64_t Lq, int64_t n_cols, int64_t q_pos0, int causal,
                                 const float* scores, int64_t ld, const float* center, const double* stats,
                                 int32_t K, int32_t cap, int32_t* cand_idx, float* cand_score, int32_t* cand_count,
-                                int32_t* fail_list, int32_t* fail_count, int num_sms, int* err,
+                                int32_t* fail_list, int32_t* fail_count, int32_t* seg_count, int num_sms, int* err,
                                 cudaStream_t stream);
 int launch_select_finalize_warp(int64_t R, int32_t cand_ld, const int32_t* cand_idx, const float* cand_score,
                                 const int32_t* cand_count, const int32_t* k, int32_t* sel_idx, int64_t sel_ld,

@@ -152,7 +152,8 @@ __global__ void __launch_bounds__(256) proj_epilogue_bf16_kernel(EpiArgs a) {
   const int nki = a.ki_out ? a.d.d_idx / 8 : 0;
   const int ntask = nq + nk + nv + ng + nki;
   const int64_t kv_off = epi_kv_off(a, t);
-  for (int task = threadIdx.x; task < ntask; task += blockDim.x) {
+  // gridDim.y CTAs share a token's tasks (few tokens: decode)
+  for (int task = blockIdx.y * blockDim.x + threadIdx.x; task < ntask; task += gridDim.y * blockDim.x) {
     if (task < nq + nk) {
       const bool isq = task < nq;
       const int tt = isq ? task : task - nq;
@@ -194,7 +195,7 @@ __global__ void __launch_bounds__(256) proj_epilogue_bf16_kernel(EpiArgs a) {
       st8_bf16(go + t * (int64_t)H * D + i, g);
     }
   }
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == 0 && blockIdx.y == 0) {
     float sum = 0.f;
     for (int j = 0; j < HI; ++j) {
       float w = rnd(sigmoid_precise(__bfloat162float(prow[a.lay.wi + j])), dt);
@@ -226,10 +227,12 @@ int launch_proj_epilogue(const EpiArgs& a, cudaStream_t stream) {
   if (a.T == 0) return GSA_OK;
   if (a.T > 0x7fffffffLL) return GSA_ERR_BAD_ARG;
   if (epilogue_vec_ok(a)) {
+    // few tokens (decode): four CTAs per token, so that the copy latency is spread over more SMs
+    const dim3 grid((unsigned)a.T, a.T < 512 ? 4u : 1u);
     if (a.tab_dtype == GSA_DTYPE_BF16)
-      proj_epilogue_bf16_kernel<__nv_bfloat16><<<(unsigned)a.T, 256, 0, stream>>>(a);
+      proj_epilogue_bf16_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(a);
     else
-      proj_epilogue_bf16_kernel<float><<<(unsigned)a.T, 256, 0, stream>>>(a);
+      proj_epilogue_bf16_kernel<float><<<grid, 256, 0, stream>>>(a);
   } else {
     proj_epilogue_kernel<<<(unsigned)a.T, 128, 0, stream>>>(a);
   }

@@ -143,6 +143,23 @@ __global__ void __launch_bounds__(MAXW * 32) sdpa_tc_kernel(SdpaArgs a) {
             j = -1;
           }
         }
+        // few rows (DRAM-latency bound): warm L2 with the keys a.prefetch stages ahead, so that
+        // the ring's copies, which hold shared memory until the consumers take them, land sooner
+        if (a.prefetch) {
+          const int pkey = key + a.prefetch * kKeysPerStage;
+          if (pkey < cnt && pkey < kb_hi * kKeysPerStage) {
+            const int64_t j2 = idx[pkey];
+            if (j2 >= 0 && j2 < a.Lkv) {
+              if (a.interleaved) {
+                if (lane < 8) bulk_prefetch_l2(kbase + j2 * kv_row, (uint32_t)(2 * row_bytes));
+              } else if (lane < 8) {
+                bulk_prefetch_l2(kbase + j2 * kv_row, (uint32_t)row_bytes);
+              } else if (lane < 16) {
+                bulk_prefetch_l2(vbase + j2 * kv_row, (uint32_t)row_bytes);
+              }
+            }
+          }
+        }
         uint8_t* dst = stages + s * stage_bytes + slot * rs;
         if (a.interleaved) {
           // one copy per key: K row and V row are adjacent
@@ -372,27 +389,34 @@ __global__ void sdpa_f32_kernel(SdpaF32Args a) {
   }
 }
 
-// Merge the key-range partials of each row: out = bf16(sum_s 2^(lse_s - M) o_s / sum_s 2^(lse_s - M)),
-// times the G1 gate (the unsplit epilogue's roundings).  One CTA per row.
+// Merge the key-range partials of each (row, head): out = bf16(sum_s 2^(lse_s - M) o_s /
+// sum_s 2^(lse_s - M)), times the G1 gate (the unsplit epilogue's roundings).  One CTA per
+// (row, head), one thread per dimension; the split weights are computed once per CTA.
 __global__ void sdpa_combine_kernel(int64_t R, int H, int D, int splits, const float* part,
                                     const __nv_bfloat16* gate, __nv_bfloat16* out) {
   const int64_t row = blockIdx.x;
+  const int h = blockIdx.y;
   const int64_t NW = R * splits;
-  const float* lse = part + NW * H * D + row * splits * H;
-  for (int e = threadIdx.x; e < H * D; e += blockDim.x) {
-    const int h = e / D;
+  __shared__ float wsh[16];
+  __shared__ float inv_den;
+  if (threadIdx.x == 0) {
+    const float* lse = part + NW * H * D + row * splits * H + h;
     float M = -INFINITY;
-    for (int s = 0; s < splits; ++s) M = fmaxf(M, lse[s * H + h]);
-    float num = 0.f, den = 0.f;
-    if (M > -INFINITY) {
-      for (int s = 0; s < splits; ++s) {
-        const float w = exp2f(lse[s * H + h] - M);
-        num = fmaf(w, part[((row * splits + s) * H) * D + e], num);
-        den += w;
-      }
+    for (int s = 0; s < splits; ++s) M = fmaxf(M, lse[s * H]);
+    float den = 0.f;
+    for (int s = 0; s < splits; ++s) {
+      const float w = M > -INFINITY ? exp2f(lse[s * H] - M) : 0.f;
+      wsh[s] = w;
+      den += w;
     }
-    const int64_t off = row * H * D + e;
-    float y = __bfloat162float(__float2bfloat16_rn(den > 0.f ? num / den : 0.f));
+    inv_den = den > 0.f ? 1.f / den : 0.f;
+  }
+  __syncthreads();
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float num = 0.f;
+    for (int s = 0; s < splits; ++s) num = fmaf(wsh[s], part[((row * splits + s) * H + h) * D + d], num);
+    const int64_t off = (row * H + h) * D + d;
+    float y = __bfloat162float(__float2bfloat16_rn(num * inv_den));
     if (gate) y *= __bfloat162float(gate[off]);
     out[off] = __float2bfloat16_rn(y);
   }
@@ -426,20 +450,24 @@ static int launch_tc_w(SdpaArgs a, int num_sms, cudaStream_t stream) {
   const int64_t R = a.B * a.Lq;
   const int H = a.Hk * NREP;
   int64_t grid = (int64_t)num_sms * per_sm;
-  // fewer rows than resident CTAs: cut each row's keys into ranges (as many as the partials
-  // buffer holds) so that every CTA streams keys
+  // fewer rows than resident CTAs: cut each row's keys into ranges (one per CTA, as many as the
+  // partials buffer holds) so that every CTA streams keys; finer ranges cost more in per-range
+  // set-up and partials than they gain in balance.  Those launches are bound by DRAM latency,
+  // so their producers also prefetch into L2 four stages ahead.
   a.splits = 1;
+  a.prefetch = 0;
   if (a.part && R < grid) {
     int64_t sp = std::min<int64_t>(grid / R, kMaxSplits);
     while (sp > 1 && R * sp * H * (D + 1) > a.part_floats) --sp;
     a.splits = (int)sp;
+    a.prefetch = 4;
   }
   const int64_t items = R * a.splits;
   if (grid > items) grid = items;
   kern<<<(unsigned)grid, threads, smem, stream>>>(a);
   if (cudaGetLastError() != cudaSuccess) return GSA_ERR_LAUNCH;
   if (a.splits > 1) {
-    sdpa_combine_kernel<<<(unsigned)R, 256, 0, stream>>>(R, H, D, a.splits, a.part, a.gate, a.out);
+    sdpa_combine_kernel<<<dim3((unsigned)R, (unsigned)H), D, 0, stream>>>(R, H, D, a.splits, a.part, a.gate, a.out);
     if (cudaGetLastError() != cudaSuccess) return GSA_ERR_LAUNCH;
   }
   return GSA_OK;

@@ -788,6 +788,123 @@ __global__ void __launch_bounds__(kCmpThreads) threshold_compact_kernel(CmpArgs 
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// The same compaction for few rows (decode: one row per sequence): each row is cut into kFewSegs
+// column segments taken by separate CTAs, in two passes over the scores (the second mostly from
+// L2): count each segment's survivors, then write them from the segment's offset (the counts of
+// the row's earlier segments).  Output identical to threshold_compact_kernel.
+// ---------------------------------------------------------------------------------------------
+constexpr int kFewThreads = 256;
+constexpr int kFewSegsMax = 16;
+constexpr int kFewCols = 32;                          // consecutive columns per thread per round
+constexpr int kFewRound = kFewThreads * kFewCols;     // 8192 columns
+
+__device__ __forceinline__ void few_segment(const CmpArgs& a, int64_t r, int nseg, int sg, int64_t& n, int64_t& c0,
+                                            int64_t& c1) {
+  n = cmp_row_cols(a, r);
+  // segments of whole 1024-column groups
+  const int64_t groups = (n + 1023) / 1024;
+  const int64_t per = (groups + nseg - 1) / nseg;
+  c0 = min(n, (int64_t)sg * per * 1024);
+  c1 = min(n, c0 + per * 1024);
+}
+
+// The survivor flags of this thread's kFewCols consecutive columns from c (bit i: column c + i).
+__device__ __forceinline__ uint32_t few_flags(const float* row, int64_t c, int64_t c1, float tau, float (&v)[kFewCols]) {
+#pragma unroll
+  for (int j = 0; j < kFewCols / 4; ++j) {
+    float4 f = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+    if (c + 4 * j < c1) f = __ldg(reinterpret_cast<const float4*>(row + c + 4 * j));
+    v[4 * j] = f.x; v[4 * j + 1] = f.y; v[4 * j + 2] = f.z; v[4 * j + 3] = f.w;
+  }
+  uint32_t fl = 0;
+#pragma unroll
+  for (int i = 0; i < kFewCols; ++i)
+    if (c + i < c1 && v[i] >= tau && v[i] > -INFINITY) fl |= 1u << i;  // NaN fails both
+  return fl;
+}
+
+__global__ void __launch_bounds__(kFewThreads) compact_few_count_kernel(CmpArgs a, int nseg, int32_t* seg_count) {
+  const int64_t r = blockIdx.x;
+  const int sg = blockIdx.y;
+  int64_t n, c0, c1;
+  few_segment(a, r, nseg, sg, n, c0, c1);
+  const float tau = cmp_threshold(a, r, n);
+  const float* row = a.scores + r * a.ld;
+  uint32_t cnt = 0;
+  for (int64_t g0 = c0; g0 < c1; g0 += kFewRound) {
+    float v[kFewCols];
+    cnt += __popc(few_flags(row, g0 + (int64_t)kFewCols * threadIdx.x, c1, tau, v));
+  }
+  __shared__ uint32_t ws[kFewThreads / 32];
+  cnt = warp_sum(cnt);
+  if ((threadIdx.x & 31) == 0) ws[threadIdx.x >> 5] = cnt;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t t = 0;
+    for (int w = 0; w < kFewThreads / 32; ++w) t += ws[w];
+    seg_count[r * kFewSegsMax + sg] = (int32_t)t;
+  }
+}
+
+__global__ void __launch_bounds__(kFewThreads) compact_few_write_kernel(CmpArgs a, int nseg, const int32_t* seg_count) {
+  const int64_t r = blockIdx.x;
+  const int sg = blockIdx.y;
+  int64_t n, c0, c1;
+  few_segment(a, r, nseg, sg, n, c0, c1);
+  const float tau = cmp_threshold(a, r, n);
+  const float* row = a.scores + r * a.ld;
+  uint32_t base = 0, total = 0;
+  for (int s2 = 0; s2 < nseg; ++s2) {
+    const uint32_t c = (uint32_t)seg_count[r * kFewSegsMax + s2];
+    if (s2 < sg) base += c;
+    total += c;
+  }
+  int32_t* oi = a.idx + r * a.cap;
+  float* os = a.score + r * a.cap;
+  __shared__ uint32_t ws[kFewThreads / 32];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  for (int64_t g0 = c0; g0 < c1; g0 += kFewRound) {
+    const int64_t c = g0 + (int64_t)kFewCols * threadIdx.x;
+    float v[kFewCols];
+    const uint32_t fl = few_flags(row, c, c1, tau, v);
+    // exclusive prefix of the survivor counts in column order (thread order = column order)
+    const uint32_t k = __popc(fl);
+    uint32_t x = k;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) ws[wid] = x;
+    __syncthreads();
+    uint32_t off = 0, tot = 0;
+#pragma unroll
+    for (int w = 0; w < kFewThreads / 32; ++w) {
+      const uint32_t cw = ws[w];
+      if (w < wid) off += cw;
+      tot += cw;
+    }
+    __syncthreads();
+    uint32_t pos = base + off + x - k;
+#pragma unroll
+    for (int i = 0; i < kFewCols; ++i)
+      if (fl & (1u << i)) {
+        if (pos < (uint32_t)a.cap) {
+          oi[pos] = (int32_t)(c + i);
+          os[pos] = v[i];
+        }
+        ++pos;
+      }
+    base += tot;
+  }
+  if (sg == 0 && threadIdx.x == 0) {
+    const int64_t need = min((int64_t)a.K, n);
+    if ((int64_t)total > a.cap || (int64_t)total < need) a.fail_list[atomicAdd(a.fail_count, 1)] = (int32_t)r;
+    a.count[r] = (int32_t)min(total, (uint32_t)a.cap);
+  }
+}
+
 // Exact selection (topk_row) of the rows the compaction could not settle.
 __global__ void __launch_bounds__(kSelThreads) topk_fallback_kernel(CmpArgs a) {
   extern __shared__ __align__(16) uint8_t topk_dyn[];
@@ -803,24 +920,36 @@ __global__ void __launch_bounds__(kSelThreads) topk_fallback_kernel(CmpArgs a) {
 int launch_threshold_candidates(int64_t R, int64_t Lq, int64_t n_cols, int64_t q_pos0, int causal,
                                 const float* scores, int64_t ld, const float* center, const double* stats,
                                 int32_t K, int32_t cap, int32_t* cand_idx, float* cand_score, int32_t* cand_count,
-                                int32_t* fail_list, int32_t* fail_count, int num_sms, int* err,
+                                int32_t* fail_list, int32_t* fail_count, int32_t* seg_count, int num_sms, int* err,
                                 cudaStream_t stream) {
   if (R == 0) return GSA_OK;
   if (R > 0x7fffffffLL || ld % 4 != 0 || (reinterpret_cast<uintptr_t>(scores) % 16) != 0) return GSA_ERR_BAD_ARG;
   CmpArgs a{R, Lq, n_cols, q_pos0, causal, scores, ld, center, stats, K, cap, cand_idx, cand_score, cand_count,
             fail_list, fail_count, err};
   if (cudaMemsetAsync(fail_count, 0, sizeof(int32_t), stream) != cudaSuccess) return GSA_ERR_CUDA;
-  if (cudaFuncSetAttribute(threshold_compact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kCmpSmem) !=
-      cudaSuccess)
-    return GSA_ERR_LAUNCH;
-  int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, threshold_compact_kernel, kCmpThreads, kCmpSmem) !=
-          cudaSuccess ||
-      per_sm < 1)
-    return GSA_ERR_LAUNCH;
-  int64_t grid = (int64_t)num_sms * per_sm;
-  if (grid > R) grid = R;
-  threshold_compact_kernel<<<(unsigned)grid, kCmpThreads, kCmpSmem, stream>>>(a);
+  if (seg_count && R < num_sms && R <= 65535) {
+    // few rows: about four CTAs per SM in all, and segments of at most one 8192-column round
+    // where 16 segments allow it
+    const int64_t groups = (n_cols + 1023) / 1024;
+    int64_t ns = std::max<int64_t>((groups + 7) / 8, (4LL * num_sms + R - 1) / R);
+    ns = std::min<int64_t>(std::min<int64_t>(ns, kFewSegsMax), std::max<int64_t>(1, groups));
+    const int nseg = (int)ns;
+    const dim3 grid((unsigned)R, (unsigned)nseg);
+    compact_few_count_kernel<<<grid, kFewThreads, 0, stream>>>(a, nseg, seg_count);
+    compact_few_write_kernel<<<grid, kFewThreads, 0, stream>>>(a, nseg, seg_count);
+  } else {
+    if (cudaFuncSetAttribute(threshold_compact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kCmpSmem) !=
+        cudaSuccess)
+      return GSA_ERR_LAUNCH;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, threshold_compact_kernel, kCmpThreads, kCmpSmem) !=
+            cudaSuccess ||
+        per_sm < 1)
+      return GSA_ERR_LAUNCH;
+    int64_t grid = (int64_t)num_sms * per_sm;
+    if (grid > R) grid = R;
+    threshold_compact_kernel<<<(unsigned)grid, kCmpThreads, kCmpSmem, stream>>>(a);
+  }
   if (cudaGetLastError() != cudaSuccess) return GSA_ERR_LAUNCH;
   const size_t dyn = 2 * kCap * sizeof(float) + kCap + kRankCap * sizeof(uint32_t);
   if (cudaFuncSetAttribute(topk_fallback_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn) !=

@@ -76,7 +76,7 @@ SIGNATURES = {
     "gsa_sdpa_workspace_size": [P, I64, I64],
     "gsa_decode_workspace_size": [P, P, INT, I64, I64, I64],
     "gsa_decode_attend": [P, P, P, INT, I64, I64, I64, P, I64, P, P, P, INT, I64, P, I64, P, I64, P, F32, F32, P, P,
-                          P, I64, P],
+                          P, INT, P, I64, P],
     "gsa_workspace_size": [I64, I64],
     "gsa_indexer_select": [P, INT, I64, I64, I64, I64, INT, P, I64, I64, P, I64, I64, P, P, F32, P,
                            I32, P, P, P, P, I64, P, I64, P],

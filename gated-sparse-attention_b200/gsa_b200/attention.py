@@ -595,14 +595,16 @@ class GatedSparseAttention(nn.Module):
         proj = torch.addmm(bvec, x.reshape(B * L, self.d_model), W.t())
         n_all = past_len + L
         if (store is not None and self.native_step and self.selection_path == "auto" and mark_fn is None
-                and capture is None and not output_attentions and self.sequence_shards is None
+                and capture is None and not output_attentions
                 and B * L * ((n_all + 3) // 4 * 4) * 4 <= ops.SCORE_CHUNK_BYTES):
             # everything between the two GEMMs in one native call, scratch kept on the store
             dims, tp, idx_bias = self._step_constants()
             nbytes = ops.decode_workspace_bytes(dims, tp, dt, B, L, store.capacity)
             attn = ops.decode_attend(dims, layout, tp, proj, B, L, past_len, positions if positions_given else None,
                                      self.rotary_emb.cos_cached, self.rotary_emb.sin_cached, store.kv, store.ki,
-                                     idx_bias, self.indexer.scale, self.scale, store.scratch((B, L), nbytes))
+                                     idx_bias, self.indexer.scale, self.scale, store.scratch((B, L), nbytes),
+                                     allreduce=(self.sequence_shards.allreduce if self.sequence_shards is not None
+                                                and cfg.use_adaptive_k else None))
             out = F.linear(attn.view(B, L, H * D), self.o_proj.weight)
             present = None
             if use_cache:

@@ -195,20 +195,33 @@ def decode_workspace_bytes(dims: Dims, tp: TopkParams, dt: torch.dtype, B: int, 
     return int(_lib.lib().gsa_decode_workspace_size(C.byref(dims), C.byref(tp), dtype_code(dt), B, L, n_keys))
 
 
+DECODE_ALL, DECODE_SCORE, DECODE_ATTEND = 0, 1, 2
+
+
 def decode_attend(dims: Dims, layout: ProjLayout, tp: TopkParams, proj: torch.Tensor, B: int, L: int, past: int,
                   positions, cos_tab, sin_tab, kv_store: torch.Tensor, ki_store: torch.Tensor, idx_bias: torch.Tensor,
-                  idx_scale: float, attn_scale: float, workspace: torch.Tensor) -> torch.Tensor:
-    """The attention of one step between its two GEMMs in one native call (gsa_decode_attend):
+                  idx_scale: float, attn_scale: float, workspace: torch.Tensor, allreduce=None) -> torch.Tensor:
+    """The attention of one step between its two GEMMs in native calls (gsa_decode_attend):
     the new tokens' K, V, k^I appended to the stores at slot ``past``, the indexer over all
-    past + L keys, the selection and the gated SDPA.  Returns attn [B*L, H*D]."""
+    past + L keys, the selection and the gated SDPA.  ``allreduce(t)`` (sequences spread over
+    several GPUs): the step runs in two phases with the variance sum all-reduced in between.
+    Returns attn [B*L, H*D]."""
     dt = proj.dtype
     attn = torch.empty(B * L, dims.n_heads * dims.d_head, device=proj.device, dtype=dt)
     if positions is not None:
         positions = positions.reshape(-1).to(torch.int64).contiguous()
-    _lib.call("gsa_decode_attend", C.byref(dims), C.byref(layout), C.byref(tp), dtype_code(dt), B, L, past,
-              _p(proj), proj.stride(0), _p(positions), _p(cos_tab), _p(sin_tab), dtype_code(cos_tab.dtype),
-              cos_tab.shape[0], _p(kv_store), kv_store.stride(0), _p(ki_store), ki_store.stride(0), _p(idx_bias),
-              float(idx_scale), float(attn_scale), _p(attn), None, _p(workspace), workspace.numel(), _stream())
+    args = [C.byref(dims), C.byref(layout), C.byref(tp), dtype_code(dt), B, L, past, _p(proj), proj.stride(0),
+            _p(positions), _p(cos_tab), _p(sin_tab), dtype_code(cos_tab.dtype), cos_tab.shape[0], _p(kv_store),
+            kv_store.stride(0), _p(ki_store), ki_store.stride(0), _p(idx_bias), float(idx_scale), float(attn_scale),
+            _p(attn), None]
+    tail = [_p(workspace), workspace.numel(), _stream()]
+    if allreduce is None:
+        _lib.call("gsa_decode_attend", *args, None, DECODE_ALL, *tail)
+    else:
+        total = torch.empty(2, device=proj.device, dtype=torch.float64)
+        _lib.call("gsa_decode_attend", *args, _p(total), DECODE_SCORE, *tail)
+        total = allreduce(total)
+        _lib.call("gsa_decode_attend", *args, _p(total), DECODE_ATTEND, *tail)
     _after("decode_attend")
     return attn
 

@@ -313,9 +313,16 @@ int gsa_indexer_select_static(const gsa_dims* dims, int dtype, int64_t B, int64_
  *   idx_bias   [H_I] fp32 (GatedLightningIndexer.bias); idx_scale = 1/sqrt(d_I); attn_scale = 1/sqrt(D)
  *   attn_out   [B*L, H*D] dtype: the gated attention output (o_proj's input)
  *   k_out      [B*L] int32 or NULL: each row's k_t
+ *   phase      GSA_DECODE_ALL: the whole step.  When the batch's sequences are spread over several
+ *              GPUs (the adaptive k's variance mean spans all of them, adaptive_topk.py:93-96):
+ *              GSA_DECODE_SCORE runs up to the row variances and leaves (sum of variances, row
+ *              count) in var_total [2] fp64; the caller all-reduces it; GSA_DECODE_ATTEND with the
+ *              same arguments and workspace finishes the step from var_total.
+ *   var_total  [2] fp64, required for the two phases (NULL with GSA_DECODE_ALL)
  *   workspace  gsa_decode_workspace_size(dims, tp, dtype, B, L, n_keys) bytes with n_keys >= past + L
  *              (size it once for the cache capacity), 256-byte aligned.
  */
+enum { GSA_DECODE_ALL = 0, GSA_DECODE_SCORE = 1, GSA_DECODE_ATTEND = 2 };
 int64_t gsa_decode_workspace_size(const gsa_dims* dims, const gsa_topk_params* tp, int dtype,
                                   int64_t B, int64_t L, int64_t n_keys);
 int gsa_decode_attend(const gsa_dims* dims, const gsa_proj_layout* layout, const gsa_topk_params* tp,
@@ -323,8 +330,8 @@ int gsa_decode_attend(const gsa_dims* dims, const gsa_proj_layout* layout, const
                       const int64_t* positions, const void* cos_tab, const void* sin_tab, int tab_dtype,
                       int64_t tab_rows, void* kv_store, int64_t kv_bstride, void* ki_store,
                       int64_t ki_bstride, const float* idx_bias, float idx_scale, float attn_scale,
-                      void* attn_out, int32_t* k_out, void* workspace, int64_t workspace_bytes,
-                      gsa_stream_t stream);
+                      void* attn_out, int32_t* k_out, double* var_total, int phase, void* workspace,
+                      int64_t workspace_bytes, gsa_stream_t stream);
 
 #ifdef __cplusplus
 }

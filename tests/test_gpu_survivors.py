@@ -2,8 +2,9 @@
 (gsa_indexer_select) on the same inputs: each row's survivors are in ascending column order,
 contain its k_eff best keys, and the final selection (gsa_select_finalize) from them equals the
 selection from the exact candidates.  Covered: rows short enough to keep every key, thresholded
-rows, batch > 1 with a query offset, non-causal rows, H_I = 4, the fp32 indexer, and tied
-scores that defeat the threshold so that the exact per-row selection takes over."""
+rows, batch > 1 with a query offset, non-causal rows, H_I = 4, the fp32 indexer, tied
+scores that defeat the threshold so that the exact per-row selection takes over, and decode
+rows (one or two per sequence, many sequences per pass: the few-row compaction)."""
 
 import math
 
@@ -34,6 +35,9 @@ def _inputs(B, Lq, Lkv, HI, seed, dtype=torch.bfloat16, dI=64, zero_keys_from=No
     (torch.float32, 1, 400, 12000, 8, 11600, True, 1024, None, 128),   # fp32 indexer kernel
     (torch.bfloat16, 1, 256, 20000, 8, 19744, True, 4096, 0, 100),     # all keys tie: exact fallback
     (torch.bfloat16, 1, 512, 24000, 8, 23488, True, 4096, 12000, 512), # half the keys tie
+    (torch.bfloat16, 37, 1, 30000, 8, 29999, True, 4096, None, 64),   # decode rows: few-row compaction
+    (torch.bfloat16, 20, 1, 20000, 8, 19999, True, 4096, 0, 64),      # decode rows, all tie: exact fallback
+    (torch.bfloat16, 9, 2, 9000, 4, 8998, True, 2048, None, 64),      # two tokens per sequence, H_I = 4
 ])
 def test_survivors_select_the_exact_keys(cuda_ok, dtype, B, Lq, Lkv, HI, q_pos0, causal, k_eff, zero_from,
                                          chunk):

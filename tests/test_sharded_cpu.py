@@ -1,6 +1,7 @@
 """Query-sequence sharding on CPU ranks (gloo, world size 2): the decomposition the layer uses
 across GPUs (gsa_b200.sharded) -- contiguous query blocks, an all-gather of K / V / k^I, an
-offset-causal indexer and an all-reduce of the variance sum -- reproduces the unsharded layer.
+offset-causal indexer and an all-reduce of the variance sum -- reproduces the unsharded layer,
+and so does the batch split by sequence (the decode layout: only the variance sum is shared).
 The kernels' roles are played by the CPU oracle; the sharding code is the product's.  Also:
 a rank that fails before the exchange makes the other rank's collective end with an error
 instead of waiting forever."""
@@ -104,6 +105,75 @@ def test_query_sharded_layer_matches_unsharded(layout, folds):
     q = ctx.Queue()
     port = _free_port()
     procs = [ctx.Process(target=_worker_equivalence, args=(r, 2, port, layout, folds, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    status, err, kdiff = q.get(timeout=10)
+    assert status == "ok", err
+    assert err < 1e-5, err
+    assert kdiff == 0
+
+
+def _worker_sequence_shards(rank, world, port, q):
+    """Each rank runs the oracle layer on its own sequences of the batch; only the variance sum
+    is all-reduced (SequenceShards, the decode layout across GPUs)."""
+    import sys
+    for p in (ROOT / "gated-sparse-attention_b200", ROOT / "oracle", ROOT / "tests"):
+        sys.path.insert(0, str(p))
+    torch.set_num_threads(1)
+    import torch.nn.functional as F
+    import gsa_oracle as O
+    from gsa_b200.sharded import SequenceShards
+
+    try:
+        _init(rank, world, port)
+        _, meta = load_golden("tiny_fp32_b2_l192")
+        cfg, m, x = golden_inputs(meta)
+        W = dict(m.state_dict())
+        B, L = x.shape[0], x.shape[1]
+        per = B // world
+        x_local = x[rank * per:(rank + 1) * per]
+        shards = SequenceShards(dist.group.WORLD)
+        oc = O.OracleConfig.from_config(cfg)
+        pos = torch.arange(L).unsqueeze(0).expand(per, -1)
+        cos, sin = O.rope_cache(cfg.d_head, cfg.max_position_embeddings, cfg.rope_base, cfg.rope_scaling)
+        qh, k, v = O.project(W, oc, x_local, pos, cos, sin)
+        q_idx = F.linear(x_local, W["indexer.q_proj.weight"]).view(per, L, cfg.n_indexer_heads, cfg.d_indexer)
+        k_idx = F.linear(x_local, W["indexer.k_proj.weight"])
+        wts = torch.sigmoid(F.linear(x_local, W["indexer.weight_proj.weight"], W["indexer.weight_proj.bias"]))
+        scores = O.indexer_scores_from_proj(q_idx, k_idx, wts, W["indexer.bias"], "sigmoid", q_offset=0)
+        var, valid = O.row_variance(scores)
+        total = shards.allreduce(torch.tensor([float(var.double().sum()), float(var.numel())], dtype=torch.float64))
+        mean = torch.tensor(float(total[0]) / float(total[1]), dtype=var.dtype)
+        kv = O.adaptive_k(var, valid, mean, cfg.k_base, cfg.k_min, cfg.k_max, cfg.adaptive_k_temperature)
+        idx, msk = O.topk_select(scores, min(cfg.k_max, L), kv)
+        attn, _ = O.sparse_attention(qh, k, v, idx, msk, cfg.n_heads // cfg.n_kv_heads, 1.0 / math.sqrt(cfg.d_head))
+        g = F.linear(x_local, W["output_gate.gate_proj.weight"], W["output_gate.gate_proj.bias"])
+        out = F.linear((attn * torch.sigmoid(g.view(per, L, cfg.n_heads, cfg.d_head))).reshape(per, L, -1),
+                       W["o_proj.weight"])
+        outs = [torch.empty_like(out) for _ in range(world)]
+        ks = [torch.empty_like(kv) for _ in range(world)]
+        dist.all_gather(outs, out)
+        dist.all_gather(ks, kv)
+        if rank == 0:
+            ref = O.gsa_forward(W, oc, x, chunk=64, keep=("k_values",))
+            full = torch.cat(outs)
+            err = float((full - ref["out"]).norm() / ref["out"].norm())
+            q.put(("ok", err, int((torch.cat(ks) != ref["k_values"]).sum())))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # pragma: no cover - reported to the parent
+        q.put(("error", repr(e), -1))
+
+
+def test_sequence_sharded_batch_matches_unsharded():
+    """The batch's sequences split over two ranks (SequenceShards): with the variance sum
+    all-reduced, every k_t and output equals the one-process layer over the whole batch."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_sequence_shards, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
