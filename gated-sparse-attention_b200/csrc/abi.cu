@@ -276,10 +276,12 @@ int64_t gsa_sdpa_workspace_size(const gsa_dims* dims, int64_t B, int64_t Lq) {
   return R * splits * (int64_t)dims->n_heads * (dims->d_head + 1) * (int64_t)sizeof(float);
 }
 
-int gsa_sparse_sdpa_strided(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int64_t Lkv, const void* q,
-                            const void* k, const void* v, int64_t kv_ld, int64_t kv_bstride, const int32_t* sel_idx,
-                            int64_t sel_ld, const int32_t* sel_count, const void* gate, void* out, float scale,
-                            void* workspace, int64_t workspace_bytes, gsa_stream_t stream) {
+}  // extern "C"
+
+static int sdpa_impl(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int64_t Lkv, const void* q, const void* k,
+                     const void* v, int64_t kv_ld, int64_t kv_bstride, const int32_t* sel_idx, int64_t sel_ld,
+                     const int32_t* sel_count, const void* gate, void* out, float scale, void* workspace,
+                     int64_t workspace_bytes, float* lse_out, gsa_stream_t stream) {
   if (!dims_ok(dims) || B < 0 || Lq < 0 || Lkv < 0 || sel_ld < 0) return GSA_ERR_BAD_ARG;
   if (B * Lq == 0) return GSA_OK;
   if (!q || !k || !v || !sel_idx || !sel_count || !out) return GSA_ERR_BAD_ARG;
@@ -300,17 +302,62 @@ int gsa_sparse_sdpa_strided(const gsa_dims* dims, int dtype, int64_t B, int64_t 
                static_cast<const __nv_bfloat16*>(gate), static_cast<__nv_bfloat16*>(out),
                scale * 1.4426950408889634f, 0, 2, di->err, kv_bstride, 1,
                (workspace && aligned(workspace, 16)) ? static_cast<float*>(workspace) : nullptr,
-               workspace ? workspace_bytes / (int64_t)sizeof(float) : 0};
+               workspace ? workspace_bytes / (int64_t)sizeof(float) : 0, 0, lse_out};
     return launch_sdpa_bf16(a, dims->d_head, dims->n_heads / dims->n_kv_heads, di->num_sms, s);
   }
   if (dtype == GSA_DTYPE_F32) {
     SdpaF32Args a{B, Lq, Lkv, dims->n_heads, dims->n_kv_heads, dims->d_head,
                   static_cast<const float*>(q), static_cast<const float*>(k), static_cast<const float*>(v),
                   kv_ld, sel_idx, sel_ld, sel_count, static_cast<const float*>(gate), static_cast<float*>(out),
-                  scale, di->err, kv_bstride};
+                  scale, di->err, kv_bstride, lse_out};
     return launch_sdpa_f32(a, s);
   }
   return GSA_ERR_BAD_ARG;
+}
+
+extern "C" {
+
+int gsa_sparse_sdpa_strided(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int64_t Lkv, const void* q,
+                            const void* k, const void* v, int64_t kv_ld, int64_t kv_bstride, const int32_t* sel_idx,
+                            int64_t sel_ld, const int32_t* sel_count, const void* gate, void* out, float scale,
+                            void* workspace, int64_t workspace_bytes, gsa_stream_t stream) {
+  return sdpa_impl(dims, dtype, B, Lq, Lkv, q, k, v, kv_ld, kv_bstride, sel_idx, sel_ld, sel_count, gate, out, scale,
+                   workspace, workspace_bytes, nullptr, stream);
+}
+
+int gsa_sparse_sdpa_lse(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int64_t Lkv, const void* q,
+                        const void* k, const void* v, int64_t kv_ld, int64_t kv_bstride, const int32_t* sel_idx,
+                        int64_t sel_ld, const int32_t* sel_count, const void* gate, void* out, float* lse_out,
+                        float scale, gsa_stream_t stream) {
+  if (!lse_out) return GSA_ERR_BAD_ARG;
+  return sdpa_impl(dims, dtype, B, Lq, Lkv, q, k, v, kv_ld, kv_bstride, sel_idx, sel_ld, sel_count, gate, out, scale,
+                   nullptr, 0, lse_out, stream);
+}
+
+int gsa_sparse_sdpa_backward(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int64_t Lkv, const void* q,
+                             const void* k, const void* v, int64_t kv_ld, int64_t kv_bstride, const int32_t* sel_idx,
+                             int64_t sel_ld, const int32_t* sel_count, const void* o, const void* d_o,
+                             const float* lse, float* dq, float* dk, float* dv, int64_t dkv_ld, int64_t dkv_bstride,
+                             float scale, gsa_stream_t stream) {
+  if (!dims_ok(dims) || B < 0 || Lq < 0 || Lkv < 0 || sel_ld < 0 || (dtype != GSA_DTYPE_F32 && dtype != GSA_DTYPE_BF16))
+    return GSA_ERR_BAD_ARG;
+  if (B * Lq == 0) return GSA_OK;
+  if (!q || !k || !v || !sel_idx || !sel_count || !o || !d_o || !lse || !dq || !dk || !dv) return GSA_ERR_BAD_ARG;
+  const int64_t row_elems = (int64_t)dims->n_kv_heads * dims->d_head;
+  if (kv_ld < row_elems || kv_bstride < Lkv * kv_ld || dkv_ld < row_elems || dkv_bstride < Lkv * dkv_ld)
+    return GSA_ERR_BAD_ARG;
+  const size_t esz = dtype == GSA_DTYPE_BF16 ? 2 : 4;
+  // vector loads of a lane's D/32 consecutive elements, vector atomics into dk / dv
+  if (!aligned(q, 16) || !aligned(k, 8) || !aligned(v, 8) || !aligned(o, 8) || !aligned(d_o, 8) || !aligned(dk, 16) ||
+      !aligned(dv, 16) || !aligned(dq, 16) || (kv_ld * esz) % 8 || (kv_bstride * esz) % 8 || dkv_ld % 4 ||
+      dkv_bstride % 4)
+    return GSA_ERR_BAD_ARG;
+  DeviceInfo* di;
+  int st = device_info(&di);
+  if (st) return st;
+  SdpaBwdArgs a{B, Lq, Lkv, dims->n_heads, dims->n_kv_heads, dims->d_head, dtype, q, k, v, kv_ld, kv_bstride,
+                sel_idx, sel_ld, sel_count, o, d_o, lse, dq, dk, dv, dkv_ld, dkv_bstride, scale, di->err};
+  return launch_sdpa_backward(a, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int64_t gsa_workspace_size(int64_t chunk_rows, int64_t n_cols) {

@@ -88,6 +88,7 @@ struct SdpaArgs {
   float* part;
   int64_t part_floats; // capacity of part
   int prefetch;        // stages ahead whose keys the producers prefetch into L2 (0: none)
+  float* lse_out;      // [R, H] natural-log sum-exp of the scaled scores (unsplit launches), or NULL
 };
 
 struct SdpaF32Args {
@@ -105,7 +106,34 @@ struct SdpaF32Args {
   float scale;
   int* err;
   int64_t kv_bstride;
+  float* lse_out;      // [R, H] natural-log sum-exp of the scaled scores, or NULL
 };
+
+// Backward of the sparse SDPA (without the gate): per row r and head h, with p = exp(scale q.k_s
+// - lse) over the row's selected keys s, D = dO.O:
+//   dq_h = scale sum_s p_s (dO.v_s - D) k_s;  dk_s += scale p_s (dO.v_s - D) q_h;  dv_s += p_s dO_h
+struct SdpaBwdArgs {
+  int64_t B, Lq, Lkv;
+  int H, Hk, D;
+  int dtype;
+  const void* q;       // [R, H, D]
+  const void* k;       // key s of batch b at b * kv_bstride + s * kv_ld (elements)
+  const void* v;
+  int64_t kv_ld, kv_bstride;
+  const int32_t* sel_idx;
+  int64_t sel_ld;
+  const int32_t* sel_count;
+  const void* o;       // [R, H, D] the forward output (ungated)
+  const void* d_o;     // [R, H, D]
+  const float* lse;    // [R, H]
+  float* dq;           // [R, H, D] fp32
+  float* dk;           // fp32 accumulators, key s of batch b at b * dkv_bstride + s * dkv_ld
+  float* dv;
+  int64_t dkv_ld, dkv_bstride;
+  float scale;
+  int* err;
+};
+int launch_sdpa_backward(const SdpaBwdArgs& a, cudaStream_t stream);
 
 int launch_proj_epilogue(const EpiArgs& a, cudaStream_t stream);
 int launch_apply_gate(int dtype, int act, int64_t n, const void* x, const void* logits, void* out, void* gate_out,

@@ -307,6 +307,12 @@ __global__ void __launch_bounds__(MAXW * 32) sdpa_tc_kernel(SdpaArgs a) {
       }
       continue;
     }
+    if (a.lse_out && grp == 0) {
+      // natural-log sum-exp of scale * q.k (m is in log2 units of it)
+      float* lr = a.lse_out + row * H + g * NREP;
+      if (h0 < NREP) lr[h0] = l0 > 0.f ? (m0 + log2f(l0)) * 0.6931471805599453f : -INFINITY;
+      if (h1 < NREP) lr[h1] = l1 > 0.f ? (m1 + log2f(l1)) * 0.6931471805599453f : -INFINITY;
+    }
 #pragma unroll
     for (int mt = 0; mt < D / 16; ++mt) {
 #pragma unroll
@@ -377,6 +383,7 @@ __global__ void sdpa_f32_kernel(SdpaF32Args a) {
       m = mn;
     }
     float inv = l > 0.f ? 1.f / l : 0.f;
+    if (a.lse_out && lane == 0) a.lse_out[row * a.H + h] = l > 0.f ? m + logf(l) : -INFINITY;
     for (int i = 0; i < kMaxPerLane; ++i) {
       int d = lane + 32 * i;
       if (d < a.D) {
@@ -456,7 +463,7 @@ static int launch_tc_w(SdpaArgs a, int num_sms, cudaStream_t stream) {
   // so their producers also prefetch into L2 four stages ahead.
   a.splits = 1;
   a.prefetch = 0;
-  if (a.part && R < grid) {
+  if (a.part && R < grid && !a.lse_out) {
     int64_t sp = std::min<int64_t>(grid / R, kMaxSplits);
     while (sp > 1 && R * sp * H * (D + 1) > a.part_floats) --sp;
     a.splits = (int)sp;

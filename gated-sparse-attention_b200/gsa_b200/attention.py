@@ -389,7 +389,110 @@ class _ForwardOnly(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, *grads):
-        raise NotImplementedError("the B200 GSA layer implements the forward pass only")
+        raise NotImplementedError("the B200 GSA layer's backward covers the prefill without a KV cache, "
+                                  "unsharded, without output_attentions")
+
+
+def _act(logits: torch.Tensor, act: str) -> torch.Tensor:
+    """The gate activations in fp32 (value_gate.py:98-106: tanh is rescaled to (0, 1))."""
+    x = logits.float()
+    if act == "sigmoid":
+        return torch.sigmoid(x)
+    if act == "tanh":
+        return (torch.tanh(x) + 1) / 2
+    if act == "silu":
+        return F.silu(x)
+    raise ValueError(f"Unknown activation: {act}")
+
+
+def _act_grad(logits: torch.Tensor, act: str) -> torch.Tensor:
+    """d act(x) / dx in fp32 for the gate activations (value_gate.py:98-106, output_gate.py:111-119)."""
+    x = logits.float()
+    if act == "sigmoid":
+        g = torch.sigmoid(x)
+        return g * (1 - g)
+    if act == "tanh":
+        return (1 - torch.tanh(x) ** 2) / 2
+    if act == "silu":
+        g = torch.sigmoid(x)
+        return g * (1 + x * (1 - g))
+    raise ValueError(f"Unknown activation: {act}")
+
+
+def _rope_backward(dy: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """Transpose of y = x cos + rotate_half(x) sin (rope.py:151-185): rotate_half maps (x1, x2) to
+    (-x2, x1), its transpose maps (y1, y2) to (y2, -y1).  dy [T, heads, D] fp32, cos/sin [T, D]."""
+    c, s_ = cos.float().unsqueeze(1), sin.float().unsqueeze(1)
+    ys = dy * s_
+    h = dy.shape[-1] // 2
+    return dy * c + torch.cat([ys[..., h:], -ys[..., :h]], dim=-1)
+
+
+class _GSATrain(torch.autograd.Function):
+    """The layer's forward on the B200 kernels with the backward of the differentiable part:
+    o_proj, the G1 gate, the sparse SDPA over the selected keys (gsa_sparse_sdpa_backward), RoPE,
+    the G2 gate and the fused q/k/v/gate projections.  The selection (torch.topk indices,
+    adaptive_topk.py:177) carries no gradient, so neither does the indexer -- as in the
+    reference, whose only path from the indexer to the output is through those indices."""
+
+    @staticmethod
+    def forward(ctx, layer, x, W, bvec, Wo, positions):
+        with torch.no_grad():
+            saved = {}
+            out, _, _ = layer._forward_impl(x, positions, None, False, False, train=saved)
+        ctx.layer = layer
+        ctx.saved = saved
+        ctx.save_for_backward(x, W, Wo)
+        return out
+
+    @staticmethod
+    def backward(ctx, d_out):
+        layer, sv = ctx.layer, ctx.saved
+        x, W, Wo = ctx.saved_tensors
+        B, L, dm = x.shape
+        H, Hk, D = layer.n_heads, layer.n_kv_heads, layer.d_head
+        T = B * L
+        lay = sv["layout"]
+        with torch.no_grad():
+            dout = d_out.reshape(T, dm).float()
+            gated = sv["gated"].reshape(T, H * D)
+            dWo = (dout.t() @ gated.float()).to(Wo.dtype)
+            d_gated = (dout @ Wo.float()).view(T, H, D)
+            O, g1 = sv["O"].view(T, H, D), sv["g1"]
+            proj = sv["proj"]
+            if g1 is not None:
+                g1 = g1.view(T, H, D)
+                dO = d_gated * g1.float()
+                act = layer.output_gate.activation
+                d_g1 = (d_gated * O.float()) * _act_grad(proj[:, lay.g1:lay.g1 + H * D].view(T, H, D), act)
+            else:
+                dO, d_g1 = d_gated, None
+            dq, dk, dv = ops.sparse_sdpa_backward(sv["dims"], sv["q"], sv["k"], sv["v"], sv["sel"], sv["cnt"],
+                                                  sv["O"], dO.view(B, L, H, D), sv["lse"], layer.scale)
+            pos = sv["positions"].reshape(-1)
+            cos, sin = layer.rotary_emb.cos_cached[pos], layer.rotary_emb.sin_cached[pos]
+            dq_raw = _rope_backward(dq.view(T, H, D), cos, sin)
+            dk_raw = _rope_backward(dk.reshape(T, Hk, D), cos, sin)
+            dv = dv.reshape(T, Hk * D)
+            d_proj = torch.zeros(T, W.shape[0], device=x.device, dtype=torch.float32)
+            d_proj[:, lay.q:lay.q + H * D] = dq_raw.reshape(T, H * D)
+            d_proj[:, lay.k:lay.k + Hk * D] = dk_raw.reshape(T, Hk * D)
+            if lay.g2 >= 0:
+                act = layer.value_gate.activation
+                v_raw = proj[:, lay.v:lay.v + Hk * D].float()
+                g2l = proj[:, lay.g2:lay.g2 + Hk * D]
+                g2 = _act(g2l, act)
+                d_proj[:, lay.v:lay.v + Hk * D] = dv * g2
+                d_proj[:, lay.g2:lay.g2 + Hk * D] = dv * v_raw * _act_grad(g2l, act)
+            else:
+                d_proj[:, lay.v:lay.v + Hk * D] = dv
+            if d_g1 is not None:
+                d_proj[:, lay.g1:lay.g1 + H * D] = d_g1.reshape(T, H * D)
+            x2 = x.reshape(T, dm)
+            dx = (d_proj @ W.float()).to(x.dtype).view(B, L, dm) if ctx.needs_input_grad[1] else None
+            dW = (d_proj.t() @ x2.float()).to(W.dtype) if ctx.needs_input_grad[2] else None
+            db = d_proj.sum(0).to(W.dtype) if ctx.needs_input_grad[3] else None
+        return None, dx, dW, db, (dWo if ctx.needs_input_grad[4] else None), None
 
 
 # ---------------------------------------------------------------------------------------------
@@ -538,15 +641,44 @@ class GatedSparseAttention(nn.Module):
         if (self.value_gate is not None and self.output_gate is not None
                 and self.value_gate.activation != self.output_gate.activation):
             raise NotImplementedError("value and output gates must share one activation")
+        params = [self.q_proj.weight, self.k_proj.weight, self.v_proj.weight, self.o_proj.weight]
+        for gate in (self.value_gate, self.output_gate):
+            if gate is not None:
+                params += [gate.gate_proj.weight, gate.gate_proj.bias]
+        needs_grad = torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in params))
+        if (needs_grad and past_key_value is None and not use_cache and not output_attentions
+                and self.query_shards is None and self.sequence_shards is None):
+            W, bvec = self._train_projection()
+            out = _GSATrain.apply(self, x, W, bvec, self.o_proj.weight, positions)
+            return out, None, None
         with torch.no_grad():
             out, present, weights = self._forward_impl(x, positions, past_key_value, use_cache,
                                                        output_attentions)
-        if torch.is_grad_enabled() and (x.requires_grad or self.q_proj.weight.requires_grad):
+        if needs_grad:
             out = _ForwardOnly.apply(out, x, self.q_proj.weight)
         return out, present, weights if output_attentions else None
 
+    def _train_projection(self):
+        """The fused projection weight and bias built inside the autograd graph: gradients reach
+        q/k/v and the gate projections; the indexer's segments are detached (no gradient, as in
+        the reference)."""
+        ws, bs = [], []
+        for name, w, b in self._segments():
+            diff = name in ("q", "k", "v", "g2", "g1")
+            ws.append(w if diff else w.detach())
+            if b is None:
+                bs.append(torch.zeros(w.shape[0], device=w.device, dtype=w.dtype))
+            else:
+                bs.append(b if diff else b.detach())
+        n = sum(w.shape[0] for w in ws)
+        pad = (-n) % 64
+        if pad:
+            ws.append(torch.zeros(pad, self.d_model, device=ws[0].device, dtype=ws[0].dtype))
+            bs.append(torch.zeros(pad, device=ws[0].device, dtype=ws[0].dtype))
+        return torch.cat(ws, 0), torch.cat(bs, 0)
+
     def _forward_impl(self, x, positions, past_key_value, use_cache, output_attentions,
-                      mark=None, capture=None):
+                      mark=None, capture=None, train=None):
         """The forward computation.  ``mark(name)`` (optional) is called after each stage and
         ``capture`` (optional dict) receives the SDPA inputs; both are for measurement (and
         keep the stages apart, one call each)."""
@@ -706,7 +838,15 @@ class GatedSparseAttention(nn.Module):
             kv_all = kv_finish()
             k_all, v_all = kv_all[:, :, 0], kv_all[:, :, 1]
             present = GSAKVCache(k_all, v_all, indexer_keys, kv_all) if use_cache else None
-        attn = ops.sparse_sdpa(dims, q, k_all, v_all, sel, cnt, g1, self.scale)
+        if train is None:
+            attn = ops.sparse_sdpa(dims, q, k_all, v_all, sel, cnt, g1, self.scale)
+        else:
+            # ungated output and softmax statistics kept for the backward; the gate applied as the
+            # fused epilogue applies it (one product rounded to the dtype)
+            O, lse = ops.sparse_sdpa_lse(dims, q, k_all, v_all, sel, cnt, self.scale)
+            attn = O * g1.view_as(O) if g1 is not None else O
+            train.update(dims=dims, layout=layout, proj=proj, positions=positions, q=q, k=k_all, v=v_all,
+                         sel=sel, cnt=cnt, O=O, lse=lse, g1=g1, gated=attn)
         mark("sparse_sdpa")
         out = F.linear(attn.view(B, L, H * D), self.o_proj.weight)
         mark("o_proj")

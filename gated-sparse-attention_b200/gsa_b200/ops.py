@@ -275,6 +275,46 @@ def sparse_sdpa(dims: Dims, q, k, v, sel_idx, sel_count, gate, scale: float) -> 
     return out
 
 
+def sparse_sdpa_lse(dims: Dims, q, k, v, sel_idx, sel_count, scale: float):
+    """Ungated sparse SDPA that also returns the per-(row, head) natural-log sum-exp of the scaled
+    scores [B*Lq, H] fp32 (the backward's softmax statistics)."""
+    _cuda(q, k, v, sel_idx, sel_count)
+    B, Lq = q.shape[0], q.shape[1]
+    Lkv = k.shape[1]
+    q = q.contiguous()
+    k = _kv_rows(k)
+    v = _kv_rows(v)
+    if k.stride(1) != v.stride(1) or _kv_bstride(k) != _kv_bstride(v):
+        k, v = k.contiguous(), v.contiguous()
+    out = torch.empty_like(q)
+    lse = torch.empty(B * Lq, dims.n_heads, device=q.device, dtype=torch.float32)
+    _lib.call("gsa_sparse_sdpa_lse", C.byref(dims), dtype_code(q.dtype), B, Lq, Lkv, _p(q), _p(k), _p(v),
+              k.stride(1), _kv_bstride(k), _p(sel_idx), sel_idx.stride(0), _p(sel_count), None, _p(out), _p(lse),
+              float(scale), _stream())
+    _after("sparse_sdpa_lse")
+    return out, lse
+
+
+def sparse_sdpa_backward(dims: Dims, q, k, v, sel_idx, sel_count, o, d_o, lse, scale: float):
+    """Gradients of the ungated sparse SDPA: (dq [B, Lq, H, D], dk, dv [B, Lkv, Hk, D]), fp32."""
+    _cuda(q, k, v, sel_idx, sel_count, o, d_o, lse)
+    B, Lq, H, D = q.shape
+    Lkv, Hk = k.shape[1], k.shape[2]
+    q, o, d_o = q.contiguous(), o.contiguous(), d_o.contiguous().to(q.dtype)
+    k = _kv_rows(k)
+    v = _kv_rows(v)
+    if k.stride(1) != v.stride(1) or _kv_bstride(k) != _kv_bstride(v):
+        k, v = k.contiguous(), v.contiguous()
+    dq = torch.empty(B, Lq, H, D, device=q.device, dtype=torch.float32)
+    dkv = torch.zeros(B, Lkv, 2, Hk, D, device=q.device, dtype=torch.float32)
+    dk, dv = dkv[:, :, 0], dkv[:, :, 1]
+    _lib.call("gsa_sparse_sdpa_backward", C.byref(dims), dtype_code(q.dtype), B, Lq, Lkv, _p(q), _p(k), _p(v),
+              k.stride(1), _kv_bstride(k), _p(sel_idx), sel_idx.stride(0), _p(sel_count), _p(o), _p(d_o),
+              _p(lse.contiguous()), _p(dq), _p(dk), _p(dv), dk.stride(1), dk.stride(0), float(scale), _stream())
+    _after("sparse_sdpa_backward")
+    return dq, dk, dv
+
+
 def apply_gate(x: torch.Tensor, logits: torch.Tensor, act: str, want_gate: bool = False):
     _cuda(x, logits)
     x = x.contiguous()

@@ -229,6 +229,35 @@ int gsa_sparse_sdpa_strided(const gsa_dims* dims, int dtype, int64_t B, int64_t 
                             void* workspace, int64_t workspace_bytes, gsa_stream_t stream);
 
 /*
+ * gsa_sparse_sdpa_strided (no workspace) that also writes lse_out [B*Lq, H] fp32: the
+ * natural-log sum-exp of scale * q.k over each row's selected keys per head (-inf for a row
+ * without keys), which gsa_sparse_sdpa_backward needs.
+ */
+int gsa_sparse_sdpa_lse(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int64_t Lkv,
+                        const void* q, const void* k, const void* v, int64_t kv_ld,
+                        int64_t kv_bstride, const int32_t* sel_idx, int64_t sel_ld,
+                        const int32_t* sel_count, const void* gate, void* out, float* lse_out,
+                        float scale, gsa_stream_t stream);
+
+/*
+ * Backward of the sparse SDPA without the gate (gated_sparse_attention.py:256-290 under
+ * autograd; the selected indices carry no gradient, adaptive_topk.py:177).  With p = exp(scale
+ * q.k - lse) over row r's selected keys and D = dO.O per head:
+ *   dq [B*Lq, H, D] fp32 (written):  scale * sum_s p (dO.v_s - D) k_s
+ *   dk, dv fp32 accumulators (added to; the caller zeroes them), key s of batch b at
+ *     b * dkv_bstride + s * dkv_ld: dk_s += scale p (dO.v_s - D) q, dv_s += p dO (over the
+ *     rows and the group's heads that selected s; atomics, so the last bits vary run to run)
+ *   q, o, d_o [B*Lq, H, D] dtype; k, v, sel as in gsa_sparse_sdpa_strided; lse from
+ *   gsa_sparse_sdpa_lse.  D in {64, 128}.
+ */
+int gsa_sparse_sdpa_backward(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int64_t Lkv,
+                             const void* q, const void* k, const void* v, int64_t kv_ld,
+                             int64_t kv_bstride, const int32_t* sel_idx, int64_t sel_ld,
+                             const int32_t* sel_count, const void* o, const void* d_o,
+                             const float* lse, float* dq, float* dk, float* dv, int64_t dkv_ld,
+                             int64_t dkv_bstride, float scale, gsa_stream_t stream);
+
+/*
  * Workspace for gsa_indexer_select: bytes needed for a query chunk of ``chunk_rows`` rows
  * against n_cols keys.
  */

@@ -271,7 +271,13 @@ class OracleConfig:
 
     @classmethod
     def from_config(cls, cfg) -> "OracleConfig":
-        return cls(**{f: getattr(cfg, f) for f in cls.__dataclass_fields__})
+        """The layer the reference builds from a GSAConfig.  GatedSparseAttention does not pass
+        config.gate_activation to its ValueGate / OutputGate (gated_sparse_attention.py:81-99),
+        so both gates use their default sigmoid (value_gate.py:43, output_gate.py:46) whatever
+        the config says; set gate_activation on the result to model gates built otherwise."""
+        d = {f: getattr(cfg, f) for f in cls.__dataclass_fields__}
+        d["gate_activation"] = "sigmoid"
+        return cls(**d)
 
 
 def project(W: dict, cfg: OracleConfig, x: torch.Tensor, positions: torch.Tensor,
