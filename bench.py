@@ -583,6 +583,95 @@ def run_decode(args, world, rank):
 
 
 # ---------------------------------------------------------------------------------------------
+# training step: forward + backward of the layer
+# ---------------------------------------------------------------------------------------------
+TRAIN_METRIC = "GSA layer fwd+bwd tokens/sec (training step, B200)"
+
+
+def sdpa_backward_bytes(cfg, cnt: torch.Tensor) -> float:
+    """Bytes the SDPA backward must move: per selected key the K and V rows (bf16) read and the
+    dK, dV rows (fp32) accumulated; per row q, O, dO read (bf16), dq written (fp32), lse."""
+    Hk, H, D = cfg.n_kv_heads, cfg.n_heads, cfg.d_head
+    sum_k = float(cnt.double().sum().item())
+    return sum_k * (2 * Hk * D * 2 + 2 * Hk * D * 4 + 4) + cnt.numel() * (3 * H * D * 2 + H * D * 4 + H * 4)
+
+
+def run_train(args, world, rank):
+    from gsa_b200 import GSAConfig, GatedSparseAttention, ops
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    L = args.seq_len
+    cfg = GSAConfig(**WORKLOAD, max_position_embeddings=max(131072, L))
+    torch.manual_seed(0)
+    m = GatedSparseAttention(cfg).to(torch.bfloat16).to(dev).train()
+    gen = torch.Generator().manual_seed(1)
+    x = torch.randn(1, L, cfg.d_model, generator=gen).to(torch.bfloat16).to(dev).requires_grad_(True)
+    dy = torch.randn(1, L, cfg.d_model, generator=gen).to(torch.bfloat16).to(dev)
+
+    def step():
+        m.zero_grad(set_to_none=True)
+        x.grad = None
+        out = m(x)[0]
+        out.backward(dy)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    ops.check_device_error()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clk:
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    # forward alone (the training forward: the SDPA without its fused gate, log-sum-exp kept)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(args.steps):
+        m(x)[0]
+    f1.record()
+    torch.cuda.synchronize()
+    fwd_ms = f0.elapsed_time(f1) / args.steps
+    # the SDPA backward kernel alone on this step's selection
+    saved = {}
+    with torch.no_grad():
+        m._forward_impl(x.detach(), None, None, False, False, train=saved)
+        d_o = torch.randn_like(saved["O"])
+        ops.sparse_sdpa_backward(saved["dims"], saved["q"], saved["k"], saved["v"], saved["sel"], saved["cnt"],
+                                 saved["O"], d_o, saved["lse"], m.scale)
+        torch.cuda.synchronize()
+        b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        b0.record()
+        reps = 3
+        for _ in range(reps):
+            ops.sparse_sdpa_backward(saved["dims"], saved["q"], saved["k"], saved["v"], saved["sel"], saved["cnt"],
+                                     saved["O"], d_o, saved["lse"], m.scale)
+        b1.record()
+        torch.cuda.synchronize()
+    bwd_kernel_ms = b0.elapsed_time(b1) / reps
+    pk, pk_kind = peaks()
+    nbytes = sdpa_backward_bytes(cfg, saved["cnt"])
+    achieved = nbytes / (bwd_kernel_ms / 1e3) / 1e9
+    return {
+        "metric": TRAIN_METRIC, "value": round(L / (ms / 1e3), 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: x, dy ~ N(0,1) seed 1, default-init weights seed 0",
+        "config": {"workload": f"GSA layer fwd+bwd B=1 L={L} d4096 h32/8x128 idx8x64 k2048[256,4096] bf16",
+                   "batch": 1, "seq_len": L, "parallelism": "single GPU"},
+        "forward_ms": round(fwd_ms, 3), "backward_ms": round(ms - fwd_ms, 3),
+        "roofline": {"kernel": "gsa::bwd::sdpa_bwd_kernel<bf16,4,4>", "bound": "hbm", "achieved": round(achieved, 1),
+                     "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
+                     "peak_kind": pk_kind, "algorithmic_bytes": nbytes, "kernel_ms": round(bwd_kernel_ms, 3),
+                     "traffic": None},
+        "gpu_launches": None, "clocks": clk.summary(),
+    }
+
+
+# ---------------------------------------------------------------------------------------------
 # CPU path of the reference algorithm (oracle restatement), sampled and extrapolated
 # ---------------------------------------------------------------------------------------------
 def cpu_reference_estimate(L: int, proj_rows: int, chunk_rows: int, n_chunks: int, seed: int = 0):
@@ -807,8 +896,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--launch-list", type=int, default=0, metavar="N",
                     help="run N untimed forwards and exit (a short command for profilers)")
-    ap.add_argument("--workload", default="prefill", choices=["prefill", "decode"],
-                    help="prefill: one 131072-token sequence; decode: 64 sequences x 1 token vs 65,536 cached")
+    ap.add_argument("--workload", default="prefill", choices=["prefill", "decode", "train"],
+                    help="prefill: one 131072-token sequence; decode: 64 sequences x 1 token vs 65,536 cached; "
+                         "train: forward + backward of one --seq-len sequence")
     ap.add_argument("--cached", type=int, default=DECODE_CACHED, help="decode: cached tokens per sequence")
     args = ap.parse_args()
     quiet_stdout()
@@ -828,6 +918,11 @@ def main():
 
     world, rank, local = dist_setup(args.gpus)
     try:
+        if args.workload == "train":
+            res = run_train(args, world, rank)
+            if rank == 0:
+                emit(res)
+            return
         if args.workload == "decode":
             res = run_decode(args, world, rank)
             if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -20,8 +20,13 @@ library's kernels for RoPE / G2 / G1 gate / indexer weights, the chunked indexer
 candidates, the adaptive k, the final selection, and the gathered sparse SDPA with the G1 gate
 in its epilogue; ``o_proj`` is a cuBLAS GEMM.  No [B, L, L] score tensor and no gathered
 [B, L, k, H, D] tensor is ever formed.  Inputs must be CUDA tensors in float32 or bfloat16;
-there is no CPU path.  The layer computes forward only: calling backward through its output
-raises ``NotImplementedError``.
+there is no CPU path.
+
+Steps that write into a KV cache (decode) append K, V and the indexer keys to a preallocated
+store in place and run everything between the two GEMMs as one native call.  Under autograd the
+prefill (no cache, unsharded) is differentiable: the backward runs the sparse-SDPA backward
+kernel and cuBLAS GEMMs; the indexer gets no gradient, as in the reference.  Other autograd uses
+raise ``NotImplementedError``.
 """
 
 from __future__ import annotations
@@ -454,10 +459,13 @@ class _GSATrain(torch.autograd.Function):
         T = B * L
         lay = sv["layout"]
         with torch.no_grad():
-            dout = d_out.reshape(T, dm).float()
+            # GEMMs in the parameters' dtype (tensor cores for bf16, fp32 accumulation), as torch
+            # autograd runs them; the elementwise parts in fp32
+            dt = Wo.dtype
+            dout = d_out.reshape(T, dm).to(dt)
             gated = sv["gated"].reshape(T, H * D)
-            dWo = (dout.t() @ gated.float()).to(Wo.dtype)
-            d_gated = (dout @ Wo.float()).view(T, H, D)
+            dWo = dout.t() @ gated
+            d_gated = (dout @ Wo).view(T, H, D).float()
             O, g1 = sv["O"].view(T, H, D), sv["g1"]
             proj = sv["proj"]
             if g1 is not None:
@@ -489,9 +497,10 @@ class _GSATrain(torch.autograd.Function):
             if d_g1 is not None:
                 d_proj[:, lay.g1:lay.g1 + H * D] = d_g1.reshape(T, H * D)
             x2 = x.reshape(T, dm)
-            dx = (d_proj @ W.float()).to(x.dtype).view(B, L, dm) if ctx.needs_input_grad[1] else None
-            dW = (d_proj.t() @ x2.float()).to(W.dtype) if ctx.needs_input_grad[2] else None
             db = d_proj.sum(0).to(W.dtype) if ctx.needs_input_grad[3] else None
+            d_proj = d_proj.to(W.dtype)
+            dx = (d_proj @ W).to(x.dtype).view(B, L, dm) if ctx.needs_input_grad[1] else None
+            dW = d_proj.t() @ x2.to(W.dtype) if ctx.needs_input_grad[2] else None
         return None, dx, dW, db, (dWo if ctx.needs_input_grad[4] else None), None
 
 
