@@ -672,6 +672,63 @@ def run_train(args, world, rank):
 
 
 # ---------------------------------------------------------------------------------------------
+# decoder layer: RMSNorm + GSA + residual + RMSNorm + SwiGLU MLP + residual
+# ---------------------------------------------------------------------------------------------
+LAYER_METRIC = "GSA decoder layer fwd tokens/sec (RMSNorm, GSA, SwiGLU d_ffn 11008; B200)"
+
+
+def run_layer(args, world, rank):
+    from gsa_b200 import GSAConfig, GSADecoderLayer, ops
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    L = args.seq_len
+    cfg = GSAConfig(**WORKLOAD, max_position_embeddings=max(131072, L))
+    torch.manual_seed(0)
+    m = GSADecoderLayer(cfg, 0).eval().to(torch.bfloat16).to(dev)
+    gen = torch.Generator().manual_seed(1)
+    x = torch.randn(1, L, cfg.d_model, generator=gen).to(torch.bfloat16).to(dev)
+
+    def step():
+        with torch.no_grad():
+            return m(x)[0]
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    ops.check_device_error()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clk:
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    # the attention alone on the normed input, for the split
+    with torch.no_grad():
+        normed = m.input_layernorm(x)
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        for _ in range(args.steps):
+            m.self_attn(normed)
+        a1.record()
+        torch.cuda.synchronize()
+    attn_ms = a0.elapsed_time(a1) / args.steps
+    mlp_flops = 2.0 * L * cfg.d_model * cfg.d_ffn * 3
+    return {
+        "metric": LAYER_METRIC, "value": round(L / (ms / 1e3), 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: x ~ N(0,1) seed 1, default-init weights seed 0",
+        "config": {"workload": f"GSA decoder layer fwd B=1 L={L} d4096 h32/8x128 idx8x64 k2048[256,4096] "
+                               f"ffn{cfg.d_ffn} bf16", "batch": 1, "seq_len": L, "parallelism": "single GPU"},
+        "attention_ms": round(attn_ms, 3), "rest_ms": round(ms - attn_ms, 3),
+        "mlp_tflops": round(mlp_flops / ((ms - attn_ms) / 1e3) / 1e12, 1),
+        "gpu_launches": None, "clocks": clk.summary(),
+    }
+
+
+# ---------------------------------------------------------------------------------------------
 # CPU path of the reference algorithm (oracle restatement), sampled and extrapolated
 # ---------------------------------------------------------------------------------------------
 def cpu_reference_estimate(L: int, proj_rows: int, chunk_rows: int, n_chunks: int, seed: int = 0):
@@ -896,9 +953,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--launch-list", type=int, default=0, metavar="N",
                     help="run N untimed forwards and exit (a short command for profilers)")
-    ap.add_argument("--workload", default="prefill", choices=["prefill", "decode", "train"],
+    ap.add_argument("--workload", default="prefill", choices=["prefill", "decode", "train", "layer"],
                     help="prefill: one 131072-token sequence; decode: 64 sequences x 1 token vs 65,536 cached; "
-                         "train: forward + backward of one --seq-len sequence")
+                         "train: forward + backward of one --seq-len sequence; layer: a whole decoder layer")
     ap.add_argument("--cached", type=int, default=DECODE_CACHED, help="decode: cached tokens per sequence")
     args = ap.parse_args()
     quiet_stdout()
@@ -918,8 +975,8 @@ def main():
 
     world, rank, local = dist_setup(args.gpus)
     try:
-        if args.workload == "train":
-            res = run_train(args, world, rank)
+        if args.workload in ("train", "layer"):
+            res = (run_train if args.workload == "train" else run_layer)(args, world, rank)
             if rank == 0:
                 emit(res)
             return

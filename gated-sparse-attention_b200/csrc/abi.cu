@@ -360,6 +360,26 @@ int gsa_sparse_sdpa_backward(const gsa_dims* dims, int dtype, int64_t B, int64_t
   return launch_sdpa_backward(a, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int gsa_add_rmsnorm(int dtype, int64_t T, int64_t d, const void* x, int64_t x_ld, const void* a, int64_t a_ld,
+                    const void* weight, float eps, void* h_out, int64_t h_ld, void* y_out, int64_t y_ld,
+                    gsa_stream_t stream) {
+  if (T < 0 || d < 1 || (dtype != GSA_DTYPE_F32 && dtype != GSA_DTYPE_BF16)) return GSA_ERR_BAD_ARG;
+  if (T == 0) return GSA_OK;
+  if (!x || x_ld < d || (a && a_ld < d) || (h_out && (!a || h_ld < d)) || (y_out && (!weight || y_ld < d)) ||
+      (!h_out && !y_out))
+    return GSA_ERR_BAD_ARG;
+  return launch_add_rmsnorm(dtype, T, d, x, x_ld, a, a_ld, weight, eps, h_out, h_ld, y_out, y_ld,
+                            reinterpret_cast<cudaStream_t>(stream));
+}
+
+int gsa_silu_mul(int dtype, int64_t T, int64_t n, const void* gu, int64_t gu_ld, void* z, int64_t z_ld,
+                 gsa_stream_t stream) {
+  if (T < 0 || n < 0 || (dtype != GSA_DTYPE_F32 && dtype != GSA_DTYPE_BF16)) return GSA_ERR_BAD_ARG;
+  if (T * n == 0) return GSA_OK;
+  if (!gu || !z || gu_ld < 2 * n || z_ld < n) return GSA_ERR_BAD_ARG;
+  return launch_silu_mul(dtype, T, n, gu, gu_ld, z, z_ld, reinterpret_cast<cudaStream_t>(stream));
+}
+
 int64_t gsa_workspace_size(int64_t chunk_rows, int64_t n_cols) {
   if (chunk_rows <= 0 || n_cols <= 0) return 0;
   const int64_t ld = (n_cols + 3) / 4 * 4;

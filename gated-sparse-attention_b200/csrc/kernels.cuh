@@ -134,6 +134,11 @@ struct SdpaBwdArgs {
   int* err;
 };
 int launch_sdpa_backward(const SdpaBwdArgs& a, cudaStream_t stream);
+int launch_add_rmsnorm(int dtype, int64_t T, int64_t d, const void* x, int64_t x_ld, const void* a, int64_t a_ld,
+                       const void* w, float eps, void* h_out, int64_t h_ld, void* y_out, int64_t y_ld,
+                       cudaStream_t stream);
+int launch_silu_mul(int dtype, int64_t T, int64_t n, const void* gu, int64_t gu_ld, void* z, int64_t z_ld,
+                    cudaStream_t stream);
 
 int launch_proj_epilogue(const EpiArgs& a, cudaStream_t stream);
 int launch_apply_gate(int dtype, int act, int64_t n, const void* x, const void* logits, void* out, void* gate_out,

@@ -17,6 +17,17 @@ from .attention import (
     apply_rotary_pos_emb,
 )
 
+from .models import (
+    GSACausalLMOutput,
+    GSADecoderLayer,
+    GSAForCausalLM,
+    GSALlamaForCausalLM,
+    GSALlamaModel,
+    GSAMlp,
+    GSAModelOutput,
+    RMSNorm,
+)
+
 __version__ = "0.1.0"
 __all__ = [
     "GSAConfig",
@@ -28,4 +39,12 @@ __all__ = [
     "RotaryEmbedding",
     "apply_rotary_pos_emb",
     "GSAKVCache",
+    "RMSNorm",
+    "GSAMlp",
+    "GSADecoderLayer",
+    "GSAModelOutput",
+    "GSACausalLMOutput",
+    "GSALlamaModel",
+    "GSALlamaForCausalLM",
+    "GSAForCausalLM",
 ]

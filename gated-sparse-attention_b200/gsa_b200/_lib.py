@@ -74,6 +74,8 @@ SIGNATURES = {
     "gsa_sparse_sdpa": [P, INT, I64, I64, I64, P, P, P, I64, P, I64, P, P, P, F32, P],
     "gsa_sparse_sdpa_strided": [P, INT, I64, I64, I64, P, P, P, I64, I64, P, I64, P, P, P, F32, P, I64, P],
     "gsa_sdpa_workspace_size": [P, I64, I64],
+    "gsa_add_rmsnorm": [INT, I64, I64, P, I64, P, I64, P, F32, P, I64, P, I64, P],
+    "gsa_silu_mul": [INT, I64, I64, P, I64, P, I64, P],
     "gsa_sparse_sdpa_lse": [P, INT, I64, I64, I64, P, P, P, I64, I64, P, I64, P, P, P, P, F32, P],
     "gsa_sparse_sdpa_backward": [P, INT, I64, I64, I64, P, P, P, I64, I64, P, I64, P, P, P, P, P, P, P, I64, I64,
                                  F32, P],

@@ -315,6 +315,43 @@ def sparse_sdpa_backward(dims: Dims, q, k, v, sel_idx, sel_count, o, d_o, lse, s
     return dq, dk, dv
 
 
+def add_rmsnorm(x: torch.Tensor, a, weight, eps: float, want_sum: bool = True, want_norm: bool = True):
+    """(h = x + a, RMSNorm(h) * weight) over the last dimension (a None: no add, h = x).  Either
+    output may be skipped; returns (h or None, y or None)."""
+    _cuda(x, a, weight)
+    d = x.shape[-1]
+    x2 = x.reshape(-1, d)
+    if x2.stride(1) != 1:
+        x2 = x2.contiguous()
+    a2 = None
+    if a is not None:
+        a2 = a.reshape(-1, d)
+        if a2.stride(1) != 1:
+            a2 = a2.contiguous()
+    T = x2.shape[0]
+    h = torch.empty_like(x2) if (a is not None and want_sum) else None
+    y = torch.empty_like(x2) if want_norm else None
+    w = weight.contiguous() if weight is not None else None
+    _lib.call("gsa_add_rmsnorm", dtype_code(x.dtype), T, d, _p(x2), x2.stride(0), _p(a2),
+              a2.stride(0) if a2 is not None else 0, _p(w), float(eps), _p(h), d, _p(y), d, _stream())
+    _after("add_rmsnorm")
+    return (h.view(x.shape) if h is not None else None), (y.view(x.shape) if y is not None else None)
+
+
+def silu_mul(gu: torch.Tensor) -> torch.Tensor:
+    """silu(gu[..., :n]) * gu[..., n:] for gu [..., 2n]."""
+    _cuda(gu)
+    n2 = gu.shape[-1]
+    g2 = gu.reshape(-1, n2)
+    if g2.stride(1) != 1:
+        g2 = g2.contiguous()
+    n = n2 // 2
+    z = torch.empty(g2.shape[0], n, device=gu.device, dtype=gu.dtype)
+    _lib.call("gsa_silu_mul", dtype_code(gu.dtype), g2.shape[0], n, _p(g2), g2.stride(0), _p(z), n, _stream())
+    _after("silu_mul")
+    return z.view(*gu.shape[:-1], n)
+
+
 def apply_gate(x: torch.Tensor, logits: torch.Tensor, act: str, want_gate: bool = False):
     _cuda(x, logits)
     x = x.contiguous()

@@ -258,6 +258,20 @@ int gsa_sparse_sdpa_backward(const gsa_dims* dims, int dtype, int64_t B, int64_t
                              int64_t dkv_bstride, float scale, gsa_stream_t stream);
 
 /*
+ * Decoder-layer elementwise ops around the attention (gsa/models/gsa_llama.py), each evaluated
+ * as torch evaluates it for the dtype.  Rows of d (n) elements with row strides *_ld.
+ *   gsa_add_rmsnorm: h = x + a (a nullable: no add; h_out then NULL) and
+ *     y = (h * rsqrt(mean(h^2) + eps)).type_as(h) * weight        (RMSNorm, gsa_llama.py:18-30,
+ *     after the residual adds of GSADecoderLayer.forward, :100-110); y_out or h_out may be NULL.
+ *   gsa_silu_mul: z = silu(gu[:, :n]) * gu[:, n:2n]               (GSAMlp, gsa_llama.py:45-46)
+ */
+int gsa_add_rmsnorm(int dtype, int64_t T, int64_t d, const void* x, int64_t x_ld, const void* a,
+                    int64_t a_ld, const void* weight, float eps, void* h_out, int64_t h_ld,
+                    void* y_out, int64_t y_ld, gsa_stream_t stream);
+int gsa_silu_mul(int dtype, int64_t T, int64_t n, const void* gu, int64_t gu_ld, void* z,
+                 int64_t z_ld, gsa_stream_t stream);
+
+/*
  * Workspace for gsa_indexer_select: bytes needed for a query chunk of ``chunk_rows`` rows
  * against n_cols keys.
  */

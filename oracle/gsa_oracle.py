@@ -375,3 +375,58 @@ def gsa_forward(W: dict, cfg: OracleConfig, x: torch.Tensor, positions: torch.Te
         res["indices"] = torch.cat(idx_parts, dim=1)
         res["mask"] = torch.cat(mask_parts, dim=1)
     return res
+
+
+# --------------------------------------------------------------------------------------------
+# Decoder layer and model  (gsa/models/gsa_llama.py)
+# --------------------------------------------------------------------------------------------
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    """RMSNorm.forward, gsa_llama.py:26-30."""
+    xf = x.float()
+    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)).type_as(x) * weight
+
+
+def swiglu_mlp(W: dict, prefix: str, x: torch.Tensor) -> torch.Tensor:
+    """GSAMlp.forward, gsa_llama.py:45-46."""
+    return F.linear(F.silu(F.linear(x, W[prefix + "gate_proj.weight"])) * F.linear(x, W[prefix + "up_proj.weight"]),
+                    W[prefix + "down_proj.weight"])
+
+
+def _sub(W: dict, prefix: str) -> dict:
+    return {k[len(prefix):]: v for k, v in W.items() if k.startswith(prefix)}
+
+
+def decoder_layer(W: dict, prefix: str, cfg: OracleConfig, eps: float, x: torch.Tensor, positions,
+                  cos_cached, sin_cached, chunk: int = 256, keep: tuple = ()) -> dict:
+    """GSADecoderLayer.forward without a cache, gsa_llama.py:93-112: x + GSA(norm(x)), then
+    h + MLP(norm(h)).  Returns out plus the kept intermediates (normed, attn)."""
+    normed = rms_norm(x, W[prefix + "input_layernorm.weight"], eps)
+    attn = gsa_forward(_sub(W, prefix + "self_attn."), cfg, normed, positions, cos_cached, sin_cached,
+                       chunk=chunk)["out"]
+    h = x + attn
+    out = h + swiglu_mlp(W, prefix + "mlp.", rms_norm(h, W[prefix + "post_attention_layernorm.weight"], eps))
+    res = {"out": out}
+    if "normed" in keep:
+        res["normed"] = normed
+    if "attn" in keep:
+        res["attn"] = attn
+    return res
+
+
+def causal_lm_forward(W: dict, cfg: OracleConfig, n_layers: int, eps: float, input_ids: torch.Tensor,
+                      cos_cached, sin_cached, chunk: int = 256, keep_layers: bool = False) -> dict:
+    """GSALlamaForCausalLM.forward without labels or cache, gsa_llama.py:164-242 and 278-330:
+    embedding, the decoder layers, the final norm and the LM head."""
+    B, L = input_ids.shape
+    positions = torch.arange(L).unsqueeze(0).expand(B, -1)
+    h = F.embedding(input_ids, W["model.embed_tokens.weight"])
+    res = {}
+    for i in range(n_layers):
+        r = decoder_layer(W, f"model.layers.{i}.", cfg, eps, h, positions, cos_cached, sin_cached, chunk,
+                          keep=("normed", "attn") if keep_layers else ())
+        h = r["out"]
+        if keep_layers:
+            res[f"layer{i}_normed"], res[f"layer{i}_attn"], res[f"layer{i}_out"] = r["normed"], r["attn"], h
+    res["logits"] = F.linear(rms_norm(h, W["model.norm.weight"], eps), W["lm_head.weight"])
+    return res
+

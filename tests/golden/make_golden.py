@@ -16,7 +16,9 @@ Each fixture follows the reference forward step by step
 (``gsa/attention/gated_sparse_attention.py:139-232``) through the reference's own submodules,
 and checks that the step-by-step output equals ``module(x, positions)`` bit for bit.
 
-Usage:  python tests/golden/make_golden.py [--reference PATH]
+The model fixtures run the reference's GSALlamaForCausalLM (gsa/models/gsa_llama.py) the same way.
+
+Usage:  python tests/golden/make_golden.py [--reference PATH] [--only NAME]
 """
 
 from __future__ import annotations
@@ -62,6 +64,22 @@ WEIGHT_SEED = 0
 INPUT_SEED = 1
 
 
+# name -> (config kwargs, batch, seq_len, dtype): GSALlamaForCausalLM (gsa/models/gsa_llama.py),
+# every layer's output and the logits stored in full
+MODEL_FIXTURES = {
+    "model2_fp32_b2_l96": (dict(d_model=256, n_heads=4, n_kv_heads=2, d_indexer=32, n_indexer_heads=4,
+                                k_base=24, k_min=8, k_max=48, n_layers=2, d_ffn=512, vocab_size=384,
+                                max_position_embeddings=512), 2, 96, "float32"),
+    "model2_bf16_b2_l96": (dict(d_model=256, n_heads=4, n_kv_heads=2, d_indexer=32, n_indexer_heads=4,
+                                k_base=24, k_min=8, k_max=48, n_layers=2, d_ffn=512, vocab_size=384,
+                                max_position_embeddings=512), 2, 96, "bfloat16"),
+    # every row keeps all its causal keys: no selection can flip on rounding-level differences
+    "model2dense_fp32_b2_l96": (dict(d_model=256, n_heads=4, n_kv_heads=2, d_indexer=32, n_indexer_heads=4,
+                                     k_base=96, k_min=96, k_max=96, n_layers=2, d_ffn=512, vocab_size=384,
+                                     max_position_embeddings=512), 2, 96, "float32"),
+}
+
+
 def _import_reference(ref_root: Path):
     tmp = Path(tempfile.mkdtemp(prefix="gsa_ref_shim_"))
     stub = tmp / "omegaconf"
@@ -76,7 +94,8 @@ def _import_reference(ref_root: Path):
     import gsa  # noqa: F401  (the reference package)
     from gsa import GSAConfig, GatedSparseAttention
     from gsa.attention.rope import apply_rotary_pos_emb
-    return GSAConfig, GatedSparseAttention, apply_rotary_pos_emb
+    from gsa.models.gsa_llama import GSALlamaForCausalLM
+    return GSAConfig, GatedSparseAttention, apply_rotary_pos_emb, GSALlamaForCausalLM
 
 
 def _sample_rows(L: int, n: int | None):
@@ -98,7 +117,7 @@ def _checksums(module) -> dict:
 
 @torch.no_grad()
 def make_fixture(name, spec, refs):
-    GSAConfig, GatedSparseAttention, apply_rotary_pos_emb = refs
+    GSAConfig, GatedSparseAttention, apply_rotary_pos_emb, _ = refs
     cfg_kwargs, B, L, dtype_name, n_rows = spec
     dtype = getattr(torch, dtype_name)
     cfg = GSAConfig(**cfg_kwargs)
@@ -165,6 +184,52 @@ def make_fixture(name, spec, refs):
           f"{k_values.float().mean():.1f}, rows {len(rows)}")
 
 
+@torch.no_grad()
+def make_model_fixture(name, spec, refs):
+    """GSALlamaForCausalLM forward (gsa_llama.py:164-242, 278-330) on seeded token ids, stepping
+    through the reference's own modules; the step-by-step logits must equal model(input_ids)."""
+    GSAConfig, _, _, GSALlamaForCausalLM = refs
+    cfg_kwargs, B, L, dtype_name = spec
+    dtype = getattr(torch, dtype_name)
+    cfg = GSAConfig(**cfg_kwargs)
+    torch.manual_seed(WEIGHT_SEED)
+    model = GSALlamaForCausalLM(cfg).eval().to(dtype)
+    # distinct token ids: a repeated token has the same indexer key (k^I carries no position), so
+    # its scores tie exactly and torch.topk would break the tie at a k_t boundary arbitrarily
+    gen = torch.Generator().manual_seed(INPUT_SEED)
+    ids = torch.randperm(cfg.vocab_size, generator=gen)[:B * L].view(B, L)
+    positions = torch.arange(L).unsqueeze(0).expand(B, -1)
+    h = model.model.embed_tokens(ids)
+    t = {"input_ids": ids.to(torch.int32), "embed": h.contiguous()}
+    for i, layer in enumerate(model.model.layers):
+        normed = layer.input_layernorm(h)
+        attn, _, _ = layer.self_attn(normed, positions=positions)
+        h1 = h + attn
+        normed2 = layer.post_attention_layernorm(h1)
+        h = h1 + layer.mlp(normed2)
+        t[f"layer{i}_normed"] = normed.contiguous()
+        t[f"layer{i}_attn"] = attn.contiguous()
+        t[f"layer{i}_out"] = h.contiguous()
+    h = model.model.norm(h)
+    logits = model.lm_head(h)
+    full = model(ids).logits
+    assert torch.equal(full, logits), f"{name}: step-by-step logits differ from model(input_ids)"
+    t["logits"] = logits.contiguous()
+    meta = {
+        "config": json.dumps(cfg_kwargs),
+        "batch": str(B),
+        "seq_len": str(L),
+        "dtype": dtype_name,
+        "weight_seed": str(WEIGHT_SEED),
+        "input_seed": str(INPUT_SEED),
+        "param_checksums": json.dumps(_checksums(model)),
+        "torch": torch.__version__,
+    }
+    path = HERE / f"{name}.safetensors"
+    save_file(t, str(path), metadata=meta)
+    print(f"{name}: {path.stat().st_size / 1024:.0f} KiB")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("GSA_REFERENCE", "/root/reference"))
@@ -176,6 +241,10 @@ def main():
         if args.only and name != args.only:
             continue
         make_fixture(name, spec, refs)
+    for name, spec in MODEL_FIXTURES.items():
+        if args.only and name != args.only:
+            continue
+        make_model_fixture(name, spec, refs)
 
 
 if __name__ == "__main__":

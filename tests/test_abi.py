@@ -121,3 +121,35 @@ def test_cache_entry_points_validate_before_any_launch():
     assert sdpa(100, 99 * kv_ld) == 1
     assert lib.gsa_sparse_sdpa_strided(C.byref(dims), 1, 0, 1, 100, p, p, p, kv_ld, 100 * kv_ld, p, 16, p, None, p,
                                        0.1, None, 0, None) == 0
+
+
+def test_training_and_decoder_entry_points_validate_before_any_launch():
+    """gsa_sparse_sdpa_lse, gsa_sparse_sdpa_backward, gsa_add_rmsnorm and gsa_silu_mul reject bad
+    arguments without touching the device (CPU only)."""
+    import ctypes as C
+
+    from gsa_b200 import _lib, ops
+
+    lib = _lib.lib()
+    dims = ops.make_dims(4096, 32, 8, 128, 8, 64)
+    p = C.c_void_p(256)  # a stand-in pointer: every case below returns before using it
+    kv_ld = 2 * 8 * 128
+    # lse output is required
+    assert lib.gsa_sparse_sdpa_lse(C.byref(dims), 1, 1, 4, 100, p, p, p, kv_ld, 100 * kv_ld, p, 16, p, None, p, None,
+                                   0.1, None) == 1
+
+    def bwd(dtype=1, kv_bstride=100 * kv_ld, dkv_ld=1024, dkv_bstride=100 * 1024, dq=p):
+        return lib.gsa_sparse_sdpa_backward(C.byref(dims), dtype, 1, 4, 100, p, p, p, kv_ld, kv_bstride, p, 16, p, p,
+                                            p, p, dq, p, p, dkv_ld, dkv_bstride, 0.1, None)
+
+    assert bwd(dtype=7) == 1                   # unknown dtype
+    assert bwd(kv_bstride=99 * kv_ld) == 1     # batch stride below the keys
+    assert bwd(dkv_ld=512) == 1                # gradient rows narrower than Hk * D
+    assert bwd(dq=None) == 1                   # dq required
+    # decoder-layer elementwise ops
+    assert lib.gsa_add_rmsnorm(1, 4, 0, p, 8, None, 0, p, 1e-5, None, 0, p, 8, None) == 1       # d < 1
+    assert lib.gsa_add_rmsnorm(1, 4, 8, p, 8, None, 0, p, 1e-5, p, 8, p, 8, None) == 1          # h_out without a
+    assert lib.gsa_add_rmsnorm(1, 4, 8, p, 8, None, 0, None, 1e-5, None, 0, p, 8, None) == 1    # y_out without w
+    assert lib.gsa_add_rmsnorm(1, 0, 8, None, 8, None, 0, None, 1e-5, None, 0, None, 8, None) == 0  # empty
+    assert lib.gsa_silu_mul(1, 4, 8, p, 15, p, 8, None) == 1    # gu row shorter than 2n
+    assert lib.gsa_silu_mul(1, 0, 8, None, 16, None, 8, None) == 0
