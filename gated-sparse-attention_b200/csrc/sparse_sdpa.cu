@@ -129,19 +129,27 @@ __global__ void __launch_bounds__(MAXW * 32) sdpa_tc_kernel(SdpaArgs a) {
         if ((int)(it % groups) != grp) continue;
         const int s = it % nst;
         const uint32_t ph = (it / nst) & 1u;
+        // this warp's 8 slots of the stage; with separate K and V, lanes 8-15 copy the V rows.
+        // The key index is loaded before the wait for the slot, so that its latency overlaps
+        // the wait instead of delaying the refill.
+        const int slot = half * 8 + (lane & 7);
+        const int key = kb * kKeysPerStage + slot;
+        int64_t j = key < cnt ? (int64_t)idx[key] : -1;
         if (!mbar_wait(&empty[s], ph ^ 1u, a.err)) { ok = false; break; }
         if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(kKeysPerStage * row_bytes));
         __syncwarp();
-        // this warp's 8 slots of the stage; with separate K and V, lanes 8-15 copy the V rows
-        const int slot = half * 8 + (lane & 7);
-        const int key = kb * kKeysPerStage + slot;
-        int64_t j = -1;
-        if (key < cnt) {
-          j = idx[key];
-          if (j < 0 || j >= a.Lkv) {
-            set_error(a.err, GSA_ERR_INDEX);
-            j = -1;
-          }
+        if (key < cnt && (j < 0 || j >= a.Lkv)) {
+          set_error(a.err, GSA_ERR_INDEX);
+          j = -1;
+        }
+        uint8_t* dst = stages + s * stage_bytes + slot * rs;
+        if (a.interleaved) {
+          // one copy per key: K row and V row are adjacent
+          if (lane < 8) bulk_g2s(dst, j >= 0 ? kbase + j * kv_row : g_zero_row, (uint32_t)(2 * row_bytes), &full[s]);
+        } else if (lane < 8) {
+          bulk_g2s(dst, j >= 0 ? kbase + j * kv_row : g_zero_row, (uint32_t)row_bytes, &full[s]);
+        } else if (lane < 16) {
+          bulk_g2s(dst + row_bytes, j >= 0 ? vbase + j * kv_row : g_zero_row, (uint32_t)row_bytes, &full[s]);
         }
         // few rows (DRAM-latency bound): warm L2 with the keys a.prefetch stages ahead, so that
         // the ring's copies, which hold shared memory until the consumers take them, land sooner
@@ -159,15 +167,6 @@ __global__ void __launch_bounds__(MAXW * 32) sdpa_tc_kernel(SdpaArgs a) {
               }
             }
           }
-        }
-        uint8_t* dst = stages + s * stage_bytes + slot * rs;
-        if (a.interleaved) {
-          // one copy per key: K row and V row are adjacent
-          if (lane < 8) bulk_g2s(dst, j >= 0 ? kbase + j * kv_row : g_zero_row, (uint32_t)(2 * row_bytes), &full[s]);
-        } else if (lane < 8) {
-          bulk_g2s(dst, j >= 0 ? kbase + j * kv_row : g_zero_row, (uint32_t)row_bytes, &full[s]);
-        } else if (lane < 16) {
-          bulk_g2s(dst + row_bytes, j >= 0 ? vbase + j * kv_row : g_zero_row, (uint32_t)row_bytes, &full[s]);
         }
       }
     }
