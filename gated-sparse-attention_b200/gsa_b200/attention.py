@@ -136,7 +136,44 @@ def _gate_stats(scores: Optional[torch.Tensor], per_head: bool = False) -> dict:
     return out
 
 
-class ValueGate(nn.Module):
+def _gate_torch(logits: torch.Tensor, act: str) -> torch.Tensor:
+    """act(logits) with the reference's torch ops, in the logits' dtype (value_gate.py:98-106)."""
+    if act == "sigmoid":
+        return torch.sigmoid(logits)
+    if act == "tanh":
+        return (torch.tanh(logits) + 1) / 2
+    if act == "silu":
+        return F.silu(logits)
+    raise ValueError(f"Unknown activation: {act}")
+
+
+class _GateScores:
+    """``last_gate_scores`` of a gate module (value_gate.py:109-110, output_gate.py:122-123).  The
+    fused attention layer does not run the gate modules: it hands each gate its logits (a view of
+    the fused projection's output) and the activation is computed from them, with the reference's
+    torch ops, when the scores are first read -- so the forward pays nothing for this analysis
+    output.  Holding the view keeps the projection output alive until the scores are read or the
+    next forward replaces them."""
+
+    @property
+    def last_gate_scores(self) -> Optional[torch.Tensor]:
+        pending = self.__dict__.get("_pending_logits")
+        if pending is not None:
+            self.__dict__["_pending_logits"] = None
+            self.__dict__["_last_scores"] = _gate_torch(pending, self.activation).detach()
+        return self.__dict__.get("_last_scores")
+
+    @last_gate_scores.setter
+    def last_gate_scores(self, value: Optional[torch.Tensor]):
+        self.__dict__["_pending_logits"] = None
+        self.__dict__["_last_scores"] = value
+
+    def _set_pending_logits(self, logits: torch.Tensor):
+        self.__dict__["_pending_logits"] = logits
+        self.__dict__["_last_scores"] = None
+
+
+class ValueGate(_GateScores, nn.Module):
     """G2: v * act(h W^T + b) per KV-head element (value_gate.py:16-127)."""
 
     def __init__(self, d_model: int, n_kv_heads: int, d_head: int, bias_init: float = 0.5,
@@ -167,7 +204,7 @@ class ValueGate(nn.Module):
         return _gate_stats(self.last_gate_scores)
 
 
-class OutputGate(nn.Module):
+class OutputGate(_GateScores, nn.Module):
     """G1: o * act(h W^T + b), per head element or per head scalar (output_gate.py:15-142)."""
 
     def __init__(self, d_model: int, n_heads: int, d_head: int, bias_init: float = 0.5,
@@ -734,6 +771,12 @@ class GatedSparseAttention(nn.Module):
                 store.filled = past_len
 
         proj = torch.addmm(bvec, x.reshape(B * L, self.d_model), W.t())
+        if not self.training:
+            # the gates' analysis output (last_gate_scores), computed from these logits when read
+            if self.value_gate is not None:
+                self.value_gate._set_pending_logits(proj[:, layout.g2:layout.g2 + Hk * D].view(B, L, Hk, D))
+            if self.output_gate is not None:
+                self.output_gate._set_pending_logits(proj[:, layout.g1:layout.g1 + H * D].view(B, L, H, D))
         n_all = past_len + L
         if (store is not None and self.native_step and self.selection_path == "auto" and mark_fn is None
                 and capture is None and not output_attentions

@@ -9,7 +9,8 @@ are covered, in fp32 and bf16.
 
 Analysis: GatedLightningIndexer.get_indexer_statistics and
 AdaptiveTopKSelector.get_selection_statistics against the same statistics computed from the
-oracle's scores and k values (gated_indexer.py:157-175, adaptive_topk.py:195-211)."""
+oracle's scores and k values (gated_indexer.py:157-175, adaptive_topk.py:195-211), and the gates'
+last_gate_scores after a layer forward."""
 
 import pytest
 import torch
@@ -111,3 +112,26 @@ def test_batch_rows_equal_separate_calls(cuda_ok, dtype):
     torch.cuda.synchronize()
     # the same kernels on the same rows; only the GEMMs' blocking may differ with the row count
     assert _rel(both, each) < (1e-5 if dtype == torch.float32 else 1e-2)
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-5), (torch.bfloat16, 1e-2)])
+def test_gate_scores_after_layer_forward(cuda_ok, dtype, tol):
+    """After an eval-mode layer forward the gates hold their activations for analysis
+    (value_gate.py:109-110, output_gate.py:122-123): act(h W^T + b) of the layer's input, per
+    KV-head (G2) and per head (G1) element; get_gate_statistics reads them."""
+    import torch.nn.functional as F
+
+    m = _layer(dtype, adaptive=True)
+    x = torch.randn(2, 300, 512, generator=torch.Generator().manual_seed(6)).to(DEV, dtype)
+    with torch.no_grad():
+        m(x)
+        vg, og = m.value_gate, m.output_gate
+        ref_v = torch.sigmoid(F.linear(x, vg.gate_proj.weight, vg.gate_proj.bias)).view(2, 300, 2, 64)
+        ref_o = torch.sigmoid(F.linear(x, og.gate_proj.weight, og.gate_proj.bias)).view(2, 300, 8, 64)
+        got_v, got_o = vg.last_gate_scores, og.last_gate_scores
+    torch.cuda.synchronize()
+    assert got_v.shape == ref_v.shape and got_o.shape == ref_o.shape and got_v.dtype == dtype
+    assert float((got_v.float() - ref_v.float()).abs().max()) < tol
+    assert float((got_o.float() - ref_o.float()).abs().max()) < tol
+    stats = vg.get_gate_statistics()
+    assert abs(stats["mean"] - float(ref_v.float().mean())) < tol
