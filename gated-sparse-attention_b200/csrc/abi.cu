@@ -599,7 +599,11 @@ int gsa_decode_attend(const gsa_dims* dims, const gsa_proj_layout* layout, const
                             o.idx_ws_bytes, stream);
   if (st) return st;
   // 3. per-row variances and their sum (all-reduced between the phases when the sequences of
-  // the batch are spread over several GPUs)
+  // the batch are spread over several GPUs); one call with the adaptive k for few rows
+  if (phase == GSA_DECODE_ALL && tp->use_adaptive && R <= 1024) {
+    if ((st = launch_variance_adaptive_k(R, n, dtype, *tp, stats, shift, var, total, kt, s))) return st;
+    goto select;
+  }
   if (tp->use_adaptive) {
     if ((st = gsa_row_variance(R, n, dtype, stats, shift, var, total, stream))) return st;
   } else if (var_total && cudaMemsetAsync(var_total, 0, 2 * sizeof(double), s) != cudaSuccess) {
@@ -610,6 +614,7 @@ int gsa_decode_attend(const gsa_dims* dims, const gsa_proj_layout* layout, const
 attend:
   // 4. adaptive k (variance mean over every row of the batch), final selection
   if ((st = gsa_adaptive_k(R, n, dtype, tp, var, total, stats, kt, stream))) return st;
+select:
   if ((st = gsa_select_finalize(R, o.cand_ld, cidx, cscore, ccount, kt, sel, o.k_eff, scount, nullptr, stream)))
     return st;
   // 5. sparse SDPA with the G1 gate

@@ -134,6 +134,9 @@ struct SdpaBwdArgs {
   int* err;
 };
 int launch_sdpa_backward(const SdpaBwdArgs& a, cudaStream_t stream);
+int launch_variance_adaptive_k(int64_t R, int64_t n_cols, int dtype, const gsa_topk_params& p,
+                               const double* stats, const float* shift, float* var_out, double* total,
+                               int32_t* k_out, cudaStream_t stream);
 int launch_add_rmsnorm(int dtype, int64_t T, int64_t d, const void* x, int64_t x_ld, const void* a, int64_t a_ld,
                        const void* w, float eps, void* h_out, int64_t h_ld, void* y_out, int64_t y_ld,
                        cudaStream_t stream);

@@ -1309,6 +1309,58 @@ __global__ void adaptive_k_kernel(int64_t R, int64_t n_cols, int dtype, gsa_topk
   k_out[r] = kt;
 }
 
+// Row variances, their sum and k_t in one CTA for R <= 1024 rows (decode): the same arithmetic
+// and the same summation order as row_variance_kernel, sum_variance_kernel and adaptive_k_kernel
+// (thread t holds row t; the same 1024-entry tree), so the results are identical bit for bit.
+__global__ void __launch_bounds__(1024) variance_adaptive_k_kernel(int64_t R, int64_t n_cols, int dtype,
+                                                                   gsa_topk_params p, const double* stats,
+                                                                   const float* shift, float* var_out,
+                                                                   double* total, int32_t* k_out) {
+  __shared__ double red[1024];
+  const int t = threadIdx.x;
+  const double N = (double)n_cols;
+  float v = 0.f;
+  if (t < R) {
+    const double c = shift ? (double)shift[t] : 0.0;
+    v = rnd((float)row_var(stats + (int64_t)t * 3, c, N), dtype);
+    var_out[t] = v;
+  }
+  red[t] = t < R ? (double)v : 0.0;
+  __syncthreads();
+  for (int o = 512; o > 0; o >>= 1) {
+    if (t < o) red[t] += red[t + o];
+    __syncthreads();
+  }
+  if (t == 0) {
+    total[0] = red[0];
+    total[1] = (double)R;
+  }
+  __syncthreads();
+  if (t >= R) return;
+  const double tot[2] = {red[0], (double)R};
+  float mean = rnd(__fdiv_rn((float)tot[0], (float)tot[1]), dtype);
+  float den = rnd(fadd(mean, 1e-8f), dtype);
+  float vn = rnd(__fdiv_rn(v, den), dtype);
+  float vt = rnd(fmul(vn, p.temperature), dtype);
+  float ks = rnd(__fdiv_rn(1.0f, rnd(fadd(1.0f, vt), dtype)), dtype);
+  float ka = rnd(fmul((float)p.k_base, rnd(fadd(0.5f, ks), dtype)), dtype);
+  float lo = rnd((float)p.k_min, dtype), hi = rnd((float)p.k_max, dtype);
+  float kc = fminf(fmaxf(ka, lo), hi);
+  if (ka != ka) kc = ka;
+  float valid = (float)stats[(int64_t)t * 3 + 2];
+  float km = (kc != kc) ? kc : fminf(kc, valid);
+  k_out[t] = (km != km) ? 0 : (int32_t)truncf(km);
+}
+
+int launch_variance_adaptive_k(int64_t R, int64_t n_cols, int dtype, const gsa_topk_params& p,
+                               const double* stats, const float* shift, float* var_out, double* total,
+                               int32_t* k_out, cudaStream_t stream) {
+  if (R == 0) return GSA_OK;
+  if (R > 1024 || !p.use_adaptive) return GSA_ERR_BAD_ARG;
+  variance_adaptive_k_kernel<<<1, 1024, 0, stream>>>(R, n_cols, dtype, p, stats, shift, var_out, total, k_out);
+  return cudaGetLastError() == cudaSuccess ? GSA_OK : GSA_ERR_LAUNCH;
+}
+
 // ---------------------------------------------------------------------------------------------
 int launch_topk_candidates(int64_t R, int64_t Lq, int64_t n_cols, int64_t q_pos0, int causal,
                            const float* scores, int64_t ld, const float* row_center, const double* row_stats,
