@@ -394,9 +394,19 @@ def run_ours(args, world, rank):
                 "peak_kind": pk_kind, "traffic": traffic, "traffic_note": traffic_note,
                 "algorithmic_bytes": sdpa_bytes,
                 "kernel_ms": round(sdpa_ms, 3), "mean_k": float(cap["cnt"].double().mean().item())}
+    # the bound that explains it: every selected key's K and V rows are written into shared memory
+    # by a bulk copy and read back once by ldmatrix; shared memory moves 128 B / clock / SM
+    clocks = clk.summary()
+    sm_mhz = clocks.get("sm_mhz") or pk.get("sm_max_mhz", 1965.0)
+    smem_bytes = float(cap["cnt"].double().sum().item()) * 2 * (2 * cfg.n_kv_heads * cfg.d_head * 2)
+    smem_peak = 128.0 * torch.cuda.get_device_properties(dev).multi_processor_count * sm_mhz * 1e6 / 1e9
+    smem_rate = smem_bytes / (sdpa_ms / 1e3) / 1e9
+    roofline["smem"] = {"bytes": smem_bytes, "achieved": round(smem_rate, 1), "peak": round(smem_peak, 1),
+                        "unit": "GB/s", "frac": round(smem_rate / smem_peak, 4),
+                        "note": "K/V rows written by bulk copy + read by ldmatrix; peak 128 B/clk/SM at the "
+                                "median SM clock sampled during the timed steps"}
 
     roofline_indexer = indexer_roofline(cap, cfg, pk)
-    clocks = clk.summary()
     res = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),

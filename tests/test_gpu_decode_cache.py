@@ -194,16 +194,27 @@ def test_decode_without_use_cache_leaves_the_cache_unclaimed(cuda_ok):
     assert torch.equal(o1, o2)
 
 
-def test_split_sdpa_matches_unsplit_and_reference(cuda_ok):
+_SPLIT_COUNTS = {
+    "ragged": [0, 1, 15, 16, 17, 700, 2049, 4096],
+    "mostly_empty": [0, 1, 0, 0, 17, 0, 0, 16],
+    "decode64": [0, 4096, 3] + [int(x) for x in torch.randint(0, 4097, (61,),
+                                                             generator=torch.Generator().manual_seed(5))],
+    "four_rows": [5, 4096, 0, 333],
+}
+
+
+@pytest.mark.parametrize("case", sorted(_SPLIT_COUNTS))
+def test_split_sdpa_matches_unsplit_and_reference(cuda_ok, case):
     """Few rows (decode): gsa_sparse_sdpa_strided cuts each row's selected keys over several CTAs
-    and merges their partial softmax results; against the unsplit kernel and fp32 attention.
-    Rows with 0, 1, 15, 16, 17 and thousands of keys (empty and ragged key ranges)."""
+    (8 ranges per row at 4 and 8 rows, 2 at 64) and merges their partial softmax results; against
+    the unsplit kernel and fp32 attention.  Rows with 0, 1, 15, 16, 17 and thousands of keys
+    (empty and ragged key ranges), mostly empty rows, and 64 decode rows."""
     import ctypes as C
 
     from gsa_b200 import _lib, ops
 
     H, Hk, D, Lkv = 32, 8, 128, 6000
-    counts = [0, 1, 15, 16, 17, 700, 2049, 4096]
+    counts = _SPLIT_COUNTS[case]
     B = len(counts)
     g = torch.Generator().manual_seed(21)
     q = torch.randn(B, 1, H, D, generator=g).to(torch.bfloat16).to(DEV)
@@ -238,7 +249,9 @@ def test_split_sdpa_matches_unsplit_and_reference(cuda_ok):
         ref[b] = torch.einsum("hc,chd->hd", p, vv) * gate[b, 0].float().cpu()
     for out in (split, whole):
         o = out.view(B, H, D).float().cpu()
-        assert torch.equal(o[0], torch.zeros(H, D))                      # no keys: zeros
+        for b, c in enumerate(counts):
+            if c == 0:
+                assert torch.equal(o[b], torch.zeros(H, D))              # no keys: zeros
         err = (o - ref).norm() / ref.norm()
         assert float(err) < 1e-2, float(err)
     assert float((split.float() - whole.float()).abs().max()) < 2e-2
