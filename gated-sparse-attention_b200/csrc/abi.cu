@@ -582,12 +582,12 @@ int gsa_decode_attend(const gsa_dims* dims, const gsa_proj_layout* layout, const
   if (phase == GSA_DECODE_ATTEND) goto attend;
   {
   // 1. RoPE / gates / head weights; K, V and k^I of the new tokens into slots past .. past+L-1
+  // (it also clears the indexer's row statistics)
   EpiArgs ea{*dims, *layout, dtype, R, proj, proj_ld, positions, cos_tab, sin_tab, tab_dtype, tab_rows,
              q, kvb + past * kv_ld * esz, kvb + (past * kv_ld + row) * esz, kv_ld, g1, w, shift, di->err, L,
-             kv_bstride, kib + past * dI * esz, dI, ki_bstride, past};
+             kv_bstride, kib + past * dI * esz, dI, ki_bstride, past, stats};
   if ((st = launch_proj_epilogue(ea, s))) return st;
   // 2. indexer over every cached key + the candidates of each row
-  if (cudaMemsetAsync(stats, 0, R * 3 * sizeof(double), s) != cudaSuccess) return GSA_ERR_CUDA;
   const void* qI = static_cast<const uint8_t*>(proj) + layout->qi * esz;
   if (o.survivors)
     st = gsa_indexer_survivors(dims, dtype, B, L, n, past, 1, qI, proj_ld, L * proj_ld, ki_store, dI, ki_bstride, w,

@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "gsa_b200.h"
 
 namespace gsa {
@@ -127,6 +129,33 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gsrc, uint3
 // Prefetch a global range into L2 through the bulk-copy engine (16-byte aligned, multiple of 16).
 __device__ __forceinline__ void bulk_prefetch_l2(const void* gsrc, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gsrc), "r"(bytes) : "memory");
+}
+
+// ---------------------------------------------------------------------------------------------
+// Programmatic dependent launch.  A kernel launched by launch_chained may be scheduled while the
+// previous kernel of its stream is still running.  Every CTA of such a kernel executes
+// chain_wait() before anything else (it returns once the previous grid has completed and its
+// memory is visible; a kernel launched the ordinary way passes straight through), so each
+// chained kernel completes after its predecessor and the stream keeps its order.  chain_release()
+// lets the next chained kernel be scheduled once every CTA of this one has started.
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ void chain_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void chain_release() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+static inline cudaError_t launch_chained(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                         cudaStream_t stream, Args&&... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // ---------------------------------------------------------------------------------------------

@@ -66,6 +66,8 @@ __device__ __forceinline__ void split8(const uint4& lo, const uint4& hi, uint32_
 // Each warp scores keys_per_warp consecutive keys (a multiple of 16 * U).
 template <int HI, int NT, int U>
 __global__ void __launch_bounds__(kThreads, 2) indexer_decode_kernel(IdxArgs a, int keys_per_warp) {
+  chain_wait();
+  chain_release();
   constexpr int TPM = 8 / HI;
   constexpr int MAXT = NT * TPM;
   const int64_t b = blockIdx.y;
@@ -237,8 +239,9 @@ static int launch(const IdxArgs& a, int64_t B, int64_t key_limit, int num_sms, c
   const int64_t ranges = (key_limit + kWarps * kpw - 1) / (kWarps * kpw);
   if (ranges > 0x7fffffffLL) return GSA_ERR_BAD_ARG;
   dim3 grid((unsigned)ranges, (unsigned)B);
-  indexer_decode_kernel<HI, NT, U><<<grid, kThreads, 0, s>>>(a, (int)kpw);
-  return cudaGetLastError() == cudaSuccess ? GSA_OK : GSA_ERR_LAUNCH;
+  return launch_chained(indexer_decode_kernel<HI, NT, U>, grid, dim3(kThreads), 0, s, a, (int)kpw) == cudaSuccess
+             ? GSA_OK
+             : GSA_ERR_LAUNCH;
 }
 
 }  // namespace dec

@@ -33,6 +33,7 @@ struct EpiArgs {
   void* ki_out;
   int64_t ki_ld, ki_bstride;
   int64_t pos0;       // positions == NULL: token t = b * L + i sits at position pos0 + i
+  double* zero_stats; // [T, 3] set to zero (the indexer's row statistics of a decode step), or NULL
 };
 
 // RoPE position of the epilogue's token t.

@@ -33,6 +33,8 @@ __device__ __forceinline__ void rope_head(const EpiArgs& a, int64_t src_row, int
 }
 
 __global__ void proj_epilogue_kernel(EpiArgs a) {
+  chain_wait();
+  chain_release();
   const int64_t t = blockIdx.x;
   if (t >= a.T) return;
   const int H = a.d.n_heads, Hk = a.d.n_kv_heads, D = a.d.d_head, HI = a.d.n_idx_heads;
@@ -85,6 +87,7 @@ __global__ void proj_epilogue_kernel(EpiArgs a) {
     }
     a.shift_out[t] = 0.5f * sum;
   }
+  if (a.zero_stats && threadIdx.x < 3) a.zero_stats[t * 3 + threadIdx.x] = 0.0;
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -130,6 +133,8 @@ __device__ __forceinline__ void st8_bf16(__nv_bfloat16* p, const Vec8& v) {
 
 template <typename TabT>
 __global__ void __launch_bounds__(256) proj_epilogue_bf16_kernel(EpiArgs a) {
+  chain_wait();
+  chain_release();
   const int64_t t = blockIdx.x;
   if (t >= a.T) return;
   constexpr int dt = GSA_DTYPE_BF16;
@@ -204,6 +209,7 @@ __global__ void __launch_bounds__(256) proj_epilogue_bf16_kernel(EpiArgs a) {
     }
     a.shift_out[t] = 0.5f * sum;
   }
+  if (a.zero_stats && blockIdx.y == 0 && threadIdx.x < 3) a.zero_stats[t * 3 + threadIdx.x] = 0.0;
 }
 
 static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) % 16) == 0; }
@@ -229,14 +235,14 @@ int launch_proj_epilogue(const EpiArgs& a, cudaStream_t stream) {
   if (epilogue_vec_ok(a)) {
     // few tokens (decode): four CTAs per token, so that the copy latency is spread over more SMs
     const dim3 grid((unsigned)a.T, a.T < 512 ? 4u : 1u);
-    if (a.tab_dtype == GSA_DTYPE_BF16)
-      proj_epilogue_bf16_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(a);
-    else
-      proj_epilogue_bf16_kernel<float><<<grid, 256, 0, stream>>>(a);
-  } else {
-    proj_epilogue_kernel<<<(unsigned)a.T, 128, 0, stream>>>(a);
+    const cudaError_t e = a.tab_dtype == GSA_DTYPE_BF16
+                              ? launch_chained(proj_epilogue_bf16_kernel<__nv_bfloat16>, grid, dim3(256), 0, stream, a)
+                              : launch_chained(proj_epilogue_bf16_kernel<float>, grid, dim3(256), 0, stream, a);
+    if (e != cudaSuccess) return GSA_ERR_LAUNCH;
+  } else if (launch_chained(proj_epilogue_kernel, dim3((unsigned)a.T), dim3(128), 0, stream, a) != cudaSuccess) {
+    return GSA_ERR_LAUNCH;
   }
-  return cudaGetLastError() == cudaSuccess ? GSA_OK : GSA_ERR_LAUNCH;
+  return GSA_OK;
 }
 
 // Standalone gate (ValueGate / OutputGate modules): out = x * act(logits).

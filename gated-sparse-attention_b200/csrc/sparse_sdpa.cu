@@ -78,6 +78,8 @@ __device__ __forceinline__ int row_count(const SdpaArgs& a, int64_t row) {
 
 template <int D, int NREP, int MAXW>
 __global__ void __launch_bounds__(MAXW * 32) sdpa_tc_kernel(SdpaArgs a) {
+  chain_wait();
+  chain_release();
   static_assert(D % 16 == 0 && NREP >= 1 && NREP <= 8, "tile shape");
   extern __shared__ __align__(128) uint8_t smem[];
   const int Hk = a.Hk;
@@ -400,6 +402,8 @@ __global__ void sdpa_f32_kernel(SdpaF32Args a) {
 // (row, head), one thread per dimension; the split weights are computed once per CTA.
 __global__ void sdpa_combine_kernel(int64_t R, int H, int D, int splits, const float* part,
                                     const __nv_bfloat16* gate, __nv_bfloat16* out) {
+  chain_wait();
+  chain_release();
   const int64_t row = blockIdx.x;
   const int h = blockIdx.y;
   const int64_t NW = R * splits;
@@ -470,12 +474,11 @@ static int launch_tc_w(SdpaArgs a, int num_sms, cudaStream_t stream) {
   }
   const int64_t items = R * a.splits;
   if (grid > items) grid = items;
-  kern<<<(unsigned)grid, threads, smem, stream>>>(a);
-  if (cudaGetLastError() != cudaSuccess) return GSA_ERR_LAUNCH;
-  if (a.splits > 1) {
-    sdpa_combine_kernel<<<dim3((unsigned)R, (unsigned)H), D, 0, stream>>>(R, H, D, a.splits, a.part, a.gate, a.out);
-    if (cudaGetLastError() != cudaSuccess) return GSA_ERR_LAUNCH;
-  }
+  if (launch_chained(kern, dim3((unsigned)grid), dim3(threads), smem, stream, a) != cudaSuccess) return GSA_ERR_LAUNCH;
+  if (a.splits > 1 &&
+      launch_chained(sdpa_combine_kernel, dim3((unsigned)R, (unsigned)H), dim3(D), 0, stream, R, H, D, a.splits,
+                     (const float*)a.part, a.gate, a.out) != cudaSuccess)
+    return GSA_ERR_LAUNCH;
   return GSA_OK;
 }
 

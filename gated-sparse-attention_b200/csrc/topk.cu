@@ -525,6 +525,8 @@ __global__ void __launch_bounds__(kSelThreads) topk_candidates_kernel(
 __global__ void __launch_bounds__(kSelThreads) select_finalize_kernel(
     int32_t k_eff, const int32_t* cand_idx, const float* cand_score, const int32_t* cand_count,
     const int32_t* k, int32_t* sel_idx, int64_t sel_ld, int32_t* sel_count, uint8_t* sel_mask, int stage) {
+  chain_wait();
+  chain_release();
   __shared__ uint32_t hist[kBins];
   __shared__ uint32_t ws[48];
   __shared__ uint32_t sel[4];
@@ -825,8 +827,11 @@ __device__ __forceinline__ uint32_t few_flags(const float* row, int64_t c, int64
 }
 
 __global__ void __launch_bounds__(kFewThreads) compact_few_count_kernel(CmpArgs a, int nseg, int32_t* seg_count) {
+  chain_wait();
+  chain_release();
   const int64_t r = blockIdx.x;
   const int sg = blockIdx.y;
+  if (r == 0 && sg == 0 && threadIdx.x == 0) *a.fail_count = 0;
   int64_t n, c0, c1;
   few_segment(a, r, nseg, sg, n, c0, c1);
   const float tau = cmp_threshold(a, r, n);
@@ -848,6 +853,8 @@ __global__ void __launch_bounds__(kFewThreads) compact_few_count_kernel(CmpArgs 
 }
 
 __global__ void __launch_bounds__(kFewThreads) compact_few_write_kernel(CmpArgs a, int nseg, const int32_t* seg_count) {
+  chain_wait();
+  chain_release();
   const int64_t r = blockIdx.x;
   const int sg = blockIdx.y;
   int64_t n, c0, c1;
@@ -907,6 +914,8 @@ __global__ void __launch_bounds__(kFewThreads) compact_few_write_kernel(CmpArgs 
 
 // Exact selection (topk_row) of the rows the compaction could not settle.
 __global__ void __launch_bounds__(kSelThreads) topk_fallback_kernel(CmpArgs a) {
+  chain_wait();
+  chain_release();
   extern __shared__ __align__(16) uint8_t topk_dyn[];
   const int32_t nf = *a.fail_count;
   for (int32_t i = blockIdx.x; i < nf; i += gridDim.x) {
@@ -926,7 +935,6 @@ int launch_threshold_candidates(int64_t R, int64_t Lq, int64_t n_cols, int64_t q
   if (R > 0x7fffffffLL || ld % 4 != 0 || (reinterpret_cast<uintptr_t>(scores) % 16) != 0) return GSA_ERR_BAD_ARG;
   CmpArgs a{R, Lq, n_cols, q_pos0, causal, scores, ld, center, stats, K, cap, cand_idx, cand_score, cand_count,
             fail_list, fail_count, err};
-  if (cudaMemsetAsync(fail_count, 0, sizeof(int32_t), stream) != cudaSuccess) return GSA_ERR_CUDA;
   if (seg_count && R < num_sms && R <= 65535) {
     // few rows: about four CTAs per SM in all, and segments of at most one 8192-column round
     // where 16 segments allow it
@@ -935,9 +943,14 @@ int launch_threshold_candidates(int64_t R, int64_t Lq, int64_t n_cols, int64_t q
     ns = std::min<int64_t>(std::min<int64_t>(ns, kFewSegsMax), std::max<int64_t>(1, groups));
     const int nseg = (int)ns;
     const dim3 grid((unsigned)R, (unsigned)nseg);
-    compact_few_count_kernel<<<grid, kFewThreads, 0, stream>>>(a, nseg, seg_count);
-    compact_few_write_kernel<<<grid, kFewThreads, 0, stream>>>(a, nseg, seg_count);
+    // the count kernel also clears the failed-row count
+    if (launch_chained(compact_few_count_kernel, grid, dim3(kFewThreads), 0, stream, a, nseg, seg_count) !=
+            cudaSuccess ||
+        launch_chained(compact_few_write_kernel, grid, dim3(kFewThreads), 0, stream, a, nseg,
+                       (const int32_t*)seg_count) != cudaSuccess)
+      return GSA_ERR_LAUNCH;
   } else {
+    if (cudaMemsetAsync(fail_count, 0, sizeof(int32_t), stream) != cudaSuccess) return GSA_ERR_CUDA;
     if (cudaFuncSetAttribute(threshold_compact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kCmpSmem) !=
         cudaSuccess)
       return GSA_ERR_LAUNCH;
@@ -955,8 +968,9 @@ int launch_threshold_candidates(int64_t R, int64_t Lq, int64_t n_cols, int64_t q
   if (cudaFuncSetAttribute(topk_fallback_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn) !=
       cudaSuccess)
     return GSA_ERR_LAUNCH;
-  topk_fallback_kernel<<<(unsigned)num_sms, kSelThreads, dyn, stream>>>(a);
-  return cudaGetLastError() == cudaSuccess ? GSA_OK : GSA_ERR_LAUNCH;
+  return launch_chained(topk_fallback_kernel, dim3((unsigned)num_sms), dim3(kSelThreads), dyn, stream, a) == cudaSuccess
+             ? GSA_OK
+             : GSA_ERR_LAUNCH;
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -1020,6 +1034,8 @@ __device__ __forceinline__ void warp_find_bin(const uint32_t* hist, int nb, uint
 __global__ void __launch_bounds__(kWarpSelWarps * 32) select_finalize_warp_kernel(
     int64_t R, int32_t cand_ld, const int32_t* cand_idx, const float* cand_score, const int32_t* cand_count,
     const int32_t* k, int32_t* sel_idx, int64_t sel_ld, int32_t* sel_count) {
+  chain_wait();
+  chain_release();
   extern __shared__ __align__(16) uint8_t wsel_smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint32_t* hist = reinterpret_cast<uint32_t*>(wsel_smem) + warp * kWarpBins;
@@ -1213,9 +1229,11 @@ int launch_select_finalize_warp(int64_t R, int32_t cand_ld, const int32_t* cand_
   int64_t grid = (int64_t)num_sms * per_sm;
   const int64_t need = (R + kWarpSelWarps - 1) / kWarpSelWarps;
   if (grid > need) grid = need;
-  select_finalize_warp_kernel<<<(unsigned)grid, kWarpSelWarps * 32, kWarpSelSmem, stream>>>(
-      R, cand_ld, cand_idx, cand_score, cand_count, k, sel_idx, sel_ld, sel_count);
-  return cudaGetLastError() == cudaSuccess ? GSA_OK : GSA_ERR_LAUNCH;
+  return launch_chained(select_finalize_warp_kernel, dim3((unsigned)grid), dim3(kWarpSelWarps * 32),
+                        (size_t)kWarpSelSmem, stream, R, cand_ld, cand_idx, cand_score, cand_count, k, sel_idx, sel_ld,
+                        sel_count) == cudaSuccess
+             ? GSA_OK
+             : GSA_ERR_LAUNCH;
 }
 
 // Row statistics of a materialised score matrix: sum, sum of squares, finite count (fp64).
@@ -1316,6 +1334,8 @@ __global__ void __launch_bounds__(1024) variance_adaptive_k_kernel(int64_t R, in
                                                                    gsa_topk_params p, const double* stats,
                                                                    const float* shift, float* var_out,
                                                                    double* total, int32_t* k_out) {
+  chain_wait();
+  chain_release();
   __shared__ double red[1024];
   const int t = threadIdx.x;
   const double N = (double)n_cols;
@@ -1357,8 +1377,10 @@ int launch_variance_adaptive_k(int64_t R, int64_t n_cols, int dtype, const gsa_t
                                int32_t* k_out, cudaStream_t stream) {
   if (R == 0) return GSA_OK;
   if (R > 1024 || !p.use_adaptive) return GSA_ERR_BAD_ARG;
-  variance_adaptive_k_kernel<<<1, 1024, 0, stream>>>(R, n_cols, dtype, p, stats, shift, var_out, total, k_out);
-  return cudaGetLastError() == cudaSuccess ? GSA_OK : GSA_ERR_LAUNCH;
+  return launch_chained(variance_adaptive_k_kernel, dim3(1), dim3(1024), 0, stream, R, n_cols, dtype, p, stats, shift,
+                        var_out, total, k_out) == cudaSuccess
+             ? GSA_OK
+             : GSA_ERR_LAUNCH;
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -1394,9 +1416,10 @@ int launch_select_finalize(int64_t R, int32_t k_eff, const int32_t* cand_idx, co
       cudaFuncSetAttribute(select_finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn) !=
           cudaSuccess)
     return GSA_ERR_LAUNCH;
-  select_finalize_kernel<<<(unsigned)R, kSelThreads, stage ? dyn : 0, stream>>>(
-      k_eff, cand_idx, cand_score, cand_count, k, sel_idx, sel_ld, sel_count, sel_mask, stage);
-  return cudaGetLastError() == cudaSuccess ? GSA_OK : GSA_ERR_LAUNCH;
+  return launch_chained(select_finalize_kernel, dim3((unsigned)R), dim3(kSelThreads), stage ? dyn : 0, stream, k_eff,
+                        cand_idx, cand_score, cand_count, k, sel_idx, sel_ld, sel_count, sel_mask, stage) == cudaSuccess
+             ? GSA_OK
+             : GSA_ERR_LAUNCH;
 }
 
 int launch_row_stats(int64_t R, int64_t n_cols, const float* scores, int64_t ld, double* stats,
