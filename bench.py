@@ -595,10 +595,12 @@ def run_decode(args, world, rank):
     parts = {"indexer": rl("gsa::dec::indexer_decode_kernel<8,1,4>", nbytes["indexer_keys"], idx_ms),
              "sdpa": rl("gsa::sdpa_tc_kernel<128,4>", nbytes["kv_rows"] + B * 3 * cfg.n_heads * cfg.d_head * 2,
                         sdpa_ms)}
-    # our kernels per step (one gsa_decode_attend call): projection epilogue, decode indexer,
-    # survivor compaction + exact fallback, row variance (2) + adaptive k, final selection, split
-    # SDPA + merge
-    launches_per_step = 1 + 1 + 2 + (3 if cfg.use_adaptive_k else 1) + 1 + 2
+    # our kernels per step (gsa_decode_attend): projection epilogue, decode indexer, survivor count +
+    # write + exact fallback, variance and adaptive k (one kernel for one GPU; row variance + their
+    # sum, then adaptive k, around the all-reduce of the sharded step), final selection, split SDPA
+    # + merge
+    var_launches = (1 if world == 1 else 3) if cfg.use_adaptive_k else 1
+    launches_per_step = 1 + 1 + 3 + var_launches + 1 + 2
     return {
         "metric": DECODE_METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
