@@ -155,7 +155,9 @@ static inline cudaError_t launch_chained(void (*kernel)(KArgs...), dim3 grid, di
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (e != cudaSuccess) (void)cudaGetLastError();  // reported here; not left for the next launch check
+  return e;
 }
 
 // ---------------------------------------------------------------------------------------------
