@@ -153,3 +153,31 @@ def test_training_and_decoder_entry_points_validate_before_any_launch():
     assert lib.gsa_add_rmsnorm(1, 0, 8, None, 8, None, 0, None, 1e-5, None, 0, None, 8, None) == 0  # empty
     assert lib.gsa_silu_mul(1, 4, 8, p, 15, p, 8, None) == 1    # gu row shorter than 2n
     assert lib.gsa_silu_mul(1, 0, 8, None, 16, None, 8, None) == 0
+
+
+def test_header_is_plain_c_and_a_c_program_links():
+    """A C99 program includes gsa_b200.h (no CUDA or torch headers needed), links the library and
+    calls the entry points that touch no GPU; the header also compiles as C++."""
+    import shutil
+    import subprocess
+
+    import pytest
+
+    from gsa_b200 import _lib
+
+    if shutil.which("gcc") is None or shutil.which("g++") is None:
+        pytest.skip("no host C compiler")
+    out = ROOT / "tests" / "_build" / "c_abi"
+    out.mkdir(parents=True, exist_ok=True)
+    src = out / "use.c"
+    src.write_text('#include "gsa_b200.h"\n#include <stdio.h>\n'
+                   "int main(void) {\n  puts(gsa_version());\n"
+                   "  return gsa_workspace_size(2, 8) == 64 ? 0 : 1;\n}\n")
+    lib = _lib.LIB_PATH
+    exe = out / "use"
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-Werror", "-I", str(ROOT / "include"), str(src),
+                    str(lib), f"-Wl,-rpath,{lib.parent}", "-o", str(exe)], check=True)
+    p = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert p.returncode == 0 and "sm_100a" in p.stdout
+    subprocess.run(["g++", "-std=c++17", "-Wall", "-Werror", "-fsyntax-only", "-x", "c++", "-I",
+                    str(ROOT / "include"), str(src)], check=True)
