@@ -9,31 +9,38 @@ namespace gsa {
 __device__ int g_device_error;
 
 // ---------------------------------------------------------------------------------------------
-// Per-device state: address of the error word and the SM count.
+// Per-call device state: the address of the error word in the current context, and the SM count.
+// The address is looked up on every call: it belongs to the CUDA context (a cudaDeviceReset, or a
+// driver-API caller's own context on the same device, loads the module at another address), and
+// once the module is loaded in a context the lookup is a table search.  The SM count is a
+// property of the device and is cached per ordinal.
 // ---------------------------------------------------------------------------------------------
 struct DeviceInfo {
   int* err = nullptr;
   int num_sms = 0;
-  bool ready = false;
 };
 static std::mutex g_mu;
-static DeviceInfo g_dev[64];
+static int g_num_sms[64];
 
-static int device_info(DeviceInfo** out) {
+static int device_info(DeviceInfo* out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return GSA_ERR_CUDA;
-  std::lock_guard<std::mutex> lk(g_mu);
-  DeviceInfo& d = g_dev[dev];
-  if (!d.ready) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return GSA_ERR_CUDA;
-    int sms = 0;
-    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return GSA_ERR_CUDA;
-    d.err = static_cast<int*>(p);
-    d.num_sms = sms;
-    d.ready = true;
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess || p == nullptr) {
+    cudaGetLastError();
+    return GSA_ERR_CUDA;
   }
-  *out = &d;
+  out->err = static_cast<int*>(p);
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g_num_sms[dev] == 0) {
+      int sms = 0;
+      if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+        return GSA_ERR_CUDA;
+      g_num_sms[dev] = sms;
+    }
+    out->num_sms = g_num_sms[dev];
+  }
   return GSA_OK;
 }
 
@@ -72,11 +79,6 @@ struct ChunkIter {
   }
 };
 
-static bool dims_ok(const gsa_dims* d) {
-  return d && d->d_model > 0 && d->n_heads > 0 && d->n_kv_heads > 0 && d->n_heads % d->n_kv_heads == 0 &&
-         d->d_head > 0 && d->d_head % 2 == 0 && d->n_idx_heads > 0 && d->d_idx > 0;
-}
-
 }  // namespace gsa
 
 using namespace gsa;
@@ -86,8 +88,8 @@ extern "C" {
 const char* gsa_version(void) { return "gsa_b200 0.1.0 (sm_100a)"; }
 
 int gsa_get_device_error(int* code_out, gsa_stream_t stream) {
-  DeviceInfo* di;
-  int st = device_info(&di);
+  DeviceInfo dinfo, *di = &dinfo;
+  int st = device_info(di);
   if (st) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   int h = 0;
@@ -112,8 +114,8 @@ int gsa_proj_epilogue(const gsa_dims* dims, const gsa_proj_layout* layout, int d
     return GSA_ERR_BAD_ARG;
   if (dims->gate_act < GSA_ACT_SIGMOID || dims->gate_act > GSA_ACT_SILU) return GSA_ERR_UNSUPPORTED;
   if (kv_ld < (int64_t)dims->n_kv_heads * dims->d_head) return GSA_ERR_BAD_ARG;
-  DeviceInfo* di;
-  int st = device_info(&di);
+  DeviceInfo dinfo, *di = &dinfo;
+  int st = device_info(di);
   if (st) return st;
   EpiArgs a{*dims, *layout, dtype, T, proj, proj_ld, positions, cos_tab, sin_tab, tab_dtype, tab_rows,
             q_out, k_out, v_out, kv_ld, g1_out, w_out, shift_out, di->err};
@@ -135,8 +137,8 @@ int gsa_proj_epilogue_cache(const gsa_dims* dims, const gsa_proj_layout* layout,
   if (dims->gate_act < GSA_ACT_SIGMOID || dims->gate_act > GSA_ACT_SILU) return GSA_ERR_UNSUPPORTED;
   if (kv_ld < (int64_t)dims->n_kv_heads * dims->d_head || kv_bstride < L * kv_ld) return GSA_ERR_BAD_ARG;
   if (ki_out && (layout->ki < 0 || ki_ld < dims->d_idx || ki_bstride < L * ki_ld)) return GSA_ERR_BAD_ARG;
-  DeviceInfo* di;
-  int st = device_info(&di);
+  DeviceInfo dinfo, *di = &dinfo;
+  int st = device_info(di);
   if (st) return st;
   EpiArgs a{*dims, *layout, dtype, B * L, proj, proj_ld, positions, cos_tab, sin_tab, tab_dtype, tab_rows,
             q_out, k_out, v_out, kv_ld, g1_out, w_out, shift_out, di->err, L, kv_bstride, ki_out, ki_ld,
@@ -159,15 +161,15 @@ int gsa_indexer_scores(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, i
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (indexer_decode_eligible(a, B)) {
     // a few tokens per sequence (decode): every sequence in one launch, streaming k^I once
-    DeviceInfo* di;
-    int st = device_info(&di);
+    DeviceInfo dinfo, *di = &dinfo;
+    int st = device_info(di);
     if (st) return st;
     return launch_indexer_decode(a, B, di->num_sms, s);
   }
   if (indexer_tc_eligible(a)) {
     // tensor-core kernel: bf16, d_I = 64, H_I in {4, 8}, sigmoid; one launch per batch row
-    DeviceInfo* di;
-    int st = device_info(&di);
+    DeviceInfo dinfo, *di = &dinfo;
+    int st = device_info(di);
     if (st) return st;
     const int64_t HI = dims->n_idx_heads;
     for (int64_t b = 0; b < B; ++b) {
@@ -236,8 +238,8 @@ int gsa_select_finalize(int64_t R, int32_t k_eff, const int32_t* cand_idx, const
     // one warp per row when the rows fill the GPU; few rows (decode) take a CTA each, since a
     // row's passes over its candidates are latency-bound on one warp (the selection mask needs
     // the per-row CTA kernel as well)
-    DeviceInfo* di;
-    int st = device_info(&di);
+    DeviceInfo dinfo, *di = &dinfo;
+    int st = device_info(di);
     if (st) return st;
     if (R >= 2LL * di->num_sms)
       return launch_select_finalize_warp(R, k_eff, cand_idx, cand_score, cand_count, k, sel_idx, sel_ld, sel_count,
@@ -265,8 +267,8 @@ int gsa_sparse_sdpa(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int6
 
 int64_t gsa_sdpa_workspace_size(const gsa_dims* dims, int64_t B, int64_t Lq) {
   if (!dims_ok(dims) || B <= 0 || Lq <= 0) return 0;
-  DeviceInfo* di;
-  if (device_info(&di)) return 0;
+  DeviceInfo dinfo, *di = &dinfo;
+  if (device_info(di)) return 0;
   // room for the most key ranges the launch may choose (one per resident CTA, at most 8 per
   // row; at most two resident CTAs per SM)
   const int64_t R = B * Lq, slots = 2LL * di->num_sms;
@@ -287,8 +289,8 @@ static int sdpa_impl(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int
   if (!q || !k || !v || !sel_idx || !sel_count || !out) return GSA_ERR_BAD_ARG;
   const int64_t row_elems = (int64_t)dims->n_kv_heads * dims->d_head;
   if (kv_ld < row_elems || kv_bstride < Lkv * kv_ld) return GSA_ERR_BAD_ARG;
-  DeviceInfo* di;
-  int st = device_info(&di);
+  DeviceInfo dinfo, *di = &dinfo;
+  int st = device_info(di);
   if (st) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == GSA_DTYPE_BF16) {
@@ -352,8 +354,8 @@ int gsa_sparse_sdpa_backward(const gsa_dims* dims, int dtype, int64_t B, int64_t
       !aligned(dv, 16) || !aligned(dq, 16) || (kv_ld * esz) % 8 || (kv_bstride * esz) % 8 || dkv_ld % 4 ||
       dkv_bstride % 4)
     return GSA_ERR_BAD_ARG;
-  DeviceInfo* di;
-  int st = device_info(&di);
+  DeviceInfo dinfo, *di = &dinfo;
+  int st = device_info(di);
   if (st) return st;
   SdpaBwdArgs a{B, Lq, Lkv, dims->n_heads, dims->n_kv_heads, dims->d_head, dtype, q, k, v, kv_ld, kv_bstride,
                 sel_idx, sel_ld, sel_count, o, d_o, lse, dq, dk, dv, dkv_ld, dkv_bstride, scale, di->err};
@@ -443,8 +445,8 @@ int gsa_indexer_survivors(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq
   if (dims->idx_act != GSA_ACT_SIGMOID || 2 * (int64_t)cap < 3 * (int64_t)k_eff + 2048) return GSA_ERR_UNSUPPORTED;
   if (!workspace || !aligned(workspace, 256) || workspace_bytes < gsa_survivors_workspace_size(chunk_rows, Lkv))
     return GSA_ERR_WORKSPACE;
-  DeviceInfo* di;
-  int st = device_info(&di);
+  DeviceInfo dinfo, *di = &dinfo;
+  int st = device_info(di);
   if (st) return st;
   const int64_t ld = (Lkv + 3) / 4 * 4;
   uint8_t* wsb = static_cast<uint8_t*>(workspace);
@@ -557,8 +559,8 @@ int gsa_decode_attend(const gsa_dims* dims, const gsa_proj_layout* layout, const
   if (kv_bstride < n * kv_ld || ki_bstride < n * dI) return GSA_ERR_BAD_ARG;
   const DecodeLayout o = decode_layout(dims, tp, dtype, B, L, n);
   if (!workspace || !aligned(workspace, 256) || workspace_bytes < o.bytes) return GSA_ERR_WORKSPACE;
-  DeviceInfo* di;
-  int st = device_info(&di);
+  DeviceInfo dinfo, *di = &dinfo;
+  int st = device_info(di);
   if (st) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);

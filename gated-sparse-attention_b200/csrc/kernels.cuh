@@ -6,6 +6,12 @@
 
 namespace gsa {
 
+// Layer shape the kernels can take (shared by every entry point's argument check).
+inline bool dims_ok(const gsa_dims* d) {
+  return d && d->d_model > 0 && d->n_heads > 0 && d->n_kv_heads > 0 && d->n_heads % d->n_kv_heads == 0 &&
+         d->d_head > 0 && d->d_head % 2 == 0 && d->n_idx_heads > 0 && d->d_idx > 0;
+}
+
 struct EpiArgs {
   gsa_dims d;
   gsa_proj_layout lay;

@@ -7,12 +7,14 @@
 // bounded scratch: GSA_STATIC_SCRATCH_BYTES (64 MiB) per device, which caps one chunk at
 // 64 MiB / (4 * round4(Lkv)) query rows and the key length at 16,777,216.
 //
-// The buffer is a file-scope __device__ array; its address is looked up once per device (with
-// that device current) and cached.  Because every call on a device shares the one buffer, calls
-// that overlap in time on the same device (two streams, two host threads) race on it: callers
-// serialise them.
-#include <mutex>
-
+// The buffer is a file-scope __device__ array.  In host code its name only stands for the
+// symbol; the kernels get the device address that cudaGetSymbolAddress returns in the calling
+// thread's current context.  That address belongs to the context (a cudaDeviceReset, or a
+// driver-API caller's own context on the same device, places the module elsewhere), so it is
+// looked up on every call; once the module is loaded in a context the lookup is a table search.
+// The first call in a context loads the module: make it before any stream capture.  Because every
+// call on a device shares the one buffer, calls that overlap in time on the same device (two
+// streams, two host threads) race on it: callers serialise them.
 #include "kernels.cuh"
 
 namespace gsa {
@@ -23,25 +25,15 @@ static __device__ __align__(256) float g_select_scratch[GSA_STATIC_SCRATCH_BYTES
 
 namespace {
 
-constexpr int kMaxDevices = 64;
-std::mutex g_scratch_mu;
-float* g_scratch_ptr[kMaxDevices] = {};
-
-// Address of this device's scratch; the first call on a device performs the lookup.
+// Device address of the scratch in the current context.
 int static_scratch(float** out) {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return GSA_ERR_CUDA;
-  std::lock_guard<std::mutex> lk(g_scratch_mu);
-  if (!g_scratch_ptr[dev]) {
-    void* p = nullptr;
-    const cudaError_t rc = cudaGetSymbolAddress(&p, g_select_scratch);
-    if (rc != cudaSuccess || p == nullptr) {
-      cudaGetLastError();  // clear the (non-sticky) error so the caller's next CUDA call is clean
-      return GSA_ERR_CUDA;
-    }
-    g_scratch_ptr[dev] = static_cast<float*>(p);
+  void* p = nullptr;
+  const cudaError_t rc = cudaGetSymbolAddress(&p, g_select_scratch);
+  if (rc != cudaSuccess || p == nullptr) {
+    cudaGetLastError();  // clear the (non-sticky) error so the caller's next CUDA call is clean
+    return GSA_ERR_CUDA;
   }
-  *out = g_scratch_ptr[dev];
+  *out = static_cast<float*>(p);
   return GSA_OK;
 }
 
@@ -56,8 +48,14 @@ extern "C" int gsa_indexer_select_static(const gsa_dims* dims, int dtype, int64_
                                          const float* w, const float* bias, float scale, const float* shift,
                                          int32_t k_eff, int32_t* cand_idx, float* cand_score, int32_t* cand_count,
                                          double* row_stats, gsa_stream_t stream) {
-  if (!dims || B < 0 || Lq < 0 || Lkv < 0 || k_eff < 1) return GSA_ERR_BAD_ARG;
+  // every check gsa_indexer_select and its stages make, before this call writes anything
+  if (!dims_ok(dims) || B < 0 || Lq < 0 || Lkv < 0 || k_eff < 1 ||
+      (dtype != GSA_DTYPE_F32 && dtype != GSA_DTYPE_BF16))
+    return GSA_ERR_BAD_ARG;
   if (B * Lq == 0 || Lkv == 0) return GSA_OK;
+  if (!qI || !kI || !w || !bias || !cand_idx || !cand_score || !cand_count || Lkv > 0x7fffffffLL)
+    return GSA_ERR_BAD_ARG;
+  if (dims->idx_act != GSA_ACT_SIGMOID && dims->idx_act != GSA_ACT_RELU) return GSA_ERR_UNSUPPORTED;
   // one row of scores must fit; a chunk is as many rows as fit
   const int64_t row_bytes = gsa_workspace_size(1, Lkv);
   if (row_bytes <= 0 || row_bytes > (int64_t)GSA_STATIC_SCRATCH_BYTES) return GSA_ERR_WORKSPACE;

@@ -326,8 +326,10 @@ int gsa_indexer_survivors(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq
  * query rows and Lkv may be at most 16,777,216; a longer key length returns
  * GSA_ERR_WORKSPACE.  row_stats (if given) is zeroed by the call itself, on ``stream``.
  *
- * The first call on each device performs set-up (it looks up the buffer's device address with
- * that device current); make that first call before any stream capture.  All calls on a device
+ * Each call looks up the buffer's device address in the calling thread's current context (the
+ * address belongs to the context, so it is never cached across calls); the first call in a
+ * context also loads the library's device code there: make it before any stream capture.
+ * Arguments are checked before anything is written.  All calls on a device
  * share the buffer: calls that overlap in time on one device (two streams or two host threads)
  * race on it, so the caller serialises them.
  */

@@ -155,6 +155,33 @@ def test_training_and_decoder_entry_points_validate_before_any_launch():
     assert lib.gsa_silu_mul(1, 0, 8, None, 16, None, 8, None) == 0
 
 
+def test_static_select_checks_arguments_before_writing_row_stats():
+    """gsa_indexer_select_static zeroes row_stats itself, but only after every argument check:
+    a call that returns an error leaves the caller's buffer as it was (CPU only: the buffer is
+    host memory and nothing reaches the device)."""
+    import ctypes as C
+
+    from gsa_b200 import _lib, ops
+
+    lib = _lib.lib()
+    good = ops.make_dims(4096, 32, 8, 128, 8, 64)
+    bad = ops.make_dims(4096, 32, 8, 128, 8, 64)
+    bad.n_kv_heads = 5  # 32 heads do not group over 5 KV heads
+    p = C.c_void_p(256)  # a stand-in device pointer: every case below returns before using it
+    stats = (C.c_double * 12)(*([7.5] * 12))
+
+    def call(d, dtype=1, qI=p, k_eff=16, cand=p):
+        return lib.gsa_indexer_select_static(C.byref(d), dtype, 1, 4, 100, 0, 1, qI, 512, 0, p, 64, 0, p, p,
+                                             0.125, p, k_eff, cand, p, p, stats, None)
+
+    assert call(bad) == 1            # dims that no kernel takes
+    assert call(good, dtype=9) == 1  # unknown dtype
+    assert call(good, qI=None) == 1  # missing indexer queries
+    assert call(good, k_eff=0) == 1  # k_eff < 1
+    assert call(good, cand=None) == 1
+    assert list(stats) == [7.5] * 12, "row_stats was written by a call that failed its checks"
+
+
 def test_header_is_plain_c_and_a_c_program_links():
     """A C99 program includes gsa_b200.h (no CUDA or torch headers needed), links the library and
     calls the entry points that touch no GPU; the header also compiles as C++."""
