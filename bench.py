@@ -35,7 +35,16 @@ import torch  # noqa: E402
 ZIGZAG_FOLDS = 4  # query layout across ranks (gsa_b200.sharded): 2 x folds segments per rank
 WORKLOAD = dict(d_model=4096, n_heads=32, n_kv_heads=8, d_indexer=64, n_indexer_heads=8,
                 k_base=2048, k_min=256, k_max=4096)
+# prefill shapes of the 4096-wide layer (batch, tokens per sequence, k clamps): the 128K headline
+# sequence, the README quickstart batch (two 8192-token sequences whose adaptive-k variance mean
+# spans both) and one 32768-token sequence with k clipped to [512, 4096]
+PREFILL_SHAPES = {"prefill": (1, 131072, 256, 4096), "c2": (2, 8192, 256, 4096), "c3": (1, 32768, 512, 4096)}
 METRIC = "GSA layer fwd tokens/sec at 128K ctx (1/2/4/8 B200); % HBM / tensor roofline"
+PREFILL_METRIC = "GSA layer fwd tokens/sec (B200)"
+
+
+def prefill_workload_name(B, L, k_min, k_max):
+    return f"GSA layer fwd B={B} L={L} d4096 h32/8x128 idx8x64 k2048[{k_min},{k_max}] bf16"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 
 
@@ -241,27 +250,105 @@ def indexer_roofline(cap, cfg, pk, chunk_bytes=4 << 30, reps=2):
                                  "maximum SM clock"}}
 
 
+SDPA_TRAFFIC = ROOT / "profiles" / "sparse_sdpa_traffic.json"
+SDPA_SOURCE = ROOT / "gated-sparse-attention_b200" / "csrc" / "sparse_sdpa.cu"
+
+
+def source_sha(path: Path) -> str:
+    import hashlib
+
+    return hashlib.sha256(path.read_bytes()).hexdigest()[:16]
+
+
+def sdpa_dram_traffic(workload: str, B: int, L: int, world: int, sdpa_bytes: float):
+    """DRAM bytes (read + write) of one SDPA launch from the committed ncu capture of this workload
+    (profiles/sparse_sdpa_traffic.json: one entry per captured shape, each with the sha of the
+    kernel source it was captured from).  Returns (bytes or None, note)."""
+    if not SDPA_TRAFFIC.exists():
+        return None, "no ncu capture committed"
+    caps = json.loads(SDPA_TRAFFIC.read_text()).get("captures", [])
+    sha = source_sha(SDPA_SOURCE)
+    for c in caps:
+        if c["workload"] == workload and c["batch"] == B and c["seq_len"] == L:
+            t = c["dram_bytes_read"] + c["dram_bytes_write"]
+            note = f"ncu capture of this workload ({c['launch']})"
+            if world > 1:
+                # a shard's launch: the capture's DRAM bytes per algorithmic byte
+                t = t / c["algorithmic_bytes"] * sdpa_bytes
+                note = f"one-GPU capture of this workload scaled to the shard's algorithmic bytes ({c['launch']})"
+            if c.get("source_sha") != sha:
+                note += f"; captured from an earlier kernel source (sha {c.get('source_sha')}, now {sha})"
+            return t, note
+    return None, "no ncu capture of this workload"
+
+
+def sdpa_roofline(cfg, cnt, sdpa_ms, sdpa_bytes, pk, pk_kind, clocks, dev, workload, B, L, world):
+    """The SDPA's roofline.  Its binding limit is shared-memory bandwidth: every selected key's K and V
+    rows (2*Hk*D bf16) are written into shared memory by a bulk copy and read back once by ldmatrix,
+    against 128 B / clock / SM at the median SM clock of the timed steps -- that is ``frac``.  Beside it:
+    the DRAM bytes of one launch (ncu) against the measured HBM peak, and the rate of the bytes the rows
+    gather (per row its k_t K and V rows, q, gate, out, indices), which nearby rows serve from L2 and
+    which therefore exceeds the DRAM peak ("l2_amplified")."""
+    t = sdpa_ms / 1e3
+    sm_mhz = clocks.get("sm_mhz") or pk.get("sm_max_mhz", 1965.0)
+    n_sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    sum_k = float(cnt.double().sum().item())
+    smem_bytes = sum_k * 2 * (2 * cfg.n_kv_heads * cfg.d_head * 2)
+    smem_peak = 128.0 * n_sms * sm_mhz * 1e6 / 1e9
+    smem_rate = smem_bytes / t / 1e9
+    hbm = pk["hbm_gbs"]
+    traffic, note = sdpa_dram_traffic(workload, B, L, world, sdpa_bytes)
+    alg_rate = sdpa_bytes / t / 1e9
+    return {"kernel": "gsa::sdpa_tc_kernel<128,4,14>", "bound": "smem", "achieved": round(smem_rate, 1),
+            "peak": round(smem_peak, 1), "unit": "GB/s", "frac": round(smem_rate / smem_peak, 4),
+            "peak_kind": f"128 B/clk/SM x {n_sms} SMs at the {sm_mhz:.0f} MHz median SM clock of the timed steps",
+            "bytes": smem_bytes, "traffic": traffic, "traffic_note": note, "kernel_ms": round(sdpa_ms, 3),
+            "mean_k": sum_k / cnt.numel(),
+            "dram": (None if traffic is None else
+                     {"achieved": round(traffic / t / 1e9, 1), "peak": hbm, "unit": "GB/s",
+                      "frac": round(traffic / t / 1e9 / hbm, 4), "peak_kind": pk_kind}),
+            "l2_amplified": {"algorithmic_bytes": sdpa_bytes, "achieved": round(alg_rate, 1), "unit": "GB/s",
+                             "frac_of_hbm_peak": round(alg_rate / hbm, 4),
+                             "note": "bytes the rows gather, most of them L2 hits: not a DRAM rate"}}
+
+
+def prefill_shape(args):
+    """(batch, tokens per sequence, k_min, k_max) of the prefill workload; --seq-len overrides L."""
+    B, L, k_min, k_max = PREFILL_SHAPES[args.workload]
+    return B, (args.seq_len or L), k_min, k_max
+
+
 def run_ours(args, world, rank):
     from gsa_b200 import GSAConfig, GatedSparseAttention, ops
     from gsa_b200.sharded import enable_query_sharding, zigzag_slice
 
     dev = torch.device("cuda", torch.cuda.current_device())
-    L = args.seq_len
-    cfg = GSAConfig(**WORKLOAD, max_position_embeddings=max(131072, L))
+    B, L, k_min, k_max = prefill_shape(args)
+    cfg = GSAConfig(**{**WORKLOAD, "k_min": k_min, "k_max": k_max}, max_position_embeddings=max(131072, L))
     torch.manual_seed(0)
     m = GatedSparseAttention(cfg).eval().to(torch.bfloat16).to(dev)
+    zigzag = B == 1
     if world > 1:
         import torch.distributed as dist
 
         # zigzag with 4 folds: 8 segments per rank dealt in alternating sweeps, which balances the
-        # causal indexer work exactly and the SDPA work (k_t grows with the position) to ~2%
-        enable_query_sharding(m, dist.group.WORLD, layout="zigzag", folds=ZIGZAG_FOLDS)
+        # causal indexer work exactly and the SDPA work (k_t grows with the position) to ~2%; a
+        # batch of several sequences takes contiguous blocks of every sequence
+        if zigzag:
+            enable_query_sharding(m, dist.group.WORLD, layout="zigzag", folds=ZIGZAG_FOLDS)
+        else:
+            enable_query_sharding(m, dist.group.WORLD, layout="contiguous")
     assert L % (2 * ZIGZAG_FOLDS * world) == 0
     Lr = L // world
     gen = torch.Generator().manual_seed(1)
-    x_full = torch.randn(1, L, cfg.d_model, generator=gen, dtype=torch.float32)
-    x_host = (zigzag_slice(x_full, world, rank, ZIGZAG_FOLDS) if world > 1 else x_full).to(torch.bfloat16)
-    x_host = x_host.contiguous().pin_memory()
+    x_full = torch.randn(B, L, cfg.d_model, generator=gen, dtype=torch.float32)
+    if world == 1:
+        x_host = x_full
+    elif zigzag:
+        x_host = zigzag_slice(x_full, world, rank, ZIGZAG_FOLDS)
+    else:
+        x_host = x_full[:, rank * Lr:(rank + 1) * Lr]
+    x_host = x_host.to(torch.bfloat16).contiguous().pin_memory()
     del x_full
     x = x_host.to(dev)
     torch.cuda.synchronize()
@@ -290,13 +377,13 @@ def run_ours(args, world, rank):
         barrier(world)
     ms_local = start.elapsed_time(end) / args.steps
     ms = max_over_ranks(ms_local, world)
-    value = L / (ms / 1e3)
+    value = B * L / (ms / 1e3)
 
     # end to end through the public API: every step copies its x from pinned host memory and reads
     # its output back.  The copies run on a copy stream, double-buffered as a serving loop does:
     # step i+1's input goes up and step i's output comes down while the layer computes, so only the
     # first upload and the last download are exposed.
-    out_host = torch.empty(1, Lr, cfg.d_model, dtype=torch.bfloat16).pin_memory()
+    out_host = torch.empty(B, Lr, cfg.d_model, dtype=torch.bfloat16).pin_memory()
     xd = [x, torch.empty_like(x)]
     cs = torch.cuda.current_stream(dev)
     ps = torch.cuda.Stream(dev)
@@ -330,7 +417,7 @@ def run_ours(args, world, rank):
     torch.cuda.synchronize()
     barrier(world)
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
-    e2e = {"value": L / (e2e_ms / 1e3), "unit": "tokens/s",
+    e2e = {"value": B * L / (e2e_ms / 1e3), "unit": "tokens/s",
            "h2d_bytes_per_step": x_host.numel() * x_host.element_size() * world,
            "d2h_bytes_per_step": out_host.numel() * out_host.element_size() * world,
            "ms_per_step": e2e_ms,
@@ -376,47 +463,26 @@ def run_ours(args, world, rank):
         torch.cuda.synchronize()
     sdpa_ms = s0.elapsed_time(s1) / reps
     pk, pk_kind = peaks()
-    achieved = sdpa_bytes / (sdpa_ms / 1e3) / 1e9
-    traffic, traffic_note = None, None
-    prof = ROOT / "profiles" / "sparse_sdpa_l131072_traffic.json"
-    if prof.exists():
-        # DRAM bytes of one launch from an ncu capture of this workload; for another sequence
-        # length or shard the captured traffic/algorithmic ratio is applied
-        d = json.loads(prof.read_text())
-        cap_traffic = d["dram_bytes_read"] + d["dram_bytes_write"]
-        if L == d["seq_len"] and world == 1:
-            traffic, traffic_note = cap_traffic, "ncu capture of this workload"
-        else:
-            traffic = cap_traffic / d["algorithmic_bytes"] * sdpa_bytes
-            traffic_note = "scaled from the 131072-token capture by algorithmic bytes"
-    roofline = {"kernel": "gsa::sdpa_tc_kernel<128,4>", "bound": "hbm", "achieved": round(achieved, 1),
-                "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
-                "peak_kind": pk_kind, "traffic": traffic, "traffic_note": traffic_note,
-                "algorithmic_bytes": sdpa_bytes,
-                "kernel_ms": round(sdpa_ms, 3), "mean_k": float(cap["cnt"].double().mean().item())}
-    # the bound that explains it: every selected key's K and V rows are written into shared memory
-    # by a bulk copy and read back once by ldmatrix; shared memory moves 128 B / clock / SM
     clocks = clk.summary()
-    sm_mhz = clocks.get("sm_mhz") or pk.get("sm_max_mhz", 1965.0)
-    smem_bytes = float(cap["cnt"].double().sum().item()) * 2 * (2 * cfg.n_kv_heads * cfg.d_head * 2)
-    smem_peak = 128.0 * torch.cuda.get_device_properties(dev).multi_processor_count * sm_mhz * 1e6 / 1e9
-    smem_rate = smem_bytes / (sdpa_ms / 1e3) / 1e9
-    roofline["smem"] = {"bytes": smem_bytes, "achieved": round(smem_rate, 1), "peak": round(smem_peak, 1),
-                        "unit": "GB/s", "frac": round(smem_rate / smem_peak, 4),
-                        "note": "K/V rows written by bulk copy + read by ldmatrix; peak 128 B/clk/SM at the "
-                                "median SM clock sampled during the timed steps"}
+    roofline = sdpa_roofline(cfg, cap["cnt"], sdpa_ms, sdpa_bytes, pk, pk_kind, clocks, dev,
+                             args.workload, B, L, world)
 
     roofline_indexer = indexer_roofline(cap, cfg, pk)
+    x_mib = B * L * cfg.d_model * 2 / 2**20
+    kv_mib = B * L * cfg.n_kv_heads * cfg.d_head * 2 / 2**20
     res = {
-        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+        "metric": METRIC if (args.workload == "prefill" and L == 131072) else PREFILL_METRIC,
+        "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: x ~ N(0,1) seed 1, default-init weights seed 0",
-        "config": {"workload": f"GSA layer fwd B=1 L={L} d4096 h32/8x128 idx8x64 k2048[256,4096] bf16",
-                   "batch": 1, "seq_len": L,
+        "config": {"workload": prefill_workload_name(B, L, k_min, k_max),
+                   "batch": B, "seq_len": L,
                    "parallelism": f"query-sequence shards x{world}" +
-                                  (f" (zigzag, {ZIGZAG_FOLDS} folds)" if world > 1 else ""),
-                   "l2": "inputs larger than L2 (x 1 GiB, K/V 256 MiB each)"},
+                                  ((f" (zigzag, {ZIGZAG_FOLDS} folds)" if zigzag else " (contiguous)")
+                                   if world > 1 else ""),
+                   "l2": (f"inputs larger than L2 (x {x_mib:.0f} MiB, K/V {kv_mib:.0f} MiB each)"
+                          if x_mib > 126 else f"x {x_mib:.0f} MiB: L2 not flushed between steps")},
         "e2e": e2e, "roofline": roofline, "roofline_indexer": roofline_indexer,
         "gpu_launches": launches_per_step * args.steps,
         "stages_ms": stages, "clocks": clocks,
@@ -636,7 +702,7 @@ def run_train(args, world, rank):
     from gsa_b200 import GSAConfig, GatedSparseAttention, ops
 
     dev = torch.device("cuda", torch.cuda.current_device())
-    L = args.seq_len
+    L = args.seq_len or 131072
     cfg = GSAConfig(**WORKLOAD, max_position_embeddings=max(131072, L))
     torch.manual_seed(0)
     m = GatedSparseAttention(cfg).to(torch.bfloat16).to(dev).train()
@@ -717,7 +783,7 @@ def run_layer(args, world, rank):
     from gsa_b200 import GSAConfig, GSADecoderLayer, ops
 
     dev = torch.device("cuda", torch.cuda.current_device())
-    L = args.seq_len
+    L = args.seq_len or 131072
     cfg = GSAConfig(**WORKLOAD, max_position_embeddings=max(131072, L))
     torch.manual_seed(0)
     m = GSADecoderLayer(cfg, 0).eval().to(torch.bfloat16).to(dev)
@@ -767,14 +833,28 @@ def run_layer(args, world, rank):
 # ---------------------------------------------------------------------------------------------
 # CPU path of the reference algorithm (oracle restatement), sampled and extrapolated
 # ---------------------------------------------------------------------------------------------
-def cpu_reference_estimate(L: int, proj_rows: int, chunk_rows: int, n_chunks: int, seed: int = 0):
-    """Seconds for one full-layer CPU forward at sequence length L, estimated from samples.
+CPU_SAMPLE = dict(proj_rows=128, chunk_rows=16, n_chunks=4)
+_WEIGHTS = {}
 
-    Timed with the oracle's restatement of the reference's torch ops (bf16, torch.no_grad):
-      * projections + G2 + RoPE + G1 logits + o_proj on ``proj_rows`` rows, scaled by L/rows;
+
+def _oracle_weights(O, oc, seed, dt):
+    """The layer's weights from the oracle's restatement of the reference's init, built once per
+    process (outside every timed sample)."""
+    key = (seed, dt, oc.k_min, oc.k_max)
+    if key not in _WEIGHTS:
+        _WEIGHTS[key] = O.init_layer_weights(oc, seed, dtype=dt)
+    return _WEIGHTS[key]
+
+
+def cpu_reference_estimate(B: int, L: int, k_min: int, k_max: int, proj_rows: int, chunk_rows: int,
+                           n_chunks: int, seed: int = 0):
+    """Seconds for one layer forward over B sequences of L tokens on the host cores, estimated from
+    samples timed with the oracle's restatement of the reference's torch ops (bf16, torch.no_grad,
+    weights from the oracle's restatement of the reference's seeded init):
+      * projections + G2 + RoPE + G1 logits + o_proj on ``proj_rows`` rows, scaled by B*L/rows;
       * indexer + variance for ``n_chunks`` chunks of ``chunk_rows`` queries at evenly spaced
-        offsets, scaled by the causal (query, key) pair count;
-      * top-k + sparse attention for the same chunks, scaled by L / sampled rows.
+        offsets, scaled by the causal (query, key) pair count of the B sequences;
+      * top-k + sparse attention for the same chunks, scaled by B*L / sampled rows.
     Returns (seconds, description)."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import torch.nn.functional as F
@@ -782,65 +862,58 @@ def cpu_reference_estimate(L: int, proj_rows: int, chunk_rows: int, n_chunks: in
     import gsa_oracle as O
 
     torch.set_num_threads(len(os.sched_getaffinity(0)))
-    from gsa_b200 import GSAConfig, GatedSparseAttention
-
-    cfg = GSAConfig(**WORKLOAD)
-    torch.manual_seed(seed)
-    m = GatedSparseAttention(cfg).eval().to(torch.bfloat16)
-    W = {k: v for k, v in m.state_dict().items()}
-    oc = O.OracleConfig.from_config(cfg)
-    gen = torch.Generator().manual_seed(1)
+    oc = O.OracleConfig(**{**WORKLOAD, "k_min": k_min, "k_max": k_max}, d_head=128)
     dt = torch.bfloat16
-    H, Hk, D = cfg.n_heads, cfg.n_kv_heads, cfg.d_head
+    W = _oracle_weights(O, oc, seed, dt)
+    cos_t, sin_t = (t.to(dt) for t in O.rope_cache(oc.d_head, max(proj_rows, 16), oc.rope_base, oc.rope_scaling))
+    gen = torch.Generator().manual_seed(1)
+    H, Hk, D = oc.n_heads, oc.n_kv_heads, oc.d_head
     with torch.no_grad():
         # 1. dense projections and gates, per row
-        xs = torch.randn(1, proj_rows, cfg.d_model, generator=gen).to(dt)
+        xs = torch.randn(1, proj_rows, oc.d_model, generator=gen).to(dt)
         pos = torch.arange(proj_rows).unsqueeze(0)
         t0 = time.perf_counter()
-        q, k, v = O.project(W, oc, xs, pos, m.rotary_emb.cos_cached, m.rotary_emb.sin_cached)
+        q, k, v = O.project(W, oc, xs, pos, cos_t, sin_t)
         F.linear(xs, W["indexer.q_proj.weight"])
         F.linear(xs, W["indexer.k_proj.weight"])
         g = F.linear(xs, W["output_gate.gate_proj.weight"], W["output_gate.gate_proj.bias"])
         gated = q * O.gate_activation(g.view(1, proj_rows, H, D), "sigmoid")
         F.linear(gated.reshape(1, proj_rows, -1), W["o_proj.weight"])
-        t_proj = (time.perf_counter() - t0) * L / proj_rows
+        t_proj = (time.perf_counter() - t0) * B * L / proj_rows
         # 2./3. indexer, variance, top-k, sparse attention on sampled query chunks
-        kI = torch.randn(1, L, cfg.d_indexer, generator=gen).to(dt)
+        kI = torch.randn(1, L, oc.d_indexer, generator=gen).to(dt)
         K = torch.randn(1, L, Hk, D, generator=gen).to(dt)
         V = torch.randn(1, L, Hk, D, generator=gen).to(dt)
         t_idx = t_sel = 0.0
         pairs_sampled = 0
         rows_sampled = 0
-        k_eff = min(cfg.k_max, L)
+        k_eff = min(oc.k_max, L)
         for c in range(n_chunks):
-            t_pos = int((c + 0.5) * L / n_chunks)
+            t_pos = min(int((c + 0.5) * L / n_chunks), L - chunk_rows)
             n_keys = t_pos + chunk_rows
-            xq = torch.randn(1, chunk_rows, cfg.d_model, generator=gen).to(dt)
+            xq = torch.randn(1, chunk_rows, oc.d_model, generator=gen).to(dt)
             t1 = time.perf_counter()
-            q_idx = F.linear(xq, W["indexer.q_proj.weight"]).view(1, chunk_rows, cfg.n_indexer_heads, cfg.d_indexer)
+            q_idx = F.linear(xq, W["indexer.q_proj.weight"]).view(1, chunk_rows, oc.n_indexer_heads, oc.d_indexer)
             wts = torch.sigmoid(F.linear(xq, W["indexer.weight_proj.weight"], W["indexer.weight_proj.bias"]))
-            raw = torch.einsum("bqhd,bkd->bhqk", q_idx, kI[:, :n_keys]) * (1.0 / math.sqrt(cfg.d_indexer))
-            sc = (torch.sigmoid(raw + W["indexer.bias"].view(1, -1, 1, 1)) * wts.permute(0, 2, 1).unsqueeze(-1)).sum(1)
-            tt = torch.arange(chunk_rows).view(-1, 1) + t_pos
-            sc = sc.masked_fill((torch.arange(n_keys).view(1, -1) > tt).unsqueeze(0), float("-inf"))
+            sc = O.indexer_scores_from_proj(q_idx, kI[:, :n_keys], wts, W["indexer.bias"], "sigmoid", q_offset=t_pos)
             full = torch.full((1, chunk_rows, L), float("-inf"), dtype=sc.dtype)
             full[:, :, :n_keys] = sc
             var, valid = O.row_variance(full)
             t2 = time.perf_counter()
-            kv = O.adaptive_k(var, valid, var.mean(), cfg.k_base, cfg.k_min, cfg.k_max, 1.0)
+            kv = O.adaptive_k(var, valid, var.mean(), oc.k_base, oc.k_min, oc.k_max, 1.0)
             idx, msk = O.topk_select(full, k_eff, kv)
             qc = torch.randn(1, chunk_rows, H, D, generator=gen).to(dt)
-            O.sparse_attention(qc, K, V, idx, msk, cfg.n_heads // cfg.n_kv_heads, 1.0 / math.sqrt(D))
+            O.sparse_attention(qc, K, V, idx, msk, oc.n_heads // oc.n_kv_heads, 1.0 / math.sqrt(D))
             t3 = time.perf_counter()
             t_idx += t2 - t1
             t_sel += t3 - t2
             pairs_sampled += sum(t_pos + i + 1 for i in range(chunk_rows))
             rows_sampled += chunk_rows
-        total_pairs = L * (L + 1) / 2
-        est = t_proj + t_idx * total_pairs / pairs_sampled + t_sel * L / rows_sampled
-    desc = (f"sampled + extrapolated: projections/gates/o_proj on {proj_rows} rows x L/{proj_rows}; "
+        total_pairs = B * L * (L + 1) / 2
+        est = t_proj + t_idx * total_pairs / pairs_sampled + t_sel * B * L / rows_sampled
+    desc = (f"sampled + extrapolated: projections/gates/o_proj on {proj_rows} rows x {B}*L/{proj_rows}; "
             f"indexer+variance on {n_chunks} chunks of {chunk_rows} queries x causal pairs; "
-            f"top-k+sparse attention on the same chunks x L/{rows_sampled}")
+            f"top-k+sparse attention on the same chunks x {B}*L/{rows_sampled}; weights from the oracle's init")
     return est, desc
 
 
@@ -856,15 +929,12 @@ def cpu_decode_estimate(n_cached: int, n_sample: int = 4, seed: int = 0):
     import gsa_oracle as O
 
     torch.set_num_threads(len(os.sched_getaffinity(0)))
-    from gsa_b200 import GSAConfig, GatedSparseAttention
-
-    cfg = GSAConfig(**WORKLOAD, max_position_embeddings=n_cached + 8)
-    torch.manual_seed(seed)
-    m = GatedSparseAttention(cfg).eval().to(torch.bfloat16)
-    W = {k: v for k, v in m.state_dict().items()}
-    oc = O.OracleConfig.from_config(cfg)
-    gen = torch.Generator().manual_seed(2)
+    cfg = O.OracleConfig(**WORKLOAD, d_head=128, max_position_embeddings=n_cached + 8)
+    oc = cfg
     dt = torch.bfloat16
+    W = _oracle_weights(O, oc, seed, dt)
+    cos_t, sin_t = (t.to(dt) for t in O.rope_cache(oc.d_head, n_cached + 8, oc.rope_base, oc.rope_scaling))
+    gen = torch.Generator().manual_seed(2)
     H, Hk, D, HI, dI = cfg.n_heads, cfg.n_kv_heads, cfg.d_head, cfg.n_indexer_heads, cfg.d_indexer
     S, n = n_sample, n_cached + 1
     with torch.no_grad():
@@ -874,7 +944,7 @@ def cpu_decode_estimate(n_cached: int, n_sample: int = 4, seed: int = 0):
         x = torch.randn(DECODE_SEQS, 1, cfg.d_model, generator=gen).to(dt)
         pos = torch.full((DECODE_SEQS, 1), n_cached)
         t0 = time.perf_counter()
-        q, k, v = O.project(W, oc, x, pos, m.rotary_emb.cos_cached, m.rotary_emb.sin_cached)
+        q, k, v = O.project(W, oc, x, pos, cos_t, sin_t)
         q_idx = F.linear(x, W["indexer.q_proj.weight"]).view(DECODE_SEQS, 1, HI, dI)
         k_new = F.linear(x, W["indexer.k_proj.weight"])
         wts = torch.sigmoid(F.linear(x, W["indexer.weight_proj.weight"], W["indexer.weight_proj.bias"]))
@@ -917,22 +987,23 @@ def run_reference(args, world, rank):
                 "cpu_baseline": {"value": round(v, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
                                  "sample": desc},
                 "e2e": {"value": round(v, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    L = args.seq_len
+    B, L, k_min, k_max = prefill_shape(args)
     samples = []
     desc = ""
     for i in range(args.warmup + args.steps):
-        est, desc = cpu_reference_estimate(L, proj_rows=64, chunk_rows=8, n_chunks=2, seed=0)
+        est, desc = cpu_reference_estimate(B, L, k_min, k_max, seed=0, **CPU_SAMPLE)
         if i >= args.warmup:
             samples.append(est)
     sec = statistics.median(samples)
-    v = L / sec
+    v = B * L / sec
     cores = len(os.sched_getaffinity(0))
-    return {"metric": METRIC, "value": round(v, 3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+    return {"metric": METRIC if (args.workload == "prefill" and L == 131072) else PREFILL_METRIC,
+            "value": round(v, 3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 1), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic: x ~ N(0,1), default-init weights seed 0",
-            "config": {"workload": f"GSA layer fwd B=1 L={L} d4096 h32/8x128 idx8x64 k2048[256,4096] bf16",
-                       "batch": 1, "seq_len": L, "parallelism": "host CPU"},
+            "config": {"workload": prefill_workload_name(B, L, k_min, k_max),
+                       "batch": B, "seq_len": L, "parallelism": "host CPU"},
             "impl": "reference",
             "cpu_baseline": {"value": round(v, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
                              "sample": desc},
@@ -965,13 +1036,31 @@ def run_launch_list(args):
         ops.check_device_error()
         log(f"launch list: {args.launch_list} decode steps against {args.cached} cached tokens done")
         return
-    L = args.seq_len
-    cfg = GSAConfig(**WORKLOAD, max_position_embeddings=max(131072, L))
+    B, L, k_min, k_max = prefill_shape(args)
+    cfg = GSAConfig(**{**WORKLOAD, "k_min": k_min, "k_max": k_max}, max_position_embeddings=max(131072, L))
     torch.manual_seed(0)
     m = GatedSparseAttention(cfg).eval().to(torch.bfloat16).cuda()
     gen = torch.Generator().manual_seed(1)
-    x = torch.randn(1, L, cfg.d_model, generator=gen).to(torch.bfloat16).cuda()
+    x = torch.randn(B, L, cfg.d_model, generator=gen).to(torch.bfloat16).cuda()
     with torch.no_grad():
+        if args.sdpa_replay:
+            # one forward keeps the SDPA's inputs; the forward's other buffers are released, and the
+            # SDPA alone runs --sdpa-replay more times (a capture of the last launches holds only
+            # q, gate, K/V, the selection and the output on the device)
+            cap = {}
+            m._forward_impl(x, None, None, False, False, capture=cap)
+            keep = {k: cap[k] for k in ("dims", "q", "k", "v", "sel", "cnt", "gate")}
+            del cap, x
+            torch.cuda.synchronize()
+            torch.cuda.empty_cache()
+            for _ in range(args.sdpa_replay):
+                ops.sparse_sdpa(keep["dims"], keep["q"], keep["k"], keep["v"], keep["sel"], keep["cnt"],
+                                keep["gate"], m.scale)
+            torch.cuda.synchronize()
+            ops.check_device_error()
+            log(f"sdpa replay: {args.sdpa_replay} launches after one forward at B={B} L={L}; "
+                f"{torch.cuda.memory_allocated() / 2**30:.2f} GiB held")
+            return
         for _ in range(args.launch_list):
             m(x)
     torch.cuda.synchronize()
@@ -985,12 +1074,16 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--seq-len", type=int, default=131072)
+    ap.add_argument("--seq-len", type=int, default=None,
+                    help="tokens per sequence (prefill default: the workload's; train/layer: 131072)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--launch-list", type=int, default=0, metavar="N",
                     help="run N untimed forwards and exit (a short command for profilers)")
-    ap.add_argument("--workload", default="prefill", choices=["prefill", "decode", "train", "layer"],
-                    help="prefill: one 131072-token sequence; decode: 64 sequences x 1 token vs 65,536 cached; "
+    ap.add_argument("--sdpa-replay", type=int, default=0, metavar="N",
+                    help="with --launch-list: after one forward, run the sparse SDPA alone N times and exit")
+    ap.add_argument("--workload", default="prefill", choices=["prefill", "c2", "c3", "decode", "train", "layer"],
+                    help="prefill: one 131072-token sequence; c2: two 8192-token sequences; c3: one 32768-token "
+                         "sequence with k in [512, 4096]; decode: 64 sequences x 1 token vs 65,536 cached; "
                          "train: forward + backward of one --seq-len sequence; layer: a whole decoder layer")
     ap.add_argument("--cached", type=int, default=DECODE_CACHED, help="decode: cached tokens per sequence")
     args = ap.parse_args()
@@ -1027,9 +1120,13 @@ def main():
             return
         res = run_ours(args, world, rank)
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
-            est, desc = cpu_reference_estimate(args.seq_len, proj_rows=128, chunk_rows=16, n_chunks=2)
-            res["cpu_baseline"] = {"value": round(args.seq_len / est, 3), "unit": "tokens/s",
-                                   "cores": len(os.sched_getaffinity(0)), "kind": "port", "sample": desc}
+            # the reference arm's estimate, the median of three samples
+            B, L, k_min, k_max = prefill_shape(args)
+            ests = [cpu_reference_estimate(B, L, k_min, k_max, seed=0, **CPU_SAMPLE) for _ in range(3)]
+            est, desc = statistics.median(e for e, _ in ests), ests[0][1]
+            res["cpu_baseline"] = {"value": round(B * L / est, 3), "unit": "tokens/s",
+                                   "cores": len(os.sched_getaffinity(0)), "kind": "port",
+                                   "sample": desc + "; median of 3"}
         if rank == 0:
             emit(res)
     finally:

@@ -268,6 +268,7 @@ class OracleConfig:
     rope_base: float = 10000.0
     rope_scaling: dict | None = None
     max_position_embeddings: int = 131072
+    gate_bias_init: float = 0.5
 
     @classmethod
     def from_config(cls, cfg) -> "OracleConfig":
@@ -278,6 +279,43 @@ class OracleConfig:
         d = {f: getattr(cfg, f) for f in cls.__dataclass_fields__}
         d["gate_activation"] = "sigmoid"
         return cls(**d)
+
+
+def init_layer_weights(cfg: OracleConfig, seed: int, n_layers: int = 32, dtype=torch.float32) -> dict:
+    """The parameters ``torch.manual_seed(seed); GatedSparseAttention(config)`` creates, by name.
+
+    Restates the construction order of gated_sparse_attention.py:57-121 with torch's own
+    ``nn.Linear`` (whose default init draws from the global generator): q/k/v/o projections
+    (:57-61), the indexer's three projections and bias, initialised inside its constructor
+    (gated_indexer.py:65-86), the value gate (value_gate.py:65-75) and the output gate
+    (output_gate.py:68-84, per head; both biases at gate_bias_init, :81-99), then the layer's xavier gains for q/k/v (1/sqrt 2) and o
+    (1/sqrt(2 n_layers), :116-121).  ``n_layers`` is the config field (32 by default)."""
+    torch.manual_seed(seed)
+    H, Hk, D, d = cfg.n_heads, cfg.n_kv_heads, cfg.d_head, cfg.d_model
+    HI, dI = cfg.n_indexer_heads, cfg.d_indexer
+    lin = torch.nn.Linear
+    q, k, v, o = lin(d, H * D, bias=False), lin(d, Hk * D, bias=False), lin(d, Hk * D, bias=False), \
+        lin(H * D, d, bias=False)
+    iq, ik, iw = lin(d, HI * dI, bias=False), lin(d, dI, bias=False), lin(d, HI, bias=True)
+    ibias = torch.zeros(HI)
+    torch.nn.init.xavier_uniform_(iq.weight, gain=1.0)
+    torch.nn.init.xavier_uniform_(ik.weight, gain=1.0)
+    torch.nn.init.xavier_uniform_(iw.weight, gain=0.1)
+    torch.nn.init.zeros_(iw.bias)
+    W = {"indexer.q_proj.weight": iq.weight, "indexer.k_proj.weight": ik.weight,
+         "indexer.weight_proj.weight": iw.weight, "indexer.weight_proj.bias": iw.bias, "indexer.bias": ibias}
+    for name, use, width in (("value_gate", cfg.use_value_gate, Hk * D), ("output_gate", cfg.use_output_gate, H * D)):
+        if use:
+            g = lin(d, width, bias=True)
+            torch.nn.init.xavier_uniform_(g.weight, gain=0.1)
+            torch.nn.init.constant_(g.bias, cfg.gate_bias_init)
+            W[f"{name}.gate_proj.weight"], W[f"{name}.gate_proj.bias"] = g.weight, g.bias
+    for name, m in (("q_proj", q), ("k_proj", k), ("v_proj", v)):
+        torch.nn.init.xavier_uniform_(m.weight, gain=1.0 / math.sqrt(2))
+        W[f"{name}.weight"] = m.weight
+    torch.nn.init.xavier_uniform_(o.weight, gain=1.0 / math.sqrt(2 * n_layers))
+    W["o_proj.weight"] = o.weight
+    return {kk: vv.detach().to(dtype) for kk, vv in W.items()}
 
 
 def project(W: dict, cfg: OracleConfig, x: torch.Tensor, positions: torch.Tensor,

@@ -30,7 +30,7 @@ def test_reference_arm_prints_one_contract_line():
     assert r["impl"] == "reference" and r["n_gpus"] == 1 and r["steps"] == 1
     assert r["warmup"] >= 3                                  # at least three warm-up steps, whatever is asked
     assert r["value"] > 0 and r["unit"] == "tokens/s" and r["higher_is_better"] is True
-    assert r["config"]["seq_len"] == 2048
+    assert r["config"]["seq_len"] == 2048 and r["config"]["batch"] == 1
     cb = r["cpu_baseline"]
     assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["sample"] and cb["value"] == r["value"]
     e2e = r["e2e"]
@@ -41,3 +41,13 @@ def test_reference_arm_other_ranks_exit_quietly():
     p = _run({"RANK": "1", "WORLD_SIZE": "2"})
     assert p.returncode == 0, p.stderr[-2000:]
     assert p.stdout.strip() == ""
+
+
+def test_reference_arm_takes_the_batch_of_two_workload():
+    """The two-sequence workload (B=2): the arm's config and throughput count both sequences."""
+    p = _run(None, "--warmup", "0", "--workload", "c2")
+    assert p.returncode == 0, p.stderr[-2000:]
+    r = json.loads(p.stdout.strip())
+    assert r["config"]["batch"] == 2 and r["config"]["seq_len"] == 2048
+    assert "B=2 L=2048" in r["config"]["workload"] and "k2048[256,4096]" in r["config"]["workload"]
+    assert abs(r["value"] - 2 * 2048 / (r["ms_per_step"] / 1e3)) <= 1e-3 * r["value"] + 1e-3

@@ -48,6 +48,18 @@ def test_weights_and_inputs_regenerate(case):
     assert xs == json.loads(meta["x_checksum"])
 
 
+def test_oracle_weight_init_regenerates_the_reference_parameters(case):
+    """The oracle's own initialiser (no product module involved) gives the parameters whose
+    checksums the reference recorded."""
+    name, g, meta, cfg, m, x, res = case
+    W = O.init_layer_weights(O.OracleConfig.from_config(cfg), int(meta["weight_seed"]), cfg.n_layers, x.dtype)
+    assert set(W) == set(meta["param_checksums"])
+    for k, (s, ss, first) in meta["param_checksums"].items():
+        t = W[k].double()
+        assert abs(float(t.sum()) - s) <= 1e-9 * max(1.0, abs(s)), k
+        assert [float(v) for v in t.flatten()[:4]] == first, k
+
+
 def test_projections_rope_g2(case):
     name, g, meta, cfg, m, x, res = case
     rows = g["rows"].long()
