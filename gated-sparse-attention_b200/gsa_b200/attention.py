@@ -908,6 +908,7 @@ class GatedSparseAttention(nn.Module):
                            idx_scale=self.indexer.scale,
                            idx_segments=list(segs) if len(segs) > 1 else [(0, L, q_pos0)])
             capture.update(dims=dims, q=q, k=k_all, v=v_all, sel=sel, cnt=cnt, gate=g1, k_t=kt, attn=attn,
+                           var=var, var_total=total,
                            n_chunks=ops.last_chunk_count, candidate_path="survivors" if survivors else "exact")
 
         weights = None

@@ -103,6 +103,7 @@ def test_static_scratch_rejects_key_length_beyond_its_buffer(cuda_ok):
     lib = _lib.lib()
     dims = ops.make_dims(4096, 32, 8, 128, 8, 64)
     too_long = (64 << 20) // 4 + 1
-    st = lib.gsa_indexer_select_static(C.byref(dims), 1, 1, 1, too_long, 0, 1, None, 512, 0, None, 64, 0,
-                                       None, None, 0.125, None, 16, None, None, None, None, None)
+    p = C.c_void_p(256)  # stand-in pointers: the size check returns before any is used
+    st = lib.gsa_indexer_select_static(C.byref(dims), 1, 1, 1, too_long, 0, 1, p, 512, 0, p, 64, 0,
+                                       p, p, 0.125, p, 16, p, p, p, None, None)
     assert st == 3  # GSA_ERR_WORKSPACE
