@@ -362,6 +362,33 @@ int gsa_sparse_sdpa_backward(const gsa_dims* dims, int dtype, int64_t B, int64_t
   return launch_sdpa_backward(a, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int gsa_sparse_sdpa_probs(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int64_t Lkv, const void* q,
+                          const void* k, int64_t kv_ld, int64_t kv_bstride, const int32_t* idx, const uint8_t* mask,
+                          int64_t idx_ld, int64_t k_eff, const float* lse, float scale, void* probs,
+                          gsa_stream_t stream) {
+  if (!dims_ok(dims) || B < 0 || Lq < 0 || Lkv < 0 || k_eff < 0 || idx_ld < k_eff ||
+      (dtype != GSA_DTYPE_F32 && dtype != GSA_DTYPE_BF16))
+    return GSA_ERR_BAD_ARG;
+  if (B * Lq == 0 || k_eff == 0) return GSA_OK;
+  if (!q || !k || !idx || !lse || !probs || B * Lq > 65535) return GSA_ERR_BAD_ARG;
+  const int64_t row_elems = (int64_t)dims->n_kv_heads * dims->d_head;
+  if (kv_ld < row_elems || kv_bstride < Lkv * kv_ld) return GSA_ERR_BAD_ARG;
+  DeviceInfo dinfo, *di = &dinfo;
+  int st = device_info(di);
+  if (st) return st;
+  SdpaProbsArgs a{B, Lq, Lkv, dims->n_heads, dims->n_kv_heads, dims->d_head, q, k, kv_ld, kv_bstride,
+                  idx, mask, idx_ld, k_eff, lse, scale, probs, di->err};
+  return launch_sdpa_probs(a, dtype, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int gsa_selftest_bounded_wait(uint32_t wait_limit, gsa_stream_t stream) {
+  if (wait_limit == 0) return GSA_ERR_BAD_ARG;
+  DeviceInfo dinfo, *di = &dinfo;
+  int st = device_info(di);
+  if (st) return st;
+  return launch_wait_selftest(wait_limit, di->err, reinterpret_cast<cudaStream_t>(stream));
+}
+
 int gsa_add_rmsnorm(int dtype, int64_t T, int64_t d, const void* x, int64_t x_ld, const void* a, int64_t a_ld,
                     const void* weight, float eps, void* h_out, int64_t h_ld, void* y_out, int64_t y_ld,
                     gsa_stream_t stream) {

@@ -25,6 +25,16 @@ __device__ __forceinline__ void store_elem(void* p, int64_t i, float v, int dtyp
   else reinterpret_cast<float*>(p)[i] = v;
 }
 
+// Typed element conversions (templated kernels over float / __nv_bfloat16).
+__device__ __forceinline__ float to_float(float v) { return v; }
+__device__ __forceinline__ float to_float(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <typename T>
+__device__ __forceinline__ T from_float(float v);
+template <>
+__device__ __forceinline__ float from_float<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_float<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
 // Round a float to the activation dtype and back.  torch evaluates each bf16 elementwise op
 // in fp32 and rounds the result to bf16; calling this after every op reproduces that.
 __device__ __forceinline__ float rnd(float v, int dtype) {
@@ -108,12 +118,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Each try_wait suspends for a hardware-chosen interval, so the limit is generous in time.
 constexpr uint32_t kWaitLimit = 1u << 22;
 
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, int* err, uint32_t limit) {
+  for (uint32_t i = 0; i < limit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
   }
   set_error(err, GSA_ERR_TIMEOUT);
   return false;
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+  return mbar_wait_limit(bar, parity, err, kWaitLimit);
 }
 
 // 1-D bulk copy global -> shared, completing on an mbarrier (both addresses 16-byte aligned,

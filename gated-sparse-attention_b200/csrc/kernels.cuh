@@ -141,6 +141,25 @@ struct SdpaBwdArgs {
   int* err;
 };
 int launch_sdpa_backward(const SdpaBwdArgs& a, cudaStream_t stream);
+
+// Attention probabilities of kept candidates (analysis output): out [R, H, k_eff].
+struct SdpaProbsArgs {
+  int64_t B, Lq, Lkv;
+  int H, Hk, D;
+  const void* q;        // [R, H, D]
+  const void* k;        // key s of batch b at b * kv_bstride + s * kv_ld (elements)
+  int64_t kv_ld, kv_bstride;
+  const int32_t* idx;   // [R, idx_ld] candidate key positions
+  const uint8_t* mask;  // [R, idx_ld] 1 = kept, or NULL (all k_eff kept)
+  int64_t idx_ld;
+  int64_t k_eff;
+  const float* lse;     // [R, H]
+  float scale;
+  void* out;            // [R, H, k_eff]
+  int* err;
+};
+int launch_sdpa_probs(const SdpaProbsArgs& a, int dtype, cudaStream_t stream);
+int launch_wait_selftest(uint32_t limit, int* err, cudaStream_t stream);
 int launch_variance_adaptive_k(int64_t R, int64_t n_cols, int dtype, const gsa_topk_params& p,
                                const double* stats, const float* shift, float* var_out, double* total,
                                int32_t* k_out, cudaStream_t stream);

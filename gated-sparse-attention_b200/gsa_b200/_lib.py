@@ -91,6 +91,8 @@ SIGNATURES = {
                               I32, I32, P, P, P, P, I64, P, I64, P],
     "gsa_indexer_select_static": [P, INT, I64, I64, I64, I64, INT, P, I64, I64, P, I64, I64, P, P, F32,
                                   P, I32, P, P, P, P, P],
+    "gsa_sparse_sdpa_probs": [P, INT, I64, I64, I64, P, P, I64, I64, P, P, I64, I64, P, F32, P, P],
+    "gsa_selftest_bounded_wait": [C.c_uint32, P],
 }
 _RESTYPES = {"gsa_version": C.c_char_p, "gsa_workspace_size": C.c_int64,
              "gsa_survivors_workspace_size": C.c_int64, "gsa_sdpa_workspace_size": C.c_int64,

@@ -890,7 +890,11 @@ class GatedSparseAttention(nn.Module):
             kv_all = kv_finish()
             k_all, v_all = kv_all[:, :, 0], kv_all[:, :, 1]
             present = GSAKVCache(k_all, v_all, indexer_keys, kv_all) if use_cache else None
-        if train is None:
+        lse = None
+        if train is None and output_attentions:
+            # the gated output and each (row, head)'s log-sum-exp, from which the probabilities follow
+            attn, lse = ops.sparse_sdpa_lse_gated(dims, q, k_all, v_all, sel, cnt, g1, self.scale)
+        elif train is None:
             attn = ops.sparse_sdpa(dims, q, k_all, v_all, sel, cnt, g1, self.scale)
         else:
             # ungated output and softmax statistics kept for the backward; the gate applied as the
@@ -913,21 +917,24 @@ class GatedSparseAttention(nn.Module):
 
         weights = None
         if output_attentions:
-            weights = self._attention_weights(q, k_all, cand_idx.long().view(B, L, k_eff),
-                                              mask.bool().view(B, L, k_eff))
+            weights = self._attention_weights(dims, q, k_all, cand_idx, cand_score, cand_count, mask, lse)
         return out, present, weights
 
-    def _attention_weights(self, q, k, indices, mask):
-        """Softmax weights [B, L, H, k_eff] aligned with ``indices`` (analysis output, small
-        shapes only; gated_sparse_attention.py:268-285)."""
+    def _attention_weights(self, dims, q, k, cand_idx, cand_score, cand_count, mask, lse):
+        """Softmax weights [B, L, H, k_eff] (analysis output; gated_sparse_attention.py:268-285).
+
+        Like the reference's, position p of a row holds the weight of its p-th best candidate
+        (scores descending, adaptive_topk.py:177; ties lower column first) and the kept keys come
+        first; positions past k_t are 0.  The probabilities come from a kernel pass over the kept
+        keys with the SDPA's own log-sum-exp."""
         B, L, H, D = q.shape
-        k_eff = indices.shape[-1]
-        if B * L * H * k_eff * D > (1 << 28):
+        R, k_eff = cand_idx.shape
+        if R > 65535 or R * H * k_eff > (1 << 31):
             raise NotImplementedError("output_attentions is limited to small shapes")
-        kr = self._repeat_kv(k)
-        idx = indices.unsqueeze(-1).unsqueeze(-1).expand(B, L, k_eff, H, D)
-        kg = torch.gather(kr.unsqueeze(1).expand(B, L, kr.shape[1], H, D), 2, idx).permute(0, 1, 3, 2, 4)
-        s = torch.einsum("bqhd,bqhkd->bqhk", q.float(), kg.float()) * self.scale
-        m = mask.unsqueeze(2)
-        p = torch.softmax(s.masked_fill(~m, float("-inf")), dim=-1).masked_fill(~m, 0.0)
-        return p.to(q.dtype)
+        pos = torch.arange(k_eff, device=q.device).view(1, -1)
+        valid = pos < cand_count.view(-1, 1).long()
+        key = cand_score.masked_fill(~valid, float("-inf"))
+        order = torch.sort(key, dim=1, descending=True, stable=True).indices
+        idx = torch.gather(cand_idx, 1, order).masked_fill(~torch.gather(valid, 1, order), 0)
+        keep = torch.gather(mask, 1, order) & torch.gather(valid, 1, order).to(mask.dtype)
+        return ops.sparse_sdpa_probs(dims, q, k, idx, keep, lse, self.scale)

@@ -295,6 +295,54 @@ def sparse_sdpa_lse(dims: Dims, q, k, v, sel_idx, sel_count, scale: float):
     return out, lse
 
 
+def sparse_sdpa_probs(dims: Dims, q, k, idx, mask, lse, scale: float) -> torch.Tensor:
+    """Attention probabilities [B, Lq, H, k_eff] (dtype of q) of the candidates ``idx``
+    [B*Lq, k_eff] that ``mask`` (uint8, or None: all) keeps, from the per-(row, head) log-sum-exp
+    ``lse`` [B*Lq, H] of the SDPA over the same keys; 0 for candidates not kept."""
+    _cuda(q, k, idx, mask, lse)
+    B, Lq, H, D = q.shape
+    Lkv = k.shape[1]
+    q = q.contiguous()
+    k = _kv_rows(k)
+    idx = idx.to(torch.int32).contiguous()
+    mask = mask.to(torch.uint8).contiguous() if mask is not None else None
+    R, k_eff = idx.shape
+    out = torch.empty(R, H, k_eff, device=q.device, dtype=q.dtype)
+    _lib.call("gsa_sparse_sdpa_probs", C.byref(dims), dtype_code(q.dtype), B, Lq, Lkv, _p(q), _p(k), k.stride(1),
+              _kv_bstride(k), _p(idx), _p(mask), k_eff, k_eff, _p(lse.contiguous()), float(scale), _p(out), _stream())
+    _after("sparse_sdpa_probs")
+    return out.view(B, Lq, H, k_eff)
+
+
+def sparse_sdpa_lse_gated(dims: Dims, q, k, v, sel_idx, sel_count, gate, scale: float):
+    """sparse_sdpa with the G1 gate in its epilogue that also returns the log-sum-exp [B*Lq, H]."""
+    _cuda(q, k, v, sel_idx, sel_count, gate)
+    B, Lq = q.shape[0], q.shape[1]
+    Lkv = k.shape[1]
+    q = q.contiguous()
+    k = _kv_rows(k)
+    v = _kv_rows(v)
+    if k.stride(1) != v.stride(1) or _kv_bstride(k) != _kv_bstride(v):
+        k, v = k.contiguous(), v.contiguous()
+    gate = gate.contiguous() if gate is not None else None
+    out = torch.empty_like(q)
+    lse = torch.empty(B * Lq, dims.n_heads, device=q.device, dtype=torch.float32)
+    _lib.call("gsa_sparse_sdpa_lse", C.byref(dims), dtype_code(q.dtype), B, Lq, Lkv, _p(q), _p(k), _p(v),
+              k.stride(1), _kv_bstride(k), _p(sel_idx), sel_idx.stride(0), _p(sel_count), _p(gate), _p(out),
+              _p(lse), float(scale), _stream())
+    _after("sparse_sdpa_lse")
+    return out, lse
+
+
+def selftest_bounded_wait(wait_limit: int = 4096) -> int:
+    """Run the bounded-wait diagnostic kernel and return the device error code it left (expected:
+    GSA_ERR_TIMEOUT, 4); the error word is cleared by the read."""
+    _lib.call("gsa_selftest_bounded_wait", int(wait_limit), _stream())
+    code = C.c_int(0)
+    _lib.call("gsa_get_device_error", C.byref(code), _stream())
+    return code.value
+
+
 def sparse_sdpa_backward(dims: Dims, q, k, v, sel_idx, sel_count, o, d_o, lse, scale: float):
     """Gradients of the ungated sparse SDPA: (dq [B, Lq, H, D], dk, dv [B, Lkv, Hk, D]), fp32."""
     _cuda(q, k, v, sel_idx, sel_count, o, d_o, lse)

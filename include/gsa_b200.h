@@ -258,6 +258,27 @@ int gsa_sparse_sdpa_backward(const gsa_dims* dims, int dtype, int64_t B, int64_t
                              int64_t dkv_bstride, float scale, gsa_stream_t stream);
 
 /*
+ * Attention probabilities of the sparse SDPA, the analysis output of output_attentions
+ * (gated_sparse_attention.py:268-285): probs[r, h, j] = exp(scale * q[r, h] . k[idx[r, j]] - lse[r, h])
+ * for every candidate j that mask[r, j] keeps (mask NULL: all k_eff), 0 for the others.  lse is what
+ * gsa_sparse_sdpa_lse wrote for the same kept keys, so a row's probabilities of one head sum to 1.
+ *   q [B*Lq, H, D] dtype; k as in gsa_sparse_sdpa_strided; idx, mask [B*Lq, idx_ld] (int32, uint8);
+ *   probs [B*Lq, H, k_eff] dtype.  B*Lq <= 65535: an output of small shapes.
+ */
+int gsa_sparse_sdpa_probs(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int64_t Lkv,
+                          const void* q, const void* k, int64_t kv_ld, int64_t kv_bstride,
+                          const int32_t* idx, const uint8_t* mask, int64_t idx_ld, int64_t k_eff,
+                          const float* lse, float scale, void* probs, gsa_stream_t stream);
+
+/*
+ * Diagnostic of the failure path (no counterpart in the reference, whose only failure handling is
+ * a try/except around its Triton calls): one CTA waits, with the bounded mbarrier wait of the
+ * pipelined kernels, on a barrier nothing arrives on; after wait_limit polls it records
+ * GSA_ERR_TIMEOUT in the device error word and returns.  Read the code with gsa_get_device_error.
+ */
+int gsa_selftest_bounded_wait(uint32_t wait_limit, gsa_stream_t stream);
+
+/*
  * Decoder-layer elementwise ops around the attention (gsa/models/gsa_llama.py), each evaluated
  * as torch evaluates it for the dtype.  Rows of d (n) elements with row strides *_ld.
  *   gsa_add_rmsnorm: h = x + a (a nullable: no add; h_out then NULL) and

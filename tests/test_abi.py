@@ -182,6 +182,29 @@ def test_static_select_checks_arguments_before_writing_row_stats():
     assert list(stats) == [7.5] * 12, "row_stats was written by a call that failed its checks"
 
 
+def test_probability_and_diagnostic_entry_points_validate_before_any_launch():
+    """gsa_sparse_sdpa_probs and gsa_selftest_bounded_wait reject bad arguments on the host (CPU only)."""
+    import ctypes as C
+
+    from gsa_b200 import _lib, ops
+
+    lib = _lib.lib()
+    dims = ops.make_dims(512, 8, 2, 64, 4, 32)
+    p = C.c_void_p(256)  # a stand-in pointer: every case below returns before using it
+
+    def probs(B=1, Lq=4, k_eff=16, idx_ld=16, kv_ld=256, kv_bstride=100 * 256, q=p):
+        return lib.gsa_sparse_sdpa_probs(C.byref(dims), 1, B, Lq, 100, q, p, kv_ld, kv_bstride, p, None, idx_ld,
+                                         k_eff, p, 0.125, p, None)
+
+    assert probs(idx_ld=8) == 1               # candidate rows shorter than k_eff
+    assert probs(kv_ld=64) == 1               # key rows narrower than Hk * D
+    assert probs(kv_bstride=99 * 256) == 1    # batch stride below the keys
+    assert probs(q=None) == 1
+    assert probs(B=2, Lq=40000) == 1          # more rows than an analysis output takes
+    assert probs(Lq=0) == 0 and probs(k_eff=0) == 0
+    assert lib.gsa_selftest_bounded_wait(0, None) == 1   # a zero poll limit is refused, nothing launched
+
+
 def test_header_is_plain_c_and_a_c_program_links():
     """A C99 program includes gsa_b200.h (no CUDA or torch headers needed), links the library and
     calls the entry points that touch no GPU; the header also compiles as C++."""

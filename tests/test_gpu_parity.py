@@ -246,3 +246,85 @@ def test_layer_output(gcase):
     print(f"{name}: bf16 ours vs reference {err:.2e}; vs exact: ours {ours_vs_exact:.2e}, "
           f"reference {ref_vs_exact:.2e}")
     assert ours_vs_exact <= max(2e-2, ref_vs_exact)
+
+
+BF16_GOLDEN = ["tiny_bf16_b2_l192", "w4096_bf16_l384"]
+
+
+@pytest.mark.parametrize("name", BF16_GOLDEN)
+def test_bf16_selection_agreement_is_accounted_for(cuda_ok, name):
+    """bf16 end to end, row by row against the reference's own bf16 layer (golden fixture).
+
+    Our selection runs on fp32-accurate scores; the reference's on scores computed and rounded in
+    bf16 at every op (gated_indexer.py:126-145), and torch.topk breaks the resulting ties in an
+    unspecified order (adaptive_topk.py:177).  Every row whose kept set differs from the
+    reference's must be accounted for by that rounding:
+      * tie: the reference's own k_t-th and (k_t+1)-th scores are equal (its order is arbitrary);
+      * near cut: every key in the symmetric difference has an exact (fp32) score within the row's
+        reference rounding error (max |bf16 score - fp32 score| over the row) plus the bf16
+        indexer's tanh.approx tolerance of the cut band between the k_lo-th and (k_hi+1)-th exact
+        scores, where k_lo/k_hi are the smaller/larger of the two k_t -- which differ by at most one
+        bf16 step of k_adaptive (their variances round apart).
+    No row may be unaccounted for.  On the rows whose sets agree, the layer output is within 2e-2
+    (relative, Frobenius) of the reference's."""
+    import torch.nn.functional as F
+
+    g, meta = load_golden(name)
+    cfg, m, x = golden_inputs(meta)
+    m = m.to(DEV)
+    B, L, _ = x.shape
+    rows = g["rows"].long()
+    cap = {}
+    with torch.no_grad():
+        out, _, _ = m._forward_impl(x.to(DEV), None, None, False, False, capture=cap)
+    torch.cuda.synchronize()
+    from gsa_b200 import ops
+    ops.check_device_error()
+    sel, cnt = cap["sel"].cpu(), cap["cnt"].cpu()
+    k_ours = cap["k_t"].long().cpu().view(B, L)
+    k_ref = g["k_values"].long()
+    # exact scores from the bf16 projections (what both implementations score)
+    W = {k: v for k, v in m.state_dict().items()}
+    xc = x.cpu()
+    HI, dI = cfg.n_indexer_heads, cfg.d_indexer
+    qI = F.linear(xc, W["indexer.q_proj.weight"].cpu()).view(B, L, HI, dI).float()
+    kI = F.linear(xc, W["indexer.k_proj.weight"].cpu()).float()
+    w = torch.sigmoid(F.linear(xc, W["indexer.weight_proj.weight"].cpu(), W["indexer.weight_proj.bias"].cpu()).float())
+    exact = O.indexer_scores_from_proj(qI, kI, w, W["indexer.bias"].cpu().float(), "sigmoid", 0)
+    counts = {"agree": 0, "tie": 0, "near_cut": 0}
+    agree_rows = []
+    for b in range(B):
+        ref_s = g["scores"][b].float()                  # [R, L] the reference's bf16 scores
+        ties = set(O.boundary_tie_rows(ref_s, k_ref[b][rows]).tolist())
+        ref_sets = sets_from(g["indices"][b], g["mask"][b])
+        for i, r in enumerate(rows.tolist()):
+            n = int(cnt[b * L + r])
+            ours = np.sort(sel[b * L + r, :n].numpy().astype(np.int64))
+            if np.array_equal(ours, ref_sets[i]):
+                counts["agree"] += 1
+                agree_rows.append((b, i))
+                continue
+            if i in ties:
+                counts["tie"] += 1
+                continue
+            ex = exact[b, r]
+            fin = torch.isfinite(ex)
+            err = float((ref_s[i][fin] - ex[fin]).abs().max())
+            tol = err + 2e-3 * float(w[b, r].sum())
+            srt = torch.sort(ex[fin], descending=True).values
+            k_lo, k_hi = sorted((int(k_ours[b, r]), int(k_ref[b, r])))
+            assert k_hi - k_lo <= 16, (name, b, r, k_lo, k_hi)   # one bf16 step of k_adaptive at most
+            top = float(srt[k_lo - 1]) + tol
+            bottom = (float(srt[k_hi]) if k_hi < len(srt) else float(srt[-1])) - tol
+            diff = np.setxor1d(ours, ref_sets[i])
+            vals = ex[torch.from_numpy(diff)]
+            assert bool(((vals >= bottom) & (vals <= top)).all()), (name, b, r, diff, float(vals.min()),
+                                                                    float(vals.max()), bottom, top)
+            counts["near_cut"] += 1
+    print(f"{name}: rows {counts} of {B * len(rows)}")
+    assert counts["agree"] >= 0.5 * B * len(rows)
+    ours_rows = torch.stack([out[b, rows[i]].float().cpu() for b, i in agree_rows])
+    ref_rows = torch.stack([g["out"][b, i].float() for b, i in agree_rows])
+    err = rel_fro(ours_rows, ref_rows)
+    print(f"{name}: layer output on the {len(agree_rows)} agreeing rows: rel err {err:.2e}")
+    assert err < 2e-2
