@@ -173,6 +173,37 @@ class _GateScores:
         self.__dict__["_last_scores"] = None
 
 
+class _GateFn(torch.autograd.Function):
+    """out = x * act(logits) on the gate kernel.  The backward (the standalone gate modules under
+    autograd; value_gate.py:95-113, output_gate.py:111-126) is fp32 elementwise:
+    dx = dy * act(logits), dlogits = dy * x * act'(logits)."""
+
+    @staticmethod
+    def forward(ctx, x, logits, act, want_gate, holder):
+        out, gate = ops.apply_gate(x, logits, act, want_gate=want_gate)
+        holder.append(gate)
+        ctx.act = act
+        ctx.save_for_backward(x, logits)
+        return out
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, logits = ctx.saved_tensors
+        dyf = dy.float()
+        dx = (dyf * _act(logits, ctx.act)).to(x.dtype) if ctx.needs_input_grad[0] else None
+        dl = (dyf * x.float() * _act_grad(logits, ctx.act)).to(logits.dtype) if ctx.needs_input_grad[1] else None
+        return dx, dl, None, None, None
+
+
+def _gated(x: torch.Tensor, logits: torch.Tensor, act: str, want_gate: bool):
+    """(x * act(logits), act(logits) or None): differentiable when autograd needs it."""
+    if torch.is_grad_enabled() and (x.requires_grad or logits.requires_grad):
+        holder = []
+        out = _GateFn.apply(x, logits, act, want_gate, holder)
+        return out, holder[0]
+    return ops.apply_gate(x, logits, act, want_gate=want_gate)
+
+
 class ValueGate(_GateScores, nn.Module):
     """G2: v * act(h W^T + b) per KV-head element (value_gate.py:16-127)."""
 
@@ -195,9 +226,9 @@ class ValueGate(_GateScores, nn.Module):
         if self.activation not in _ACTS:
             raise ValueError(f"Unknown activation: {self.activation}")
         logits = self.gate_proj(hidden_states).view_as(v)
-        out, gate = ops.apply_gate(v, logits, self.activation, want_gate=not self.training)
+        out, gate = _gated(v, logits, self.activation, not self.training)
         if not self.training:
-            self.last_gate_scores = gate
+            self.last_gate_scores = gate.detach()
         return out
 
     def get_gate_statistics(self) -> dict:
@@ -230,9 +261,9 @@ class OutputGate(_GateScores, nn.Module):
         B, L, H, D = attn_output.shape
         logits = self.gate_proj(hidden_states)
         logits = logits.view(B, L, H, D) if self.per_head else logits.view(B, L, H, 1).expand(B, L, H, D)
-        out, gate = ops.apply_gate(attn_output, logits, self.activation, want_gate=not self.training)
+        out, gate = _gated(attn_output, logits, self.activation, not self.training)
         if not self.training:
-            self.last_gate_scores = gate if self.per_head else gate[..., :1]
+            self.last_gate_scores = (gate if self.per_head else gate[..., :1]).detach()
         return out
 
     def get_gate_statistics(self) -> dict:
@@ -242,6 +273,48 @@ class OutputGate(_GateScores, nn.Module):
 # ---------------------------------------------------------------------------------------------
 # Indexer and selector
 # ---------------------------------------------------------------------------------------------
+class _IndexerScoresFn(torch.autograd.Function):
+    """Indexer scores on the indexer kernel (gated_indexer.py:123-153).  The backward (the standalone
+    indexer module under autograd) recomputes the pre-activations z = scale q^I.k^I + b in fp32 and
+    returns, with dI the incoming gradient (zero at masked entries, as masked_fill makes it):
+      dz = dI * w_j * act'(z); dw_j = sum_s dI * act(z); dq^I = scale dz k^I; dk^I = scale sum_j dz q^I_j;
+      db_j = sum dz."""
+
+    @staticmethod
+    def forward(ctx, q_idx, k_idx, w, bias, dims, scale, causal, act):
+        scores = ops.indexer_scores(dims, q_idx, k_idx, w, bias, scale, q_pos0=0, causal=causal)
+        ctx.save_for_backward(q_idx, k_idx, w, bias)
+        ctx.meta = (dims.n_idx_heads, dims.d_idx, scale, causal, act)
+        return scores
+
+    @staticmethod
+    def backward(ctx, d_scores):
+        q_idx, k_idx, w, bias = ctx.saved_tensors
+        HI, dI, scale, causal, act = ctx.meta
+        B, Lq, _ = q_idx.shape
+        Lkv = k_idx.shape[1]
+        q = q_idx.float().reshape(B, Lq, HI, dI)
+        k = k_idx.float()
+        g = d_scores.float()
+        if causal:
+            fut = torch.ones(Lq, Lkv, dtype=torch.bool, device=g.device).triu(1)
+            g = g.masked_fill(fut, 0.0)
+        z = torch.einsum("bqhd,bkd->bhqk", q, k) * scale + bias.float().view(1, -1, 1, 1)
+        if act == "sigmoid":
+            a = torch.sigmoid(z)
+            da = a * (1 - a)
+        else:
+            a = F.relu(z)
+            da = (z > 0).float()
+        wt = w.float().permute(0, 2, 1).unsqueeze(-1)               # [B, HI, Lq, 1]
+        dz = g.unsqueeze(1) * wt * da                               # [B, HI, Lq, Lkv]
+        dw = (g.unsqueeze(1) * a).sum(-1).permute(0, 2, 1)          # [B, Lq, HI]
+        dq = (torch.einsum("bhqk,bkd->bqhd", dz, k) * scale).reshape(B, Lq, HI * dI)
+        dk = torch.einsum("bhqk,bqhd->bkd", dz, q) * scale
+        db = dz.sum(dim=(0, 2, 3))
+        return dq.to(q_idx.dtype), dk.to(k_idx.dtype), dw.to(w.dtype), db.to(bias.dtype), None, None, None, None
+
+
 class GatedLightningIndexer(nn.Module):
     """I[t,s] = sum_j sigmoid(h_t W_j^Iw) * act(q^I_{t,j} . k^I_s / sqrt(d_I) + b_j)
     (gated_indexer.py:16-175).  ``forward`` materialises [B, Lq, Lkv] scores for callers that
@@ -281,13 +354,16 @@ class GatedLightningIndexer(nn.Module):
             kv_hidden_states = hidden_states
         B, Lq, _ = hidden_states.shape
         Lkv = kv_hidden_states.shape[1]
-        with torch.no_grad():
-            q_idx = F.linear(hidden_states, self.q_proj.weight)
-            k_idx = F.linear(kv_hidden_states, self.k_proj.weight)
-            w = torch.sigmoid(self.weight_proj(hidden_states))
-            causal = self.use_causal_mask and Lq == Lkv
-            scores = ops.indexer_scores(self._dims(), q_idx, k_idx, w, self.bias, self.scale,
-                                        q_pos0=0, causal=causal)
+        causal = self.use_causal_mask and Lq == Lkv
+        q_idx = F.linear(hidden_states, self.q_proj.weight)
+        k_idx = F.linear(kv_hidden_states, self.k_proj.weight)
+        w = torch.sigmoid(self.weight_proj(hidden_states))
+        if torch.is_grad_enabled() and any(t.requires_grad for t in (q_idx, k_idx, w, self.bias)):
+            scores = _IndexerScoresFn.apply(q_idx, k_idx, w, self.bias, self._dims(), self.scale, causal,
+                                            self.activation)
+        else:
+            scores = ops.indexer_scores(self._dims(), q_idx, k_idx, w, self.bias, self.scale, q_pos0=0,
+                                        causal=causal)
         return scores.to(hidden_states.dtype)
 
     def get_indexer_statistics(self, hidden_states: torch.Tensor) -> dict:

@@ -140,8 +140,19 @@ class GSACausalLMOutput:
     attentions: Optional[Tuple[torch.Tensor, ...]] = None
 
 
+def _cache_length(past_key_values) -> int:
+    """Tokens already held by the first layer's cache (0 without caches)."""
+    if not past_key_values or past_key_values[0] is None:
+        return 0
+    return past_key_values[0][0].shape[1]
+
+
 class GSALlamaModel(nn.Module):
-    """Token embedding, decoder layers and the final norm (gsa_llama.py:134-242)."""
+    """Token embedding, decoder layers and the final norm (gsa_llama.py:134-242).
+
+    The layers' caches are the attention layers' in-place stores: a cache returned by one call is a
+    view of a buffer with headroom, and passing it back lets the next call append K, V and the
+    indexer keys in place (``allocate_caches`` sizes them up front)."""
 
     def __init__(self, config: GSAConfig):
         super().__init__()
@@ -157,41 +168,94 @@ class GSALlamaModel(nn.Module):
     def _init_weights(self):
         nn.init.normal_(self.embed_tokens.weight, std=self.config.initializer_range)
 
+    def allocate_caches(self, batch_size: int, capacity: int):
+        """Empty per-layer caches with room for ``capacity`` tokens of each sequence; pass them as
+        ``past_key_values`` (with ``use_cache=True``) and every call writes into them in place."""
+        return tuple(layer.self_attn.allocate_cache(batch_size, capacity) for layer in self.layers)
+
+    def _layer_call(self, layer, h, positions, attention_mask, cache, use_cache, output_attentions):
+        if self.gradient_checkpointing and self.training:
+            return torch.utils.checkpoint.checkpoint(layer, h, positions, attention_mask, cache, use_cache,
+                                                     output_attentions, use_reentrant=False)
+        return layer(h, positions=positions, attention_mask=attention_mask, past_key_value=cache,
+                     use_cache=use_cache, output_attentions=output_attentions)
+
     def forward(self, input_ids: torch.Tensor, positions: Optional[torch.Tensor] = None,
                 attention_mask: Optional[torch.Tensor] = None,
                 past_key_values: Optional[Tuple[Tuple[torch.Tensor, torch.Tensor], ...]] = None,
                 use_cache: bool = False, output_attentions: bool = False,
                 output_hidden_states: bool = False) -> GSAModelOutput:
-        batch_size, seq_len = input_ids.shape
-        hidden_states = self.embed_tokens(input_ids)
+        B, L = input_ids.shape
         if positions is None:
-            past_len = past_key_values[0][0].shape[1] if past_key_values else 0
-            positions = torch.arange(past_len, past_len + seq_len,
-                                     device=input_ids.device).unsqueeze(0).expand(batch_size, -1)
-        all_hidden_states = () if output_hidden_states else None
-        all_attentions = () if output_attentions else None
-        next_cache = () if use_cache else None
-        for i, layer in enumerate(self.layers):
-            if output_hidden_states:
-                all_hidden_states = all_hidden_states + (hidden_states,)
-            past_key_value = past_key_values[i] if past_key_values else None
-            if self.gradient_checkpointing and self.training:
-                hidden_states, present_key_value, attn_weights = torch.utils.checkpoint.checkpoint(
-                    layer, hidden_states, positions, attention_mask, past_key_value, use_cache, output_attentions,
-                    use_reentrant=False)
-            else:
-                hidden_states, present_key_value, attn_weights = layer(
-                    hidden_states, positions=positions, attention_mask=attention_mask,
-                    past_key_value=past_key_value, use_cache=use_cache, output_attentions=output_attentions)
-            if use_cache:
-                next_cache = next_cache + (present_key_value,)
-            if output_attentions:
-                all_attentions = all_attentions + (attn_weights,)
-        hidden_states = self.norm(hidden_states)
-        if output_hidden_states:
-            all_hidden_states = all_hidden_states + (hidden_states,)
-        return GSAModelOutput(last_hidden_state=hidden_states, past_key_values=next_cache,
-                              hidden_states=all_hidden_states, attentions=all_attentions)
+            start = _cache_length(past_key_values)
+            positions = (torch.arange(L, device=input_ids.device) + start).expand(B, L)
+        caches = list(past_key_values) if past_key_values else [None] * len(self.layers)
+        h = self.embed_tokens(input_ids)
+        seen, presents, weights = [], [], []
+        for layer, cache in zip(self.layers, caches):
+            seen.append(h)
+            h, present, attn = self._layer_call(layer, h, positions, attention_mask, cache, use_cache,
+                                                output_attentions)
+            presents.append(present)
+            weights.append(attn)
+        h = self.norm(h)
+        seen.append(h)
+        return GSAModelOutput(last_hidden_state=h,
+                              past_key_values=tuple(presents) if use_cache else None,
+                              hidden_states=tuple(seen) if output_hidden_states else None,
+                              attentions=tuple(weights) if output_attentions else None)
+
+
+def next_token_loss(logits: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
+    """Mean cross-entropy of token t+1 predicted at position t; labels of -100 do not count
+    (gsa_llama.py:323-336)."""
+    V = logits.shape[-1]
+    return F.cross_entropy(logits[:, :-1].reshape(-1, V), labels[:, 1:].reshape(-1), ignore_index=-100)
+
+
+def filter_logits(logits: torch.Tensor, temperature: float = 1.0, top_k: int = 0,
+                  top_p: float = 1.0) -> torch.Tensor:
+    """The sampling filter of generate (gsa_llama.py:388-410) as one function, on a copy of [B, V]
+    logits: divide by the temperature; keep the logits not below the k-th largest (ties at it kept);
+    then nucleus filtering -- in descending order (torch.sort), a token is dropped when the
+    probabilities of the tokens ahead of it already sum to more than top_p (so the most likely
+    token always stays).  Dropped logits become -inf."""
+    out = logits / temperature if temperature != 1.0 else logits.clone()
+    if top_k > 0:
+        kth = torch.topk(out, top_k, dim=-1).values[..., -1:]
+        out = out.masked_fill(out < kth, float("-inf"))
+    if top_p < 1.0:
+        srt, order = torch.sort(out, dim=-1, descending=True)
+        ahead = torch.cumsum(F.softmax(srt, dim=-1), dim=-1)
+        # probability mass strictly ahead of each sorted position (the inclusive sum, shifted by one)
+        ahead = torch.cat([torch.zeros_like(ahead[..., :1]), ahead[..., :-1]], dim=-1)
+        keep = torch.zeros_like(out, dtype=torch.bool).scatter(-1, order, ahead <= top_p)
+        out = out.masked_fill(~keep, float("-inf"))
+    return out
+
+
+def sample_tokens(logits: torch.Tensor, do_sample: bool) -> torch.Tensor:
+    """[B, 1] next tokens: a draw from softmax(logits) (torch.multinomial on the global generator), or
+    the argmax."""
+    if do_sample:
+        return torch.multinomial(F.softmax(logits, dim=-1), num_samples=1)
+    return torch.argmax(logits, dim=-1, keepdim=True)
+
+
+def decode_loop(step, input_ids: torch.Tensor, max_new_tokens: int, temperature: float, top_k: int,
+                top_p: float, do_sample: bool, eos_token_id: Optional[int]) -> torch.Tensor:
+    """The token loop of generate: ``step(tokens, first)`` returns the [B, V] logits of the last
+    position after feeding ``tokens`` (the whole prompt when ``first``, else the newest token)."""
+    tokens = [input_ids]
+    feed, first = input_ids, True
+    for _ in range(max_new_tokens):
+        logits = filter_logits(step(feed, first), temperature, top_k, top_p)
+        nxt = sample_tokens(logits, do_sample)
+        tokens.append(nxt)
+        feed, first = nxt, False
+        if eos_token_id is not None and bool((nxt == eos_token_id).all()):
+            break
+    return torch.cat(tokens, dim=-1)
 
 
 class GSALlamaForCausalLM(nn.Module):
@@ -215,81 +279,58 @@ class GSALlamaForCausalLM(nn.Module):
                 past_key_values: Optional[Tuple[Tuple[torch.Tensor, torch.Tensor], ...]] = None,
                 use_cache: bool = False, output_attentions: bool = False,
                 output_hidden_states: bool = False) -> GSACausalLMOutput:
-        outputs = self.model(input_ids=input_ids, positions=positions, attention_mask=attention_mask,
-                             past_key_values=past_key_values, use_cache=use_cache,
-                             output_attentions=output_attentions, output_hidden_states=output_hidden_states)
-        logits = self.lm_head(outputs.last_hidden_state)
-        loss = None
-        if labels is not None:
-            shift_logits = logits[..., :-1, :].contiguous()
-            shift_labels = labels[..., 1:].contiguous()
-            loss = F.cross_entropy(shift_logits.view(-1, self.config.vocab_size), shift_labels.view(-1),
-                                   ignore_index=-100)
-        return GSACausalLMOutput(loss=loss, logits=logits, past_key_values=outputs.past_key_values,
-                                 hidden_states=outputs.hidden_states, attentions=outputs.attentions)
+        base = self.model(input_ids=input_ids, positions=positions, attention_mask=attention_mask,
+                          past_key_values=past_key_values, use_cache=use_cache,
+                          output_attentions=output_attentions, output_hidden_states=output_hidden_states)
+        logits = self.lm_head(base.last_hidden_state)
+        return GSACausalLMOutput(loss=None if labels is None else next_token_loss(logits, labels), logits=logits,
+                                 past_key_values=base.past_key_values, hidden_states=base.hidden_states,
+                                 attentions=base.attentions)
 
     @torch.no_grad()
     def generate(self, input_ids: torch.Tensor, max_new_tokens: int = 100, temperature: float = 1.0,
                  top_p: float = 0.9, top_k: int = 50, do_sample: bool = True, pad_token_id: Optional[int] = None,
                  eos_token_id: Optional[int] = None) -> torch.Tensor:
-        """Autoregressive sampling (gsa_llama.py:332-430).  Each step after the first feeds the
-        last token against the layers' KV caches, which carry the indexer keys and grow in place."""
-        past_key_values = None
-        generated = input_ids
-        for _ in range(max_new_tokens):
-            curr_input = generated[:, -1:] if past_key_values is not None else generated
-            outputs = self.forward(input_ids=curr_input, past_key_values=past_key_values, use_cache=True)
-            past_key_values = outputs.past_key_values
-            logits = outputs.logits[:, -1, :]
-            if temperature != 1.0:
-                logits = logits / temperature
-            if top_k > 0:
-                indices_to_remove = logits < torch.topk(logits, top_k)[0][..., -1, None]
-                logits[indices_to_remove] = float("-inf")
-            if top_p < 1.0:
-                sorted_logits, sorted_indices = torch.sort(logits, descending=True)
-                cumulative_probs = torch.cumsum(F.softmax(sorted_logits, dim=-1), dim=-1)
-                sorted_indices_to_remove = cumulative_probs > top_p
-                sorted_indices_to_remove[..., 1:] = sorted_indices_to_remove[..., :-1].clone()
-                sorted_indices_to_remove[..., 0] = 0
-                indices_to_remove = sorted_indices_to_remove.scatter(1, sorted_indices, sorted_indices_to_remove)
-                logits[indices_to_remove] = float("-inf")
-            if do_sample:
-                next_token = torch.multinomial(F.softmax(logits, dim=-1), num_samples=1)
-            else:
-                next_token = torch.argmax(logits, dim=-1, keepdim=True)
-            generated = torch.cat([generated, next_token], dim=-1)
-            if eos_token_id is not None and (next_token == eos_token_id).all():
-                break
-        return generated
+        """Autoregressive decoding (gsa_llama.py:344-430), same arguments and sampling.  Every layer's
+        cache is allocated once for the prompt plus ``max_new_tokens``; the prompt and then each new
+        token are written into it in place, and each step scores the new token against every cached
+        indexer key."""
+        caches = [self.model.allocate_caches(input_ids.shape[0], input_ids.shape[1] + max_new_tokens)]
+
+        def step(tokens, first):
+            out = self.forward(input_ids=tokens, past_key_values=caches[0], use_cache=True)
+            caches[0] = out.past_key_values
+            return out.logits[:, -1, :]
+
+        return decode_loop(step, input_ids, max_new_tokens, temperature, top_k, top_p, do_sample, eos_token_id)
+
+    _WEIGHT_FILES = ("model.safetensors", "pytorch_model.bin")
 
     @classmethod
     def from_pretrained(cls, path: str) -> "GSALlamaForCausalLM":
-        """config.json + model.safetensors (or pytorch_model.bin), as the reference saves them."""
-        import json
+        """A model directory written by save_pretrained (or the reference's): config.json and
+        model.safetensors, else pytorch_model.bin (gsa_llama.py:432-458)."""
         from pathlib import Path
 
-        path = Path(path)
-        with open(path / "config.json", "r") as f:
-            config = GSAConfig.from_dict(json.load(f))
-        model = cls(config)
-        if (path / "model.safetensors").exists():
+        root = Path(path)
+        model = cls(GSAConfig.from_pretrained(str(root)))
+        found = [root / n for n in cls._WEIGHT_FILES if (root / n).exists()]
+        if not found:
+            raise FileNotFoundError(f"no {' or '.join(cls._WEIGHT_FILES)} in {root}")
+        if found[0].suffix == ".safetensors":
             from safetensors.torch import load_file
-            state_dict = load_file(path / "model.safetensors")
+            state = load_file(str(found[0]))
         else:
-            state_dict = torch.load(path / "pytorch_model.bin", map_location="cpu")
-        model.load_state_dict(state_dict)
+            state = torch.load(found[0], map_location="cpu")
+        model.load_state_dict(state)
         return model
 
     def save_pretrained(self, path: str):
-        from pathlib import Path
-
+        """config.json and model.safetensors into ``path`` (gsa_llama.py:460-469)."""
         from safetensors.torch import save_file
 
-        path = Path(path)
-        path.mkdir(parents=True, exist_ok=True)
         self.config.save_pretrained(path)
-        save_file(self.state_dict(), path / "model.safetensors")
+        save_file(self.state_dict(), f"{path}/model.safetensors")
 
 
 GSAForCausalLM = GSALlamaForCausalLM

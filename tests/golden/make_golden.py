@@ -16,7 +16,8 @@ Each fixture follows the reference forward step by step
 (``gsa/attention/gated_sparse_attention.py:139-232``) through the reference's own submodules,
 and checks that the step-by-step output equals ``module(x, positions)`` bit for bit.
 
-The model fixtures run the reference's GSALlamaForCausalLM (gsa/models/gsa_llama.py) the same way.
+The model fixtures run the reference's GSALlamaForCausalLM (gsa/models/gsa_llama.py) the same way; the
+sampling fixture runs its generate() with the model's forward replaced by seeded logits.
 
 Usage:  python tests/golden/make_golden.py [--reference PATH] [--only NAME]
 """
@@ -230,6 +231,56 @@ def make_model_fixture(name, spec, refs):
     print(f"{name}: {path.stat().st_size / 1024:.0f} KiB")
 
 
+# name -> (batch, vocab, prompt length, steps, [(temperature, top_k, top_p, do_sample, seed), ...])
+SAMPLING_FIXTURES = {
+    "sampling_b3_v96": (3, 96, 5, 12, [(1.0, 50, 0.9, True, 11), (0.7, 8, 0.8, True, 12), (1.3, 0, 0.5, True, 13),
+                                       (1.0, 20, 1.0, True, 14), (1.0, 50, 0.9, False, 15)]),
+}
+
+
+def make_sampling_fixture(name, spec, refs):
+    """The reference's GSALlamaForCausalLM.generate (gsa_llama.py:344-430) with its forward replaced
+    by a stub that returns seeded logits, one [B, 1, V] block per step: what is recorded is the
+    sampling alone -- temperature, top-k, top-p filtering and torch.multinomial / argmax -- for
+    several settings, each under torch.manual_seed(seed) before the call.  The logits are quantised
+    to quarters, so equal values (ties at the top-k and top-p cuts) occur."""
+    GSAConfig, _, _, GSALlamaForCausalLM = refs
+    B, V, P, steps, settings = spec
+    cfg = GSAConfig(d_model=64, n_heads=2, n_kv_heads=1, d_indexer=16, n_indexer_heads=2, k_base=8, k_min=4,
+                    k_max=16, n_layers=1, d_ffn=128, vocab_size=V, max_position_embeddings=64)
+    torch.manual_seed(WEIGHT_SEED)
+    model = GSALlamaForCausalLM(cfg).eval()
+    gen = torch.Generator().manual_seed(INPUT_SEED)
+    logits = (torch.randn(steps, B, 1, V, generator=gen) * 8).round() / 4
+    prompt = torch.randint(0, V, (B, P), generator=gen)
+    calls = []
+
+    class _Out:
+        def __init__(self, lg):
+            self.logits = lg
+            self.past_key_values = ("cache",)
+
+    def stub(input_ids=None, past_key_values=None, use_cache=False, **kw):
+        i = len(calls)
+        calls.append(int(input_ids.shape[1]))
+        return _Out(logits[i].clone())
+
+    model.forward = stub
+    t = {"logits": logits.contiguous(), "prompt": prompt.to(torch.int32)}
+    for j, (temp, top_k, top_p, do_sample, seed) in enumerate(settings):
+        calls.clear()
+        torch.manual_seed(seed)
+        out = model.generate(prompt, max_new_tokens=steps, temperature=temp, top_p=top_p, top_k=top_k,
+                             do_sample=do_sample)
+        assert calls == [P] + [1] * (steps - 1), calls
+        t[f"tokens{j}"] = out.to(torch.int32).contiguous()
+    meta = {"settings": json.dumps(settings), "batch": str(B), "vocab": str(V), "steps": str(steps),
+            "torch": torch.__version__}
+    path = HERE / f"{name}.safetensors"
+    save_file(t, str(path), metadata=meta)
+    print(f"{name}: {path.stat().st_size / 1024:.0f} KiB")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("GSA_REFERENCE", "/root/reference"))
@@ -245,6 +296,10 @@ def main():
         if args.only and name != args.only:
             continue
         make_model_fixture(name, spec, refs)
+    for name, spec in SAMPLING_FIXTURES.items():
+        if args.only and name != args.only:
+            continue
+        make_sampling_fixture(name, spec, refs)
 
 
 if __name__ == "__main__":
