@@ -1010,6 +1010,52 @@ def run_reference(args, world, rank):
             "e2e": {"value": round(v, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def run_selection_overlap(args):
+    """Key sharing between nearby rows' selections (one 1-GPU forward of the prefill workload): for
+    sampled row blocks across the sequence, |S_t & S_(t+j)| / |S_t| for j = 1..16, and the union of
+    the selections of 8 and 16 consecutive rows against the sum of their sizes.  Prints one JSON
+    line (a measurement, not a benchmark)."""
+    from gsa_b200 import GSAConfig, GatedSparseAttention
+
+    torch.cuda.set_device(0)
+    B, L, k_min, k_max = prefill_shape(args)
+    cfg = GSAConfig(**{**WORKLOAD, "k_min": k_min, "k_max": k_max}, max_position_embeddings=max(131072, L))
+    torch.manual_seed(0)
+    m = GatedSparseAttention(cfg).eval().to(torch.bfloat16).cuda()
+    x = torch.randn(B, L, cfg.d_model, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16).cuda()
+    cap = {}
+    with torch.no_grad():
+        m._forward_impl(x, None, None, False, False, capture=cap)
+    sel, cnt = cap["sel"], cap["cnt"].long()
+    del cap, x
+    torch.cuda.empty_cache()
+    starts = [int(f * L) // 16 * 16 for f in (0.125, 0.25, 0.375, 0.5, 0.625, 0.75, 0.875)]
+    starts = [t for t in starts if t + 32 <= L]
+    lag = {j: [] for j in range(1, 17)}
+    union8, union16 = [], []
+    for t0 in starts:
+        rows = torch.arange(t0, t0 + 32, device="cuda")
+        mask = torch.zeros(32, L, dtype=torch.bool, device="cuda")
+        for i, r in enumerate(rows.tolist()):
+            mask[i, sel[r, :cnt[r]].long()] = True
+        sizes = mask.sum(-1).double()
+        for j in range(1, 17):
+            inter = (mask[:16] & mask[j:16 + j]).sum(-1).double()
+            lag[j].append(float((inter / sizes[:16]).mean()))
+        for blk, out in ((8, union8), (16, union16)):
+            for b0 in range(0, 32, blk):
+                u = mask[b0:b0 + blk].any(0).sum().double()
+                out.append(float(u / sizes[b0:b0 + blk].sum()))
+    res = {"workload": prefill_workload_name(B, L, k_min, k_max), "row_blocks": starts,
+           "mean_k": float(cnt.double().mean()),
+           "shared_fraction_at_lag": {j: round(statistics.mean(v), 4) for j, v in lag.items()},
+           "union_over_sum_8_rows": round(statistics.mean(union8), 4),
+           "union_over_sum_16_rows": round(statistics.mean(union16), 4),
+           "note": "shared_fraction_at_lag[j] = mean |S_t & S_(t+j)| / |S_t| over 16 rows t of each block; "
+                   "union_over_sum = |S_t u ... u S_(t+n-1)| / sum |S_i| (1.0: no key shared)"}
+    emit(res)
+
+
 def run_launch_list(args):
     """N untimed forwards of the 1-GPU workload at --seq-len (or N decode steps against
     --cached tokens), for kernel profilers."""
@@ -1079,6 +1125,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--launch-list", type=int, default=0, metavar="N",
                     help="run N untimed forwards and exit (a short command for profilers)")
+    ap.add_argument("--selection-overlap", action="store_true",
+                    help="measure key sharing between nearby rows' selections (prefill workloads) and exit")
     ap.add_argument("--sdpa-replay", type=int, default=0, metavar="N",
                     help="with --launch-list: after one forward, run the sparse SDPA alone N times and exit")
     ap.add_argument("--workload", default="prefill", choices=["prefill", "c2", "c3", "decode", "train", "layer"],
@@ -1088,6 +1136,8 @@ def main():
     ap.add_argument("--cached", type=int, default=DECODE_CACHED, help="decode: cached tokens per sequence")
     args = ap.parse_args()
     quiet_stdout()
+    if args.selection_overlap:
+        return run_selection_overlap(args)
     if args.launch_list:
         return run_launch_list(args)
     args.warmup = max(args.warmup, 3)
