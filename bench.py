@@ -442,6 +442,25 @@ def run_ours(args, world, rank):
     for name, ev in marks:
         stages[name] = round(prev.elapsed_time(ev), 3)
         prev = ev
+    shard_balance = None
+    if world > 1:
+        # every rank's stage times (the step waits for the slowest) and the SDPA work per rank
+        import torch.distributed as dist
+
+        names = sorted(stages)
+        t = torch.tensor([stages[n] for n in names], device=dev, dtype=torch.float64)
+        t_max = t.clone()
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+        stages = {n: round(float(v), 3) for n, v in zip(names, t.tolist())}
+        stages_max = {n: round(float(v), 3) for n, v in zip(names, t_max.tolist())}
+        keys = torch.tensor([float(cap["cnt"].double().sum())], device=dev, dtype=torch.float64)
+        allk = [torch.zeros_like(keys) for _ in range(world)]
+        dist.all_gather(allk, keys)
+        allk = [float(v) for v in torch.cat(allk).tolist()]
+        shard_balance = {"stages_ms_max_over_ranks": stages_max,
+                         "sdpa_keys_busiest_over_mean": round(max(allk) / (sum(allk) / world), 4),
+                         "note": "stages_ms is rank 0's; kv = the blocking k^I all-gather and the start of the "
+                                 "asynchronous K/V all-gather; kv_gather_wait = the wait for K/V before the SDPA"}
     # our kernels per forward: the projection epilogue; per query chunk the indexer and the
     # candidate pass (survivor compaction + exact fallback, or the exact top-k); row variance
     # (2) and adaptive k; the final selection; the SDPA
@@ -487,6 +506,8 @@ def run_ours(args, world, rank):
         "gpu_launches": launches_per_step * args.steps,
         "stages_ms": stages, "clocks": clocks,
     }
+    if shard_balance is not None:
+        res["shards"] = shard_balance
     return res
 
 

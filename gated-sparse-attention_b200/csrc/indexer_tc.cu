@@ -149,78 +149,20 @@ __device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
   return d;
 }
 
-__device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-
-// tanh on the FMA pipe for two arguments at once (f32x2), so that part of a token's heads leaves the
-// MUFU pipe: an odd polynomial u * Q(u^2) fitted to tanh on [0, 4] as a near-minimax approximation
-// (Lawson's iteratively reweighted least squares on a dense grid), the argument clamped to [-4, 4].
-// Maximum error 9.2e-4 over the real line (6.7e-4 of it is the clamp: 1 - tanh(4)), next to
-// tanh.approx.f32's ~5e-4.
-constexpr int kPolyTerms = 9;
-__device__ __constant__ float kTanhPoly[kPolyTerms] = {
-    9.954115834e-01f, -3.090948458e-01f, 9.358453286e-02f, -2.046632490e-02f, 2.983608011e-03f,
-    -2.784788446e-04f, 1.587204025e-05f, -5.012048611e-07f, 6.704957846e-09f};
-
-#ifndef GSA_IDX_POLY_SCALAR
-#define GSA_IDX_POLY_SCALAR 0
-#endif
-__device__ __forceinline__ float tanh_poly1(float z) {
-  const float u = fminf(fmaxf(z, -4.0f), 4.0f);
-  const float v = u * u;
-  float q = 6.704957846e-09f;
-  q = fmaf(q, v, -5.012048611e-07f);
-  q = fmaf(q, v, 1.587204025e-05f);
-  q = fmaf(q, v, -2.784788446e-04f);
-  q = fmaf(q, v, 2.983608011e-03f);
-  q = fmaf(q, v, -2.046632490e-02f);
-  q = fmaf(q, v, 9.358453286e-02f);
-  q = fmaf(q, v, -3.090948458e-01f);
-  q = fmaf(q, v, 9.954115834e-01f);
-  return q * u;
-}
-
-__device__ __forceinline__ void tanh_poly2(float z0, float z1, float& t0, float& t1) {
-  if (GSA_IDX_POLY_SCALAR) {
-    t0 = tanh_poly1(z0);
-    t1 = tanh_poly1(z1);
-    return;
-  }
-  const float c = 4.0f;
-  const uint64_t u = pack2(fminf(fmaxf(z0, -c), c), fminf(fmaxf(z1, -c), c));
-  const uint64_t v = fmul2(u, u);
-  uint64_t q = pack2(kTanhPoly[kPolyTerms - 1], kTanhPoly[kPolyTerms - 1]);
-#pragma unroll
-  for (int i = kPolyTerms - 2; i >= 0; --i) q = ffma2(q, v, pack2(kTanhPoly[i], kTanhPoly[i]));
-  unpack2(fmul2(q, u), t0, t1);
-}
-
 // One (token, key) of the epilogue: y = sum_j (w_j / 2) tanh((scale * acc_j + b_j) / 2), two heads
 // per f32x2 FMA; the score c + y is stored and (y + c - shift) enters the row statistics.  FULL:
-// the tile is unmasked for every token, so no per-token check.  The last NPOLY heads (an even
-// number) take the FMA-pipe tanh, the others tanh.approx on the MUFU pipe.
-#ifndef GSA_IDX_POLY_HEADS
-#define GSA_IDX_POLY_HEADS 0
-#endif
-template <int HI, bool FULL, int NPOLY = GSA_IDX_POLY_HEADS>
+// the tile is unmasked for every token, so no per-token check.
+template <int HI, bool FULL>
 __device__ __forceinline__ void epi_token(const uint32_t* r, uint64_t hs2, const uint64_t* hb2, const float* w_t,
                                           float2 cd, bool ok, float* dst, float& s1, float& s2) {
-  static_assert(NPOLY % 2 == 0 && NPOLY <= HI, "polynomial heads come in pairs");
   float th[HI];
 #pragma unroll
   for (int j = 0; j < HI / 2; ++j) {
     const uint64_t z2 = ffma2(pack2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])), hs2, hb2[j]);
     float z0, z1;
     unpack2(z2, z0, z1);
-    if (2 * j >= HI - NPOLY) {
-      tanh_poly2(z0, z1, th[2 * j], th[2 * j + 1]);
-    } else {
-      th[2 * j] = tanh_fast(z0);
-      th[2 * j + 1] = tanh_fast(z1);
-    }
+    th[2 * j] = tanh_fast(z0);
+    th[2 * j + 1] = tanh_fast(z1);
   }
   const float4* w4 = reinterpret_cast<const float4*>(w_t);
   uint64_t y2 = pack2(0.f, 0.f);

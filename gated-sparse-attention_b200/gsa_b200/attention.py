@@ -964,6 +964,7 @@ class GatedSparseAttention(nn.Module):
         mark("adaptive_k_select")
         if kv_finish is not None:
             kv_all = kv_finish()
+            mark("kv_gather_wait")
             k_all, v_all = kv_all[:, :, 0], kv_all[:, :, 1]
             present = GSAKVCache(k_all, v_all, indexer_keys, kv_all) if use_cache else None
         lse = None
