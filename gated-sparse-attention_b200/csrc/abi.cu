@@ -146,6 +146,37 @@ int gsa_proj_epilogue_cache(const gsa_dims* dims, const gsa_proj_layout* layout,
   return launch_proj_epilogue(a, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int64_t gsa_proj_fused_rows(const gsa_dims* dims) {
+  if (!dims_ok(dims)) return 0;
+  return proj_gemm_columns(*dims);
+}
+
+int gsa_proj_fused(const gsa_dims* dims, int dtype, int64_t T, int64_t L, const void* x, int64_t x_ld,
+                   const void* wp, const float* bias, const int64_t* positions, int64_t pos0, const void* cos_tab,
+                   const void* sin_tab, int tab_dtype, int64_t tab_rows, void* q_out, void* k_out, void* v_out,
+                   int64_t kv_ld, int64_t kv_bstride, void* g1_out, void* qi_out, int64_t qi_ld, void* ki_out,
+                   int64_t ki_ld, int64_t ki_bstride, float* w_out, float* shift_out, gsa_stream_t stream) {
+  if (!dims_ok(dims) || T < 0 || L < 0 || (tab_dtype != GSA_DTYPE_F32 && tab_dtype != GSA_DTYPE_BF16))
+    return GSA_ERR_BAD_ARG;
+  if (dtype != GSA_DTYPE_BF16) return GSA_ERR_UNSUPPORTED;
+  if (T == 0) return GSA_OK;
+  if (!x || !wp || !bias || !cos_tab || !sin_tab || !q_out || !k_out || !v_out || !g1_out || !qi_out || !ki_out ||
+      !w_out || !shift_out || tab_rows <= 0 || x_ld < dims->d_model)
+    return GSA_ERR_BAD_ARG;
+  const int64_t seq = L > 0 ? L : T;
+  if (T % seq != 0 || kv_ld < (int64_t)dims->n_kv_heads * dims->d_head || qi_ld < (int64_t)dims->n_idx_heads * dims->d_idx ||
+      ki_ld < dims->d_idx || (T > seq && (kv_bstride < seq * kv_ld || ki_bstride < seq * ki_ld)))
+    return GSA_ERR_BAD_ARG;
+  DeviceInfo dinfo, *di = &dinfo;
+  int st = device_info(di);
+  if (st) return st;
+  ProjGemmArgs a{*dims, T, seq, x, x_ld, wp, bias, positions, pos0, cos_tab, sin_tab, tab_dtype, tab_rows,
+                 q_out, k_out, v_out, kv_ld, kv_bstride, g1_out, qi_out, qi_ld, ki_out, ki_ld, ki_bstride,
+                 w_out, shift_out, di->err};
+  if (!proj_gemm_eligible(a)) return GSA_ERR_UNSUPPORTED;
+  return launch_proj_gemm(a, di->num_sms, reinterpret_cast<cudaStream_t>(stream));
+}
+
 int gsa_indexer_scores(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int64_t Lkv, int64_t q_pos0,
                        int causal, int write_masked, const void* qI, int64_t qi_ld, int64_t qi_bstride,
                        const void* kI, int64_t ki_ld, int64_t ki_bstride, const float* w, const float* bias,

@@ -23,7 +23,8 @@ LIB = OUT_DIR / "libgsa_b200.so"
 OBJ_DIR = PKG_ROOT / "_build"
 
 SOURCES = ["abi.cu", "proj_epilogue.cu", "indexer_simt.cu", "indexer_tc.cu", "indexer_decode.cu", "topk.cu",
-           "sparse_sdpa.cu", "sparse_sdpa_bwd.cu", "select_static.cu", "decoder.cu", "sdpa_probs.cu", "selftest.cu"]
+           "sparse_sdpa.cu", "sparse_sdpa_bwd.cu", "select_static.cu", "decoder.cu", "sdpa_probs.cu", "selftest.cu",
+           "proj_gemm.cu"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -159,6 +159,38 @@ struct SdpaProbsArgs {
   int* err;
 };
 int launch_sdpa_probs(const SdpaProbsArgs& a, int dtype, cudaStream_t stream);
+
+// Fused projection GEMM + epilogue (bf16): see proj_gemm.cu for the weight row order.
+struct ProjGemmArgs {
+  gsa_dims d;
+  int64_t T;
+  int64_t L;                  // rows per sequence (K/V/k^I batch strides apply per sequence)
+  const void* x;              // [T, d_model]
+  int64_t x_ld;
+  const void* w;              // [proj_gemm_columns(d), d_model]
+  const float* bias;          // [proj_gemm_columns(d)]
+  const int64_t* positions;   // [T] or NULL
+  int64_t pos0;
+  const void* cos_tab;
+  const void* sin_tab;
+  int tab_dtype;
+  int64_t tab_rows;
+  void* q_out;
+  void* k_out;
+  void* v_out;
+  int64_t kv_ld, kv_bstride;
+  void* g1_out;
+  void* qi_out;
+  int64_t qi_ld;
+  void* ki_out;
+  int64_t ki_ld, ki_bstride;
+  float* w_out;
+  float* shift_out;
+  int* err;
+};
+bool proj_gemm_eligible(const ProjGemmArgs& a);
+int64_t proj_gemm_columns(const gsa_dims& d);
+int launch_proj_gemm(const ProjGemmArgs& a, int num_sms, cudaStream_t stream);
 int launch_wait_selftest(uint32_t limit, int* err, cudaStream_t stream);
 int launch_variance_adaptive_k(int64_t R, int64_t n_cols, int dtype, const gsa_topk_params& p,
                                const double* stats, const float* shift, float* var_out, double* total,

@@ -93,10 +93,13 @@ SIGNATURES = {
                                   P, I32, P, P, P, P, P],
     "gsa_sparse_sdpa_probs": [P, INT, I64, I64, I64, P, P, I64, I64, P, P, I64, I64, P, F32, P, P],
     "gsa_selftest_bounded_wait": [C.c_uint32, P],
+    "gsa_proj_fused_rows": [P],
+    "gsa_proj_fused": [P, INT, I64, I64, P, I64, P, P, P, I64, P, P, INT, I64, P, P, P, I64, I64, P, P, I64, P, I64,
+                       I64, P, P, P],
 }
 _RESTYPES = {"gsa_version": C.c_char_p, "gsa_workspace_size": C.c_int64,
              "gsa_survivors_workspace_size": C.c_int64, "gsa_sdpa_workspace_size": C.c_int64,
-             "gsa_decode_workspace_size": C.c_int64}
+             "gsa_decode_workspace_size": C.c_int64, "gsa_proj_fused_rows": C.c_int64}
 
 _lib = None
 _lock = threading.Lock()

@@ -147,6 +147,18 @@ def _gate_torch(logits: torch.Tensor, act: str) -> torch.Tensor:
     raise ValueError(f"Unknown activation: {act}")
 
 
+class _LazyLogits:
+    """A gate's logits h W^T + b, computed (torch GEMM) only if its scores are read: the fused
+    projection kernel never writes them."""
+
+    def __init__(self, x, weight, bias, shape):
+        self.x, self.weight, self.bias, self.shape = x, weight, bias, shape
+
+    def __call__(self) -> torch.Tensor:
+        with torch.no_grad():
+            return F.linear(self.x, self.weight, self.bias).view(self.shape)
+
+
 class _GateScores:
     """``last_gate_scores`` of a gate module (value_gate.py:109-110, output_gate.py:122-123).  The
     fused attention layer does not run the gate modules: it hands each gate its logits (a view of
@@ -160,6 +172,8 @@ class _GateScores:
         pending = self.__dict__.get("_pending_logits")
         if pending is not None:
             self.__dict__["_pending_logits"] = None
+            if isinstance(pending, _LazyLogits):
+                pending = pending()
             self.__dict__["_last_scores"] = _gate_torch(pending, self.activation).detach()
         return self.__dict__.get("_last_scores")
 
@@ -666,6 +680,10 @@ class GatedSparseAttention(nn.Module):
         # native call (gsa_decode_attend); False runs the same kernels one by one from Python
         self.native_step = True
         self._static = None
+        # bf16 prefill: one tensor-core GEMM with the projection epilogue fused (when the shapes allow
+        # it: both gates, d_head 64 or 128, ...); False runs cuBLAS and the separate epilogue kernel
+        self.fused_gemm = True
+        self._fused_tiles = None
 
     def allocate_cache(self, batch_size: int, capacity: int, dtype: Optional[torch.dtype] = None,
                        device=None) -> "GSAKVCache":
@@ -730,6 +748,43 @@ class GatedSparseAttention(nn.Module):
         layout = ProjLayout(*(offs.get(n, -1) for n in ("q", "k", "v", "g2", "g1", "qi", "ki", "wi")))
         self._fused = (key, W, bvec, layout)
         return W, bvec, layout
+
+    def fused_projection_tiles(self):
+        """(Wp [rows, d_model], bias [rows] fp32): the projection weights and biases in the row order of
+        the fused projection GEMM -- q, k, then v_h and g2_h head by head, g1, q^I, k^I, w, zero rows
+        to gsa_proj_fused_rows -- cached until a parameter changes."""
+        segs = self._segments()
+        key = tuple((n, w.data_ptr(), w._version, None if b is None else (b.data_ptr(), b._version))
+                    for n, w, b in segs)
+        if self._fused_tiles is not None and self._fused_tiles[0] == key:
+            return self._fused_tiles[1:]
+        by = {n: (w.detach(), None if b is None else b.detach()) for n, w, b in segs}
+        H, Hk, D = self.n_heads, self.n_kv_heads, self.d_head
+        ws, bs = [], []
+
+        def add(w, b):
+            ws.append(w)
+            bs.append(torch.zeros(w.shape[0], device=w.device, dtype=torch.float32) if b is None else b.float())
+
+        add(*by["q"])
+        add(*by["k"])
+        vw, g2w, g2b = by["v"][0], by["g2"][0], by["g2"][1]
+        for h in range(Hk):
+            add(vw[h * D:(h + 1) * D], None)
+            add(g2w[h * D:(h + 1) * D], g2b[h * D:(h + 1) * D])
+        add(*by["g1"])
+        add(*by["qi"])
+        add(*by["ki"])
+        add(*by["wi"])
+        rows = ops.proj_fused_rows(self._dims())
+        n = sum(w.shape[0] for w in ws)
+        if rows > n:
+            ws.append(torch.zeros(rows - n, self.d_model, device=ws[0].device, dtype=ws[0].dtype))
+            bs.append(torch.zeros(rows - n, device=ws[0].device, dtype=torch.float32))
+        Wp = torch.cat(ws, 0).contiguous()
+        bp = torch.cat(bs, 0).contiguous()
+        self._fused_tiles = (key, Wp, bp)
+        return Wp, bp
 
     def _dims(self):
         return ops.make_dims(self.d_model, self.n_heads, self.n_kv_heads, self.d_head,
@@ -846,17 +901,35 @@ class GatedSparseAttention(nn.Module):
                     store.ki[:, :past_len] = past_key_value.indexer_keys
                 store.filled = past_len
 
-        proj = torch.addmm(bvec, x.reshape(B * L, self.d_model), W.t())
-        if not self.training:
-            # the gates' analysis output (last_gate_scores), computed from these logits when read
-            if self.value_gate is not None:
-                self.value_gate._set_pending_logits(proj[:, layout.g2:layout.g2 + Hk * D].view(B, L, Hk, D))
-            if self.output_gate is not None:
-                self.output_gate._set_pending_logits(proj[:, layout.g1:layout.g1 + H * D].view(B, L, H, D))
         n_all = past_len + L
-        if (store is not None and self.native_step and self.selection_path == "auto" and mark_fn is None
-                and capture is None and not output_attentions
-                and B * L * ((n_all + 3) // 4 * 4) * 4 <= ops.SCORE_CHUNK_BYTES):
+        native = (store is not None and self.native_step and self.selection_path == "auto" and mark_fn is None
+                  and capture is None and not output_attentions
+                  and B * L * ((n_all + 3) // 4 * 4) * 4 <= ops.SCORE_CHUNK_BYTES)
+        if not positions_given and not native:
+            positions = torch.cat([torch.arange(p0, p0 + n, device=x.device) for _, n, p0 in segs])
+            positions = positions.unsqueeze(0).expand(B, -1)
+        fused = None
+        if not native and train is None and dt == torch.bfloat16 and self.fused_gemm:
+            # the projections and their epilogue in one tensor-core GEMM (no projection tensor)
+            Wp, bp = self.fused_projection_tiles()
+            fused = ops.proj_fused(dims, Wp, bp, x.reshape(B * L, self.d_model), B, L, positions,
+                                   self.rotary_emb.cos_cached, self.rotary_emb.sin_cached,
+                                   kv_out=store.kv[:, past_len:past_len + L] if store is not None else None,
+                                   ki_out=store.ki[:, past_len:past_len + L] if store is not None else None)
+        if fused is None:
+            proj = torch.addmm(bvec, x.reshape(B * L, self.d_model), W.t())
+        if not self.training:
+            # the gates' analysis output (last_gate_scores), computed from their logits when read
+            if fused is None:
+                if self.value_gate is not None:
+                    self.value_gate._set_pending_logits(proj[:, layout.g2:layout.g2 + Hk * D].view(B, L, Hk, D))
+                if self.output_gate is not None:
+                    self.output_gate._set_pending_logits(proj[:, layout.g1:layout.g1 + H * D].view(B, L, H, D))
+            else:
+                for gate, shape in ((self.value_gate, (B, L, Hk, D)), (self.output_gate, (B, L, H, D))):
+                    if gate is not None:
+                        gate._set_pending_logits(_LazyLogits(x, gate.gate_proj.weight, gate.gate_proj.bias, shape))
+        if native:
             # everything between the two GEMMs in one native call, scratch kept on the store
             dims, tp, idx_bias = self._step_constants()
             nbytes = ops.decode_workspace_bytes(dims, tp, dt, B, L, store.capacity)
@@ -871,21 +944,22 @@ class GatedSparseAttention(nn.Module):
                 store.filled = n_all
                 present = store.view(n_all)
             return out, present, None
-        if not positions_given:
-            positions = torch.cat([torch.arange(p0, p0 + n, device=x.device) for _, n, p0 in segs])
-            positions = positions.unsqueeze(0).expand(B, -1)
         mark("proj_gemm")
-        q, kv, g1, w, shift = ops.proj_epilogue(
-            dims, layout, proj, positions, self.rotary_emb.cos_cached, self.rotary_emb.sin_cached,
-            self.output_gate is not None, return_kv=True,
-            kv_out=store.kv[:, past_len:past_len + L] if store is not None else None,
-            ki_out=store.ki[:, past_len:past_len + L] if store is not None else None)
+        if fused is not None:
+            q, kv, g1, w, shift, qI, kI = fused
+            proj = None
+        else:
+            q, kv, g1, w, shift = ops.proj_epilogue(
+                dims, layout, proj, positions, self.rotary_emb.cos_cached, self.rotary_emb.sin_cached,
+                self.output_gate is not None, return_kv=True,
+                kv_out=store.kv[:, past_len:past_len + L] if store is not None else None,
+                ki_out=store.ki[:, past_len:past_len + L] if store is not None else None)
+            proj3 = proj.view(B, L, proj.shape[1])
+            qI = proj3[..., layout.qi:layout.qi + HI * dI]
+            kI = proj3[..., layout.ki:layout.ki + dI]
         mark("proj_epilogue")
         q = q.view(B, L, H, D)
         kv = kv.view(B, L, 2, Hk, D)  # k and v interleaved per token
-        proj3 = proj.view(B, L, proj.shape[1])
-        qI = proj3[..., layout.qi:layout.qi + HI * dI]
-        kI = proj3[..., layout.ki:layout.ki + dI]
 
         indexer_keys = None
         kv_finish = None

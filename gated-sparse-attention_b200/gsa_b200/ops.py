@@ -113,6 +113,46 @@ def proj_epilogue(dims: Dims, layout: ProjLayout, proj: torch.Tensor, positions:
     return q, k, v, g1, w, shift
 
 
+def proj_fused_rows(dims: Dims) -> int:
+    return int(_lib.lib().gsa_proj_fused_rows(C.byref(dims)))
+
+
+def proj_fused(dims: Dims, wp: torch.Tensor, bias: torch.Tensor, x2d: torch.Tensor, B: int, L: int,
+               positions: torch.Tensor, cos_tab: torch.Tensor, sin_tab: torch.Tensor,
+               kv_out: torch.Tensor | None = None, ki_out: torch.Tensor | None = None):
+    """The fused projection GEMM (gsa_proj_fused) on x2d [B*L, d_model] bf16: (q [T, H, D], kv
+    [B, L, 2, Hk, D] (or ``kv_out``, a KV-cache view), g1 [T, H, D], w [T, H_I] fp32, shift [T] fp32,
+    qI [B, L, H_I*d_I], kI [B, L, d_I] (or ``ki_out``)).  None when the kernel does not take these
+    shapes (the caller then runs the GEMM and gsa_proj_epilogue)."""
+    _cuda(wp, bias, x2d, positions, cos_tab, sin_tab, kv_out, ki_out)
+    T = x2d.shape[0]
+    H, Hk, D, HI, dI = dims.n_heads, dims.n_kv_heads, dims.d_head, dims.n_idx_heads, dims.d_idx
+    dev, dt = x2d.device, x2d.dtype
+    if dt != torch.bfloat16 or x2d.stride(1) != 1 or wp.dtype != dt or not wp.is_contiguous():
+        return None
+    q = torch.empty(T, H, D, device=dev, dtype=dt)
+    g1 = torch.empty(T, H, D, device=dev, dtype=dt)
+    w = torch.empty(T, HI, device=dev, dtype=torch.float32)
+    shift = torch.empty(T, device=dev, dtype=torch.float32)
+    qI = torch.empty(B, L, HI * dI, device=dev, dtype=dt)
+    kv = kv_out if kv_out is not None else torch.empty(B, L, 2, Hk, D, device=dev, dtype=dt)
+    kI = ki_out if ki_out is not None else torch.empty(B, L, dI, device=dev, dtype=dt)
+    k, v = kv[:, :, 0], kv[:, :, 1]
+    pos = positions.reshape(-1).to(torch.int64).contiguous()
+    cos_tab, sin_tab = cos_tab.contiguous(), sin_tab.contiguous()
+    st = _lib.lib().gsa_proj_fused(C.byref(dims), dtype_code(dt), T, L, _p(x2d), x2d.stride(0), _p(wp),
+                                   _p(bias.float().contiguous()), _p(pos), 0, _p(cos_tab), _p(sin_tab),
+                                   dtype_code(cos_tab.dtype), cos_tab.shape[0], _p(q), _p(k), _p(v), kv.stride(1),
+                                   kv.stride(0), _p(g1), _p(qI), qI.stride(1), _p(kI), kI.stride(1), kI.stride(0),
+                                   _p(w), _p(shift), _stream())
+    if st == 2:  # GSA_ERR_UNSUPPORTED
+        return None
+    if st != 0:
+        raise _lib.GSAError("gsa_proj_fused", st)
+    _after("proj_fused")
+    return q, kv, g1, w, shift, qI, kI
+
+
 def indexer_scores(dims: Dims, qI: torch.Tensor, kI: torch.Tensor, w: torch.Tensor,
                    bias: torch.Tensor, scale: float, q_pos0: int = 0, causal: bool = True,
                    shift=None, row_stats=None) -> torch.Tensor:

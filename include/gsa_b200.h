@@ -94,6 +94,31 @@ int gsa_proj_epilogue(const gsa_dims* dims, const gsa_proj_layout* layout, int d
                       float* w_out, float* shift_out, gsa_stream_t stream);
 
 /*
+ * The layer's projections and their epilogue in one tensor-core GEMM (bf16): replaces the GEMM
+ * proj = x . Wcat^T + b followed by gsa_proj_epilogue (gated_sparse_attention.py:175-186,
+ * value_gate.py:95-113, output_gate.py:101-117, gated_indexer.py:114-121, rope.py:151-185), with
+ * the epilogue applied to the accumulator tile in registers so that no projection tensor exists.
+ *   x     [T, d_model] bf16, rows of stride x_ld
+ *   wp    [gsa_proj_fused_rows(dims), d_model] bf16: the projection weights with rows in this order
+ *         (D = d_head): q (H*D), k (Hk*D), then for each KV head h: v_h (D) followed by g2_h (D),
+ *         g1 (H*D), q^I (H_I*d_I), k^I (d_I), w (H_I), zero rows up to the returned count
+ *   bias  [gsa_proj_fused_rows(dims)] fp32 in the same order (0 for the bias-free projections)
+ *   positions [T] int64 or NULL (row t = b*L + i at position pos0 + i)
+ *   outputs as gsa_proj_epilogue_cache (L rows per sequence; K/V/k^I at the batch strides) plus
+ *   qi_out [T, qi_ld] bf16 (the indexer queries) and ki_out (the indexer keys, required).
+ * Supported: d_head 64 or 128 with H*D, Hk*D multiples of 256, d_I and H_I*d_I multiples of 32,
+ * H_I <= 32, d_model a multiple of 64, both gates present (per-head G1), 16-byte aligned rows;
+ * otherwise GSA_ERR_UNSUPPORTED (use the GEMM + gsa_proj_epilogue pair).
+ */
+int64_t gsa_proj_fused_rows(const gsa_dims* dims);
+int gsa_proj_fused(const gsa_dims* dims, int dtype, int64_t T, int64_t L, const void* x, int64_t x_ld,
+                   const void* wp, const float* bias, const int64_t* positions, int64_t pos0,
+                   const void* cos_tab, const void* sin_tab, int tab_dtype, int64_t tab_rows,
+                   void* q_out, void* k_out, void* v_out, int64_t kv_ld, int64_t kv_bstride,
+                   void* g1_out, void* qi_out, int64_t qi_ld, void* ki_out, int64_t ki_ld,
+                   int64_t ki_bstride, float* w_out, float* shift_out, gsa_stream_t stream);
+
+/*
  * gsa_proj_epilogue writing K, V and the indexer keys k^I straight into a KV cache that holds
  * room for more tokens than it has (the append-in-place cache of GatedSparseAttention).  The
  * T = B * L rows of ``proj`` are L new tokens of each of B sequences; token t of sequence b goes to
