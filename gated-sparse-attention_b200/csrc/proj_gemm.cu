@@ -17,10 +17,11 @@
 //   [q (H*D)] [k (Hk*D)] [v_0 g2_0 v_1 g2_1 ... (2*Hk*D)] [g1 (H*D)] [q^I (H_I*d_I)] [k^I (d_I)] [w (H_I)] [0 pad]
 // padded to a multiple of 256 rows; bias likewise (fp32; 0 where a projection has none).
 //
-// Roles (192 threads, one CTA per SM, persistent over (row block, column tile) work items):
+// Roles (320 threads, one CTA per SM, persistent over (row block, column tile) work items):
 // warp 0 = TMA producer (x tile 128 x 64 and Wp tile 256 x 64 per stage, 128-byte swizzle),
 // warp 1 = TMEM allocator + MMA issuer (one lane; M = 128, N = 256, K = 16 per instruction),
-// warps 2-5 = epilogue, one per TMEM lane quarter: a thread owns one token row of the tile.
+// warps 2-9 = epilogue, two per TMEM lane quarter (each takes half of the tile's columns): a thread
+// owns one token row of the tile.
 // The 512 TMEM columns hold two accumulators, so a tile's epilogue overlaps the next tile's MMAs.
 // Every wait is bounded; on a timeout the kernel records GSA_ERR_TIMEOUT and returns.
 #include "kernels.cuh"
@@ -35,7 +36,13 @@ constexpr int kBM = 128;   // token rows per tile (TMEM lanes)
 constexpr int kBN = 256;   // output columns per tile (fp32 TMEM columns per accumulator)
 constexpr int kBK = 64;    // K per stage: one 128-byte swizzle atom of bf16
 constexpr int kStages = 4;
-constexpr int kEpiWarps = 4;
+#ifndef PG_EPI_WARPS
+#define PG_EPI_WARPS 16
+#endif
+constexpr int kEpiWarps = PG_EPI_WARPS;  // kSplit per TMEM lane quarter, each taking 1/kSplit of the columns
+constexpr int kSplit = kEpiWarps / 4;
+constexpr int kCols = kBN / kSplit;      // columns of a tile per epilogue warp
+constexpr int kPairs = kBN / 2 / kSplit; // RoPE pairs (or v / g2 pairs) of a tile per epilogue warp
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kATile = kBM * kBK * 2;  // 16 KiB
 constexpr int kBTile = kBN * kBK * 2;  // 32 KiB
@@ -71,63 +78,97 @@ struct Params {
   int* err;
 };
 
-// 32 fp32 accumulator columns of this thread's row as the bf16-rounded projection values.
-__device__ __forceinline__ void acc_to_bf16(const uint32_t (&r)[32], const float* bias, int col, float (&x)[32]) {
+// Eight fp32 accumulator columns of this thread's row as the bf16-rounded projection values
+// p = bf16(acc + bias) (bias NULL: none).
+__device__ __forceinline__ void acc8(const uint32_t* r, const float* bias, float (&x)[8]) {
+  float b[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (bias) {  // 32-byte aligned: two vector loads
+    const float4 b0 = reinterpret_cast<const float4*>(bias)[0], b1 = reinterpret_cast<const float4*>(bias)[1];
+    b[0] = b0.x; b[1] = b0.y; b[2] = b0.z; b[3] = b0.w;
+    b[4] = b1.x; b[5] = b1.y; b[6] = b1.z; b[7] = b1.w;
+  }
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
+  for (int i = 0; i < 8; ++i) {
     float v = __uint_as_float(r[i]);
-    if (bias) v = fadd(v, bias[col + i]);
+    if (bias) v = fadd(v, b[i]);
     x[i] = __bfloat162float(__float2bfloat16_rn(v));
   }
 }
 
-__device__ __forceinline__ void store32(__nv_bfloat16* dst, const float (&v)[32]) {
+// Eight values rounded to bf16 into one 16-byte store.
+__device__ __forceinline__ void store8(__nv_bfloat16* dst, const float (&v)[8]) {
+  uint32_t w[4];
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    uint32_t w[4];
+  for (int k = 0; k < 4; ++k) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * k], v[2 * k + 1]);
+    w[k] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// Eight RoPE table entries (16-byte aligned) as fp32.
+__device__ __forceinline__ void tab8(const __nv_bfloat16* p, float (&v)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const __nv_bfloat162 h = __floats2bfloat162_rn(v[8 * c + 2 * k], v[8 * c + 2 * k + 1]);
-      w[k] = *reinterpret_cast<const uint32_t*>(&h);
-    }
-    reinterpret_cast<uint4*>(dst)[c] = make_uint4(w[0], w[1], w[2], w[3]);
+  for (int k = 0; k < 4; ++k) {
+    v[2 * k] = __uint_as_float(w[k] << 16);
+    v[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
   }
 }
-
-template <typename TabT>
-__device__ __forceinline__ float tab(const TabT* p, int i) {
-  if constexpr (sizeof(TabT) == 2) return __bfloat162float(p[i]);
-  else return p[i];
+__device__ __forceinline__ void tab8(const float* p, float (&v)[8]) {
+  const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 
-// RoPE of one head (D columns starting at TMEM column c0): rotate-half with the row's cos / sin.
+// RoPE of 32 element pairs (i, i + D/2) of one head, i = i0 .. i0+31: TMEM columns c1 (first half)
+// and c2 (second half) of this thread's row; rotate-half with the row's cos / sin.
 template <typename TabT>
-__device__ __forceinline__ void rope_head(uint32_t taddr, int c0, int D, const TabT* cr, const TabT* sr,
-                                          __nv_bfloat16* dst, bool ok) {
+__device__ __forceinline__ void rope32(uint32_t taddr, int c1, int c2, int i0, int half, const TabT* cr,
+                                       const TabT* sr, __nv_bfloat16* dst, bool ok) {
   constexpr int dt = GSA_DTYPE_BF16;
-  const int half = D / 2;
-  for (int i0 = 0; i0 < half; i0 += 32) {
-    uint32_t r1[32], r2[32];
-    tmem_ld32(taddr + c0 + i0, r1);
-    tmem_ld32(taddr + c0 + half + i0, r2);
-    tmem_wait_ld(r1);
-    tmem_wait_ld(r2);
-    float x1[32], x2[32], o1[32], o2[32];
-    acc_to_bf16(r1, nullptr, 0, x1);
-    acc_to_bf16(r2, nullptr, 0, x2);
+  uint32_t r1[32], r2[32];
+  tmem_ld32(taddr + c1, r1);
+  tmem_ld32(taddr + c2, r2);
+  tmem_wait_ld(r1);
+  tmem_wait_ld(r2);
 #pragma unroll
-    for (int e = 0; e < 32; ++e) {
-      const float c1 = tab(cr, i0 + e), s1 = tab(sr, i0 + e);
-      const float c2 = tab(cr, half + i0 + e), s2 = tab(sr, half + i0 + e);
+  for (int g = 0; g < 4; ++g) {
+    float x1[8], x2[8], cs1[8], sn1[8], cs2[8], sn2[8], o1[8], o2[8];
+    acc8(r1 + 8 * g, nullptr, x1);
+    acc8(r2 + 8 * g, nullptr, x2);
+    tab8(cr + i0 + 8 * g, cs1);
+    tab8(sr + i0 + 8 * g, sn1);
+    tab8(cr + half + i0 + 8 * g, cs2);
+    tab8(sr + half + i0 + 8 * g, sn2);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
       // (x * cos) + (rotate_half(x) * sin), rotate_half = cat(-x2, x1); each op rounded
-      o1[e] = fadd(rnd(fmul(x1[e], c1), dt), rnd(fmul(-x2[e], s1), dt));
-      o2[e] = fadd(rnd(fmul(x2[e], c2), dt), rnd(fmul(x1[e], s2), dt));
+      o1[e] = fadd(rnd(fmul(x1[e], cs1[e]), dt), rnd(fmul(-x2[e], sn1[e]), dt));
+      o2[e] = fadd(rnd(fmul(x2[e], cs2[e]), dt), rnd(fmul(x1[e], sn2[e]), dt));
     }
     if (ok) {
-      store32(dst + i0, o1);
-      store32(dst + half + i0, o2);
+      store8(dst + i0 + 8 * g, o1);
+      store8(dst + half + i0 + 8 * g, o2);
     }
   }
+}
+
+#ifndef PG_GROUP_M
+#define PG_GROUP_M 4
+#endif
+// Work item -> (row block m, column tile n).  Items run in groups of kGroupM row blocks: inside a
+// group the column tile advances every kGroupM items, so the CTAs in flight share a few Wp tiles and
+// a few x row blocks, and Wp stays resident in L2 from one group to the next.
+constexpr int kGroupM = PG_GROUP_M;
+__device__ __forceinline__ void tile_of(const Params& p, int64_t item, int& m, int& n) {
+  const int64_t per_group = (int64_t)kGroupM * p.n_tiles;
+  const int64_t g = item / per_group, r = item % per_group;
+  const int64_t m0 = g * kGroupM;
+  const int64_t rows = min((int64_t)kGroupM, (int64_t)p.m_tiles - m0);  // the last group may be short
+  n = (int)(r / rows);
+  m = (int)(m0 + r % rows);
 }
 
 template <typename TabT>
@@ -175,7 +216,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t it = 0;
       bool ok = true;
       for (int64_t item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
-        const int m = (int)(item / p.n_tiles), n = (int)(item % p.n_tiles);
+        int m, n;
+        tile_of(p, item, m, n);
         for (int kb = 0; kb < p.n_kblk; ++kb, ++it) {
           const int s = it % kStages;
           if (!mbar_wait(&a_empty[s], ((it / kStages) & 1u) ^ 1u, p.err)) { ok = false; break; }
@@ -215,13 +257,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // -------------------------------------- epilogue --------------------------------------
     constexpr int dt = GSA_DTYPE_BF16;
-    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int quarter = warp & 3;           // TMEM lane quarter this warp may access
+    const int sp = (warp - 2) / 4;          // which 1/kSplit of the tile's columns
     uint32_t tc = 0;
     for (int64_t item = blockIdx.x; item < n_items; item += gridDim.x, ++tc) {
       const int buf = tc & 1;
       if (!mbar_wait(&t_full[buf], (tc >> 1) & 1u, p.err)) break;
       fence_after();
-      const int m = (int)(item / p.n_tiles), n = (int)(item % p.n_tiles);
+      int m, n;
+      tile_of(p, item, m, n);
       const int64_t t = (int64_t)m * kBM + quarter * 32 + lane;
       const bool ok = t < p.T;
       const int64_t tr = ok ? t : p.T - 1;  // rows past T read a valid position, store nothing
@@ -229,79 +273,84 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float* bias = p.bias + (int64_t)n * kBN;
       const int64_t b_of_t = tr / p.L, i_of_t = tr % p.L;
       const int kind = n < p.t_k ? kQ : n < p.t_vg ? kK : n < p.t_g1 ? kVG : n < p.t_idx ? kG1 : kIdx;
+      const int D = p.D, half = D / 2;
       if (kind == kQ || kind == kK) {
         int64_t pos = p.positions ? p.positions[tr] : p.pos0 + i_of_t;
         if (pos < 0 || pos >= p.tab_rows) {
           set_error(p.err, GSA_ERR_INDEX);
           pos = pos < 0 ? 0 : p.tab_rows - 1;
         }
-        const TabT* cr = reinterpret_cast<const TabT*>(p.cos_tab) + pos * p.D;
-        const TabT* sr = reinterpret_cast<const TabT*>(p.sin_tab) + pos * p.D;
-        const int heads = kBN / p.D;
-        for (int hh = 0; hh < heads; ++hh) {
-          __nv_bfloat16* dst;
-          if (kind == kQ) {
-            const int h = (n - p.t_q) * heads + hh;
-            dst = p.q_out + (tr * p.H + h) * (int64_t)p.D;
-          } else {
-            const int h = (n - p.t_k) * heads + hh;
-            dst = p.k_out + b_of_t * p.kv_bstride + i_of_t * p.kv_ld + (int64_t)h * p.D;
-          }
-          rope_head<TabT>(taddr, hh * p.D, p.D, cr, sr, dst, ok);
+        const TabT* cr = reinterpret_cast<const TabT*>(p.cos_tab) + pos * D;
+        const TabT* sr = reinterpret_cast<const TabT*>(p.sin_tab) + pos * D;
+        // this warp's RoPE pairs (i, i + D/2) of the tile's heads, 32 at a time
+        for (int slot = sp * kPairs; slot < (sp + 1) * kPairs; slot += 32) {
+          const int hh = slot / half, i0 = slot % half, c0 = hh * D;
+          const int h = (n - (kind == kQ ? p.t_q : p.t_k)) * (kBN / D) + hh;
+          __nv_bfloat16* dst = kind == kQ ? p.q_out + (tr * p.H + h) * (int64_t)D
+                                          : p.k_out + b_of_t * p.kv_bstride + i_of_t * p.kv_ld + (int64_t)h * D;
+          rope32<TabT>(taddr, c0 + i0, c0 + half + i0, i0, half, cr, sr, dst, ok);
         }
       } else if (kind == kVG) {
-        // columns [v_h | g2_h] per head: 256 / (2D) heads per tile
-        const int pairs = kBN / (2 * p.D);
-        for (int hh = 0; hh < pairs; ++hh) {
-          const int h = (n - p.t_vg) * pairs + hh;
-          __nv_bfloat16* dst = p.v_out + b_of_t * p.kv_bstride + i_of_t * p.kv_ld + (int64_t)h * p.D;
-          for (int i0 = 0; i0 < p.D; i0 += 32) {
-            uint32_t rv[32], rg[32];
-            const int cv = hh * 2 * p.D + i0, cg = cv + p.D;
-            tmem_ld32(taddr + cv, rv);
-            tmem_ld32(taddr + cg, rg);
-            tmem_wait_ld(rv);
-            tmem_wait_ld(rg);
-            float v[32], g[32];
-            acc_to_bf16(rv, nullptr, cv, v);  // v has no bias
-            acc_to_bf16(rg, bias, cg, g);
+        // [v_h | g2_h] column blocks of D per KV head: this warp's v dims, 32 at a time
+        for (int slot = sp * kPairs; slot < (sp + 1) * kPairs; slot += 32) {
+          const int pair = slot / D, i0 = slot % D;
+          const int h = (n - p.t_vg) * (kBN / (2 * D)) + pair;
+          __nv_bfloat16* dst = p.v_out + b_of_t * p.kv_bstride + i_of_t * p.kv_ld + (int64_t)h * D;
+          const int cv = pair * 2 * D + i0, cg = cv + D;
+          uint32_t rv[32], rg[32];
+          tmem_ld32(taddr + cv, rv);
+          tmem_ld32(taddr + cg, rg);
+          tmem_wait_ld(rv);
+          tmem_wait_ld(rg);
 #pragma unroll
-            for (int e = 0; e < 32; ++e) v[e] = fmul(v[e], gate_act(g[e], p.gate_act, dt));
-            if (ok) store32(dst + i0, v);
+          for (int g = 0; g < 4; ++g) {
+            float v[8], gl[8];
+            acc8(rv + 8 * g, nullptr, v);  // v has no bias
+            acc8(rg + 8 * g, bias + cg + 8 * g, gl);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] = fmul(v[e], gate_act(gl[e], p.gate_act, dt));
+            if (ok) store8(dst + i0 + 8 * g, v);
           }
         }
       } else if (kind == kG1) {
-        __nv_bfloat16* dst = p.g1_out + tr * (int64_t)p.H * p.D + (int64_t)(n - p.t_g1) * kBN;
-        for (int c0 = 0; c0 < kBN; c0 += 32) {
+        __nv_bfloat16* dst = p.g1_out + tr * (int64_t)p.H * D + (int64_t)(n - p.t_g1) * kBN;
+        for (int c0 = sp * kCols; c0 < (sp + 1) * kCols; c0 += 32) {
           uint32_t r[32];
           tmem_ld32(taddr + c0, r);
           tmem_wait_ld(r);
-          float g[32];
-          acc_to_bf16(r, bias, c0, g);
 #pragma unroll
-          for (int e = 0; e < 32; ++e) g[e] = gate_act(g[e], p.gate_act, dt);
-          if (ok) store32(dst + c0, g);
+          for (int g = 0; g < 4; ++g) {
+            float x[8];
+            acc8(r + 8 * g, bias + c0 + 8 * g, x);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x[e] = gate_act(x[e], p.gate_act, dt);
+            if (ok) store8(dst + c0 + 8 * g, x);
+          }
         }
       } else {
         // q^I | k^I | w | padding; every 32-column chunk lies inside one segment
         const int nqi = p.HI * p.dI;
         const int col0 = (n - p.t_idx) * kBN;
-        for (int c0 = 0; c0 < kBN; c0 += 32) {
+        for (int c0 = sp * kCols; c0 < (sp + 1) * kCols; c0 += 32) {
           const int col = col0 + c0;
           if (col >= nqi + p.dI + p.HI) break;
           uint32_t r[32];
           tmem_ld32(taddr + c0, r);
           tmem_wait_ld(r);
-          float x[32];
-          acc_to_bf16(r, col < nqi + p.dI ? nullptr : bias, c0, x);  // q^I, k^I have no bias
-          if (col < nqi) {
-            if (ok) store32(p.qi_out + tr * p.qi_ld + col, x);
-          } else if (col < nqi + p.dI) {
-            if (ok) store32(p.ki_out + b_of_t * p.ki_bstride + i_of_t * p.ki_ld + (col - nqi), x);
+          if (col < nqi + p.dI) {
+            __nv_bfloat16* dst = col < nqi ? p.qi_out + tr * p.qi_ld + col
+                                           : p.ki_out + b_of_t * p.ki_bstride + i_of_t * p.ki_ld + (col - nqi);
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              float x[8];
+              acc8(r + 8 * g, nullptr, x);  // q^I, k^I have no bias
+              if (ok) store8(dst + 8 * g, x);
+            }
           } else if (ok) {
             float sum = 0.f;
             for (int j = 0; j < p.HI; ++j) {
-              const float w = rnd(sigmoid_precise(x[j]), dt);
+              const float xb = __bfloat162float(__float2bfloat16_rn(fadd(__uint_as_float(r[j]), bias[c0 + j])));
+              const float w = rnd(sigmoid_precise(xb), dt);
               p.w_out[tr * p.HI + j] = w;
               sum += w;
             }
