@@ -45,8 +45,9 @@ __device__ __forceinline__ float rnd(float v, int dtype) {
 __device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b); }
 __device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }
 
-// Logistic sigmoid evaluated as 1 / (1 + e^-x) with the accurate expf.
-__device__ __forceinline__ float sigmoid_precise(float x) { return 1.0f / (1.0f + expf(-x)); }
+// Logistic sigmoid evaluated as 1 / (1 + e^-x) with the accurate expf; the reciprocal is the
+// correctly rounded one, the same value as the IEEE division 1.0f / d.
+__device__ __forceinline__ float sigmoid_precise(float x) { return __frcp_rn(1.0f + expf(-x)); }
 
 // Gate activations of the value / output gates (value_gate.py:98-106).
 __device__ __forceinline__ float gate_act(float x, int act, int dtype) {

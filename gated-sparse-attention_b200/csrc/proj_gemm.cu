@@ -17,11 +17,11 @@
 //   [q (H*D)] [k (Hk*D)] [v_0 g2_0 v_1 g2_1 ... (2*Hk*D)] [g1 (H*D)] [q^I (H_I*d_I)] [k^I (d_I)] [w (H_I)] [0 pad]
 // padded to a multiple of 256 rows; bias likewise (fp32; 0 where a projection has none).
 //
-// Roles (320 threads, one CTA per SM, persistent over (row block, column tile) work items):
+// Roles (576 threads, one CTA per SM, persistent over (row block, column tile) work items):
 // warp 0 = TMA producer (x tile 128 x 64 and Wp tile 256 x 64 per stage, 128-byte swizzle),
 // warp 1 = TMEM allocator + MMA issuer (one lane; M = 128, N = 256, K = 16 per instruction),
-// warps 2-9 = epilogue, two per TMEM lane quarter (each takes half of the tile's columns): a thread
-// owns one token row of the tile.
+// warps 2-17 = epilogue, four per TMEM lane quarter (each takes a quarter of the tile's columns): a
+// thread owns one token row of the tile.  Outputs leave through shared memory and TMA stores.
 // The 512 TMEM columns hold two accumulators, so a tile's epilogue overlaps the next tile's MMAs.
 // Every wait is bounded; on a timeout the kernel records GSA_ERR_TIMEOUT and returns.
 #include "kernels.cuh"
@@ -36,17 +36,20 @@ constexpr int kBM = 128;   // token rows per tile (TMEM lanes)
 constexpr int kBN = 256;   // output columns per tile (fp32 TMEM columns per accumulator)
 constexpr int kBK = 64;    // K per stage: one 128-byte swizzle atom of bf16
 constexpr int kStages = 4;
-#ifndef PG_EPI_WARPS
-#define PG_EPI_WARPS 16
-#endif
-constexpr int kEpiWarps = PG_EPI_WARPS;  // kSplit per TMEM lane quarter, each taking 1/kSplit of the columns
+constexpr int kEpiWarps = 16;            // kSplit per TMEM lane quarter, each taking 1/kSplit of the columns
 constexpr int kSplit = kEpiWarps / 4;
 constexpr int kCols = kBN / kSplit;      // columns of a tile per epilogue warp
-constexpr int kPairs = kBN / 2 / kSplit; // RoPE pairs (or v / g2 pairs) of a tile per epilogue warp
+constexpr int kPairs = kBN / 2 / kSplit; // v / g2 column pairs of a tile per epilogue warp
 constexpr int kThreads = 64 + 32 * kEpiWarps;
-constexpr int kATile = kBM * kBK * 2;  // 16 KiB
-constexpr int kBTile = kBN * kBK * 2;  // 32 KiB
-constexpr int kSmem = 1024 + kStages * (kATile + kBTile) + 256;
+constexpr int kATile = kBM * kBK * 2;    // 16 KiB
+constexpr int kBTile = kBN * kBK * 2;    // 32 KiB
+// Output staging: per epilogue warp two 1 KiB buffers, each a 32-row x 16-column bf16 chunk that a
+// TMA store writes out (32-byte swizzle), so the epilogue's global writes leave the SM as bulk copies
+// instead of one 16-byte store per row per instruction.
+constexpr int kStgBytes = 1024;
+constexpr int kStaging = kEpiWarps * 2 * kStgBytes;
+constexpr int kSmem = 1024 + kStages * (kATile + kBTile) + kStaging + 256;
+static_assert(kSmem <= 232448, "shared memory per CTA");
 
 enum Kind { kQ = 0, kK = 1, kVG = 2, kG1 = 3, kIdx = 4 };
 
@@ -60,9 +63,8 @@ struct Params {
   const float* bias;          // [n_tiles * 256]
   const int64_t* positions;   // [T] or NULL: row t at pos0 + t % L
   int64_t pos0, L;
-  const void* cos_tab;
-  const void* sin_tab;
-  int tab_dtype;
+  const __nv_bfloat16* cos_tab;  // [tab_rows, D] bf16: the module's RoPE buffers
+  const __nv_bfloat16* sin_tab;
   int64_t tab_rows;
   __nv_bfloat16* q_out;       // [T, H, D]
   __nv_bfloat16* k_out;       // token t's [Hk, D] K row at (t / L) * kv_bstride + (t % L) * kv_ld
@@ -76,92 +78,152 @@ struct Params {
   float* w_out;               // [T, H_I]
   float* shift_out;           // [T]
   int* err;
+  // token rows per batch entry of the K / V and k^I tensor maps (T and 1 batch when contiguous)
+  int64_t kv_rows, kv_batches, ki_rows, ki_batches;
 };
 
-// Eight fp32 accumulator columns of this thread's row as the bf16-rounded projection values
-// p = bf16(acc + bias) (bias NULL: none).
-__device__ __forceinline__ void acc8(const uint32_t* r, const float* bias, float (&x)[8]) {
-  float b[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  if (bias) {  // 32-byte aligned: two vector loads
-    const float4 b0 = reinterpret_cast<const float4*>(bias)[0], b1 = reinterpret_cast<const float4*>(bias)[1];
-    b[0] = b0.x; b[1] = b0.y; b[2] = b0.z; b[3] = b0.w;
-    b[4] = b1.x; b[5] = b1.y; b[6] = b1.z; b[7] = b1.w;
-  }
+// Tensor maps of the outputs written by TMA stores (box: 16 columns x 32 rows).
+struct OutMaps {
+  CUtensorMap q;   // [T, H*D]
+  CUtensorMap k;   // [batches, rows, Hk*D] (strides kv_bstride, kv_ld)
+  CUtensorMap v;
+  CUtensorMap g1;  // [T, H*D]
+  CUtensorMap qi;  // [T, H_I*d_I] (row stride qi_ld)
+  CUtensorMap ki;  // [batches, rows, d_I]
+};
+
+// ---- bf16 arithmetic on packed pairs ----
+// torch evaluates a bf16 product or sum in fp32 and rounds the result to bf16.  The fp32 product of
+// two bf16 values is exact, and an fp32 sum rounded again to bf16 is the correctly rounded bf16 sum
+// (24 >= 2 * 8 + 2 significand bits: the double rounding is innocuous), so both equal the correctly
+// rounded bf16x2 instructions below, two elements per instruction.
+__device__ __forceinline__ uint32_t bmul2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t badd2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t bneg2(uint32_t a) { return a ^ 0x80008000u; }
+// two fp32 values rounded to a bf16 pair (lo in the low half)
+__device__ __forceinline__ uint32_t bpack(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ float blo(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bhi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
+
+// 16 accumulator columns (+ bias, NULL: none) as 8 bf16 pairs: the projection values torch stores.
+__device__ __forceinline__ void acc16(const uint32_t (&r)[16], const float* bias, uint32_t (&x)[8]) {
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    float v = __uint_as_float(r[i]);
-    if (bias) v = fadd(v, b[i]);
-    x[i] = __bfloat162float(__float2bfloat16_rn(v));
+  for (int k = 0; k < 8; ++k) {
+    float lo = __uint_as_float(r[2 * k]), hi = __uint_as_float(r[2 * k + 1]);
+    if (bias) {
+      const float2 b = reinterpret_cast<const float2*>(bias)[k];
+      lo = fadd(lo, b.x);
+      hi = fadd(hi, b.y);
+    }
+    x[k] = bpack(lo, hi);
   }
 }
 
-// Eight values rounded to bf16 into one 16-byte store.
-__device__ __forceinline__ void store8(__nv_bfloat16* dst, const float (&v)[8]) {
-  uint32_t w[4];
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * k], v[2 * k + 1]);
-    w[k] = *reinterpret_cast<const uint32_t*>(&h);
-  }
-  *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+__device__ __forceinline__ void store16(__nv_bfloat16* dst, const uint32_t (&v)[8]) {
+  reinterpret_cast<uint4*>(dst)[0] = make_uint4(v[0], v[1], v[2], v[3]);
+  reinterpret_cast<uint4*>(dst)[1] = make_uint4(v[4], v[5], v[6], v[7]);
 }
 
-// Eight RoPE table entries (16-byte aligned) as fp32.
-__device__ __forceinline__ void tab8(const __nv_bfloat16* p, float (&v)[8]) {
-  const uint4 u = *reinterpret_cast<const uint4*>(p);
-  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    v[2 * k] = __uint_as_float(w[k] << 16);
-    v[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
-  }
-}
-__device__ __forceinline__ void tab8(const float* p, float (&v)[8]) {
-  const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+__device__ __forceinline__ void load16(const __nv_bfloat16* src, uint32_t (&v)[8]) {
+  const uint4 a = reinterpret_cast<const uint4*>(src)[0], b = reinterpret_cast<const uint4*>(src)[1];
   v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
   v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 
-// RoPE of 32 element pairs (i, i + D/2) of one head, i = i0 .. i0+31: TMEM columns c1 (first half)
-// and c2 (second half) of this thread's row; rotate-half with the row's cos / sin.
-template <typename TabT>
-__device__ __forceinline__ void rope32(uint32_t taddr, int c1, int c2, int i0, int half, const TabT* cr,
-                                       const TabT* sr, __nv_bfloat16* dst, bool ok) {
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int c0, int c1, const void* src) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(map), "r"(c0),
+               "r"(c1), "r"(smem_u32(src))
+               : "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, int c0, int c1, int c2, const void* src) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(map),
+               "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(src))
+               : "memory");
+}
+
+// One warp's output chunk on its way out: rows [t0, t0 + 32) x 16 columns, lane = row.  The chunk is
+// written to the warp's next staging buffer in the 32-byte swizzle (16-byte half c of row r at
+// r * 32 + (c ^ (r / 4 % 2)) * 16: the eight rows of a shared-memory phase hit distinct banks), then
+// lane 0 issues the TMA store.  A buffer is rewritten only after the store issued from it before has
+// read it (at most one store group in flight per warp).
+struct Stager {
+  uint8_t* buf;  // the warp's two buffers
+  int next;
+  __device__ __forceinline__ uint8_t* put(const uint32_t (&v)[8], int lane) {
+    uint8_t* b = buf + next * kStgBytes;
+    next ^= 1;
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+    __syncwarp();
+    const int sw = (lane >> 2) & 1;
+    *reinterpret_cast<uint4*>(b + lane * 32 + (sw << 4)) = make_uint4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<uint4*>(b + lane * 32 + ((sw ^ 1) << 4)) = make_uint4(v[4], v[5], v[6], v[7]);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    return b;
+  }
+  __device__ __forceinline__ void store2d(const CUtensorMap* map, int col, int64_t row, const uint32_t (&v)[8],
+                                          int lane) {
+    uint8_t* b = put(v, lane);
+    if (lane == 0) {
+      tma_store_2d(map, col, (int)row, b);
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    }
+  }
+  __device__ __forceinline__ void store3d(const CUtensorMap* map, int col, int64_t row, int64_t batch,
+                                          const uint32_t (&v)[8], int lane) {
+    uint8_t* b = put(v, lane);
+    if (lane == 0) {
+      tma_store_3d(map, col, (int)row, (int)batch, b);
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    }
+  }
+};
+
+// The gate activation of 8 bf16 pairs, rounded to bf16, as torch evaluates it.
+__device__ __forceinline__ void gate16(uint32_t (&x)[8], int act) {
   constexpr int dt = GSA_DTYPE_BF16;
-  uint32_t r1[32], r2[32];
-  tmem_ld32(taddr + c1, r1);
-  tmem_ld32(taddr + c2, r2);
-  tmem_wait_ld(r1);
-  tmem_wait_ld(r2);
 #pragma unroll
-  for (int g = 0; g < 4; ++g) {
-    float x1[8], x2[8], cs1[8], sn1[8], cs2[8], sn2[8], o1[8], o2[8];
-    acc8(r1 + 8 * g, nullptr, x1);
-    acc8(r2 + 8 * g, nullptr, x2);
-    tab8(cr + i0 + 8 * g, cs1);
-    tab8(sr + i0 + 8 * g, sn1);
-    tab8(cr + half + i0 + 8 * g, cs2);
-    tab8(sr + half + i0 + 8 * g, sn2);
+  for (int k = 0; k < 8; ++k) x[k] = bpack(gate_act(blo(x[k]), act, dt), gate_act(bhi(x[k]), act, dt));
+}
+
+// RoPE of 16 element pairs (i, i + D/2), i = i0 .. i0+15, of one head: TMEM columns c1 (first half)
+// and c2 (second half) of this thread's row, rotate-half with the row's bf16 cos / sin entries
+// (cs1 / sn1 at i, cs2 / sn2 at i + D/2):
+//   out_i = x_i cos_i - x_{i+D/2} sin_i,   out_{i+D/2} = x_{i+D/2} cos_{i+D/2} + x_i sin_{i+D/2}
+// ((x * cos) + (rotate_half(x) * sin), each op rounded to bf16).
+__device__ __forceinline__ void rope16(uint32_t taddr, int c1, int c2, const uint32_t (&cs1)[8],
+                                       const uint32_t (&sn1)[8], const uint32_t (&cs2)[8], const uint32_t (&sn2)[8],
+                                       uint32_t (&x1)[8], uint32_t (&x2)[8]) {
+  uint32_t r1[16], r2[16];
+  tmem_ld16(taddr + c1, r1);
+  tmem_ld16(taddr + c2, r2);
+  tmem_wait_ld(r1, r2);
+  acc16(r1, nullptr, x1);
+  acc16(r2, nullptr, x2);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      // (x * cos) + (rotate_half(x) * sin), rotate_half = cat(-x2, x1); each op rounded
-      o1[e] = fadd(rnd(fmul(x1[e], cs1[e]), dt), rnd(fmul(-x2[e], sn1[e]), dt));
-      o2[e] = fadd(rnd(fmul(x2[e], cs2[e]), dt), rnd(fmul(x1[e], sn2[e]), dt));
-    }
-    if (ok) {
-      store8(dst + i0 + 8 * g, o1);
-      store8(dst + half + i0 + 8 * g, o2);
-    }
+  for (int k = 0; k < 8; ++k) {
+    const uint32_t a = badd2(bmul2(x1[k], cs1[k]), bmul2(bneg2(x2[k]), sn1[k]));
+    const uint32_t b = badd2(bmul2(x2[k], cs2[k]), bmul2(x1[k], sn2[k]));
+    x1[k] = a;
+    x2[k] = b;
   }
 }
 
-#ifndef PG_GROUP_M
-#define PG_GROUP_M 4
-#endif
 // Work item -> (row block m, column tile n).  Items run in groups of kGroupM row blocks: inside a
 // group the column tile advances every kGroupM items, so the CTAs in flight share a few Wp tiles and
 // a few x row blocks, and Wp stays resident in L2 from one group to the next.
-constexpr int kGroupM = PG_GROUP_M;
+constexpr int kGroupM = 4;
 __device__ __forceinline__ void tile_of(const Params& p, int64_t item, int& m, int& n) {
   const int64_t per_group = (int64_t)kGroupM * p.n_tiles;
   const int64_t g = item / per_group, r = item % per_group;
@@ -171,15 +233,16 @@ __device__ __forceinline__ void tile_of(const Params& p, int64_t item, int& m, i
   m = (int)(m0 + r % rows);
 }
 
-template <typename TabT>
 __global__ void __launch_bounds__(kThreads, 1)
-    proj_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+    proj_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ OutMaps om, Params p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* base = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
   uint8_t* sA = base;
   uint8_t* sB = base + kStages * kATile;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + kStages * kBTile);
+  uint8_t* sStg = sB + kStages * kBTile;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sStg + kStaging);
   uint64_t* a_full = bars;
   uint64_t* a_empty = bars + kStages;
   uint64_t* t_full = bars + 2 * kStages;
@@ -256,9 +319,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // -------------------------------------- epilogue --------------------------------------
-    constexpr int dt = GSA_DTYPE_BF16;
     const int quarter = warp & 3;           // TMEM lane quarter this warp may access
     const int sp = (warp - 2) / 4;          // which 1/kSplit of the tile's columns
+    Stager stg{sStg + (warp - 2) * 2 * kStgBytes, 0};
     uint32_t tc = 0;
     for (int64_t item = blockIdx.x; item < n_items; item += gridDim.x, ++tc) {
       const int buf = tc & 1;
@@ -266,95 +329,123 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_after();
       int m, n;
       tile_of(p, item, m, n);
-      const int64_t t = (int64_t)m * kBM + quarter * 32 + lane;
-      const bool ok = t < p.T;
-      const int64_t tr = ok ? t : p.T - 1;  // rows past T read a valid position, store nothing
-      const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + buf * kBN;
-      const float* bias = p.bias + (int64_t)n * kBN;
-      const int64_t b_of_t = tr / p.L, i_of_t = tr % p.L;
-      const int kind = n < p.t_k ? kQ : n < p.t_vg ? kK : n < p.t_g1 ? kVG : n < p.t_idx ? kG1 : kIdx;
-      const int D = p.D, half = D / 2;
-      if (kind == kQ || kind == kK) {
-        int64_t pos = p.positions ? p.positions[tr] : p.pos0 + i_of_t;
-        if (pos < 0 || pos >= p.tab_rows) {
-          set_error(p.err, GSA_ERR_INDEX);
-          pos = pos < 0 ? 0 : p.tab_rows - 1;
-        }
-        const TabT* cr = reinterpret_cast<const TabT*>(p.cos_tab) + pos * D;
-        const TabT* sr = reinterpret_cast<const TabT*>(p.sin_tab) + pos * D;
-        // this warp's RoPE pairs (i, i + D/2) of the tile's heads, 32 at a time
-        for (int slot = sp * kPairs; slot < (sp + 1) * kPairs; slot += 32) {
-          const int hh = slot / half, i0 = slot % half, c0 = hh * D;
-          const int h = (n - (kind == kQ ? p.t_q : p.t_k)) * (kBN / D) + hh;
-          __nv_bfloat16* dst = kind == kQ ? p.q_out + (tr * p.H + h) * (int64_t)D
-                                          : p.k_out + b_of_t * p.kv_bstride + i_of_t * p.kv_ld + (int64_t)h * D;
-          rope32<TabT>(taddr, c0 + i0, c0 + half + i0, i0, half, cr, sr, dst, ok);
-        }
-      } else if (kind == kVG) {
-        // [v_h | g2_h] column blocks of D per KV head: this warp's v dims, 32 at a time
-        for (int slot = sp * kPairs; slot < (sp + 1) * kPairs; slot += 32) {
-          const int pair = slot / D, i0 = slot % D;
-          const int h = (n - p.t_vg) * (kBN / (2 * D)) + pair;
-          __nv_bfloat16* dst = p.v_out + b_of_t * p.kv_bstride + i_of_t * p.kv_ld + (int64_t)h * D;
-          const int cv = pair * 2 * D + i0, cg = cv + D;
-          uint32_t rv[32], rg[32];
-          tmem_ld32(taddr + cv, rv);
-          tmem_ld32(taddr + cg, rg);
-          tmem_wait_ld(rv);
-          tmem_wait_ld(rg);
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            float v[8], gl[8];
-            acc8(rv + 8 * g, nullptr, v);  // v has no bias
-            acc8(rg + 8 * g, bias + cg + 8 * g, gl);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) v[e] = fmul(v[e], gate_act(gl[e], p.gate_act, dt));
-            if (ok) store8(dst + i0 + 8 * g, v);
+      const int64_t t0 = (int64_t)m * kBM + quarter * 32;  // this warp's first row
+      if (t0 < p.T) {
+        const int64_t t = t0 + lane;
+        const bool ok = t < p.T;
+        const int64_t tr = ok ? t : p.T - 1;  // rows past T read a valid position; TMA clips their stores
+        const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + buf * kBN;
+        const float* bias = p.bias + (int64_t)n * kBN;
+        const int kind = n < p.t_k ? kQ : n < p.t_vg ? kK : n < p.t_g1 ? kVG : n < p.t_idx ? kG1 : kIdx;
+        const int D = p.D, half = D / 2;
+        // where the warp's 32 rows sit in the K / V (k^I) maps; a group that runs from one sequence into
+        // the next (L % 32 != 0, batches not contiguous) is stored row by row instead
+        const int64_t kv_i = t0 % p.kv_rows, kv_b = t0 / p.kv_rows;
+        const bool kv_bulk = kv_i + 32 <= p.kv_rows || kv_b == p.kv_batches - 1;
+        const int64_t ki_i = t0 % p.ki_rows, ki_b = t0 / p.ki_rows;
+        const bool ki_bulk = ki_i + 32 <= p.ki_rows || ki_b == p.ki_batches - 1;
+        const int64_t b_of_t = tr / p.L, i_of_t = tr % p.L;
+        if (kind == kQ || kind == kK) {
+          int64_t pos = p.positions ? p.positions[tr] : p.pos0 + i_of_t;
+          if (pos < 0 || pos >= p.tab_rows) {
+            set_error(p.err, GSA_ERR_INDEX);
+            pos = pos < 0 ? 0 : p.tab_rows - 1;
           }
-        }
-      } else if (kind == kG1) {
-        __nv_bfloat16* dst = p.g1_out + tr * (int64_t)p.H * D + (int64_t)(n - p.t_g1) * kBN;
-        for (int c0 = sp * kCols; c0 < (sp + 1) * kCols; c0 += 32) {
-          uint32_t r[32];
-          tmem_ld32(taddr + c0, r);
-          tmem_wait_ld(r);
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            float x[8];
-            acc8(r + 8 * g, bias + c0 + 8 * g, x);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) x[e] = gate_act(x[e], p.gate_act, dt);
-            if (ok) store8(dst + c0 + 8 * g, x);
+          const __nv_bfloat16* cr = p.cos_tab + pos * D;
+          const __nv_bfloat16* sr = p.sin_tab + pos * D;
+          // This warp's RoPE pairs: pairs (i, i + D/2), i in [i0, i0 + 16), of every (kSplit / nc)-th head
+          // of the tile, so that the warp reads its table entries once for all of its heads.
+          const int nc = half / 16;  // 16-pair chunks per head
+          const int i0 = (sp % nc) * 16;
+          uint32_t cs1[8], sn1[8], cs2[8], sn2[8];
+          load16(cr + i0, cs1);
+          load16(sr + i0, sn1);
+          load16(cr + half + i0, cs2);
+          load16(sr + half + i0, sn2);
+          for (int hh = sp / nc; hh < kBN / D; hh += kSplit / nc) {
+            const int c0 = hh * D;
+            const int h = (n - (kind == kQ ? p.t_q : p.t_k)) * (kBN / D) + hh;
+            uint32_t x1[8], x2[8];
+            rope16(taddr, c0 + i0, c0 + half + i0, cs1, sn1, cs2, sn2, x1, x2);
+            if (kind == kQ) {
+              stg.store2d(&om.q, h * D + i0, t0, x1, lane);
+              stg.store2d(&om.q, h * D + half + i0, t0, x2, lane);
+            } else if (kv_bulk) {
+              stg.store3d(&om.k, h * D + i0, kv_i, kv_b, x1, lane);
+              stg.store3d(&om.k, h * D + half + i0, kv_i, kv_b, x2, lane);
+            } else if (ok) {
+              __nv_bfloat16* dst = p.k_out + b_of_t * p.kv_bstride + i_of_t * p.kv_ld + (int64_t)h * D;
+              store16(dst + i0, x1);
+              store16(dst + half + i0, x2);
+            }
           }
-        }
-      } else {
-        // q^I | k^I | w | padding; every 32-column chunk lies inside one segment
-        const int nqi = p.HI * p.dI;
-        const int col0 = (n - p.t_idx) * kBN;
-        for (int c0 = sp * kCols; c0 < (sp + 1) * kCols; c0 += 32) {
-          const int col = col0 + c0;
-          if (col >= nqi + p.dI + p.HI) break;
-          uint32_t r[32];
-          tmem_ld32(taddr + c0, r);
-          tmem_wait_ld(r);
-          if (col < nqi + p.dI) {
-            __nv_bfloat16* dst = col < nqi ? p.qi_out + tr * p.qi_ld + col
-                                           : p.ki_out + b_of_t * p.ki_bstride + i_of_t * p.ki_ld + (col - nqi);
+        } else if (kind == kVG) {
+          // [v_h | g2_h] column blocks of D per KV head: v * act(g2), this warp's v dims 16 at a time
+          for (int slot = sp * kPairs; slot < (sp + 1) * kPairs; slot += 16) {
+            const int pair = slot / D, i0 = slot % D;
+            const int h = (n - p.t_vg) * (kBN / (2 * D)) + pair;
+            const int cv = pair * 2 * D + i0, cg = cv + D;
+            uint32_t rv[16], rg[16];
+            tmem_ld16(taddr + cv, rv);
+            tmem_ld16(taddr + cg, rg);
+            tmem_wait_ld(rv, rg);
+            uint32_t v[8], g[8];
+            acc16(rv, nullptr, v);  // v has no bias
+            acc16(rg, bias + cg, g);
+            gate16(g, p.gate_act);
 #pragma unroll
-            for (int g = 0; g < 4; ++g) {
-              float x[8];
-              acc8(r + 8 * g, nullptr, x);  // q^I, k^I have no bias
-              if (ok) store8(dst + 8 * g, x);
+            for (int k = 0; k < 8; ++k) v[k] = bmul2(v[k], g[k]);
+            if (kv_bulk) {
+              stg.store3d(&om.v, h * D + i0, kv_i, kv_b, v, lane);
+            } else if (ok) {
+              store16(p.v_out + b_of_t * p.kv_bstride + i_of_t * p.kv_ld + (int64_t)h * D + i0, v);
             }
-          } else if (ok) {
-            float sum = 0.f;
-            for (int j = 0; j < p.HI; ++j) {
-              const float xb = __bfloat162float(__float2bfloat16_rn(fadd(__uint_as_float(r[j]), bias[c0 + j])));
-              const float w = rnd(sigmoid_precise(xb), dt);
-              p.w_out[tr * p.HI + j] = w;
-              sum += w;
+          }
+        } else if (kind == kG1) {
+          const int cbase = (n - p.t_g1) * kBN;
+          for (int c0 = sp * kCols; c0 < (sp + 1) * kCols; c0 += 16) {
+            uint32_t r[16];
+            tmem_ld16(taddr + c0, r);
+            tmem_wait_ld(r);
+            uint32_t g[8];
+            acc16(r, bias + c0, g);
+            gate16(g, p.gate_act);
+            stg.store2d(&om.g1, cbase + c0, t0, g, lane);
+          }
+        } else {
+          // q^I | k^I | w | padding; every 16-column chunk lies inside one segment
+          const int nqi = p.HI * p.dI;
+          const int col0 = (n - p.t_idx) * kBN;
+          for (int c0 = sp * kCols; c0 < (sp + 1) * kCols; c0 += 16) {
+            const int col = col0 + c0;
+            if (col >= nqi + p.dI + p.HI) break;
+            uint32_t r[16];
+            tmem_ld16(taddr + c0, r);
+            tmem_wait_ld(r);
+            if (col < nqi + p.dI) {
+              uint32_t x[8];
+              acc16(r, nullptr, x);  // q^I, k^I have no bias
+              if (col < nqi) {
+                stg.store2d(&om.qi, col, t0, x, lane);
+              } else if (ki_bulk) {
+                stg.store3d(&om.ki, col - nqi, ki_i, ki_b, x, lane);
+              } else if (ok) {
+                store16(p.ki_out + b_of_t * p.ki_bstride + i_of_t * p.ki_ld + (col - nqi), x);
+              }
+            } else if (ok) {
+              constexpr int dt = GSA_DTYPE_BF16;
+              float sum = 0.f;
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                if (j < p.HI) {
+                  const float xb = __bfloat162float(__float2bfloat16_rn(fadd(__uint_as_float(r[j]), bias[c0 + j])));
+                  const float w = rnd(sigmoid_precise(xb), dt);
+                  p.w_out[tr * p.HI + j] = w;
+                  sum += w;
+                }
+              }
+              p.shift_out[tr] = 0.5f * sum;
             }
-            p.shift_out[tr] = 0.5f * sum;
           }
         }
       }
@@ -363,6 +454,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&t_empty[buf]);
     }
+    // the staging buffers must stay valid until the last stores have completed
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    __syncwarp();
   }
 
   fence_before();
@@ -379,8 +473,10 @@ bool proj_gemm_eligible(const ProjGemmArgs& a) {
   const int D = a.d.d_head, H = a.d.n_heads, Hk = a.d.n_kv_heads, HI = a.d.n_idx_heads, dI = a.d.d_idx;
   auto al16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) % 16) == 0; };
   auto el16 = [](int64_t x) { return (x * 2) % 16 == 0; };
+  static_assert(pg::kSplit % 4 == 0, "the RoPE split needs kSplit a multiple of D / 32 for D <= 128");
   return (D == 64 || D == 128) && (H * D) % pg::kBN == 0 && (2 * Hk * D) % pg::kBN == 0 && (Hk * D) % pg::kBN == 0 &&
-         dI % 32 == 0 && (HI * dI) % 32 == 0 && HI <= 32 && a.d.d_model % pg::kBK == 0 &&
+         dI % 16 == 0 && (HI * dI) % 16 == 0 && HI <= 16 && a.d.d_model % pg::kBK == 0 &&
+         a.tab_dtype == GSA_DTYPE_BF16 && a.tab_rows > 0 &&
          a.d.gate_act >= GSA_ACT_SIGMOID && a.d.gate_act <= GSA_ACT_SILU && al16(a.x) && el16(a.x_ld) && al16(a.w) &&
          al16(a.q_out) && al16(a.k_out) && al16(a.v_out) && al16(a.g1_out) && al16(a.qi_out) && al16(a.ki_out) &&
          el16(a.kv_ld) && el16(a.kv_bstride) && el16(a.qi_ld) && el16(a.ki_ld) && el16(a.ki_bstride) &&
@@ -440,9 +536,8 @@ int launch_proj_gemm(const ProjGemmArgs& a, int num_sms, cudaStream_t stream) {
   p.positions = a.positions;
   p.pos0 = a.pos0;
   p.L = a.L > 0 ? a.L : a.T;
-  p.cos_tab = a.cos_tab;
-  p.sin_tab = a.sin_tab;
-  p.tab_dtype = a.tab_dtype;
+  p.cos_tab = static_cast<const __nv_bfloat16*>(a.cos_tab);
+  p.sin_tab = static_cast<const __nv_bfloat16*>(a.sin_tab);
   p.tab_rows = a.tab_rows;
   p.q_out = static_cast<__nv_bfloat16*>(a.q_out);
   p.k_out = static_cast<__nv_bfloat16*>(a.k_out);
@@ -458,19 +553,47 @@ int launch_proj_gemm(const ProjGemmArgs& a, int num_sms, cudaStream_t stream) {
   p.w_out = a.w_out;
   p.shift_out = a.shift_out;
   p.err = a.err;
+  // the row geometry of the K / V and k^I outputs: one run of T rows when the sequences are contiguous
+  const int64_t B = a.T / p.L;
+  const bool kv_contig = B == 1 || p.kv_bstride == p.L * p.kv_ld;
+  const bool ki_contig = B == 1 || p.ki_bstride == p.L * p.ki_ld;
+  p.kv_rows = kv_contig ? a.T : p.L;
+  p.kv_batches = kv_contig ? 1 : B;
+  p.ki_rows = ki_contig ? a.T : p.L;
+  p.ki_batches = ki_contig ? 1 : B;
+  OutMaps om;
+  auto map2d = [&](CUtensorMap* m, void* base, int64_t cols, int64_t rows, int64_t ld) {
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    cuuint32_t box[2] = {16, 32};
+    cuuint32_t es[2] = {1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  };
+  auto map3d = [&](CUtensorMap* m, void* base, int64_t cols, int64_t rows, int64_t batches, int64_t ld,
+                   int64_t bstride) {
+    cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)batches};
+    // a single batch entry still needs a valid stride: any multiple of 16 bytes covering the rows
+    cuuint64_t strides[2] = {(cuuint64_t)ld * 2, (cuuint64_t)(batches > 1 ? bstride : rows * ld) * 2};
+    cuuint32_t box[3] = {16, 32, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  };
+  if (!map2d(&om.q, a.q_out, (int64_t)H * D, a.T, (int64_t)H * D) ||
+      !map3d(&om.k, a.k_out, (int64_t)Hk * D, p.kv_rows, p.kv_batches, a.kv_ld, p.kv_bstride) ||
+      !map3d(&om.v, a.v_out, (int64_t)Hk * D, p.kv_rows, p.kv_batches, a.kv_ld, p.kv_bstride) ||
+      !map2d(&om.g1, a.g1_out, (int64_t)H * D, a.T, (int64_t)H * D) ||
+      !map2d(&om.qi, a.qi_out, (int64_t)a.d.n_idx_heads * a.d.d_idx, a.T, a.qi_ld) ||
+      !map3d(&om.ki, a.ki_out, a.d.d_idx, p.ki_rows, p.ki_batches, a.ki_ld, p.ki_bstride))
+    return GSA_ERR_BAD_ARG;
+  if (cudaFuncSetAttribute(proj_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
+    return GSA_ERR_LAUNCH;
   const int64_t items = (int64_t)p.m_tiles * p.n_tiles;
   const unsigned grid = (unsigned)std::min<int64_t>(items, num_sms);
-  if (a.tab_dtype == GSA_DTYPE_BF16) {
-    if (cudaFuncSetAttribute(proj_gemm_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) !=
-        cudaSuccess)
-      return GSA_ERR_LAUNCH;
-    proj_gemm_kernel<__nv_bfloat16><<<grid, kThreads, kSmem, stream>>>(tmA, tmB, p);
-  } else {
-    if (cudaFuncSetAttribute(proj_gemm_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) !=
-        cudaSuccess)
-      return GSA_ERR_LAUNCH;
-    proj_gemm_kernel<float><<<grid, kThreads, kSmem, stream>>>(tmA, tmB, p);
-  }
+  proj_gemm_kernel<<<grid, kThreads, kSmem, stream>>>(tmA, tmB, om, p);
   return cudaGetLastError() == cudaSuccess ? GSA_OK : GSA_ERR_LAUNCH;
 }
 
