@@ -106,9 +106,10 @@ int gsa_proj_epilogue(const gsa_dims* dims, const gsa_proj_layout* layout, int d
  *   positions [T] int64 or NULL (row t = b*L + i at position pos0 + i)
  *   outputs as gsa_proj_epilogue_cache (L rows per sequence; K/V/k^I at the batch strides) plus
  *   qi_out [T, qi_ld] bf16 (the indexer queries) and ki_out (the indexer keys, required).
- * Supported: d_head 64 or 128 with H*D, Hk*D multiples of 256, d_I and H_I*d_I multiples of 32,
- * H_I <= 32, d_model a multiple of 64, both gates present (per-head G1), 16-byte aligned rows;
- * otherwise GSA_ERR_UNSUPPORTED (use the GEMM + gsa_proj_epilogue pair).
+ * Supported: d_head 64 or 128 with H*D, Hk*D multiples of 256, d_I and H_I*d_I multiples of 16,
+ * H_I <= 16, d_model a multiple of 64, both gates present (per-head G1), bf16 cos / sin tables,
+ * 16-byte aligned rows and strides; otherwise GSA_ERR_UNSUPPORTED (use the GEMM +
+ * gsa_proj_epilogue pair).  Outputs are bit-identical to that pair's.
  */
 int64_t gsa_proj_fused_rows(const gsa_dims* dims);
 int gsa_proj_fused(const gsa_dims* dims, int dtype, int64_t T, int64_t L, const void* x, int64_t x_ld,
