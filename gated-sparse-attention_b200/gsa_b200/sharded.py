@@ -72,6 +72,8 @@ class QueryShards:
         self.world = dist.get_world_size(group)
         self.layout = layout
         self.folds = folds
+        self._side = None   # stream of the asynchronous gathers' reordering
+        self._perm = {}     # (device, world, segments per rank) -> segment permutation
 
     def segments(self, L_local: int):
         """[(local_start, length, absolute_position_of_first_token)] of this rank's tokens."""
@@ -91,33 +93,70 @@ class QueryShards:
 
     def gather(self, t: torch.Tensor) -> torch.Tensor:
         """All-gather every rank's [B, L_local, ...] tokens into [B, L_total, ...] in sequence order."""
-        return self._sequence_order(gather_sequence(t, self.group, self.world), t)
+        t = t.contiguous()
+        buf = torch.empty((self.world * t.shape[0],) + tuple(t.shape[1:]), device=t.device, dtype=t.dtype)
+        dist.all_gather_into_tensor(buf, t, group=self.group)
+        return self._sequence_order(buf, t)
 
     def gather_async(self, t: torch.Tensor):
         """Start the all-gather of :meth:`gather` and return ``finish()``, which makes the current
         stream wait for it and returns the same tensor.  The collective runs on NCCL's stream
-        meanwhile, so work queued in between (the indexer, for K and V) overlaps the transfer."""
+        meanwhile, so work queued in between (the indexer, for K and V) overlaps the transfer; on
+        CUDA the reordering into sequence order follows the collective on a side stream, so it
+        overlaps that work too."""
         t = t.contiguous()
         buf = torch.empty((self.world * t.shape[0],) + tuple(t.shape[1:]), device=t.device, dtype=t.dtype)
         work = dist.all_gather_into_tensor(buf, t, group=self.group, async_op=True)
+        if not t.is_cuda or self.layout == "contiguous":
+            def finish():
+                work.wait()
+                return self._sequence_order(buf, t)
+            return finish
+        main = torch.cuda.current_stream(t.device)
+        if self._side is None:
+            self._side = torch.cuda.Stream(device=t.device)
+        side = self._side
+        side.wait_stream(main)  # buf and t were made on the main stream
+        with torch.cuda.stream(side):
+            work.wait()  # the side stream waits for the collective
+            out = self._sequence_order(buf, t)
+            done = torch.cuda.Event()
+            done.record(side)
+        buf.record_stream(side)
 
         def finish():
-            work.wait()
-            return self._sequence_order(_rank_major(buf, t.shape, self.world), t)
+            main.wait_event(done)
+            out.record_stream(main)
+            return out
 
         return finish
 
     def _sequence_order(self, g: torch.Tensor, t: torch.Tensor) -> torch.Tensor:
+        """The gathered shards ([world * B, L_local, ...] in rank order) in sequence order: one
+        gather copy of whole segments (zigzag) or a view (contiguous blocks)."""
         if self.layout == "contiguous":
-            return g
+            return g if g.shape[0] == t.shape[0] else _rank_major(g, t.shape, self.world)
         B, Ll = t.shape[0], t.shape[1]
         nseg = 2 * self.folds
         S = Ll // nseg
         rest = tuple(t.shape[2:])
-        blocks = g.view((B, self.world, nseg, S) + rest)
-        # sweep k holds sequence segments k*P .. k*P+P-1, owned by ranks 0..P-1 (even k) or P-1..0
-        sweeps = [blocks[:, :, k] if k % 2 == 0 else blocks[:, :, k].flip(1) for k in range(nseg)]
-        return torch.cat([sw.reshape((B, self.world * S) + rest) for sw in sweeps], dim=1)
+        # rank-major segment r * nseg + k is rank r's k-th segment; sequence segment j = k * P + i
+        # belongs to sweep k, owned by rank i (even k) or P-1-i (odd k)
+        key = (g.device, self.world, nseg)
+        perm = self._perm.get(key)
+        if perm is None:
+            order = []
+            for j in range(self.world * nseg):
+                k, i = divmod(j, self.world)
+                r = i if k % 2 == 0 else self.world - 1 - i
+                order.append(r * nseg + k)
+            perm = torch.tensor(order, dtype=torch.long, device=g.device)
+            self._perm[key] = perm
+        blocks = g.view((self.world * nseg, S) + rest) if B == 1 else \
+            _rank_major(g, t.shape, self.world).view((B, self.world * nseg, S) + rest)
+        if B == 1:
+            return blocks.index_select(0, perm).view((1, self.world * Ll) + rest)
+        return blocks.index_select(1, perm).view((B, self.world * Ll) + rest)
 
     def allreduce(self, t):
         return allreduce_sum(t, self.group)
