@@ -227,6 +227,15 @@ int gsa_row_stats(int64_t R, int64_t n_cols, const float* scores, int64_t scores
   return launch_row_stats(R, n_cols, scores, scores_ld, row_stats, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int gsa_row_summary(int64_t R, int64_t n_cols, const float* scores, int64_t scores_ld, int dtype, float* out,
+                    gsa_stream_t stream) {
+  if (R < 0 || n_cols < 1 || scores_ld < n_cols || R > 0x7fffffffLL) return GSA_ERR_BAD_ARG;
+  if (dtype != GSA_DTYPE_F32 && dtype != GSA_DTYPE_BF16) return GSA_ERR_BAD_ARG;
+  if (R == 0) return GSA_OK;
+  if (!scores || !out) return GSA_ERR_BAD_ARG;
+  return launch_row_summary(R, n_cols, scores, scores_ld, dtype, out, reinterpret_cast<cudaStream_t>(stream));
+}
+
 int gsa_topk_candidates(int64_t R, int64_t Lq, int64_t n_cols, int64_t q_pos0, int causal, const float* scores,
                         int64_t scores_ld, const float* row_center, const double* row_stats, int32_t k_eff,
                         int32_t* cand_idx, float* cand_score, int32_t* cand_count, gsa_stream_t stream) {

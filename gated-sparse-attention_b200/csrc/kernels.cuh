@@ -223,6 +223,8 @@ int launch_select_finalize_warp(int64_t R, int32_t cand_ld, const int32_t* cand_
 int launch_select_finalize(int64_t R, int32_t k_eff, const int32_t* cand_idx, const float* cand_score,
                            const int32_t* cand_count, const int32_t* k, int32_t* sel_idx, int64_t sel_ld,
                            int32_t* sel_count, uint8_t* sel_mask, cudaStream_t stream);
+int launch_row_summary(int64_t R, int64_t n_cols, const float* scores, int64_t ld, int dtype, float* out,
+                       cudaStream_t stream);
 int launch_row_stats(int64_t R, int64_t n_cols, const float* scores, int64_t ld, double* stats,
                      cudaStream_t stream);
 int launch_row_variance(int64_t R, int64_t n_cols, int dtype, const double* stats, const float* shift,

@@ -1264,6 +1264,83 @@ __global__ void row_stats_kernel(int64_t n_cols, const float* scores, int64_t ld
   }
 }
 
+// Per-row statistics of a materialised score matrix for the entropy and learned adaptive-k methods
+// (adaptive_topk.py:84-127), each rounded to the activation dtype as torch rounds its result:
+//   out[r] = {valid count, mean, std (unbiased), max of the masked scores (masked entries count as
+//             0, over all n_cols entries), softmax entropy of the valid entries}
+// with valid = (score != -inf) and the entropy -sum_i p_i log(p_i + 1e-10), p = softmax over the
+// valid entries (exp(x - max) times the reciprocal of their sum, as torch's CPU softmax), every
+// product and log rounded to the dtype and the sum accumulated in fp32.  One CTA per row, three
+// passes over it.
+constexpr int kSumThreads = 256;
+
+template <typename T, typename Op>
+__device__ __forceinline__ T block_reduce(T v, T* red, Op op) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, o));
+  __syncthreads();  // red may still be read from a previous reduction
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  T a = red[0];
+  for (int w = 1; w < kSumThreads / 32; ++w) a = op(a, red[w]);
+  return a;
+}
+
+__global__ void __launch_bounds__(kSumThreads) row_summary_kernel(int64_t n_cols, const float* scores, int64_t ld,
+                                                                  int dtype, float* out) {
+  __shared__ double redd[kSumThreads / 32];
+  __shared__ float redf[kSumThreads / 32];
+  const int64_t r = blockIdx.x;
+  const float* row = scores + r * ld;
+  auto add_d = [](double a, double b) { return a + b; };
+  auto add_f = [](float a, float b) { return a + b; };
+  auto max_f = [](float a, float b) { return fmaxf(a, b); };
+  double s1 = 0.0, s2 = 0.0, c = 0.0;
+  float mx = -INFINITY;
+  for (int64_t i = threadIdx.x; i < n_cols; i += kSumThreads) {
+    const float f = row[i];
+    if (f != -INFINITY) {
+      s1 += (double)f;
+      s2 += (double)f * (double)f;
+      c += 1.0;
+      mx = fmaxf(mx, f);
+    }
+  }
+  s1 = block_reduce(s1, redd, add_d);
+  s2 = block_reduce(s2, redd, add_d);
+  c = block_reduce(c, redd, add_d);
+  mx = block_reduce(mx, redf, max_f);
+  const double N = (double)n_cols;
+  // softmax over the valid entries, then sum_i p_i log(p_i + 1e-10) in fp32
+  float z = 0.f;
+  for (int64_t i = threadIdx.x; i < n_cols; i += kSumThreads) {
+    const float f = row[i];
+    if (f != -INFINITY) z += expf(f - mx);
+  }
+  z = block_reduce(z, redf, add_f);
+  const float inv_z = 1.0f / z;
+  float h = 0.f;
+  for (int64_t i = threadIdx.x; i < n_cols; i += kSumThreads) {
+    const float f = row[i];
+    if (f != -INFINITY) {
+      const float pr = rnd(expf(f - mx) * inv_z, dtype);
+      const float lp = rnd(logf(rnd(pr + 1e-10f, dtype)), dtype);
+      h += rnd(pr * lp, dtype);
+    }
+  }
+  h = block_reduce(h, redf, add_f);
+  if (threadIdx.x == 0) {
+    float* o = out + r * 5;
+    o[0] = (float)c;
+    o[1] = rnd((float)(s1 / N), dtype);
+    const double var = N > 1.0 ? (s2 - s1 * s1 / N) / (N - 1.0) : (double)NAN;
+    o[2] = rnd((float)sqrt(var > 0.0 ? var : (var == var ? 0.0 : var)), dtype);
+    o[3] = c < N ? fmaxf(mx, 0.f) : mx;
+    o[4] = c > 0.0 ? -rnd(h, dtype) : (float)NAN;
+  }
+}
+
 // Unbiased variance over all N entries (masked ones count as 0), from sums taken relative to
 // a per-row shift c.  With y = x - c: the N - n masked entries have y = -c.
 __device__ __forceinline__ double row_var(const double* st, double c, double N) {
@@ -1426,6 +1503,13 @@ int launch_row_stats(int64_t R, int64_t n_cols, const float* scores, int64_t ld,
                      cudaStream_t stream) {
   if (R == 0) return GSA_OK;
   row_stats_kernel<<<(unsigned)R, 256, 0, stream>>>(n_cols, scores, ld, stats);
+  return cudaGetLastError() == cudaSuccess ? GSA_OK : GSA_ERR_LAUNCH;
+}
+
+int launch_row_summary(int64_t R, int64_t n_cols, const float* scores, int64_t ld, int dtype, float* out,
+                       cudaStream_t stream) {
+  if (R == 0) return GSA_OK;
+  row_summary_kernel<<<(unsigned)R, kSumThreads, 0, stream>>>(n_cols, scores, ld, dtype, out);
   return cudaGetLastError() == cudaSuccess ? GSA_OK : GSA_ERR_LAUNCH;
 }
 

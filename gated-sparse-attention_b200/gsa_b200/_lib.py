@@ -67,6 +67,7 @@ SIGNATURES = {
     "gsa_indexer_scores": [P, INT, I64, I64, I64, I64, INT, INT, P, I64, I64, P, I64, I64, P, P, F32,
                            P, P, I64, P, P],
     "gsa_row_stats": [I64, I64, P, I64, P, P],
+    "gsa_row_summary": [I64, I64, P, I64, INT, P, P],
     "gsa_topk_candidates": [I64, I64, I64, I64, INT, P, I64, P, P, I32, P, P, P, P],
     "gsa_row_variance": [I64, I64, INT, P, P, P, P, P],
     "gsa_adaptive_k": [I64, I64, INT, P, P, P, P, P, P],

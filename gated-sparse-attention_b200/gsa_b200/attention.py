@@ -408,21 +408,36 @@ class AdaptiveTopKSelector(nn.Module):
         self.use_adaptive = use_adaptive
         self.temperature = temperature
         self.adaptive_method = adaptive_method
-        if adaptive_method == "learned":  # parameters kept for state-dict compatibility
+        if adaptive_method == "learned":  # [mean, std, max] of a row's scores -> fraction of [k_min, k_max]
             self.k_predictor = nn.Sequential(nn.Linear(3, 32), nn.ReLU(), nn.Linear(32, 1), nn.Sigmoid())
+
+    def _k_from_summary(self, s2d: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+        """k_t of the entropy and learned methods (adaptive_topk.py:104-133): the row statistics
+        come from the native row-summary pass; the few per-row scalar ops follow on them (the
+        learned method through the module's own predictor)."""
+        summ = ops.row_summary(s2d, dtype)
+        valid = summ[:, 0]
+        if self.adaptive_method == "entropy":
+            # the entropy is a dtype value; the division promotes it to fp32
+            norm = summ[:, 4] / (torch.log(valid + 1) + 1e-8)
+            k_adaptive = self.k_base * (0.5 + norm * self.temperature)
+        else:
+            stats = summ[:, 1:4].to(dtype)
+            k_scale = self.k_predictor(stats).squeeze(-1)
+            k_adaptive = self.k_min + k_scale * (self.k_max - self.k_min)
+        k = torch.minimum(torch.clamp(k_adaptive, self.k_min, self.k_max), valid)
+        return k.long().to(torch.int32)
 
     def forward(self, scores: torch.Tensor, seq_q: int, seq_kv: int, return_k_values: bool = False):
         B, Lq, Lkv = scores.shape
-        if self.use_adaptive and self.adaptive_method != "variance":
-            if self.adaptive_method in ("entropy", "learned"):
-                raise NotImplementedError(
-                    f"adaptive_method={self.adaptive_method!r} has no kernel; the attention layer "
-                    "uses 'variance'")
+        if self.use_adaptive and self.adaptive_method not in ("variance", "entropy", "learned"):
             raise ValueError(f"Unknown adaptive method: {self.adaptive_method}")
         k_eff = min(self.k_max, seq_kv) if self.use_adaptive else min(self.k_base, seq_kv)
         s2d = scores.reshape(B * Lq, Lkv).float()
         cand_idx, cand_score, cand_count = ops.topk_candidates(s2d, k_eff)
-        if self.use_adaptive:
+        if self.use_adaptive and self.adaptive_method != "variance":
+            k = self._k_from_summary(s2d, scores.dtype)
+        elif self.use_adaptive:
             stats = ops.row_stats(s2d)
             var, total = ops.row_variance(stats, Lkv, scores.dtype)
             k = ops.adaptive_k(stats, var, total, Lkv, scores.dtype, self.k_base, self.k_min,

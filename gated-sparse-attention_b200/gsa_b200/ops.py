@@ -188,6 +188,21 @@ def row_stats(scores2d: torch.Tensor) -> torch.Tensor:
     return stats
 
 
+def row_summary(scores2d: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """fp32 [R, 5] = (valid count, mean, std, max of the masked scores, softmax entropy) per row of
+    a score matrix holding values of ``dtype`` (the statistics of the entropy and learned
+    adaptive-k methods, adaptive_topk.py:84-127, rounded to ``dtype``)."""
+    _cuda(scores2d)
+    s = scores2d.float()
+    if s.stride(1) != 1:
+        s = s.contiguous()
+    R, n = s.shape
+    out = torch.empty(R, 5, device=s.device, dtype=torch.float32)
+    _lib.call("gsa_row_summary", R, n, _p(s), s.stride(0), dtype_code(dtype), _p(out), _stream())
+    _after("row_summary")
+    return out
+
+
 def topk_candidates(scores2d: torch.Tensor, k_eff: int, Lq: int | None = None, q_pos0: int = 0,
                     causal: bool = False, row_center: torch.Tensor | None = None,
                     row_stats: torch.Tensor | None = None):

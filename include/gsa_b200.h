@@ -167,6 +167,16 @@ int gsa_row_stats(int64_t R, int64_t n_cols, const float* scores, int64_t scores
                   double* row_stats, gsa_stream_t stream);
 
 /*
+ * Per-row statistics for the entropy and learned adaptive-k methods (adaptive_topk.py:84-127), of a
+ * score matrix whose values are of dtype ``dtype`` (stored as fp32; -inf = masked):
+ *   out [R, 5] fp32 = {valid count, mean, unbiased std, max of the masked scores (masked entries
+ *   count as 0 over all n_cols columns), softmax entropy -sum p log(p + 1e-10) over the valid
+ *   entries}, every value but the count rounded to ``dtype`` as the reference's torch ops round it.
+ */
+int gsa_row_summary(int64_t R, int64_t n_cols, const float* scores, int64_t scores_ld, int dtype,
+                    float* out, gsa_stream_t stream);
+
+/*
  * Top-k candidates: for every row r, the k_eff largest finite scores among the first n_r
  * columns, ties broken lower column first, written in ascending column order
  * (the candidate set of adaptive_topk.py:174-177).  n_r = n_cols, or, with ``causal``,

@@ -173,6 +173,37 @@ def adaptive_k_prefloor(var, valid_counts, var_mean, k_base, k_min, k_max, tempe
     return torch.minimum(k_values, valid_counts)
 
 
+def adaptive_k_method(scores: torch.Tensor, method: str, k_base: int, k_min: int, k_max: int,
+                      temperature: float, predictor=None) -> torch.Tensor:
+    """k_t of the ``entropy`` and ``learned`` methods; adaptive_topk.py:84-90 (masks and counts),
+    :104-117 (entropy: softmax entropy of the valid scores over log(count + 1)), :119-127 (learned:
+    [mean, std, max] of the masked scores through the selector's predictor) and :129-133 (clamp).
+    The selector's forward never mixes rows, so rows may come in any grouping."""
+    valid = scores != NEG_INF
+    masked = scores.masked_fill(~valid, 0)
+    valid_counts = valid.sum(dim=-1).float()
+    if method == "entropy":
+        probs = torch.softmax(masked.masked_fill(~valid, NEG_INF), dim=-1).masked_fill(~valid, 0)
+        entropy = -(probs * torch.log(probs + 1e-10)).sum(dim=-1)
+        normalized = entropy / (torch.log(valid_counts + 1) + 1e-8)
+        k_adaptive = k_base * (0.5 + normalized * temperature)
+    elif method == "learned":
+        stats = torch.cat([masked.mean(dim=-1, keepdim=True), masked.std(dim=-1, keepdim=True),
+                           masked.max(dim=-1, keepdim=True).values], dim=-1)
+        k_adaptive = k_min + predictor(stats).squeeze(-1) * (k_max - k_min)
+    else:
+        raise ValueError(f"Unknown adaptive method: {method}")
+    return torch.minimum(torch.clamp(k_adaptive, k_min, k_max), valid_counts).long()
+
+
+def adaptive_method_predictor(state: dict, dtype=torch.float32) -> torch.nn.Module:
+    """The learned method's predictor (adaptive_topk.py:60-66: Linear(3, 32), ReLU, Linear(32, 1),
+    Sigmoid) holding the given weights."""
+    net = torch.nn.Sequential(torch.nn.Linear(3, 32), torch.nn.ReLU(), torch.nn.Linear(32, 1), torch.nn.Sigmoid())
+    net.load_state_dict(state)
+    return net.to(dtype)
+
+
 def topk_select(scores: torch.Tensor, k_eff: int, k_values: torch.Tensor):
     """adaptive_topk.py:174-189: sorted top-k_eff, mask p < k_t and score != -inf."""
     B, Lq, _ = scores.shape

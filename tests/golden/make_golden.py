@@ -17,7 +17,8 @@ Each fixture follows the reference forward step by step
 and checks that the step-by-step output equals ``module(x, positions)`` bit for bit.
 
 The model fixtures run the reference's GSALlamaForCausalLM (gsa/models/gsa_llama.py) the same way; the
-sampling fixture runs its generate() with the model's forward replaced by seeded logits.
+sampling fixture runs its generate() with the model's forward replaced by seeded logits; the
+adaptive fixture runs its AdaptiveTopKSelector with the entropy and learned methods.
 
 Usage:  python tests/golden/make_golden.py [--reference PATH] [--only NAME]
 """
@@ -281,6 +282,48 @@ def make_sampling_fixture(name, spec, refs):
     print(f"{name}: {path.stat().st_size / 1024:.0f} KiB")
 
 
+# name -> (batch, seq_len, k_base, k_min, k_max, temperatures): the reference's AdaptiveTopKSelector
+# with adaptive_method "entropy" and "learned" (adaptive_topk.py:84-133), which the attention layer
+# never selects but the selector module offers
+ADAPTIVE_FIXTURES = {
+    "adaptive_methods_b2_l96": (2, 96, 48, 16, 80, [1.0, 0.6]),
+}
+
+
+def make_adaptive_fixture(name, spec, ref_root: Path):
+    """k_t of the reference selector's entropy and learned methods on seeded indexer-like scores
+    (values in [0, 3], causal -inf mask), fp32 and bf16.  The learned method's predictor is the
+    selector's own seeded initialisation (torch.manual_seed(WEIGHT_SEED) before construction); its
+    weights are stored too."""
+    from gsa.attention.adaptive_topk import AdaptiveTopKSelector
+    B, L, k_base, k_min, k_max, temps = spec
+    gen = torch.Generator().manual_seed(INPUT_SEED)
+    base = torch.rand(B, L, L, generator=gen) * 3
+    causal = torch.triu(torch.ones(L, L, dtype=torch.bool), diagonal=1)
+    base = base.masked_fill(causal, float("-inf"))
+    t = {}
+    for dname in ("float32", "bfloat16"):
+        dt = getattr(torch, dname)
+        scores = base.to(dt)
+        t[f"scores_{dname}"] = scores.clone().contiguous()
+        for method in ("entropy", "learned"):
+            for j, temp in enumerate(temps):
+                torch.manual_seed(WEIGHT_SEED)
+                sel = AdaptiveTopKSelector(k_base=k_base, k_min=k_min, k_max=k_max, use_adaptive=True,
+                                           temperature=temp, adaptive_method=method).to(dt)
+                with torch.no_grad():
+                    _, _, kv = sel(scores, L, L, return_k_values=True)
+                t[f"k_{method}_{dname}_t{j}"] = kv.to(torch.int32).contiguous()
+                if method == "learned" and j == 0:
+                    for pn, pv in sel.k_predictor.state_dict().items():
+                        t[f"pred_{dname}.{pn}"] = pv.clone().contiguous()
+    meta = {"batch": str(B), "seq_len": str(L), "k_base": str(k_base), "k_min": str(k_min),
+            "k_max": str(k_max), "temperatures": json.dumps(temps), "torch": torch.__version__}
+    path = HERE / f"{name}.safetensors"
+    save_file(t, str(path), metadata=meta)
+    print(f"{name}: {path.stat().st_size / 1024:.0f} KiB")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("GSA_REFERENCE", "/root/reference"))
@@ -300,6 +343,10 @@ def main():
         if args.only and name != args.only:
             continue
         make_sampling_fixture(name, spec, refs)
+    for name, spec in ADAPTIVE_FIXTURES.items():
+        if args.only and name != args.only:
+            continue
+        make_adaptive_fixture(name, spec, Path(args.reference))
 
 
 if __name__ == "__main__":

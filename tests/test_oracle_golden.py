@@ -115,3 +115,31 @@ def test_attention_and_output(case):
     rows = g["rows"].long()
     assert torch.equal(res["attn"][:, rows], g["attn"])
     assert torch.equal(res["out"][:, rows], g["out"])
+
+
+# ---- the selector's entropy and learned methods (adaptive_topk.py:104-133) ----
+def _adaptive_golden():
+    from pathlib import Path
+    from safetensors.torch import load_file, safe_open
+    path = Path(__file__).resolve().parent / "golden" / "adaptive_methods_b2_l96.safetensors"
+    with safe_open(str(path), "pt") as f:
+        meta = f.metadata()
+    return load_file(str(path)), meta
+
+
+@pytest.mark.parametrize("dname", ["float32", "bfloat16"])
+@pytest.mark.parametrize("method", ["entropy", "learned"])
+def test_adaptive_methods_match_the_reference(method, dname):
+    import json
+    t, meta = _adaptive_golden()
+    temps = json.loads(meta["temperatures"])
+    kb, kmin, kmax = int(meta["k_base"]), int(meta["k_min"]), int(meta["k_max"])
+    scores = t[f"scores_{dname}"]
+    pred = None
+    if method == "learned":
+        state = {k.split(".", 1)[1]: v.float() for k, v in t.items() if k.startswith(f"pred_{dname}.")}
+        pred = O.adaptive_method_predictor(state, getattr(torch, dname))
+    for j, temp in enumerate(temps):
+        with torch.no_grad():
+            k = O.adaptive_k_method(scores, method, kb, kmin, kmax, temp, pred)
+        assert torch.equal(k.to(torch.int32), t[f"k_{method}_{dname}_t{j}"]), (method, dname, temp)
