@@ -5,8 +5,9 @@ oracle on a longer random case.
 
 k_t truncates a float (adaptive_topk.py:133), and the row statistics sum in a different order than
 torch's CPU kernels (the softmax normaliser, the entropy and the moments), so a k_t may land one
-below or above the reference's where its float value sits on an integer: |dk| <= 1 everywhere and
-at least 95% of the rows equal.  The statistics themselves: within 2 units in the last place of
+below or above the reference's where its float value sits on an integer: |dk| <= 1 everywhere
+(one bf16 step of k for the learned method in bf16, whose k is a bf16 value) and at least 95% of
+the rows equal.  The statistics themselves: within 2 units in the last place of
 the dtype (entropy, std) or exact (count, max)."""
 
 import json
@@ -41,9 +42,13 @@ def _selector(method, dname, t, kb, kmin, kmax, temp):
     return sel.to(dt).to(DEV)
 
 
-def _check_k(k, ref, what):
+def _check_k(k, ref, what, rel=0.0):
+    """|dk| <= max(1, rel * k_ref) everywhere, >= 95% of the rows equal.  The learned method in
+    bf16 forms k = k_min + k_scale (k_max - k_min) in bf16 (adaptive_topk.py:127), so a one-ulp
+    difference of k_scale moves k by one bf16 step of its magnitude: rel = 2^-7 there."""
     d = (k.long().cpu() - ref.long()).abs()
-    assert int(d.max()) <= 1, (what, int(d.max()))
+    tol = torch.clamp((ref.long().abs().double() * rel).ceil().long(), min=1)
+    assert bool((d <= tol).all()), (what, int(d.max()))
     assert float((d == 0).double().mean()) >= 0.95, (what, float((d == 0).double().mean()))
 
 
@@ -63,7 +68,8 @@ def test_adaptive_methods_against_the_reference(cuda_ok, method, dname):
             idx, mask, k = sel(scores.to(DEV), L, L, return_k_values=True)
         torch.cuda.synchronize()
         ops.check_device_error()
-        _check_k(k, t[f"k_{method}_{dname}_t{j}"], (method, dname, temp))
+        _check_k(k, t[f"k_{method}_{dname}_t{j}"], (method, dname, temp),
+                 2.0 ** -7 if (method, dname) == ("learned", "bfloat16") else 0.0)
         # the mask keeps k_t of each row's candidates
         assert torch.equal(mask.sum(-1).cpu(), k.cpu().to(mask.sum(-1).dtype))
 
@@ -95,7 +101,10 @@ def test_row_summary_statistics(cuda_ok, dname):
 
 
 def test_adaptive_methods_against_the_oracle_2048(cuda_ok):
-    """A longer case (2 x 2048 rows) for both methods in bf16: k_t vs the oracle."""
+    """A longer case (2 x 2048 rows) for both methods in bf16: k_t vs the oracle's torch ops run on
+    the same GPU, so that the learned method's predictor (a bf16 Linear, whose rounding differs
+    between the CPU and the GPU GEMM) is the same computation on both sides and only the native row
+    statistics are under test."""
     t, _ = _golden()
     L = 2048
     g = torch.Generator().manual_seed(4)
@@ -108,6 +117,6 @@ def test_adaptive_methods_against_the_oracle_2048(cuda_ok):
             pred = None
             if method == "learned":
                 state = {k2.split(".", 1)[1]: v.float() for k2, v in t.items() if k2.startswith("pred_bfloat16.")}
-                pred = O.adaptive_method_predictor(state, torch.bfloat16)
-            ref = O.adaptive_k_method(s, method, 512, 128, 1024, 0.8, pred)
-        _check_k(k, ref, method)
+                pred = O.adaptive_method_predictor(state, torch.bfloat16).to(DEV)
+            ref = O.adaptive_k_method(s.to(DEV), method, 512, 128, 1024, 0.8, pred).cpu()
+        _check_k(k, ref, method, 2.0 ** -7 if method == "learned" else 0.0)
