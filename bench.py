@@ -250,6 +250,50 @@ def indexer_roofline(cap, cfg, pk, chunk_bytes=4 << 30, reps=2):
                                  "maximum SM clock"}}
 
 
+def proj_roofline(m, x, pk, reps=3):
+    """The fused projection GEMM (all projections + RoPE, G2, G1 gate, q^I / k^I, w in its epilogue)
+    timed alone on this rank's input: algorithmic flops 2 * T * d_model * N (N = the regrouped
+    weight rows) against the measured bf16 GEMM peak, and the bytes it must move (x and the
+    weights read, its outputs written) against the HBM peak.  None when the layer does not take
+    the fused path (fp32, or shapes it declines)."""
+    from gsa_b200 import ops
+
+    B, L, d = x.shape
+    dims = m._step_constants()[0]
+    Wp, bp = m.fused_projection_tiles()
+    sp = m.query_shards
+    pos = (sp.positions(L, x.device) if sp is not None else torch.arange(L, device=x.device)).unsqueeze(0)
+    pos = pos.expand(B, -1)
+    xs = x.reshape(B * L, d)
+
+    def run():
+        return ops.proj_fused(dims, Wp, bp, xs, B, L, pos, m.rotary_emb.cos_cached, m.rotary_emb.sin_cached)
+
+    with torch.no_grad():
+        if run() is None:
+            return None
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            run()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    cfg = m.config
+    T, N = B * L, Wp.shape[0]
+    flops = 2.0 * T * d * N
+    H, Hk, D, HI, dI = cfg.n_heads, cfg.n_kv_heads, m.d_head, cfg.n_indexer_heads, cfg.d_indexer
+    out_bytes = T * ((2 * H * D + 2 * Hk * D + HI * dI + dI) * 2 + 4 * (HI + 1))
+    nbytes = T * d * 2 + N * d * 2 + out_bytes
+    achieved = flops / (ms / 1e3) / 1e12
+    return {"kernel": "pg::proj_gemm_kernel", "bound": "tensor", "achieved": round(achieved, 1),
+            "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": round(achieved / pk["bf16_tflops"], 4),
+            "algorithmic_flops": flops, "kernel_ms": round(ms, 3),
+            "bytes": nbytes, "hbm_frac": round(nbytes / (ms / 1e3) / 1e9 / pk["hbm_gbs"], 4),
+            "note": "timed alone (3 launches); the peak is the measured cuBLAS bf16 burst figure"}
+
+
 SDPA_TRAFFIC = ROOT / "profiles" / "sparse_sdpa_traffic.json"
 SDPA_SOURCE = ROOT / "gated-sparse-attention_b200" / "csrc" / "sparse_sdpa.cu"
 
@@ -487,6 +531,7 @@ def run_ours(args, world, rank):
                              args.workload, B, L, world)
 
     roofline_indexer = indexer_roofline(cap, cfg, pk)
+    roofline_proj = proj_roofline(m, x, pk)
     x_mib = B * L * cfg.d_model * 2 / 2**20
     kv_mib = B * L * cfg.n_kv_heads * cfg.d_head * 2 / 2**20
     res = {
@@ -502,7 +547,7 @@ def run_ours(args, world, rank):
                                    if world > 1 else ""),
                    "l2": (f"inputs larger than L2 (x {x_mib:.0f} MiB, K/V {kv_mib:.0f} MiB each)"
                           if x_mib > 126 else f"x {x_mib:.0f} MiB: L2 not flushed between steps")},
-        "e2e": e2e, "roofline": roofline, "roofline_indexer": roofline_indexer,
+        "e2e": e2e, "roofline": roofline, "roofline_indexer": roofline_indexer, "roofline_proj": roofline_proj,
         "gpu_launches": launches_per_step * args.steps,
         "stages_ms": stages, "clocks": clocks,
     }
