@@ -896,9 +896,8 @@ class GatedSparseAttention(nn.Module):
         else:
             max_pos = int(positions.max().item())  # the reference syncs here too (rope.py:133-134)
         self.rotary_emb.ensure(max_pos + 1)
-        W, bvec, layout = self.fused_projection()
-        if W.dtype != dt:
-            raise RuntimeError(f"layer parameters are {W.dtype} but the input is {dt}")
+        if self.q_proj.weight.dtype != dt:
+            raise RuntimeError(f"layer parameters are {self.q_proj.weight.dtype} but the input is {dt}")
         dims = self._step_constants()[0]
 
         # the KV cache store the new tokens' K, V and k^I are written into (None: a fresh
@@ -932,6 +931,9 @@ class GatedSparseAttention(nn.Module):
                                    kv_out=store.kv[:, past_len:past_len + L] if store is not None else None,
                                    ki_out=store.ki[:, past_len:past_len + L] if store is not None else None)
         if fused is None:
+            # the stacked weights are built (and kept) only for the paths that use them, so a layer on
+            # the fused GEMM holds one copy of its weights in the GEMM's row order, not two
+            W, bvec, layout = self.fused_projection()
             proj = torch.addmm(bvec, x.reshape(B * L, self.d_model), W.t())
         if not self.training:
             # the gates' analysis output (last_gate_scores), computed from their logits when read
