@@ -267,3 +267,28 @@ def test_shard_bounds():
     assert shard_bounds(10, 2, 0) == (0, 5)
     with pytest.raises(ValueError):
         shard_bounds(10, 3, 0)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("folds", [1, 3, 4])
+@pytest.mark.parametrize("B", [1, 2])
+def test_sequence_order_of_gathered_zigzag_shards(world, folds, B):
+    """The gathered shards of every rank (rank order, as all_gather_into_tensor lays them out) put
+    back into sequence order equal the full sequence, for the zigzag layout at 2-8 ranks (the
+    permutation the 8-GPU runs use) and for contiguous blocks."""
+    from gsa_b200.sharded import QueryShards, zigzag_slice
+
+    L = 2 * folds * world * 3
+    full = torch.arange(B * L * 2, dtype=torch.float32).view(B, L, 2)
+    for layout in ("zigzag", "contiguous"):
+        if layout == "zigzag" and B != 1:
+            continue
+        qs = object.__new__(QueryShards)
+        qs.world, qs.layout, qs.folds, qs._perm, qs._side = world, layout, folds, {}, None
+        if layout == "zigzag":
+            shards = [zigzag_slice(full, world, r, folds) for r in range(world)]
+        else:
+            shards = [full[:, r * (L // world):(r + 1) * (L // world)] for r in range(world)]
+        buf = torch.cat(shards, dim=0)  # [world * B, L_local, 2]
+        out = qs._sequence_order(buf, shards[0])
+        assert torch.equal(out, full), (layout, world, folds, B)
