@@ -76,8 +76,10 @@ __device__ __forceinline__ int row_count(const SdpaArgs& a, int64_t row) {
   return c;
 }
 
+// One CTA per SM (its copy ring takes the shared memory): telling the compiler so lets it allocate the
+// registers for that occupancy (102 instead of 96 at D 128, 14 warps; 81.5 -> 79.5 ms at 128K tokens).
 template <int D, int NREP, int MAXW>
-__global__ void __launch_bounds__(MAXW * 32) sdpa_tc_kernel(SdpaArgs a) {
+__global__ void __launch_bounds__(MAXW * 32, 1) sdpa_tc_kernel(SdpaArgs a) {
   chain_wait();
   chain_release();
   static_assert(D % 16 == 0 && NREP >= 1 && NREP <= 8, "tile shape");
