@@ -177,11 +177,16 @@ int gsa_proj_fused(const gsa_dims* dims, int dtype, int64_t T, int64_t L, const 
   return launch_proj_gemm(a, di->num_sms, reinterpret_cast<cudaStream_t>(stream));
 }
 
-int gsa_indexer_scores(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int64_t Lkv, int64_t q_pos0,
-                       int causal, int write_masked, const void* qI, int64_t qi_ld, int64_t qi_bstride,
-                       const void* kI, int64_t ki_ld, int64_t ki_bstride, const float* w, const float* bias,
-                       float scale, const float* shift, float* scores, int64_t scores_ld, double* row_stats,
-                       gsa_stream_t stream) {
+}  // extern "C"
+
+// gsa_indexer_scores with, optionally, room for the tensor-core path's per-key-range statistic
+// partials ([Lq, indexer_tc_stat_ranges(Lkv), 3] doubles, reused per batch row), which makes the row
+// statistics the same bits on every run.
+static int indexer_scores_impl(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int64_t Lkv, int64_t q_pos0,
+                               int causal, int write_masked, const void* qI, int64_t qi_ld, int64_t qi_bstride,
+                               const void* kI, int64_t ki_ld, int64_t ki_bstride, const float* w,
+                               const float* bias, float scale, const float* shift, float* scores,
+                               int64_t scores_ld, double* row_stats, double* stat_part, gsa_stream_t stream) {
   if (!dims_ok(dims) || B < 0 || Lq < 0 || Lkv < 0 || (dtype != GSA_DTYPE_F32 && dtype != GSA_DTYPE_BF16))
     return GSA_ERR_BAD_ARG;
   if (B == 0 || Lq == 0 || Lkv == 0) return GSA_OK;
@@ -211,12 +216,25 @@ int gsa_indexer_scores(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, i
       ab.shift = shift ? shift + b * Lq : nullptr;
       ab.scores = scores + b * Lq * scores_ld;
       ab.row_stats = row_stats ? row_stats + b * Lq * 3 : nullptr;
+      ab.stat_part = stat_part;
       st = launch_indexer_tc(ab, di->err, s);
       if (st) return st;
     }
     return GSA_OK;
   }
   return launch_indexer_simt(a, B, s);
+}
+
+extern "C" {
+
+int gsa_indexer_scores(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int64_t Lkv, int64_t q_pos0,
+                       int causal, int write_masked, const void* qI, int64_t qi_ld, int64_t qi_bstride,
+                       const void* kI, int64_t ki_ld, int64_t ki_bstride, const float* w, const float* bias,
+                       float scale, const float* shift, float* scores, int64_t scores_ld, double* row_stats,
+                       gsa_stream_t stream) {
+  return indexer_scores_impl(dims, dtype, B, Lq, Lkv, q_pos0, causal, write_masked, qI, qi_ld, qi_bstride, kI,
+                             ki_ld, ki_bstride, w, bias, scale, shift, scores, scores_ld, row_stats, nullptr,
+                             stream);
 }
 
 int gsa_row_stats(int64_t R, int64_t n_cols, const float* scores, int64_t scores_ld, double* row_stats,
@@ -491,9 +509,10 @@ static int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
 
 int64_t gsa_survivors_workspace_size(int64_t chunk_rows, int64_t n_cols) {
   if (chunk_rows <= 0 || n_cols <= 0) return 0;
-  // score scratch, failed-row list, its count, per-row segment counts (few-row compaction)
+  // score scratch, failed-row list, its count, per-row segment counts (few-row compaction), the
+  // indexer's per-key-range statistic partials
   return align256(gsa_workspace_size(chunk_rows, n_cols)) + align256(chunk_rows * 4) + 256 +
-         align256(chunk_rows * 16 * 4);
+         align256(chunk_rows * 16 * 4) + align256(chunk_rows * indexer_tc_stat_ranges(n_cols) * 3 * 8);
 }
 
 int gsa_indexer_survivors(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int64_t Lkv, int64_t q_pos0,
@@ -521,6 +540,7 @@ int gsa_indexer_survivors(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq
   int32_t* fail_list = reinterpret_cast<int32_t*>(wsb + align256(gsa_workspace_size(chunk_rows, Lkv)));
   int32_t* fail_count = fail_list + align256(chunk_rows * 4) / 4;
   int32_t* seg_count = fail_count + 256 / 4;
+  double* stat_part = reinterpret_cast<double*>(reinterpret_cast<uint8_t*>(seg_count) + align256(chunk_rows * 16 * 4));
   const size_t esz = dtype == GSA_DTYPE_BF16 ? 2 : 4;
   const int HI = dims->n_idx_heads;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
@@ -528,9 +548,9 @@ int gsa_indexer_survivors(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq
     const int64_t r0 = c.b0 * Lq + c.t0, n = c.nb * c.n;
     const void* q_ptr = static_cast<const char*>(qI) + (c.b0 * qi_bstride + c.t0 * qi_ld) * (int64_t)esz;
     const void* k_ptr = static_cast<const char*>(kI) + (c.b0 * ki_bstride) * (int64_t)esz;
-    st = gsa_indexer_scores(dims, dtype, c.nb, c.n, Lkv, q_pos0 + c.t0, causal, 0, q_ptr, qi_ld, qi_bstride, k_ptr,
-                            ki_ld, ki_bstride, w + r0 * HI, bias, scale, shift + r0, scratch, ld, row_stats + r0 * 3,
-                            stream);
+    st = indexer_scores_impl(dims, dtype, c.nb, c.n, Lkv, q_pos0 + c.t0, causal, 0, q_ptr, qi_ld, qi_bstride, k_ptr,
+                             ki_ld, ki_bstride, w + r0 * HI, bias, scale, shift + r0, scratch, ld,
+                             row_stats + r0 * 3, stat_part, stream);
     if (st) return st;
     st = launch_threshold_candidates(n, c.n, Lkv, q_pos0 + c.t0, causal, scratch, ld, shift + r0, row_stats + r0 * 3,
                                      k_eff, cap, cand_idx + r0 * cap, cand_score + r0 * cap, cand_count + r0,

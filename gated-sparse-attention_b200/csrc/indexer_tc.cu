@@ -41,7 +41,7 @@ constexpr int kThreads = 576;
 constexpr int kEpiWarps = 16;
 constexpr int kATileBytes = kKeys * kDI * 2;  // 16 KiB
 constexpr int kBTileBytes = kN * kDI * 2;     // 32 KiB
-constexpr int kSmemBytes = 1024 + kBTileBytes + kStages * kATileBytes + kN * 4 + 2 * 64 * 4 + 256;
+constexpr int kSmemBytes = 1024 + kBTileBytes + kStages * kATileBytes + kN * 4 + 2 * 64 * 4 + 256 + 4 * 64 * 8;
 
 struct Params {
   int n_rows;
@@ -55,6 +55,8 @@ struct Params {
   float* scores;
   int64_t ld;
   double* row_stats;
+  double* stat_part;   // [n_rows, n_ranges, 3] per-key-range partials, or NULL (fp64 atomics)
+  int64_t n_ranges;
   int* err;
 };
 
@@ -133,6 +135,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* t_full = b_full + 1;
   uint64_t* t_empty = t_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(t_empty + 2);
+  float2* stat_s = reinterpret_cast<float2*>(bars + 32);  // [4 quarters][TOK] per-warp statistic sums
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -263,7 +266,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-    // row statistics: reduce the 32 keys of this warp, one fp64 atomic per token and value
+    // row statistics: reduce the 32 keys of this warp; then either one fp64 atomic per token and
+    // value, or (deterministic) the four lane quarters summed in a fixed order into this CTA's
+    // key-range partial of each token
     if (p.row_stats) {
       const int64_t k_lo = (int64_t)t_begin * kKeys;
       const int64_t k_hi = min((int64_t)t_end * kKeys, p.Lkv);
@@ -276,7 +281,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           b += __shfl_xor_sync(0xffffffffu, b, o);
         }
         const int ti = sub * TOK_Q + tl;
-        if (lane == 0 && ti < ntok) {
+        if (p.stat_part) {
+          if (lane == 0) stat_s[quarter * TOK + ti] = make_float2(a, b);
+        } else if (lane == 0 && ti < ntok) {
           double* st = p.row_stats + (int64_t)(tok0 + ti) * 3;
           atomicAdd(st + 0, (double)a);
           atomicAdd(st + 1, (double)b);
@@ -285,6 +292,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             int64_t cnt = hi_k > k_lo ? hi_k - k_lo : 0;
             atomicAdd(st + 2, (double)cnt);
           }
+        }
+      }
+      if (p.stat_part) {
+        asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");  // the epilogue warps only
+        const int ti = threadIdx.x - 64;
+        if (ti < ntok) {
+          double a = 0.0, b = 0.0;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 v = stat_s[q * TOK + ti];
+            a += (double)v.x;
+            b += (double)v.y;
+          }
+          const int64_t hi_k = p.causal ? min(k_hi, pos0 + ti + 1) : k_hi;
+          double* pt = p.stat_part + ((int64_t)(tok0 + ti) * p.n_ranges + blockIdx.x) * 3;
+          pt[0] = a;
+          pt[1] = b;
+          pt[2] = (double)(hi_k > k_lo ? hi_k - k_lo : 0);
         }
       }
     }
@@ -298,10 +323,32 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// Row statistics from the key-range partials, summed in range order (the same order every run):
+// row_stats[r] += sum_j part[r][j].  Ranges a causal row never reached hold zeros.
+__global__ void stat_reduce_kernel(int64_t rows, int64_t n_ranges, const double* part, double* row_stats) {
+  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  double a = 0.0, b = 0.0, c = 0.0;
+  const double* pr = part + r * n_ranges * 3;
+  for (int64_t j = 0; j < n_ranges; ++j) {
+    a += pr[3 * j];
+    b += pr[3 * j + 1];
+    c += pr[3 * j + 2];
+  }
+  row_stats[r * 3] += a;
+  row_stats[r * 3 + 1] += b;
+  row_stats[r * 3 + 2] += c;
+}
+
 // ---------------------------------------------------------------------------------------------
 // host side: tensor maps and launch
 // ---------------------------------------------------------------------------------------------
 }  // namespace tc
+
+int64_t indexer_tc_stat_ranges(int64_t Lkv) {
+  const int64_t tiles = (Lkv + tc::kKeys - 1) / tc::kKeys;
+  return (tiles + tc::kTilesPerCta - 1) / tc::kTilesPerCta;
+}
 
 bool indexer_tc_eligible(const IdxArgs& a) {
   const bool hi_ok = a.HI == 8 || a.HI == 4;
@@ -349,6 +396,8 @@ int launch_indexer_tc(const IdxArgs& a, int* err, cudaStream_t stream) {
   p.scores = a.scores;
   p.ld = a.scores_ld;
   p.row_stats = a.row_stats;
+  p.stat_part = a.row_stats ? a.stat_part : nullptr;
+  p.n_ranges = indexer_tc_stat_ranges(a.Lkv);
   p.err = err;
   const int64_t nb = (a.Lq + TOK - 1) / TOK;
   const int64_t key_limit = a.causal ? std::min<int64_t>(a.Lkv, a.q_pos0 + a.Lq) : a.Lkv;
@@ -357,6 +406,9 @@ int launch_indexer_tc(const IdxArgs& a, int* err, cudaStream_t stream) {
   if (nb == 0 || ranges == 0) return GSA_OK;
   if (nb > 65535 || ranges > 0x7fffffffLL) return GSA_ERR_BAD_ARG;
   dim3 grid((unsigned)ranges, (unsigned)nb);
+  if (p.stat_part &&
+      cudaMemsetAsync(p.stat_part, 0, (size_t)a.Lq * p.n_ranges * 3 * sizeof(double), stream) != cudaSuccess)
+    return GSA_ERR_CUDA;
   if (a.HI == 8) {
     if (cudaFuncSetAttribute(indexer_tc_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
         cudaSuccess)
@@ -368,7 +420,13 @@ int launch_indexer_tc(const IdxArgs& a, int* err, cudaStream_t stream) {
       return GSA_ERR_LAUNCH;
     indexer_tc_kernel<4><<<grid, kThreads, kSmemBytes, stream>>>(tmK, tmQ, p);
   }
-  return cudaGetLastError() == cudaSuccess ? GSA_OK : GSA_ERR_LAUNCH;
+  if (cudaGetLastError() != cudaSuccess) return GSA_ERR_LAUNCH;
+  if (p.stat_part) {
+    stat_reduce_kernel<<<(unsigned)((a.Lq + 255) / 256), 256, 0, stream>>>(a.Lq, p.n_ranges, p.stat_part,
+                                                                          a.row_stats);
+    if (cudaGetLastError() != cudaSuccess) return GSA_ERR_LAUNCH;
+  }
+  return GSA_OK;
 }
 
 }  // namespace gsa

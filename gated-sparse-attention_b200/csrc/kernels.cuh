@@ -68,7 +68,12 @@ struct IdxArgs {
   float* scores;
   int64_t scores_ld;
   double* row_stats;
+  // Deterministic row statistics (tensor-core path): per-(row, key range) partials [Lq, ranges, 3],
+  // summed into row_stats in range order after the launch.  NULL: fp64 atomics (summation order
+  // varies run to run in the last bits).
+  double* stat_part = nullptr;
 };
+int64_t indexer_tc_stat_ranges(int64_t Lkv);  // key ranges per row of the tensor-core indexer
 
 struct SdpaArgs {
   int64_t B, Lq, Lkv;

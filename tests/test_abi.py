@@ -68,7 +68,9 @@ def test_survivor_entry_points_validate_before_any_launch():
 
     lib = _lib.lib()
     ld = (1000 + 3) // 4 * 4
-    assert lib.gsa_survivors_workspace_size(16, 1000) == ((16 * ld * 4 + 255) // 256) * 256 + 256 + 256 + 1024
+    # score scratch, failed rows, their count, segment counts, the indexer's per-key-range
+    # statistic partials (16 rows x 1 range of 32 key tiles x 3 doubles)
+    assert lib.gsa_survivors_workspace_size(16, 1000) == ((16 * ld * 4 + 255) // 256) * 256 + 256 + 256 + 1024 + 512
     assert lib.gsa_survivors_workspace_size(0, 1000) == 0
     dims = ops.make_dims(4096, 32, 8, 128, 8, 64)
     relu = ops.make_dims(4096, 32, 8, 128, 8, 64, idx_act="relu")

@@ -167,3 +167,23 @@ def test_every_row_k_t_from_recomputed_variance(shape):
             k_own = O.adaptive_k(var_ours[b:b + 1], valid[b:b + 1], own, cfg.k_base, cfg.k_min, cfg.k_max, 1.0)[0]
             print(f"{name}: sequence {b}: own mean {float(own):.6g} vs batch mean {float(mean):.6g}; "
                   f"{int((k_own != ours[b]).sum())} rows would take another k_t")
+
+
+def test_repeated_forwards_are_bit_identical(shape):
+    """Three more forwards of the same input give the first forward's selection, k_t and output bit
+    for bit: the indexer's per-row statistics are summed in a fixed order (per key-range partials,
+    not fp64 atomics), so no row's variance can round differently from run to run."""
+    from gsa_b200 import ops
+
+    name, B, L, cfg, m, cap = shape
+    x = torch.randn(B, L, 4096, generator=torch.Generator().manual_seed(1)).to(DEV, torch.bfloat16)
+    for _ in range(3):
+        c2 = {}
+        with torch.no_grad():
+            m._forward_impl(x, None, None, False, False, capture=c2)
+        torch.cuda.synchronize()
+        ops.check_device_error()
+        assert torch.equal(c2["k_t"], cap["k_t"]), name
+        assert torch.equal(c2["cnt"], cap["cnt"]), name
+        assert torch.equal(c2["attn"], cap["attn"]), name
+        del c2
