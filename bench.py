@@ -505,11 +505,11 @@ def run_ours(args, world, rank):
                          "sdpa_keys_busiest_over_mean": round(max(allk) / (sum(allk) / world), 4),
                          "note": "stages_ms is rank 0's; kv = the blocking k^I all-gather and the start of the "
                                  "asynchronous K/V all-gather; kv_gather_wait = the wait for K/V before the SDPA"}
-    # our kernels per forward: the projection epilogue; per query chunk the indexer and the
-    # candidate pass (survivor compaction + exact fallback, or the exact top-k); row variance
-    # (2) and adaptive k; the final selection; the SDPA
+    # our kernels per forward: the fused projection GEMM; per query chunk the indexer and the
+    # candidate pass (the indexer's ordered statistics sum, survivor compaction + exact fallback,
+    # or the exact top-k); row variance (2) and adaptive k; the final selection; the SDPA
     n_chunks = cap["n_chunks"]
-    per_chunk = 3 if cap.get("candidate_path") == "survivors" else 2
+    per_chunk = 4 if cap.get("candidate_path") == "survivors" else 2
     launches_per_step = 1 + per_chunk * n_chunks + (3 if cfg.use_adaptive_k else 1) + 1 + 1
     sdpa_bytes = sdpa_algorithmic_bytes(cfg, cap["cnt"])
     reps = 3

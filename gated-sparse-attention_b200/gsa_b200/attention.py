@@ -1022,10 +1022,12 @@ class GatedSparseAttention(nn.Module):
                      and ops.survivors_eligible(dims, k_eff, True))
         select_fn = ops.indexer_survivors if survivors else ops.indexer_select
         cand_ld = ops.SURVIVOR_CAP if survivors else k_eff
+        n_chunks = 0  # indexer launches (query chunks) of this forward, for the launch count
         if len(segs) == 1:
             cand_idx, cand_score, cand_count, stats = select_fn(
                 dims, qI, kI_all, w, self.indexer.bias, self.indexer.scale, shift, k_eff,
                 q_pos0=q_pos0, causal=True)
+            n_chunks = ops.last_chunk_count
         else:
             # one indexer pass per query segment, each with its own causal offset
             R = B * L
@@ -1039,6 +1041,7 @@ class GatedSparseAttention(nn.Module):
                           self.indexer.scale, shift[l0:l0 + n], k_eff, q_pos0=p0, causal=True,
                           row_stats=stats[l0:l0 + n],
                           out=(cand_idx[l0:l0 + n], cand_score[l0:l0 + n], cand_count[l0:l0 + n]))
+                n_chunks += ops.last_chunk_count
         mark("indexer_topk")
         if cfg.use_adaptive_k:
             var, total = ops.row_variance(stats, n_cols, dt, shift)
@@ -1081,7 +1084,7 @@ class GatedSparseAttention(nn.Module):
                            idx_segments=list(segs) if len(segs) > 1 else [(0, L, q_pos0)])
             capture.update(dims=dims, q=q, k=k_all, v=v_all, sel=sel, cnt=cnt, gate=g1, k_t=kt, attn=attn,
                            var=var, var_total=total,
-                           n_chunks=ops.last_chunk_count, candidate_path="survivors" if survivors else "exact")
+                           n_chunks=n_chunks, candidate_path="survivors" if survivors else "exact")
 
         weights = None
         if output_attentions:
