@@ -506,10 +506,16 @@ def run_ours(args, world, rank):
                          "note": "stages_ms is rank 0's; kv = the blocking k^I all-gather and the start of the "
                                  "asynchronous K/V all-gather; kv_gather_wait = the wait for K/V before the SDPA"}
     # our kernels per forward: the fused projection GEMM; per query chunk the indexer and the
-    # candidate pass (the indexer's ordered statistics sum, survivor compaction + exact fallback,
-    # or the exact top-k); row variance (2) and adaptive k; the final selection; the SDPA
+    # candidate pass -- fused survivors: the sampled-statistics pass, the survivor-emitting pass, its
+    # ordered statistics sum, the segment join, the failed blocks' recomputation and the exact
+    # fallback; materialised survivors: the scores, the ordered statistics sum, the compaction and
+    # the fallback; exact: the scores and the top-k -- row variance (2) and adaptive k; the final
+    # selection; the SDPA
     n_chunks = cap["n_chunks"]
-    per_chunk = 4 if cap.get("candidate_path") == "survivors" else 2
+    if cap.get("candidate_path") != "survivors":
+        per_chunk = 2
+    else:
+        per_chunk = 6 if cap.get("survivor_pass") == "fused" else 4
     launches_per_step = 1 + per_chunk * n_chunks + (3 if cfg.use_adaptive_k else 1) + 1 + 1
     sdpa_bytes = sdpa_algorithmic_bytes(cfg, cap["cnt"])
     reps = 3

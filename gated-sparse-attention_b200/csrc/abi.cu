@@ -560,6 +560,140 @@ int gsa_indexer_survivors(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq
   return GSA_OK;
 }
 
+// ---- the fused survivor pass ----
+static gsa::SurvivorShape survivor_shape(int32_t k_eff, int32_t cap) {
+  gsa::SurvivorShape sv;
+  sv.K = k_eff;
+  sv.cap = cap;
+  sv.K14 = (int32_t)((14LL * k_eff + 9) / 10);
+  return sv;
+}
+
+// Entries of a row's segment area for rows of n_lo..n_hi keys: the most any of them needs.
+static int64_t survivor_stride(const gsa::SurvivorShape& sv, int64_t n_lo, int64_t n_hi) {
+  using gsa::SurvivorShape;
+  int64_t best = 0;
+  if (n_lo < 1) n_lo = 1;
+  for (int64_t b = SurvivorShape::ranges(n_lo); b <= SurvivorShape::ranges(n_hi); ++b) {
+    // seg_cap falls with n inside a block of equal range counts: its first n holds the block's most
+    const int64_t n = std::max<int64_t>(n_lo, (b - 1) * SurvivorShape::kRangeKeys + 1);
+    if (n > n_hi) break;
+    best = std::max<int64_t>(best, b * sv.seg_cap(n));
+  }
+  return best;
+}
+
+int64_t gsa_survivors_fused_workspace_size(int64_t chunk_rows, int64_t n_cols, int32_t k_eff, int32_t cap) {
+  if (chunk_rows <= 0 || n_cols <= 0 || k_eff < 1 || cap < k_eff) return 0;
+  const gsa::SurvivorShape sv = survivor_shape(k_eff, cap);
+  const int64_t stride = survivor_stride(sv, 1, n_cols);
+  // the materialised pass's workspace (its scratch takes the recomputed blocks), the sampled
+  // statistics, the segment counts, the segments' columns and scores, the failed-block flags
+  return gsa_survivors_workspace_size(chunk_rows, n_cols) + align256(chunk_rows * 3 * 8) +
+         align256(chunk_rows * indexer_tc_stat_ranges(n_cols) * 4) + 2 * align256(chunk_rows * stride * 4) +
+         align256(chunk_rows * 4 + 4);
+}
+
+int gsa_indexer_survivors_fused(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq, int64_t Lkv, int64_t q_pos0,
+                                int causal, const void* qI, int64_t qi_ld, int64_t qi_bstride, const void* kI,
+                                int64_t ki_ld, int64_t ki_bstride, const float* w, const float* bias, float scale,
+                                const float* shift, int32_t k_eff, int32_t cap, int32_t* cand_idx,
+                                float* cand_score, int32_t* cand_count, double* row_stats, int64_t chunk_rows,
+                                void* workspace, int64_t workspace_bytes, gsa_stream_t stream) {
+  if (!dims_ok(dims) || B < 0 || Lq < 0 || Lkv < 0 || chunk_rows <= 0 || k_eff < 1 || cap < k_eff)
+    return GSA_ERR_BAD_ARG;
+  if (B * Lq == 0 || Lkv == 0) return GSA_OK;
+  if (!shift || !row_stats || !cand_idx || !cand_score || !cand_count || !w || !bias || !qI || !kI)
+    return GSA_ERR_BAD_ARG;
+  if (dims->idx_act != GSA_ACT_SIGMOID || 2 * (int64_t)cap < 3 * (int64_t)k_eff + 2048) return GSA_ERR_UNSUPPORTED;
+  {
+    IdxArgs probe{dtype, Lq, Lkv, q_pos0, causal, 0, dims->n_idx_heads, dims->d_idx, dims->idx_act,
+                  qI, qi_ld, qi_bstride, kI, ki_ld, ki_bstride, w, bias, scale, shift, nullptr, 0, row_stats};
+    if (dims->n_idx_heads != 8 || !indexer_tc_eligible(probe)) return GSA_ERR_UNSUPPORTED;
+  }
+  if (!workspace || !aligned(workspace, 256) ||
+      workspace_bytes < gsa_survivors_fused_workspace_size(chunk_rows, Lkv, k_eff, cap))
+    return GSA_ERR_WORKSPACE;
+  DeviceInfo dinfo, *di = &dinfo;
+  int st = device_info(di);
+  if (st) return st;
+  const gsa::SurvivorShape sv = survivor_shape(k_eff, cap);
+  const int64_t stride = survivor_stride(sv, 1, Lkv);
+  const int64_t n_ranges = indexer_tc_stat_ranges(Lkv);
+  const int64_t ld = (Lkv + 3) / 4 * 4;
+  uint8_t* wsb = static_cast<uint8_t*>(workspace);
+  float* scratch = reinterpret_cast<float*>(wsb);
+  int32_t* fail_list = reinterpret_cast<int32_t*>(wsb + align256(gsa_workspace_size(chunk_rows, Lkv)));
+  int32_t* fail_count = fail_list + align256(chunk_rows * 4) / 4;
+  int32_t* seg_count = fail_count + 256 / 4;
+  double* stat_part = reinterpret_cast<double*>(reinterpret_cast<uint8_t*>(seg_count) + align256(chunk_rows * 16 * 4));
+  uint8_t* tail = wsb + gsa_survivors_workspace_size(chunk_rows, Lkv);
+  double* samp = reinterpret_cast<double*>(tail);
+  tail += align256(chunk_rows * 3 * 8);
+  int32_t* seg_cnt = reinterpret_cast<int32_t*>(tail);
+  tail += align256(chunk_rows * n_ranges * 4);
+  int32_t* seg_idx = reinterpret_cast<int32_t*>(tail);
+  tail += align256(chunk_rows * stride * 4);
+  float* seg_score = reinterpret_cast<float*>(tail);
+  tail += align256(chunk_rows * stride * 4);
+  int32_t* blk_flag = reinterpret_cast<int32_t*>(tail);
+  const int HI = dims->n_idx_heads;
+  const int32_t blk_rows = gsa::kTcQueryBlock8;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  for (ChunkIter c(B, Lq, chunk_rows); c.next();) {
+    const int64_t r0 = c.b0 * Lq + c.t0, n = c.nb * c.n;
+    const int64_t blks = (c.n + blk_rows - 1) / blk_rows;
+    if (cudaMemsetAsync(samp, 0, (size_t)n * 3 * sizeof(double), s) != cudaSuccess ||
+        cudaMemsetAsync(blk_flag, 0, (size_t)(c.nb * blks + 1) * sizeof(int32_t), s) != cudaSuccess ||
+        cudaMemsetAsync(fail_count, 0, sizeof(int32_t), s) != cudaSuccess)
+      return GSA_ERR_CUDA;
+    for (int pass = 0; pass < 3; ++pass) {
+      // 0: sampled statistics; 1: statistics + survivors; 2: scores of the failed rows' blocks
+      for (int64_t b = 0; b < c.nb; ++b) {
+        const int64_t rb = r0 + b * c.n;  // first row of this sequence's slice, over all rows
+        const int64_t lb = b * c.n;       // the same, within the chunk
+        const void* q_ptr = static_cast<const __nv_bfloat16*>(qI) + (c.b0 + b) * qi_bstride + c.t0 * qi_ld;
+        const void* k_ptr = static_cast<const __nv_bfloat16*>(kI) + (c.b0 + b) * ki_bstride;
+        IdxArgs a{dtype, c.n, Lkv, q_pos0 + c.t0, causal, 0, HI, dims->d_idx, dims->idx_act, q_ptr, qi_ld, qi_bstride,
+                  k_ptr, ki_ld, ki_bstride, w + rb * HI, bias, scale, shift + rb, nullptr, ld, nullptr};
+        gsa::TcSurvivorArgs x;
+        int mode;
+        if (pass == 0) {
+          mode = gsa::kTcSample;
+          a.row_stats = samp + lb * 3;
+        } else if (pass == 1) {
+          mode = gsa::kTcEmit;
+          a.row_stats = row_stats + rb * 3;
+          a.stat_part = stat_part;
+          x.samp_stats = samp + lb * 3;
+          x.seg_idx = seg_idx + lb * stride;
+          x.seg_score = seg_score + lb * stride;
+          x.seg_cnt = seg_cnt + lb * n_ranges;
+          x.seg_stride = stride;
+          x.sv = sv;
+        } else {
+          mode = gsa::kTcScores;
+          a.scores = scratch + lb * ld;
+          x.blk_mask = blk_flag + b * blks;
+        }
+        st = launch_indexer_tc_mode(a, mode, x, di->err, s);
+        if (st) return st;
+      }
+      if (pass == 1) {
+        st = launch_seg_concat(n, c.n, Lkv, q_pos0 + c.t0, causal, sv, seg_idx, seg_score, seg_cnt, stride, n_ranges,
+                               cand_idx + r0 * cap, cand_score + r0 * cap, cand_count + r0, fail_list, fail_count,
+                               blk_flag, blk_rows, s);
+        if (st) return st;
+      }
+    }
+    st = launch_survivor_fallback(n, c.n, Lkv, q_pos0 + c.t0, causal, scratch, ld, shift + r0, row_stats + r0 * 3,
+                                  k_eff, cap, cand_idx + r0 * cap, cand_score + r0 * cap, cand_count + r0, fail_list,
+                                  fail_count, di->num_sms, di->err, s);
+    if (st) return st;
+  }
+  return GSA_OK;
+}
+
 }  // extern "C"
 
 // ---------------------------------------------------------------------------------------------

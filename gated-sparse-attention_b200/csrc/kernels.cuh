@@ -75,6 +75,40 @@ struct IdxArgs {
 };
 int64_t indexer_tc_stat_ranges(int64_t Lkv);  // key ranges per row of the tensor-core indexer
 
+// Rows of the fused survivor pass (the tensor-core indexer writes each row's survivors itself, in
+// segments, one per key range of kRangeKeys keys).  Host and device compute the same layout.
+struct SurvivorShape {
+  static constexpr int64_t kRangeKeys = 4096;  // keys of one range (= one indexer work item)
+  int32_t K;    // keys the final selection may need per row (k_eff)
+  int32_t cap;  // candidate row length
+  int32_t K14;  // survivors the threshold aims at per row: ceil(1.4 K)
+  __host__ __device__ static int64_t ranges(int64_t n) { return (n + kRangeKeys - 1) / kRangeKeys; }
+  // Room of one (row, range) for a row of n keys: the whole range where the row keeps every key
+  // (n <= cap); else four times the range's share of K14, plus 128, in multiples of 32.
+  __host__ __device__ int64_t seg_cap(int64_t n) const {
+    if (n <= cap) return kRangeKeys;
+    int64_t c = (4 * kRangeKeys * (int64_t)K14 + n - 1) / n;
+    c = (c + 31) / 32 * 32 + 128;
+    return c < kRangeKeys ? c : kRangeKeys;
+  }
+};
+
+// Launch modes of the tensor-core indexer (bf16, d_I 64): every score to the scratch; the row
+// statistics of every 16th key tile only (the survivor thresholds' estimate); the statistics and
+// each row's survivors written to its per-range segments (H_I = 8).
+constexpr int kTcScores = 0, kTcSample = 1, kTcEmit = 2;
+struct TcSurvivorArgs {
+  const int32_t* blk_mask = nullptr;   // kTcScores: query blocks to compute (NULL: all)
+  const double* samp_stats = nullptr;  // kTcEmit: [Lq, 3] sampled statistics of (score - shift)
+  int32_t* seg_idx = nullptr;          // kTcEmit: row r, range j at r * seg_stride + j * sv.seg_cap(n_r)
+  float* seg_score = nullptr;
+  int32_t* seg_cnt = nullptr;          // kTcEmit: [Lq, indexer_tc_stat_ranges(Lkv)]
+  int64_t seg_stride = 0;
+  SurvivorShape sv{};
+};
+int launch_indexer_tc_mode(const IdxArgs& a, int mode, const TcSurvivorArgs& x, int* err, cudaStream_t stream);
+constexpr int kTcQueryBlock8 = 32;     // query rows of one tensor-core indexer block at H_I = 8
+
 struct SdpaArgs {
   int64_t B, Lq, Lkv;
   int Hk;
@@ -222,6 +256,15 @@ int launch_threshold_candidates(int64_t R, int64_t Lq, int64_t n_cols, int64_t q
                                 int32_t K, int32_t cap, int32_t* cand_idx, float* cand_score, int32_t* cand_count,
                                 int32_t* fail_list, int32_t* fail_count, int32_t* seg_count, int num_sms, int* err,
                                 cudaStream_t stream);
+int launch_seg_concat(int64_t R, int64_t Lq, int64_t n_cols, int64_t q_pos0, int causal, const SurvivorShape& sv,
+                      const int32_t* seg_idx, const float* seg_score, const int32_t* seg_cnt, int64_t seg_stride,
+                      int64_t n_ranges, int32_t* cand_idx, float* cand_score, int32_t* cand_count,
+                      int32_t* fail_list, int32_t* fail_count, int32_t* blk_flag, int32_t blk_rows,
+                      cudaStream_t stream);
+int launch_survivor_fallback(int64_t R, int64_t Lq, int64_t n_cols, int64_t q_pos0, int causal,
+                             const float* scores, int64_t ld, const float* center, const double* stats, int32_t K,
+                             int32_t cap, int32_t* cand_idx, float* cand_score, int32_t* cand_count,
+                             int32_t* fail_list, int32_t* fail_count, int num_sms, int* err, cudaStream_t stream);
 int launch_select_finalize_warp(int64_t R, int32_t cand_ld, const int32_t* cand_idx, const float* cand_score,
                                 const int32_t* cand_count, const int32_t* k, int32_t* sel_idx, int64_t sel_ld,
                                 int32_t* sel_count, int num_sms, cudaStream_t stream);

@@ -974,6 +974,121 @@ int launch_threshold_candidates(int64_t R, int64_t Lq, int64_t n_cols, int64_t q
 }
 
 // ---------------------------------------------------------------------------------------------
+// Fused survivor pass, last step.  The tensor-core indexer wrote each row's survivors into one
+// segment per key range, in ascending key order; this joins a row's segments in range order
+// into its candidate row -- the ascending column order the streaming compaction writes.  A row
+// whose segments overflowed their room, or whose survivors number more than cap or fewer than
+// min(K, n), goes to fail_list and marks its query block for the exact recomputation (the
+// scores of the block into the scratch, then topk_fallback_kernel).  One warp per row.
+// ---------------------------------------------------------------------------------------------
+struct SegArgs {
+  int64_t R, Lq, n_cols, q_pos0;
+  int causal;
+  SurvivorShape sv;
+  const int32_t* seg_idx;
+  const float* seg_score;
+  const int32_t* seg_cnt;
+  int64_t seg_stride, n_ranges;
+  int32_t* idx;
+  float* score;
+  int32_t* count;
+  int32_t* fail_list;
+  int32_t* fail_count;
+  int32_t* blk_flag;  // [R / Lq sequences][blks_per_seq] query blocks that hold a failed row
+  int32_t blk_rows;
+  int64_t blks_per_seq;
+};
+
+constexpr int kConcatThreads = 256;
+
+__global__ void __launch_bounds__(kConcatThreads) seg_concat_kernel(SegArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = ((int64_t)blockIdx.x * kConcatThreads + threadIdx.x) >> 5;
+  if (r >= a.R) return;
+  const int64_t t = r % a.Lq;
+  int64_t n = a.causal ? min(a.n_cols, a.q_pos0 + t + 1) : a.n_cols;
+  n = n < 0 ? 0 : n;
+  const int64_t nr = SurvivorShape::ranges(n);
+  const int64_t room = a.sv.seg_cap(n);
+  const int32_t* cnt = a.seg_cnt + r * a.n_ranges;
+  uint32_t total = 0;
+  bool over = false;
+  for (int64_t j0 = 0; j0 < nr; j0 += 32) {
+    const int32_t c = j0 + lane < nr ? cnt[j0 + lane] : 0;
+    over |= c < 0 || (int64_t)c > room;
+    total += __reduce_add_sync(0xffffffffu, (uint32_t)max(c, 0));
+  }
+  over = __any_sync(0xffffffffu, over);
+  const int64_t need = min((int64_t)a.sv.K, n);
+  if (over || (int64_t)total > a.sv.cap || (int64_t)total < need) {
+    if (lane == 0) {
+      a.fail_list[atomicAdd(a.fail_count, 1)] = (int32_t)r;
+      a.blk_flag[(r / a.Lq) * a.blks_per_seq + t / a.blk_rows] = 1;
+      a.count[r] = 0;
+    }
+    return;
+  }
+  int32_t* oi = a.idx + r * a.sv.cap;
+  float* os = a.score + r * a.sv.cap;
+  uint32_t base = 0;
+  for (int64_t j0 = 0; j0 < nr; j0 += 32) {
+    const uint32_t c = j0 + lane < nr ? (uint32_t)cnt[j0 + lane] : 0u;
+    uint32_t x = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    const uint32_t excl = base + x - c;
+    const int jn = (int)min((int64_t)32, nr - j0);
+    for (int jj = 0; jj < jn; ++jj) {
+      const uint32_t cj = __shfl_sync(0xffffffffu, c, jj);
+      const uint32_t oj = __shfl_sync(0xffffffffu, excl, jj);
+      const int64_t src = r * a.seg_stride + (j0 + jj) * room;
+      for (uint32_t i = lane; i < cj; i += 32) {
+        oi[oj + i] = a.seg_idx[src + i];
+        os[oj + i] = a.seg_score[src + i];
+      }
+    }
+    base += __shfl_sync(0xffffffffu, x, 31);
+  }
+  if (lane == 0) a.count[r] = (int32_t)total;
+}
+
+int launch_seg_concat(int64_t R, int64_t Lq, int64_t n_cols, int64_t q_pos0, int causal, const SurvivorShape& sv,
+                      const int32_t* seg_idx, const float* seg_score, const int32_t* seg_cnt, int64_t seg_stride,
+                      int64_t n_ranges, int32_t* cand_idx, float* cand_score, int32_t* cand_count,
+                      int32_t* fail_list, int32_t* fail_count, int32_t* blk_flag, int32_t blk_rows,
+                      cudaStream_t stream) {
+  if (R == 0) return GSA_OK;
+  if (R > 0x7fffffffLL || Lq <= 0 || blk_rows <= 0) return GSA_ERR_BAD_ARG;
+  SegArgs a{R, Lq, n_cols, q_pos0, causal, sv, seg_idx, seg_score, seg_cnt, seg_stride, n_ranges,
+            cand_idx, cand_score, cand_count, fail_list, fail_count, blk_flag, blk_rows,
+            (Lq + blk_rows - 1) / blk_rows};
+  const int64_t grid = (R * 32 + kConcatThreads - 1) / kConcatThreads;
+  seg_concat_kernel<<<(unsigned)grid, kConcatThreads, 0, stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? GSA_OK : GSA_ERR_LAUNCH;
+}
+
+// Exact selection of the rows in fail_list from the scores in the scratch (rows of failed query
+// blocks recomputed there).
+int launch_survivor_fallback(int64_t R, int64_t Lq, int64_t n_cols, int64_t q_pos0, int causal,
+                             const float* scores, int64_t ld, const float* center, const double* stats, int32_t K,
+                             int32_t cap, int32_t* cand_idx, float* cand_score, int32_t* cand_count,
+                             int32_t* fail_list, int32_t* fail_count, int num_sms, int* err, cudaStream_t stream) {
+  if (R == 0) return GSA_OK;
+  if (R > 0x7fffffffLL || ld % 4 != 0 || (reinterpret_cast<uintptr_t>(scores) % 16) != 0) return GSA_ERR_BAD_ARG;
+  CmpArgs a{R, Lq, n_cols, q_pos0, causal, scores, ld, center, stats, K, cap, cand_idx, cand_score, cand_count,
+            fail_list, fail_count, err};
+  const size_t dyn = 2 * kCap * sizeof(float) + kCap + kRankCap * sizeof(uint32_t);
+  if (cudaFuncSetAttribute(topk_fallback_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn) !=
+      cudaSuccess)
+    return GSA_ERR_LAUNCH;
+  topk_fallback_kernel<<<(unsigned)num_sms, kSelThreads, dyn, stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? GSA_OK : GSA_ERR_LAUNCH;
+}
+
+// ---------------------------------------------------------------------------------------------
 // Final selection, one warp per row (used when no selection mask is asked for).  The k_t best
 // of a row's m candidates (ascending columns), ties lower column first, written in ascending
 // column order:

@@ -90,6 +90,9 @@ SIGNATURES = {
     "gsa_survivors_workspace_size": [I64, I64],
     "gsa_indexer_survivors": [P, INT, I64, I64, I64, I64, INT, P, I64, I64, P, I64, I64, P, P, F32, P,
                               I32, I32, P, P, P, P, I64, P, I64, P],
+    "gsa_survivors_fused_workspace_size": [I64, I64, I32, I32],
+    "gsa_indexer_survivors_fused": [P, INT, I64, I64, I64, I64, INT, P, I64, I64, P, I64, I64, P, P, F32, P,
+                                    I32, I32, P, P, P, P, I64, P, I64, P],
     "gsa_indexer_select_static": [P, INT, I64, I64, I64, I64, INT, P, I64, I64, P, I64, I64, P, P, F32,
                                   P, I32, P, P, P, P, P],
     "gsa_sparse_sdpa_probs": [P, INT, I64, I64, I64, P, P, I64, I64, P, P, I64, I64, P, F32, P, P],
@@ -100,6 +103,7 @@ SIGNATURES = {
 }
 _RESTYPES = {"gsa_version": C.c_char_p, "gsa_workspace_size": C.c_int64,
              "gsa_survivors_workspace_size": C.c_int64, "gsa_sdpa_workspace_size": C.c_int64,
+             "gsa_survivors_fused_workspace_size": C.c_int64,
              "gsa_decode_workspace_size": C.c_int64, "gsa_proj_fused_rows": C.c_int64}
 
 _lib = None

@@ -1084,7 +1084,8 @@ class GatedSparseAttention(nn.Module):
                            idx_segments=list(segs) if len(segs) > 1 else [(0, L, q_pos0)])
             capture.update(dims=dims, q=q, k=k_all, v=v_all, sel=sel, cnt=cnt, gate=g1, k_t=kt, attn=attn,
                            var=var, var_total=total,
-                           n_chunks=n_chunks, candidate_path="survivors" if survivors else "exact")
+                           n_chunks=n_chunks, candidate_path="survivors" if survivors else "exact",
+                           survivor_pass=ops.last_survivor_path if survivors else None)
 
         weights = None
         if output_attentions:

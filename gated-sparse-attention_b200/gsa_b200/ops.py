@@ -18,6 +18,7 @@ from ._lib import ACT, DTYPE_BF16, DTYPE_F32, Dims, ProjLayout, TopkParams
 DEBUG = os.environ.get("GSA_DEBUG", "0") == "1"
 # number of (indexer, top-k) chunk launches of the last indexer_select call
 last_chunk_count = 0
+last_survivor_path = None  # "fused" or "materialised": the survivor pass the last call took
 # bound of the chunk score scratch of the layer's indexer pass (fewer, larger chunks amortise
 # each launch's tail; the scratch lives only during the call)
 SCORE_CHUNK_BYTES = 4 << 30
@@ -531,20 +532,48 @@ def survivors_eligible(dims: Dims, k_eff: int, has_shift: bool) -> bool:
     return has_shift and dims.idx_act == ACT["sigmoid"] and 2 * SURVIVOR_CAP >= 3 * k_eff + 2048
 
 
+# True (or GSA_SURVIVOR_PASS=fused in the environment): the survivor pass without the score
+# matrix (gsa_indexer_survivors_fused) where it applies.  Same results, bit for bit; it moves
+# 68 GB less through HBM per 128K-token forward but is slower on B200 (the survivor emission
+# lengthens the indexer's issue-bound epilogue: 42.0 vs 22.3 ms, more than the streaming
+# compaction it replaces), so the materialised pass is the default.
+FUSED_SURVIVORS = os.environ.get("GSA_SURVIVOR_PASS", "materialised") == "fused"
+
+
+def fused_survivors_eligible(dims: Dims, qI, kI) -> bool:
+    """Whether gsa_indexer_survivors_fused applies: the bf16 tensor-core indexer at H_I = 8,
+    d_I = 64 with 16-byte aligned qI / kI rows."""
+    return (qI.dtype == torch.bfloat16 and kI.dtype == torch.bfloat16 and dims.n_idx_heads == 8
+            and dims.d_idx == 64 and dims.idx_act == ACT["sigmoid"]
+            and qI.data_ptr() % 16 == 0 and kI.data_ptr() % 16 == 0
+            and (qI.stride(1) * 2) % 16 == 0 and (kI.stride(1) * 2) % 16 == 0
+            and qI.stride(2) == 1 and kI.stride(2) == 1)
+
+
 def indexer_survivors(dims: Dims, qI, kI, w, bias, scale: float, shift, k_eff: int, q_pos0: int = 0,
-                      causal: bool = True, chunk_rows: int | None = None, row_stats=None, out=None):
+                      causal: bool = True, chunk_rows: int | None = None, row_stats=None, out=None,
+                      fused: bool | None = None):
     """Indexer + threshold survivors for all rows, chunk by chunk.  Returns (cand_idx [R, cap],
     cand_score [R, cap], cand_count [R], row_stats): each row's candidates hold its k_eff best
-    scores (and usually more), in ascending column order."""
+    scores (and usually more), in ascending column order.  ``fused`` (default: FUSED_SURVIVORS;
+    only where eligible) writes the survivors from the indexer itself instead of streaming a
+    score matrix through HBM."""
     _cuda(qI, kI, w, bias, shift)
     B, Lq, _ = qI.shape
     Lkv = kI.shape[1]
     R = B * Lq
     dev = qI.device
     cap = SURVIVOR_CAP
-    global last_chunk_count
+    if fused is None:
+        fused = FUSED_SURVIVORS
+    fused = fused and fused_survivors_eligible(dims, qI, kI)
+    global last_chunk_count, last_survivor_path
+    last_survivor_path = "fused" if fused else "materialised"
     chunk_rows, last_chunk_count = _chunking(B, Lq, Lkv, chunk_rows)
-    ws_bytes = _lib.lib().gsa_survivors_workspace_size(chunk_rows, Lkv)
+    if fused:
+        ws_bytes = _lib.lib().gsa_survivors_fused_workspace_size(chunk_rows, Lkv, int(k_eff), cap)
+    else:
+        ws_bytes = _lib.lib().gsa_survivors_workspace_size(chunk_rows, Lkv)
     workspace = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
     if out is not None:
         cand_idx, cand_score, cand_count = out
@@ -557,7 +586,8 @@ def indexer_survivors(dims: Dims, qI, kI, w, bias, scale: float, shift, k_eff: i
         row_stats = torch.zeros(R, 3, device=dev, dtype=torch.float64)
     w = w.reshape(R, -1).float().contiguous()
     bias = bias.float().contiguous()
-    _lib.call("gsa_indexer_survivors", C.byref(dims), dtype_code(qI.dtype), B, Lq, Lkv, q_pos0, int(causal),
+    _lib.call("gsa_indexer_survivors_fused" if fused else "gsa_indexer_survivors", C.byref(dims),
+              dtype_code(qI.dtype), B, Lq, Lkv, q_pos0, int(causal),
               _p(qI), qI.stride(1), qI.stride(0), _p(kI), kI.stride(1), kI.stride(0), _p(w), _p(bias),
               float(scale), _p(shift), int(k_eff), cap, _p(cand_idx), _p(cand_score), _p(cand_count),
               _p(row_stats), chunk_rows, _p(workspace), ws_bytes, _stream())

@@ -373,6 +373,37 @@ int gsa_indexer_survivors(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq
                           void* workspace, int64_t workspace_bytes, gsa_stream_t stream);
 
 /*
+ * gsa_indexer_survivors without the score matrix: same arguments, same outputs, bit for bit
+ * (candidates, their order and count, row_stats).  Each chunk runs the tensor-core indexer
+ * three times:
+ *   1. the row statistics over every 16th key tile only, from which each row's threshold is
+ *      its normal quantile of 1.4 k_eff / n_r (1/16 of the indexer's work);
+ *   2. the full pass: the row statistics, and every score at or above the row's threshold
+ *      written to the row's segment of that key range (4096 keys), in ascending column order;
+ *      the segments are then joined into cand_idx / cand_score;
+ *   3. a row whose survivors are fewer than min(k_eff, n_r), more than cap, or more than its
+ *      segment's room has its 32-row query block's scores computed into the workspace and is
+ *      selected exactly (its k_eff best), as gsa_indexer_survivors does.
+ * Since every row's candidates hold all of its scores at or above a threshold below its k_eff-th
+ * best, they hold its k_eff best, as in gsa_indexer_survivors; step 3 runs no block when no row
+ * fails.  Supported: bf16, n_idx_heads 8, d_idx 64, sigmoid, 16-byte aligned qI / kI rows;
+ * otherwise GSA_ERR_UNSUPPORTED (use gsa_indexer_survivors).
+ *   workspace: gsa_survivors_fused_workspace_size(chunk_rows, Lkv, k_eff, cap) bytes.
+ * ("Gated lightning indexer" scores and the candidate stage: gated_indexer.py:106-155,
+ * adaptive_topk.py:138-177.)
+ */
+int64_t gsa_survivors_fused_workspace_size(int64_t chunk_rows, int64_t n_cols, int32_t k_eff,
+                                           int32_t cap);
+int gsa_indexer_survivors_fused(const gsa_dims* dims, int dtype, int64_t B, int64_t Lq,
+                                int64_t Lkv, int64_t q_pos0, int causal, const void* qI,
+                                int64_t qi_ld, int64_t qi_bstride, const void* kI, int64_t ki_ld,
+                                int64_t ki_bstride, const float* w, const float* bias,
+                                float scale, const float* shift, int32_t k_eff, int32_t cap,
+                                int32_t* cand_idx, float* cand_score, int32_t* cand_count,
+                                double* row_stats, int64_t chunk_rows, void* workspace,
+                                int64_t workspace_bytes, gsa_stream_t stream);
+
+/*
  * gsa_indexer_select without a workspace argument: it allocates no device memory.  No
  * counterpart in the reference (whose indexer materialises the score matrix with torch).
  *
