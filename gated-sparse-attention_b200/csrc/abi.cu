@@ -605,15 +605,16 @@ int gsa_indexer_survivors_fused(const gsa_dims* dims, int dtype, int64_t B, int6
   if (B * Lq == 0 || Lkv == 0) return GSA_OK;
   if (!shift || !row_stats || !cand_idx || !cand_score || !cand_count || !w || !bias || !qI || !kI)
     return GSA_ERR_BAD_ARG;
-  if (dims->idx_act != GSA_ACT_SIGMOID || 2 * (int64_t)cap < 3 * (int64_t)k_eff + 2048) return GSA_ERR_UNSUPPORTED;
-  {
-    IdxArgs probe{dtype, Lq, Lkv, q_pos0, causal, 0, dims->n_idx_heads, dims->d_idx, dims->idx_act,
-                  qI, qi_ld, qi_bstride, kI, ki_ld, ki_bstride, w, bias, scale, shift, nullptr, 0, row_stats};
-    if (dims->n_idx_heads != 8 || !indexer_tc_eligible(probe)) return GSA_ERR_UNSUPPORTED;
-  }
+  if (dims->idx_act != GSA_ACT_SIGMOID || 2 * (int64_t)cap < 3 * (int64_t)k_eff + 2048 || dims->n_idx_heads != 8)
+    return GSA_ERR_UNSUPPORTED;
   if (!workspace || !aligned(workspace, 256) ||
       workspace_bytes < gsa_survivors_fused_workspace_size(chunk_rows, Lkv, k_eff, cap))
     return GSA_ERR_WORKSPACE;
+  {
+    IdxArgs probe{dtype, Lq, Lkv, q_pos0, causal, 0, dims->n_idx_heads, dims->d_idx, dims->idx_act,
+                  qI, qi_ld, qi_bstride, kI, ki_ld, ki_bstride, w, bias, scale, shift, nullptr, 0, row_stats};
+    if (!indexer_tc_eligible(probe)) return GSA_ERR_UNSUPPORTED;
+  }
   DeviceInfo dinfo, *di = &dinfo;
   int st = device_info(di);
   if (st) return st;

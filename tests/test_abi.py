@@ -94,6 +94,54 @@ def test_survivor_entry_points_validate_before_any_launch():
     assert lib.gsa_select_finalize(4, 8, p, p, p, p, p, 0, p, None, None) == 1   # sel_ld < 1
 
 
+def test_fused_survivor_entry_points_validate_before_any_launch():
+    """gsa_survivors_fused_workspace_size against its layout restated here (the segment area
+    brute-forced over every row length), and gsa_indexer_survivors_fused rejecting bad arguments
+    without touching the device (CPU only)."""
+    import ctypes as C
+
+    from gsa_b200 import _lib, ops
+
+    lib = _lib.lib()
+    a256 = lambda x: (x + 255) // 256 * 256
+
+    def seg_cap(n, K, cap):
+        if n <= cap:
+            return 4096
+        c = (4 * 4096 * ((14 * K + 9) // 10) + n - 1) // n
+        return min(4096, (c + 31) // 32 * 32 + 128)
+
+    for chunk, n_cols, K, cap in [(16, 1000, 64, 8192), (8192, 131072, 4096, 8192), (300, 50000, 1024, 4096)]:
+        stride = max((n + 4095) // 4096 * seg_cap(n, K, cap) for n in range(1, n_cols + 1))
+        ranges = (n_cols + 4095) // 4096
+        want = (lib.gsa_survivors_workspace_size(chunk, n_cols) + a256(chunk * 24) + a256(chunk * ranges * 4)
+                + 2 * a256(chunk * stride * 4) + a256(chunk * 4 + 4))
+        assert lib.gsa_survivors_fused_workspace_size(chunk, n_cols, K, cap) == want, (chunk, n_cols, K, cap)
+    assert lib.gsa_survivors_fused_workspace_size(0, 1000, 64, 8192) == 0
+    assert lib.gsa_survivors_fused_workspace_size(16, 1000, 0, 8192) == 0
+    assert lib.gsa_survivors_fused_workspace_size(16, 1000, 64, 32) == 0
+
+    dims = ops.make_dims(4096, 32, 8, 128, 8, 64)
+    relu = ops.make_dims(4096, 32, 8, 128, 8, 64, idx_act="relu")
+    hi4 = ops.make_dims(4096, 32, 8, 128, 4, 64)
+    p = C.c_void_p(16)  # a stand-in pointer: every case below returns before using it
+
+    def call(d, k_eff, cap, shift=p, ws_bytes=1 << 40, chunk=16, B=1, Lq=100):
+        return lib.gsa_indexer_survivors_fused(C.byref(d), 1, B, Lq, 1000, 0, 1, p, 512, 0, p, 64, 0, p, p, 0.125,
+                                               shift, k_eff, cap, p, p, p, p, chunk, p, ws_bytes, None)
+
+    assert call(dims, 0, 8192) == 1                 # k_eff < 1
+    assert call(dims, 4096, 1024) == 1              # cap < k_eff
+    assert call(dims, 64, 8192, shift=None) == 1    # the row centre is required
+    assert call(dims, 64, 8192, chunk=0) == 1       # no chunk rows
+    assert call(dims, 64, 8192, B=-1) == 1
+    assert call(relu, 64, 8192) == 2                # thresholds need the sigmoid indexer
+    assert call(hi4, 64, 8192) == 2                 # the emitting indexer takes 8 heads
+    assert call(dims, 6000, 8192) == 2              # no room above 1.5 k_eff in the cap
+    assert call(dims, 64, 8192, ws_bytes=100) == 3  # workspace too small
+    assert call(dims, 64, 8192, Lq=0) == 0          # empty work is a no-op success
+
+
 def test_cache_entry_points_validate_before_any_launch():
     """gsa_proj_epilogue_cache and gsa_sparse_sdpa_strided reject a batch stride that cannot
     hold the sequence, without touching the device (CPU only)."""
