@@ -241,7 +241,7 @@ def indexer_roofline(cap, cfg, pk, chunk_bytes=4 << 30, reps=2):
     achieved = flops / (ms / 1e3) / 1e12
     tanh_peak = 148 * 16 * pk.get("sm_max_mhz", 1965.0) * 1e6
     tanh_rate = HI * pairs / (ms / 1e3)
-    return {"kernel": "gsa::tc::indexer_tc_kernel<8>", "bound": "tensor", "achieved": round(achieved, 1),
+    return {"kernel": "gsa::tc::indexer_tc_kernel<8, 0>", "bound": "tensor", "achieved": round(achieved, 1),
             "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": round(achieved / pk["bf16_tflops"], 4),
             "algorithmic_flops": flops, "kernel_ms": round(ms, 3), "launches": len(launches),
             "epilogue": {"bound": "mufu", "tanh_per_s": tanh_rate, "peak_tanh_per_s": tanh_peak,
