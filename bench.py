@@ -90,18 +90,26 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
+    def __init__(self, gpu_index: int, period_ms: int = 50):
         self.gpu = gpu_index
+        self.period_ms = period_ms
         self.proc = None
         self.lines = []
+        self.skip = 0
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", str(self.period_ms)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            # nvidia-smi takes a while to start: wait for its first sample, so that the sampling
+            # loop is running when the timed region begins, and count only the samples after it
+            t0 = time.time()
+            while not self.lines and self.proc.poll() is None and time.time() - t0 < 5.0:
+                time.sleep(0.01)
+            self.skip = len(self.lines)
         except OSError:
             self.proc = None
         return self
@@ -121,7 +129,7 @@ class ClockSampler:
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in self.lines[self.skip:]:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
