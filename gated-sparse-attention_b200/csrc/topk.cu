@@ -670,7 +670,7 @@ __device__ __forceinline__ unsigned long long cmp_scan4(unsigned long long v, un
   return off + x - v;
 }
 
-__global__ void __launch_bounds__(kCmpThreads) threshold_compact_kernel(CmpArgs a) {
+__global__ void __launch_bounds__(kCmpThreads, 2) threshold_compact_kernel(CmpArgs a) {
   extern __shared__ __align__(128) uint8_t cmp_smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(cmp_smem);
   uint64_t* empty = full + kCmpStages;
@@ -738,17 +738,29 @@ __global__ void __launch_bounds__(kCmpThreads) threshold_compact_kernel(CmpArgs 
       const int32_t nn = (int32_t)n;
       uint32_t flags = 0;
       unsigned long long counts = 0;
+      if (c0 + kCmpChunk <= n && tau > -INFINITY) {
+        // a whole chunk under a finite threshold (the common case): x >= tau alone excludes
+        // -inf and NaN, and every column is inside the row
 #pragma unroll
-      for (int q = 0; q < kCmpPer / 4; ++q) {
-        const int32_t col0 = (int32_t)c0 + q * 4 * kCmpConsumers + 4 * (int32_t)threadIdx.x;
-        uint32_t fq = 0;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float x = v[4 * q + e];
-          if (col0 + e < nn && x >= tau && x > -INFINITY) fq |= 1u << e;  // NaN fails both
+        for (int q = 0; q < kCmpPer / 4; ++q) {
+          const uint32_t fq = (uint32_t)(v[4 * q] >= tau) | ((uint32_t)(v[4 * q + 1] >= tau) << 1) |
+                              ((uint32_t)(v[4 * q + 2] >= tau) << 2) | ((uint32_t)(v[4 * q + 3] >= tau) << 3);
+          flags |= fq << (4 * q);
+          counts |= (unsigned long long)__popc(fq) << (16 * q);
         }
-        flags |= fq << (4 * q);
-        counts |= (unsigned long long)__popc(fq) << (16 * q);
+      } else {
+#pragma unroll
+        for (int q = 0; q < kCmpPer / 4; ++q) {
+          const int32_t col0 = (int32_t)c0 + q * 4 * kCmpConsumers + 4 * (int32_t)threadIdx.x;
+          uint32_t fq = 0;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float x = v[4 * q + e];
+            if (col0 + e < nn && x >= tau && x > -INFINITY) fq |= 1u << e;  // NaN fails both
+          }
+          flags |= fq << (4 * q);
+          counts |= (unsigned long long)__popc(fq) << (16 * q);
+        }
       }
       // release the slot only once every lane's loads have returned (the flags consume them):
       // the next bulk copy into it must not overtake a shared-memory read still in flight
