@@ -10,7 +10,7 @@ every score to a scratch, then the streaming compaction) on the same inputs:
   k_eff-th best, so the same k_t best with the same lower-column-first ties.
 
 Cases: thresholded rows over several chunks; two sequences in one chunk; a query offset; rows
-short enough to keep every key; and planted keys whose sampled statistics mislead the threshold
+short enough to keep every key; non-causal rows; and planted keys whose sampled statistics mislead the threshold
 (too many survivors, too few, one key range holding more than its segment's room), so that rows
 fall back to the exact selection from their recomputed query block -- the test reads the failed-
 row count to make sure they did.  The gated indexer scores are gated_indexer.py:114-153; the
@@ -76,14 +76,15 @@ def _fused_fail_count(ops, dims, qI, kI, w, bias, scale, shift, q_pos0, chunk):
     return int(ws[off:off + 4].view(torch.int32).item())
 
 
-@pytest.mark.parametrize("B,Lq,Lkv,q_pos0,chunk,plant", [
-    (1, 20000, 20000, 0, 6000, None),            # thresholded rows over four chunks
-    (2, 9000, 9000, 0, 18000, None),             # two sequences in one chunk; most rows keep every key
-    (1, 3000, 40000, 37000, 3000, None),         # query offset: long rows only
-    (1, 2048, 20000, 17952, 2048, "unsampled_tie"),  # sampled statistics miss the tied keys
-    (1, 1024, 100000, 98976, 1024, "one_range"),  # one range holds the top k_eff: segment overflow
+@pytest.mark.parametrize("B,Lq,Lkv,q_pos0,chunk,plant,causal", [
+    (1, 20000, 20000, 0, 6000, None, True),            # thresholded rows over four chunks
+    (2, 9000, 9000, 0, 18000, None, True),             # two sequences in one chunk; most rows keep every key
+    (1, 3000, 40000, 37000, 3000, None, True),         # query offset: long rows only
+    (2, 700, 30000, 0, 500, None, False),              # non-causal rows, two sequences in 500-row chunks
+    (1, 2048, 20000, 17952, 2048, "unsampled_tie", True),  # sampled statistics miss the tied keys
+    (1, 1024, 100000, 98976, 1024, "one_range", True),  # one range holds the top k_eff: segment overflow
 ])
-def test_fused_survivors_match_materialised(cuda_ok, B, Lq, Lkv, q_pos0, chunk, plant):
+def test_fused_survivors_match_materialised(cuda_ok, B, Lq, Lkv, q_pos0, chunk, plant, causal):
     from gsa_b200 import ops
 
     dims = ops.make_dims(4096, 32, 8, 128, 8, 64)
@@ -91,17 +92,17 @@ def test_fused_survivors_match_materialised(cuda_ok, B, Lq, Lkv, q_pos0, chunk, 
     R = B * Lq
     scale = 1 / math.sqrt(64)
     t = torch.arange(R) % Lq
-    n = torch.clamp(t + q_pos0 + 1, max=Lkv)
+    n = torch.clamp(t + q_pos0 + 1, max=Lkv) if causal else torch.full((R,), Lkv)
     g = torch.Generator().manual_seed(7)
     kt = torch.minimum(torch.randint(1, K_EFF + 1, (R,), generator=g), n).int()
     kt[::5] = torch.minimum(torch.tensor(K_EFF), n[::5]).int()
     kt = kt.to(DEV)
 
     mi, ms, mc, mst = ops.indexer_survivors(dims, qI, kI, w, bias, scale, shift, K_EFF, q_pos0=q_pos0,
-                                            chunk_rows=chunk, fused=False)
+                                            causal=causal, chunk_rows=chunk, fused=False)
     assert ops.last_survivor_path == "materialised"
     fi, fs, fc, fst = ops.indexer_survivors(dims, qI, kI, w, bias, scale, shift, K_EFF, q_pos0=q_pos0,
-                                            chunk_rows=chunk, fused=True)
+                                            causal=causal, chunk_rows=chunk, fused=True)
     assert ops.last_survivor_path == "fused"
     m_sel, m_cnt, _ = ops.select_finalize(mi, ms, mc, kt, sel_ld=K_EFF)
     f_sel, f_cnt, _ = ops.select_finalize(fi, fs, fc, kt, sel_ld=K_EFF)
@@ -121,7 +122,7 @@ def test_fused_survivors_match_materialised(cuda_ok, B, Lq, Lkv, q_pos0, chunk, 
     for r in rows:
         b, tt = divmod(r, Lq)
         sc = ops.indexer_scores(dims, qI[b:b + 1, tt:tt + 1], kI[b:b + 1], w.view(B, Lq, -1)[b:b + 1, tt:tt + 1],
-                                bias, scale, q_pos0=q_pos0 + tt, causal=True)[0].cpu()
+                                bias, scale, q_pos0=q_pos0 + tt, causal=causal)[0].cpu()
         c = int(fc_c[r])
         cols = fi_c[r, :c].long()
         assert bool((cols[1:] > cols[:-1]).all()), r
