@@ -25,6 +25,14 @@
 // warps 2..17 = epilogue (four warps per TMEM lane quarter, each taking a quarter of the tokens).
 // Work item (CTA) = one query block x a range of up to kTilesPerCta key tiles; causal tiles
 // beyond the block's last query are never visited.  Every wait is bounded.
+//
+// Three instantiations share this pipeline (Mode): kScores stores every score (and the row
+// statistics when asked for); kSample visits every kSampleStride-th key tile and keeps only the
+// statistics (the survivor thresholds' estimate); kEmit keeps the statistics and writes the scores
+// at or above each row's threshold to the row's segment of the work item's key range, in key
+// order, the four lane-quarter warps of a token group exchanging their per-tile counts through
+// shared memory.  kEmit serves gsa_indexer_survivors_fused and has a loop of its own, so that the
+// other two modes carry none of its code.
 #include "kernels.cuh"
 #include "tcgen05.cuh"
 
