@@ -595,9 +595,9 @@ __global__ void __launch_bounds__(kSelThreads) select_finalize_kernel(
 // exactly by topk_fallback_kernel.  Either way the row's candidates hold its K best scores, in
 // ascending column order, which is all the final selection needs.
 //
-// Persistent CTAs: one producer warp streams each row in 16 KiB chunks through a 4-stage
-// shared-memory ring with 1-D bulk copies (the rows are contiguous), continuing across rows,
-// so the scores arrive at HBM rate while 8 consumer warps compact.  A chunk's survivors are
+// Persistent CTAs, three per SM: one producer warp streams each row in 16 KiB chunks through a
+// 3-stage shared-memory ring with 1-D bulk copies (the rows are contiguous), continuing across
+// rows, so the scores arrive at HBM rate while 8 consumer warps compact.  A chunk's survivors are
 // compacted into shared memory first and then copied out with consecutive threads writing
 // consecutive positions (scattered per-thread stores cost ~9 sectors per request).  Consumers
 // synchronise on a named barrier that excludes the producer.  All waits are bounded.
@@ -606,9 +606,9 @@ constexpr int kCmpConsumers = 256;
 constexpr int kCmpThreads = kCmpConsumers + 32;
 constexpr int kCmpPer = 16;                              // scores per consumer thread per chunk
 constexpr int kCmpChunk = kCmpConsumers * kCmpPer;       // 4096 scores = 16 KiB
-constexpr int kCmpStages = 5;
+constexpr int kCmpStages = 3;
 constexpr float kSurvivorFactor = 1.25f;                 // survivors aimed at per needed key
-constexpr int kCmpSmem = 256 + kCmpStages * kCmpChunk * 4 + kCmpChunk * 8;  // ring + survivor staging
+constexpr int kCmpSmem = 256 + kCmpStages * kCmpChunk * 4 + kCmpChunk * 6;  // ring + survivor staging
 
 struct CmpArgs {
   int64_t R, Lq, n_cols, q_pos0;
@@ -670,14 +670,16 @@ __device__ __forceinline__ unsigned long long cmp_scan4(unsigned long long v, un
   return off + x - v;
 }
 
-__global__ void __launch_bounds__(kCmpThreads, 2) threshold_compact_kernel(CmpArgs a) {
+__global__ void __launch_bounds__(kCmpThreads, 3) threshold_compact_kernel(CmpArgs a) {
   extern __shared__ __align__(128) uint8_t cmp_smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(cmp_smem);
   uint64_t* empty = full + kCmpStages;
   unsigned long long* wsb = reinterpret_cast<unsigned long long*>(empty + kCmpStages);  // 2 x 8
   float* stage = reinterpret_cast<float*>(cmp_smem + 256);
-  // a chunk's survivors as (column, score bits) pairs, in column order
-  uint2* keep = reinterpret_cast<uint2*>(stage + kCmpStages * kCmpChunk);  // [kCmpChunk]
+  // a chunk's survivors, in column order: their scores and their columns' offsets in the chunk
+  // (16 bits: three CTAs of three stages then fit one SM)
+  float* keep_val = stage + kCmpStages * kCmpChunk;                                 // [kCmpChunk]
+  uint16_t* keep_off = reinterpret_cast<uint16_t*>(keep_val + kCmpChunk);          // [kCmpChunk]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kCmpStages; ++s) {
@@ -777,7 +779,8 @@ __global__ void __launch_bounds__(kCmpThreads, 2) threshold_compact_kernel(CmpAr
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           if (flags & (1u << (4 * q + e))) {
-            keep[pos] = make_uint2((uint32_t)(col0 + e), __float_as_uint(v[4 * q + e]));
+            keep_off[pos] = (uint16_t)(col0 + e - (int32_t)c0);
+            keep_val[pos] = v[4 * q + e];
             ++pos;
           }
         }
@@ -788,9 +791,8 @@ __global__ void __launch_bounds__(kCmpThreads, 2) threshold_compact_kernel(CmpAr
       const uint32_t lim = base >= (uint32_t)a.cap ? 0u : min(total, (uint32_t)a.cap - base);
       if (ok)
         for (uint32_t i = threadIdx.x; i < lim; i += kCmpConsumers) {
-          const uint2 e = keep[i];
-          oi[base + i] = (int32_t)e.x;
-          os[base + i] = __uint_as_float(e.y);
+          oi[base + i] = (int32_t)c0 + (int32_t)keep_off[i];
+          os[base + i] = keep_val[i];
         }
       base += total;
     }
