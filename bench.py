@@ -560,7 +560,9 @@ def run_ours(args, world, rank):
                                   ((f" (zigzag, {ZIGZAG_FOLDS} folds)" if zigzag else " (contiguous)")
                                    if world > 1 else ""),
                    "l2": (f"inputs larger than L2 (x {x_mib:.0f} MiB, K/V {kv_mib:.0f} MiB each)"
-                          if x_mib > 126 else f"x {x_mib:.0f} MiB: L2 not flushed between steps")},
+                          if x_mib > 126 else f"x {x_mib:.0f} MiB: L2 not flushed between steps"),
+                   "candidates": (f"{cap.get('survivor_pass')} survivors"
+                                  if cap.get("candidate_path") == "survivors" else "exact top-k")},
         "e2e": e2e, "roofline": roofline, "roofline_indexer": roofline_indexer, "roofline_proj": roofline_proj,
         "gpu_launches": launches_per_step * args.steps,
         "stages_ms": stages, "clocks": clocks,
