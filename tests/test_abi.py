@@ -142,6 +142,25 @@ def test_fused_survivor_entry_points_validate_before_any_launch():
     assert call(dims, 64, 8192, Lq=0) == 0          # empty work is a no-op success
 
 
+def test_fused_survivor_eligibility():
+    """ops.fused_survivors_eligible mirrors the C side's checks: bf16 q^I / k^I, 8 indexer heads
+    of 64, the sigmoid indexer, 16-byte aligned rows with a contiguous last dimension (CPU only)."""
+    import torch
+
+    from gsa_b200 import ops
+
+    dims = ops.make_dims(4096, 32, 8, 128, 8, 64)
+    qI = torch.zeros(1, 64, 512, dtype=torch.bfloat16)
+    kI = torch.zeros(1, 64, 64, dtype=torch.bfloat16)
+    assert ops.fused_survivors_eligible(dims, qI, kI)
+    assert not ops.fused_survivors_eligible(dims, qI.float(), kI.float())
+    assert not ops.fused_survivors_eligible(ops.make_dims(4096, 32, 8, 128, 4, 64), qI[..., :256], kI)
+    assert not ops.fused_survivors_eligible(ops.make_dims(4096, 32, 8, 128, 8, 64, idx_act="relu"), qI, kI)
+    assert not ops.fused_survivors_eligible(dims, qI, torch.zeros(1, 64, 65, dtype=torch.bfloat16)[..., 1:])
+    # a switch the caller can flip: the materialised pass unless asked otherwise
+    assert isinstance(ops.FUSED_SURVIVORS, bool)
+
+
 def test_cache_entry_points_validate_before_any_launch():
     """gsa_proj_epilogue_cache and gsa_sparse_sdpa_strided reject a batch stride that cannot
     hold the sequence, without touching the device (CPU only)."""
